@@ -1,0 +1,154 @@
+/* C-ABI of the B200-native Bolt-3 dual-field attention hot path.
+ *
+ * The reference implements this path in eager PyTorch (vsa_lm/config/bolt3.py); it has no FFI of
+ * its own. These entry points are what a binding of that module's hot loops calls instead: plain
+ * device pointers, int64 sizes/strides, a cudaStream_t passed as void*, an int status return.
+ * No entry point allocates device memory, throws, or synchronises the stream; all work is
+ * stream-ordered. bf16 arrays are passed as `void*` holding IEEE bfloat16 values.
+ *
+ * Array layouts (row-major, innermost last). A "chain" is one (sequence b, KV head h) pair,
+ * chain = b * HKV + h; a query head index is chain * G + g (head h*G + g of sequence b).
+ *   q_raw, q_rope : [B*H][Tq][HD] bf16         k_raw, k_rope, v : [B*HKV][Tk][HD] bf16
+ *   beta          : [B*HKV][Tk] fp32           eta              : [B*H][Tq] fp32
+ *   bank ak, av, ak_rope : [chains][S][HD] bf16; mass, util, pm : [chains][S] fp32;
+ *   act : [chains][S] uint8; m_res : [chains][HD][HD] fp32 (= the reference's states[li]);
+ *   n_filled : [chains] int32.
+ * Supported shapes: HD in {64, 128}, S = C = 128, n_sinks = 4, G = H / HKV in [1, 16].
+ */
+#ifndef BOLT3_H_
+#define BOLT3_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BOLT3_ABI_VERSION 1
+
+enum bolt3_status {
+  BOLT3_OK = 0,
+  BOLT3_ERR_ARG = 1,       /* null pointer where one is required, or a negative size */
+  BOLT3_ERR_SHAPE = 2,     /* unsupported HD / S / C / G / token count */
+  BOLT3_ERR_ALIGN = 3,     /* a pointer or stride is not 16-byte aligned */
+  BOLT3_ERR_CAPACITY = 4,  /* a buffer described by the arguments is too small */
+  BOLT3_ERR_CUDA = 5       /* a kernel launch or CUDA runtime call failed */
+};
+
+/* ---- Phase A epilogue: per-head RMSNorm (optional), RoPE, beta = sigmoid, eta = tanh.
+ * Replaces Bolt3Attn.head_qkv + rope + gates (vsa_lm/config/bolt3.py:59-66, 196-199;
+ * vsa_lm/surgery.py:43-53, 80-93) and the same lines of Bolt3Decoder.step (bolt3.py:346-350).
+ * Input `proj` is the output of ONE fused projection GEMM, token-major [B*T][ld] with columns
+ * [q (H*HD) | k (HKV*HD) | v (HKV*HD) | beta logits (HKV) | eta logits (H)].
+ * Output element (b, head, t) of a head-major array lives at
+ *   ((b * n_heads + head) * head_stride + t_off + t) * HD      (q_*: n_heads = H, k/v: HKV). */
+typedef struct bolt3_prep_args {
+  const void* proj; int64_t ld;       /* bf16 [B*T][ld] */
+  int B, T, H, HKV, HD;
+  const float* q_norm_w;              /* [HD] or NULL (no qk_norm) */
+  const float* k_norm_w;              /* [HD] or NULL */
+  float eps;
+  const float* inv_freq;              /* [HD/2] */
+  int64_t pos0;                       /* RoPE position of token t is pos0 + t */
+  void* q_raw; void* q_rope; int64_t q_head_stride; int64_t q_t_off;
+  float* eta; int64_t eta_head_stride; int64_t eta_t_off;
+  void* k_raw; void* k_rope; void* v; int64_t k_head_stride; int64_t k_t_off;
+  float* beta; int64_t beta_head_stride; int64_t beta_t_off;
+} bolt3_prep_args;
+int bolt3_prep(const bolt3_prep_args* a, void* stream);
+
+/* ---- Phase B: sequential consolidation scan, one CTA per chain.
+ * Runs `n_steps` consecutive _consolidate_functional calls (vsa_lm/config/bolt3.py:68-192) on
+ * every chain: fill path, or full path = attractor prediction, cosine match, merge, diversity
+ * eviction (torch.topk tie order reproduced exactly) and the Gershgorin-normalised delta rule
+ * into M_res. Step i consolidates the chunk of array tokens
+ *   [token0 + i*step_tokens + (i == 0 ? skip0 : 0), token0 + i*step_tokens + chunk_len)
+ * whose RoPE position is pos0 + token index. The bank is read from / written back to the state
+ * arrays (init_blank = 1 starts from the empty bank of bolt3.py:83-92). After each step the
+ * state the attention reads is optionally written to snapshot slot snap0 + i:
+ *   snap_ak_rope, snap_av [chains][snap_cap][S][HD] bf16; snap_mass [chains][snap_cap][S] fp32;
+ *   snap_act [chains][snap_cap][S] uint8; snap_m [chains][snap_cap][HD][HD] fp32.
+ * `ak_rope` (optional) receives RoPE(ak, pm) of the final bank. `status` (optional, device int)
+ * is OR-ed with 1 when a kernel-side bounds check of the tie-order emulation fires. */
+typedef struct bolt3_consolidate_args {
+  int n_chains, hkv, HD;
+  void* ak; void* av; void* ak_rope;
+  float* mass; float* util; float* pm; uint8_t* act; float* m_res; int32_t* n_filled;
+  int init_blank;
+  const void* kr; const void* kp; const void* v; const float* beta;
+  int64_t chain_tokens;               /* tokens between chains in kr / kp / v / beta */
+  int64_t token0; int64_t step_tokens; int skip0; int chunk_len; int64_t pos0; int n_steps;
+  const float* kappa; const float* gamma; const float* inv_freq;   /* [hkv], [hkv], [HD/2] */
+  void* snap_ak_rope; void* snap_av; float* snap_mass; uint8_t* snap_act; float* snap_m;
+  int64_t snap_cap; int64_t snap0;
+  int32_t* status;
+} bolt3_consolidate_args;
+int bolt3_consolidate(const bolt3_consolidate_args* a, void* stream);
+
+/* ---- Phase C: three-field softmax attention + fused M_res read-out epilogue.
+ * Replaces the chunk body of Bolt3Attn.forward (vsa_lm/config/bolt3.py:219-256) and the
+ * attention of Bolt3Decoder.step (bolt3.py:365-402): softmax over
+ * [n_sinks sinks | S attractors (RoPE at mean position, + kappa*log(mass), -inf if inactive) |
+ * causal local window], then y = bf16(bf16(P@V) + bf16(eta * RMSNorm(normalize(q_raw) @ M_res *
+ * (1 - gamma) / sqrt(HD)))). Query block r (blockIdx.x) holds query tokens [r*128, r*128+128) of
+ * q arrays with Tq tokens per head. Window keys are two segments (previous chunk, current chunk)
+ * of [chains][*][HD] arrays; a key at window position j is visible to query row i of the block
+ * iff j <= n_before + i.
+ *   prefill = 1: block r is chunk r of a sequence of Tq tokens held in k_rope / v (Tk = Tq);
+ *     segment 0 = chunk r-1, segment 1 = chunk r, sinks = tokens 0..3, bank = snapshot r-2.
+ *   prefill = 0: one query block (Tq <= 128 new tokens); segment pointers, lengths, sinks and the
+ *     bank (snapshot slot 0 of the snap_* arrays) are given explicitly. */
+typedef struct bolt3_attend_args {
+  int n_chains, hkv, G, HD;
+  const void* q_rope; const void* q_raw; const float* eta; int64_t Tq;
+  int prefill;
+  /* window segments (prefill: seg0_k = seg1_k = k_rope, seg*_v = v, chain_tokens = Tk) */
+  const void* seg0_k; const void* seg0_v; int64_t seg0_chain_tokens; int seg0_len;
+  const void* seg1_k; const void* seg1_v; int64_t seg1_chain_tokens; int seg1_len;
+  int len_before;                      /* keys of segment 1 that precede the first query */
+  const void* sink_k; const void* sink_v; int64_t sink_chain_tokens; int has_sinks;
+  /* attractor bank: [chains][snap_cap][S]... as written by bolt3_consolidate */
+  const void* bank_ak_rope; const void* bank_av; const float* bank_mass; const uint8_t* bank_act;
+  const float* bank_m; int64_t bank_cap; int has_bank;
+  const float* kappa;                  /* [hkv] */
+  const float* coef;                   /* [hkv]: (1 - gamma) / sqrt(HD), fp32 */
+  const float* res_w; float eps;       /* res_norm weight [HD] (fp32), eps */
+  void* y; int64_t y_tokens;           /* bf16 [B][y_tokens][H][HD]; row of query token t: t */
+} bolt3_attend_args;
+int bolt3_attend(const bolt3_attend_args* a, void* stream);
+
+/* Bytes of snapshot workspace bolt3_prefill_fwd needs for n_chains chains of T tokens. */
+size_t bolt3_prefill_workspace_size(int n_chains, int64_t T, int HD);
+
+/* ---- Phases B + C of Bolt3Attn.forward (vsa_lm/config/bolt3.py:194-274) for sequences of T
+ * tokens whose projections bolt3_prep has written (q_*: Tq = T, k_* / v / beta: Tk = T).
+ * Runs the consolidation scan (chunk i consolidated after chunk i+1 when chunk i+1 is full and
+ * not last, sinks = first 4 tokens) into caller-provided snapshot workspace, then the attention
+ * over all chunks. The final bank is written to the state arrays (which may be scratch). */
+typedef struct bolt3_prefill_args {
+  int B, T, H, HKV, HD;
+  const void* q_rope; const void* q_raw; const float* eta;
+  const void* k_raw; const void* k_rope; const void* v; const float* beta;
+  const float* kappa; const float* gamma; const float* coef; const float* inv_freq;
+  const float* res_w; float eps;
+  void* workspace; size_t workspace_bytes;
+  /* final bank (chains = B*HKV) */
+  void* ak; void* av; void* ak_rope; float* mass; float* util; float* pm; uint8_t* act;
+  float* m_res; int32_t* n_filled;
+  void* y;                            /* bf16 [B][T][H][HD] */
+  int32_t* status;
+} bolt3_prefill_args;
+int bolt3_prefill_fwd(const bolt3_prefill_args* a, void* stream);
+
+/* ---- utilities */
+int bolt3_abi_version(void);
+const char* bolt3_status_string(int status);
+/* Host-only: reorder indices 0..n-1 of `vals` into the order CPU torch.topk(vals, k, largest)
+ * returns (first k written to out_idx). Returns 0, or 1 if a bounds check fired. */
+int bolt3_topk_order_host(const float* vals, int n, int k, int largest, int32_t* out_idx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BOLT3_H_ */

@@ -1,0 +1,63 @@
+"""Shared helpers for the parity tests: seeded modules on the GPU and their CPU-oracle twins."""
+from __future__ import annotations
+
+import torch
+
+from oracle import Store, oracle_cfg
+from vsa_lm_b200 import Bolt3Attn
+from vsa_lm_b200.workloads import layer_cfg, make_input, make_params
+
+# Output tolerance of the north star: rtol 2e-2 in bf16. Elements near zero are held to an absolute
+# bound of 2e-2 times the output's RMS instead.
+RTOL = 2e-2
+ATOL_RMS = 2e-2
+# fp32 state tolerance (M_res, mass, pm, util)
+STATE_RTOL = 1e-4
+NEAR = 1e-3   # merge decisions within this distance of 0.88 / 0.80 may flip
+
+
+def bf16_module(cfg: dict, seed: int, device="cuda") -> Bolt3Attn:
+    m = Bolt3Attn(cfg)
+    m.load_state_dict(make_params(cfg, seed), strict=True)
+    return m.to(device=device, dtype=torch.bfloat16).eval()
+
+
+def oracle_params(m: Bolt3Attn) -> dict:
+    """The module's own (bf16) parameters on the CPU, for the oracle."""
+    return {k: v.detach().cpu() for k, v in m.state_dict().items()}
+
+
+def oracle_cfg_of(m: Bolt3Attn, cfg: dict) -> dict:
+    oc = oracle_cfg(cfg)
+    oc["inv_freq"] = m.rope.inv_freq.detach().float().cpu()
+    return oc
+
+
+def output_close(got: torch.Tensor, ref: torch.Tensor, what: str = "output") -> dict:
+    got, ref = got.float().cpu(), ref.float().cpu()
+    rms = ref.pow(2).mean().sqrt().item()
+    err = (got - ref).abs()
+    bound = RTOL * ref.abs() + ATOL_RMS * rms
+    bad = err > bound
+    info = dict(max_abs=err.max().item(), rms=rms, frac_bad=bad.float().mean().item(),
+                max_rel_rms=(err.max().item() / max(rms, 1e-30)))
+    assert not bad.any(), f"{what}: {int(bad.sum())} elements outside rtol {RTOL} / atol {ATOL_RMS}*rms: {info}"
+    return info
+
+
+def near_threshold(rec: dict) -> torch.Tensor:
+    """Chains whose merge decision has a cosine within NEAR of a threshold (flip allowed)."""
+    if rec.get("kind") != "full":
+        return torch.zeros(rec["score"].shape[0], dtype=torch.bool)
+    nk = (rec["best_sim_k"] - 0.88).abs() < NEAR
+    nv = (rec["sim_v"] - 0.80).abs() < NEAR
+    return (nk | nv).any(dim=-1)
+
+
+def inputs(shape: str, B: int, T: int, dup, seed: int = 1, device="cuda"):
+    cfg = layer_cfg(shape)
+    x = make_input(B, T, cfg["dim"], dup=dup, seed=seed)
+    return cfg, x.to(torch.bfloat16).float(), x.to(device=device, dtype=torch.bfloat16)
+
+
+BF16 = Store("bf16")

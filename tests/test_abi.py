@@ -1,0 +1,85 @@
+"""The C-ABI library loads on a CPU-only machine and exports what include/bolt3.h declares."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+from vsa_lm_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    txt = open(os.path.join(ROOT, "include", "bolt3.h")).read()
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(bolt3_\w+)\s*\(", txt, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_symbols()
+    assert len(names) >= 8
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in include/bolt3.h but not exported"
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+    assert lib.bolt3_abi_version() == 1
+    assert lib.bolt3_status_string(0) == b"ok"
+    assert b"shape" in lib.bolt3_status_string(2)
+
+
+def test_struct_sizes_are_c_layout():
+    # every pointer field is 8 bytes and aligned; the structs have no hidden padding surprises
+    for st in (_lib.PrepArgs, _lib.ConsolidateArgs, _lib.AttendArgs, _lib.PrefillArgs):
+        assert ctypes.sizeof(st) % 8 == 0
+
+
+def test_entry_points_reject_bad_arguments_without_a_gpu():
+    lib = _lib.load()
+    assert lib.bolt3_prep(None, None) == 1
+    assert lib.bolt3_consolidate(None, None) == 1
+    assert lib.bolt3_attend(None, None) == 1
+    assert lib.bolt3_prefill_fwd(None, None) == 1
+    a = _lib.ConsolidateArgs()
+    assert lib.bolt3_consolidate(ctypes.byref(a), None) == 1      # null state pointers
+    assert lib.bolt3_prefill_workspace_size(4, 1024, 96) == 0      # unsupported head dim
+
+
+def test_workspace_size_formula():
+    lib = _lib.load()
+    # T = 1024: 8 chunks -> 6 consolidations; per chain-snapshot: 2*S*HD*2 + S*4 + S + HD*HD*4
+    n = lib.bolt3_prefill_workspace_size(5, 1024, 64)
+    per = 2 * 128 * 64 * 2 + 128 * 4 + 128 + 64 * 64 * 4
+    assert per * 5 * 6 <= n <= per * 5 * 6 + 5 * 256
+    assert lib.bolt3_prefill_workspace_size(5, 256, 64) <= 5 * 256   # no consolidation at T = 2C
+
+
+def _emulated(vals, k, largest):
+    lib = _lib.load()
+    v = np.ascontiguousarray(vals, dtype=np.float32)
+    out = np.zeros(k, dtype=np.int32)
+    bad = lib.bolt3_topk_order_host(v.ctypes.data, len(v), k, int(largest), out.ctypes.data)
+    assert bad == 0
+    return out
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_topk_tie_order_matches_torch_cpu(seed):
+    """The kernels' tie-order emulation reproduces CPU torch.topk exactly, ties and NaNs included."""
+    g = torch.Generator().manual_seed(seed)
+    for trial in range(1500):
+        n = int(torch.randint(1, 260, (1,), generator=g))
+        if trial % 3 == 0:
+            n = 128
+        k = n if trial % 4 == 0 else int(torch.randint(1, n + 1, (1,), generator=g))
+        levels = int(torch.randint(1, 9, (1,), generator=g))
+        x = torch.randint(0, levels, (n,), generator=g).float() * 0.125
+        if trial % 7 == 0:
+            x = torch.rand(n, generator=g)
+        if trial % 13 == 0:
+            x[torch.rand(n, generator=g) < 0.1] = float("nan")
+        largest = bool(trial % 2)
+        ref = torch.topk(x, k, largest=largest).indices.numpy()
+        got = _emulated(x.numpy(), k, largest)
+        assert np.array_equal(ref, got), (n, k, largest, x.tolist())

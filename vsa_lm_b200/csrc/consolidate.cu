@@ -1,0 +1,805 @@
+// Phase B: the sequential attractor-bank / M_res consolidation scan.
+//
+// One CTA (8 warps) owns one chain (sequence b, KV head h) for all of its consolidation steps, so
+// the bank never leaves the SM between steps: ak / av live in shared memory, M_res lives in the
+// registers of warps 0..HD/16-1 as the accumulator fragments of its own update GEMM. Every
+// contraction of _consolidate_functional (vsa_lm/config/bolt3.py:68-192) is a 128 x 128 x HD
+// tensor-core product with bf16 operands, fp32 accumulation:
+//   sc   = kp . RoPE(ak, pm)^T            (:97-100, :169-171)   exact bf16 products
+//   v^   = softmax(sc).bf16 @ av          (:101, :172)
+//   cos  = kr . ak^T / (|kr| |ak|)        (:104-106, :175-176)
+//   pair = ak . ak^T / (|ak| |ak|)        (:128-130)
+//   gram = |kr . kr^T| / (|kr| |kr|)      (:156-157)
+//   k^ M = kr . (M_hi + M_lo) / |kr|      (:159)   M split into two bf16 terms: ~2^-17 relative
+//   M   <- gamma M + kr^T . (E_hi + E_lo)  (:162)   E = err / |kr|, split the same way
+// Rankings use a warp bitonic sort; when it finds exactly equal keys the CPU torch.topk order is
+// reproduced with the emulation in stl_select.h (bolt3.py:133-134, 183).
+#include "../../include/bolt3.h"
+#include "common.cuh"
+#include "stl_select.h"
+
+namespace {
+
+using namespace b3;
+
+constexpr int S = 128;   // attractor slots
+constexpr int CC = 128;  // chunk rows
+constexpr int NT = 256;  // threads per CTA
+constexpr float SIM_K = 0.88f, SIM_V = 0.80f, GAMMA_U = 0.995f;  // bolt3.py:31
+
+template <int HD>
+struct Smem {
+  bf16 ak[S * HD];
+  bf16 av[S * HD];
+  bf16 kr[CC * HD];
+  bf16 vv[CC * HD];
+  bf16 x1[128 * HD];   // kp, then M_hi, then E_hi
+  bf16 x2[128 * HD];   // RoPE(ak, pm), then M_lo, then E_lo
+  float mass[S], util[S], pm[S], keep[S], na[S], bias[S], botv[S];
+  float rel[CC], score[CC], bsk[CC], beta[CC], nk[CC], nv[CC], pos[CC], wgt[CC], topv[CC];
+  int best[CC], tops[CC], bots[S], mlist[CC];
+  unsigned char act[S], mrg[CC], ins[CC];
+  int n_merged;
+  b3sel::KV selA[128], selB[128];
+};
+
+// ------------------------------------------------------------------------------------------
+// shared-memory tile movement
+
+template <int HD>
+B3_DEV void g2s_rows(bf16* s, const bf16* g, int rows_valid) {
+  constexpr int CPR = HD / 8;
+  for (int i = threadIdx.x; i < 128 * CPR; i += NT) {
+    const int r = i / CPR, ch = i % CPR;
+    const bool ok = r < rows_valid;
+    cp_async16(s + swz<HD>(r, ch * 8), ok ? g + (int64_t)r * HD + ch * 8 : g, ok);
+  }
+}
+
+template <int HD>
+B3_DEV void s2g_rows(bf16* g, const bf16* s) {
+  constexpr int CPR = HD / 8;
+  for (int i = threadIdx.x; i < 128 * CPR; i += NT) {
+    const int r = i / CPR, ch = i % CPR;
+    *reinterpret_cast<uint4*>(g + (int64_t)r * HD + ch * 8) =
+        *reinterpret_cast<const uint4*>(s + swz<HD>(r, ch * 8));
+  }
+}
+
+// squared L2 norm of row r of a swizzled tile (whole warp)
+template <int HD>
+B3_DEV float row_sumsq(const bf16* s, int r, int lane) {
+  constexpr int EPL = HD / 32;
+  const bf16* p = s + swz<HD>(r, lane * EPL);
+  float acc = 0.f;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const float x = bf2f(p[e]);
+    acc = fmaf(x, x, acc);
+  }
+  return warp_sum(acc);
+}
+
+// ------------------------------------------------------------------------------------------
+// warp-level GEMMs on 16 rows (r0 .. r0+15); fragments follow mma.m16n8k16 layouts
+
+// acc[16 x 128] = A[r0.., K] . B[0..128, K]^T   (A, B swizzled tiles with K = HD columns)
+template <int HD>
+B3_DEV void gemm_nt(float (&acc)[16][4], const bf16* A, int r0, const bf16* B, int lane) {
+#pragma unroll
+  for (int n = 0; n < 16; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+#pragma unroll
+  for (int kt = 0; kt < HD / 16; ++kt) {
+    uint32_t a[4];
+    ldsm_x4(a, A + swz<HD>(r0 + (lane & 15), kt * 16 + (lane >> 4) * 8));
+#pragma unroll
+    for (int np = 0; np < 8; ++np) {
+      uint32_t b[4];
+      ldsm_x4(b, B + swz<HD>(np * 16 + (lane & 7) + (lane >> 4) * 8, kt * 16 + ((lane >> 3) & 1) * 8));
+      mma16816(acc[2 * np], a, b[0], b[1]);
+      mma16816(acc[2 * np + 1], a, b[2], b[3]);
+    }
+  }
+}
+
+// acc[16 x HD] += P[16 x 128] . B[128 x HD]   (P as A fragments, B swizzled row-major [128][HD])
+template <int HD>
+B3_DEV void gemm_pv(float (&acc)[HD / 8][4], const uint32_t (&pa)[8][4], const bf16* B, int lane) {
+#pragma unroll
+  for (int kt = 0; kt < 8; ++kt) {
+#pragma unroll
+    for (int np = 0; np < HD / 16; ++np) {
+      uint32_t b[4];
+      ldsm_x4_t(b, B + swz<HD>(kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, np * 16 + (lane >> 4) * 8));
+      mma16816(acc[2 * np], pa[kt], b[0], b[1]);
+      mma16816(acc[2 * np + 1], pa[kt], b[2], b[3]);
+    }
+  }
+}
+
+// acc[16 x HD] += A[r0.., 0..HD] . B[HD x HD]   (A swizzled [128][HD], B swizzled [HD][HD])
+template <int HD>
+B3_DEV void gemm_nn(float (&acc)[HD / 8][4], const bf16* A, int r0, const bf16* B, int lane) {
+#pragma unroll
+  for (int kt = 0; kt < HD / 16; ++kt) {
+    uint32_t a[4];
+    ldsm_x4(a, A + swz<HD>(r0 + (lane & 15), kt * 16 + (lane >> 4) * 8));
+#pragma unroll
+    for (int np = 0; np < HD / 16; ++np) {
+      uint32_t b[4];
+      ldsm_x4_t(b, B + swz<HD>(kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, np * 16 + (lane >> 4) * 8));
+      mma16816(acc[2 * np], a, b[0], b[1]);
+      mma16816(acc[2 * np + 1], a, b[2], b[3]);
+    }
+  }
+}
+
+// acc[16 x HD] += A^T[m0.., 0..128] . B[128 x HD]   (A stored [128 tokens][HD], read transposed)
+template <int HD>
+B3_DEV void gemm_tn(float (&acc)[HD / 8][4], const bf16* A, int m0, const bf16* B, int lane) {
+#pragma unroll 2
+  for (int kt = 0; kt < 8; ++kt) {
+    uint32_t a[4];
+    ldsm_x4_t(a, A + swz<HD>(kt * 16 + (lane & 7) + (lane >> 4) * 8, m0 + ((lane >> 3) & 1) * 8));
+#pragma unroll
+    for (int np = 0; np < HD / 16; ++np) {
+      uint32_t b[4];
+      ldsm_x4_t(b, B + swz<HD>(kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, np * 16 + (lane >> 4) * 8));
+      mma16816(acc[2 * np], a, b[0], b[1]);
+      mma16816(acc[2 * np + 1], a, b[2], b[3]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// ranking: warp bitonic sort of up to 128 (value, index) entries, 4 per lane.
+// Sorted order: "largest" = descending value, else ascending; equal values by ascending index.
+// Entries with index >= n are padding and sort last. After sorting, if two adjacent entries that
+// can change the result are exactly equal (or a NaN is present) the CPU torch.topk order is
+// recomputed by lane 0 with the libstdc++-compatible emulation. Writes out_idx/out_val[0..k).
+B3_DEV void warp_topk(const float* vals, int n, int k, bool largest, float ignore_below,
+                      int* out_idx, float* out_val, b3sel::KV* buf, int lane, int32_t* status) {
+  uint64_t key[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int i = lane * 4 + r;
+    uint32_t kv = 0xffffffffu;
+    if (i < n) {
+      const uint32_t f = fkey(vals[i]);
+      kv = largest ? ~f : f;
+      if (kv == 0xffffffffu) kv = 0xfffffffeu;
+    }
+    key[r] = ((uint64_t)kv << 32) | (uint32_t)i;
+  }
+  for (int kk = 2; kk <= 128; kk <<= 1) {
+    for (int j = kk >> 1; j > 0; j >>= 1) {
+      if (j >= 4) {
+        const int lj = j >> 2;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int e = lane * 4 + r;
+          const uint64_t other = __shfl_xor_sync(0xffffffffu, key[r], lj);
+          const bool up = (e & kk) == 0;
+          const bool lower = (e & j) == 0;
+          const uint64_t mn = key[r] < other ? key[r] : other;
+          const uint64_t mx = key[r] < other ? other : key[r];
+          key[r] = (lower == up) ? mn : mx;
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int p = r ^ j;
+          if (p > r) {
+            const int e = lane * 4 + r;
+            const bool up = (e & kk) == 0;
+            const uint64_t a = key[r], b = key[p];
+            const bool sw = up ? (a > b) : (a < b);
+            if (sw) { key[r] = b; key[p] = a; }
+          }
+        }
+      }
+    }
+  }
+  // tie / NaN detection over the positions that decide the first k entries
+  bool tie = false;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int i = lane * 4 + r;
+    const int idx = (int)(key[r] & 0xffffffffu);
+    uint64_t nxt = (r < 3) ? key[r + 1] : __shfl_down_sync(0xffffffffu, key[0], 1);
+    if (r == 3 && lane == 31) nxt = ~0ull;
+    const int nidx = (int)(nxt & 0xffffffffu);
+    if (i < n) {
+      const float v = vals[idx];
+      if (v != v) tie = true;
+      if (i < k && i + 1 < n) {
+        const float w = vals[nidx];
+        if (v == w && v >= ignore_below) tie = true;
+      }
+    }
+  }
+  tie = __any_sync(0xffffffffu, tie);
+  if (!tie) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = lane * 4 + r;
+      if (i < k) {
+        const int idx = (int)(key[r] & 0xffffffffu);
+        out_idx[i] = idx;
+        out_val[i] = vals[idx];
+      }
+    }
+    __syncwarp();
+    return;
+  }
+  if (lane == 0) {
+    for (int i = 0; i < n; ++i) { buf[i].v = vals[i]; buf[i].i = i; }
+    const int bad = b3sel::topk_order(buf, n, k, largest);
+    if (bad && status) atomicOr(status, 1);
+    for (int i = 0; i < k; ++i) {
+      out_idx[i] = buf[i].i;
+      out_val[i] = buf[i].v;
+    }
+  }
+  __syncwarp();
+}
+
+// ------------------------------------------------------------------------------------------
+
+template <int HD>
+__global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_args a) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  Smem<HD>& sm = *reinterpret_cast<Smem<HD>*>(smem_raw);
+  const int c = blockIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int r0 = warp * 16;
+  const int h = c % a.hkv;
+  const float kappa = a.kappa[h];
+  const float gam = a.gamma[h];
+  constexpr float scale = HD == 128 ? 0.08838834764831845f : 0.125f;  // fp32(HD ** -0.5)
+  const bool m_owner = warp < HD / 16;
+
+  bf16* g_ak = reinterpret_cast<bf16*>(a.ak) + (int64_t)c * S * HD;
+  bf16* g_av = reinterpret_cast<bf16*>(a.av) + (int64_t)c * S * HD;
+  float* g_m = a.m_res + (int64_t)c * HD * HD;
+
+  // ---- load or initialise the bank (bolt3.py:83-92)
+  int n_filled;
+  float mr[HD / 8][4];
+  if (a.init_blank) {
+    n_filled = 0;
+    for (int i = tid; i < S * HD / 8; i += NT) {
+      *reinterpret_cast<uint4*>(sm.ak + i * 8) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(sm.av + i * 8) = make_uint4(0, 0, 0, 0);
+    }
+    for (int s = tid; s < S; s += NT) {
+      sm.mass[s] = 1.f; sm.util[s] = 0.f; sm.pm[s] = 0.f; sm.act[s] = 0;
+    }
+#pragma unroll
+    for (int n = 0; n < HD / 8; ++n) mr[n][0] = mr[n][1] = mr[n][2] = mr[n][3] = 0.f;
+  } else {
+    n_filled = a.n_filled[c];
+    g2s_rows<HD>(sm.ak, g_ak, S);
+    g2s_rows<HD>(sm.av, g_av, S);
+    cp_async_commit();
+    for (int s = tid; s < S; s += NT) {
+      sm.mass[s] = a.mass[(int64_t)c * S + s];
+      sm.util[s] = a.util[(int64_t)c * S + s];
+      sm.pm[s] = a.pm[(int64_t)c * S + s];
+      sm.act[s] = a.act[(int64_t)c * S + s];
+    }
+    if (m_owner) {
+#pragma unroll
+      for (int n = 0; n < HD / 8; ++n) {
+        const float2 u = *reinterpret_cast<const float2*>(g_m + (r0 + g) * HD + n * 8 + 2 * t4);
+        const float2 w = *reinterpret_cast<const float2*>(g_m + (r0 + g + 8) * HD + n * 8 + 2 * t4);
+        mr[n][0] = u.x; mr[n][1] = u.y; mr[n][2] = w.x; mr[n][3] = w.y;
+      }
+    } else {
+#pragma unroll
+      for (int n = 0; n < HD / 8; ++n) mr[n][0] = mr[n][1] = mr[n][2] = mr[n][3] = 0.f;
+    }
+    cp_async_wait<0>();
+  }
+  __syncthreads();
+
+  // RoPE(ak, pm) of the current bank into x2 (bolt3.py:17-20 in the storage dtype)
+  auto compute_kread = [&]() {
+    for (int i = tid; i < S * (HD / 2); i += NT) {
+      const int s = i / (HD / 2), d = i % (HD / 2);
+      const float ang = __fmul_rn(sm.pm[s], a.inv_freq[d]);
+      float sn, cs;
+      sincosf(ang, &sn, &cs);
+      cs = rbf(cs); sn = rbf(sn);
+      const float x0 = bf2f(sm.ak[swz<HD>(s, d)]);
+      const float x1 = bf2f(sm.ak[swz<HD>(s, d + HD / 2)]);
+      const float o0 = rbf(__fadd_rn(rbf(__fmul_rn(x0, cs)), rbf(__fmul_rn(-x1, sn))));
+      const float o1 = rbf(__fadd_rn(rbf(__fmul_rn(x1, cs)), rbf(__fmul_rn(x0, sn))));
+      sm.x2[swz<HD>(s, d)] = __float2bfloat16_rn(o0);
+      sm.x2[swz<HD>(s, d + HD / 2)] = __float2bfloat16_rn(o1);
+    }
+  };
+  compute_kread();
+  __syncthreads();
+
+  const bf16* g_kr = reinterpret_cast<const bf16*>(a.kr) + (int64_t)c * a.chain_tokens * HD;
+  const bf16* g_kp = reinterpret_cast<const bf16*>(a.kp) + (int64_t)c * a.chain_tokens * HD;
+  const bf16* g_v = reinterpret_cast<const bf16*>(a.v) + (int64_t)c * a.chain_tokens * HD;
+  const float* g_beta = a.beta + (int64_t)c * a.chain_tokens;
+
+  for (int st = 0; st < a.n_steps; ++st) {
+    const int skip = st == 0 ? a.skip0 : 0;
+    const int64_t t_begin = a.token0 + (int64_t)st * a.step_tokens + skip;
+    const int l_tok = a.chunk_len - skip;
+
+    // ---- load the chunk: kr, kp (x1), v; beta, positions
+    g2s_rows<HD>(sm.kr, g_kr + t_begin * HD, l_tok);
+    g2s_rows<HD>(sm.vv, g_v + t_begin * HD, l_tok);
+    if (n_filled > 0) g2s_rows<HD>(sm.x1, g_kp + t_begin * HD, l_tok);
+    cp_async_commit();
+    for (int j = tid; j < CC; j += NT) {
+      sm.beta[j] = j < l_tok ? g_beta[t_begin + j] : 0.f;
+      sm.pos[j] = (float)(a.pos0 + t_begin + j);
+      sm.mrg[j] = 0;
+      sm.ins[j] = 0;
+    }
+    for (int s = tid; s < S; s += NT) sm.util[s] = __fmul_rn(sm.util[s], GAMMA_U);  // :94
+    cp_async_wait<0>();
+    __syncthreads();
+    for (int r = warp; r < 128; r += 8) {
+      const float kk = row_sumsq<HD>(sm.kr, r, lane);
+      const float vv2 = row_sumsq<HD>(sm.vv, r, lane);
+      const float aa = row_sumsq<HD>(sm.ak, r, lane);
+      if (lane == 0) {
+        sm.nk[r] = sqrtf(kk);
+        sm.nv[r] = sqrtf(vv2);
+        sm.na[r] = sqrtf(aa);
+      }
+    }
+    __syncthreads();
+
+    const bool full = n_filled >= S;
+    if (n_filled == 0) {
+      // ---- first fill: score = unbiased var(normalize(v)) (bolt3.py:180)
+      for (int r = warp; r < l_tok; r += 8) {
+        constexpr int EPL = HD / 32;
+        const bf16* p = sm.vv + swz<HD>(r, lane * EPL);
+        const float inv = fmaxf(sm.nv[r], 1e-12f);
+        float xs[EPL], sum = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) { xs[e] = __fdiv_rn(bf2f(p[e]), inv); sum += xs[e]; }
+        const float mean = __fdiv_rn(warp_sum(sum), (float)HD);
+        float sq = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) { const float d = xs[e] - mean; sq = fmaf(d, d, sq); }
+        sq = warp_sum(sq);
+        if (lane == 0) {
+          sm.score[r] = __fdiv_rn(sq, (float)(HD - 1));
+          sm.rel[r] = 0.15f;  // initial utility of the very first fill (:181)
+        }
+      }
+      __syncthreads();
+    } else {
+      // ---- attractor prediction of each token's value (:97-103 / :169-174)
+      for (int s = tid; s < S; s += NT) {
+        const float lm = logf(fmaxf(sm.mass[s], 1.0f));
+        sm.bias[s] = full ? __fmul_rn(kappa, lm) : lm;
+      }
+      __syncthreads();
+      uint32_t pa[8][4];
+      {
+        float acc[16][4];
+        gemm_nt<HD>(acc, sm.x1, r0, sm.x2, lane);
+        float mx0 = neg_inf(), mx1 = neg_inf();
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int col = n * 8 + 2 * t4 + (q & 1);
+            float sc = __fadd_rn(__fmul_rn(acc[n][q], scale), sm.bias[col]);
+            if (!full && !sm.act[col]) sc = -1e9f;
+            acc[n][q] = sc;
+          }
+          mx0 = fmaxf(mx0, fmaxf(acc[n][0], acc[n][1]));
+          mx1 = fmaxf(mx1, fmaxf(acc[n][2], acc[n][3]));
+        }
+        mx0 = quad_max(mx0);
+        mx1 = quad_max(mx1);
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+          acc[n][0] = expf(acc[n][0] - mx0); acc[n][1] = expf(acc[n][1] - mx0);
+          acc[n][2] = expf(acc[n][2] - mx1); acc[n][3] = expf(acc[n][3] - mx1);
+          s0 += acc[n][0] + acc[n][1];
+          s1 += acc[n][2] + acc[n][3];
+        }
+        s0 = quad_sum(s0);
+        s1 = quad_sum(s1);
+#pragma unroll
+        for (int kt = 0; kt < 8; ++kt) {
+          pa[kt][0] = pack_bf16(__fdiv_rn(acc[2 * kt][0], s0), __fdiv_rn(acc[2 * kt][1], s0));
+          pa[kt][1] = pack_bf16(__fdiv_rn(acc[2 * kt][2], s1), __fdiv_rn(acc[2 * kt][3], s1));
+          pa[kt][2] = pack_bf16(__fdiv_rn(acc[2 * kt + 1][0], s0), __fdiv_rn(acc[2 * kt + 1][1], s0));
+          pa[kt][3] = pack_bf16(__fdiv_rn(acc[2 * kt + 1][2], s1), __fdiv_rn(acc[2 * kt + 1][3], s1));
+        }
+      }
+      {
+        float acc2[HD / 8][4];
+#pragma unroll
+        for (int n = 0; n < HD / 8; ++n) acc2[n][0] = acc2[n][1] = acc2[n][2] = acc2[n][3] = 0.f;
+        gemm_pv<HD>(acc2, pa, sm.av, lane);
+        float e0 = 0.f, e1 = 0.f;
+#pragma unroll
+        for (int n = 0; n < HD / 8; ++n) {
+          const int col = n * 8 + 2 * t4;
+          const float v00 = bf2f(sm.vv[swz<HD>(r0 + g, col)]), v01 = bf2f(sm.vv[swz<HD>(r0 + g, col + 1)]);
+          const float v10 = bf2f(sm.vv[swz<HD>(r0 + g + 8, col)]), v11 = bf2f(sm.vv[swz<HD>(r0 + g + 8, col + 1)]);
+          float d;
+          d = v00 - acc2[n][0]; e0 = fmaf(d, d, e0);
+          d = v01 - acc2[n][1]; e0 = fmaf(d, d, e0);
+          d = v10 - acc2[n][2]; e1 = fmaf(d, d, e1);
+          d = v11 - acc2[n][3]; e1 = fmaf(d, d, e1);
+        }
+        e0 = quad_sum(e0);
+        e1 = quad_sum(e1);
+        if (t4 == 0) {
+          sm.rel[r0 + g] = __fdiv_rn(sqrtf(e0), __fadd_rn(sm.nv[r0 + g], 1e-6f));
+          sm.rel[r0 + g + 8] = __fdiv_rn(sqrtf(e1), __fadd_rn(sm.nv[r0 + g + 8], 1e-6f));
+        }
+      }
+      // ---- cosine match against the slots (:104-106, :175-177)
+      {
+        float acc[16][4];
+        gemm_nt<HD>(acc, sm.kr, r0, sm.ak, lane);
+        const float nk0 = fmaxf(sm.nk[r0 + g], 1e-12f), nk1 = fmaxf(sm.nk[r0 + g + 8], 1e-12f);
+        float b0 = neg_inf(), b1 = neg_inf();
+        int i0 = 0x7fffffff, i1 = 0x7fffffff;
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int col = n * 8 + 2 * t4 + q;
+            const float na = fmaxf(sm.na[col], 1e-12f);
+            float c0 = __fdiv_rn(acc[n][q], __fmul_rn(nk0, na));
+            float c1 = __fdiv_rn(acc[n][2 + q], __fmul_rn(nk1, na));
+            if (!full && !sm.act[col]) { c0 = 0.f; c1 = 0.f; }
+            if (c0 > b0) { b0 = c0; i0 = col; }
+            if (c1 > b1) { b1 = c1; i1 = col; }
+          }
+        }
+#pragma unroll
+        for (int o = 1; o <= 2; o <<= 1) {
+          const float ob0 = __shfl_xor_sync(0xffffffffu, b0, o);
+          const int oi0 = __shfl_xor_sync(0xffffffffu, i0, o);
+          const float ob1 = __shfl_xor_sync(0xffffffffu, b1, o);
+          const int oi1 = __shfl_xor_sync(0xffffffffu, i1, o);
+          if (ob0 > b0 || (ob0 == b0 && oi0 < i0)) { b0 = ob0; i0 = oi0; }
+          if (ob1 > b1 || (ob1 == b1 && oi1 < i1)) { b1 = ob1; i1 = oi1; }
+        }
+        if (t4 == 0) {
+          sm.bsk[r0 + g] = b0; sm.best[r0 + g] = i0;
+          sm.bsk[r0 + g + 8] = b1; sm.best[r0 + g + 8] = i1;
+        }
+      }
+      __syncthreads();
+      if (!full) {
+        for (int j = tid; j < CC; j += NT)
+          sm.score[j] = __fmul_rn(sm.rel[j], 1.0f - fminf(fmaxf(sm.bsk[j], 0.f), 1.f));  // :177
+        __syncthreads();
+      }
+    }
+
+    if (!full) {
+      // ---- fill: the m best tokens take the next empty slots (:183-192)
+      const int m = min(S - n_filled, l_tok);
+      if (warp == 0) warp_topk(sm.score, l_tok, m, true, neg_inf(), sm.tops, sm.topv, sm.selA, lane, a.status);
+      __syncthreads();
+      for (int i = warp; i < m; i += 8) {
+        const int j = sm.tops[i], s = n_filled + i;
+        constexpr int EPL = HD / 32;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          sm.ak[swz<HD>(s, lane * EPL + e)] = sm.kr[swz<HD>(j, lane * EPL + e)];
+          sm.av[swz<HD>(s, lane * EPL + e)] = sm.vv[swz<HD>(j, lane * EPL + e)];
+        }
+        if (lane == 0) {
+          sm.pm[s] = sm.pos[j];
+          sm.mass[s] = 1.f;
+          sm.util[s] = sm.rel[j];
+          sm.act[s] = 1;
+        }
+      }
+      n_filled += m;
+      __syncthreads();
+    } else {
+      // ---- sim_v, score, merge mask (:107-110)
+      for (int r = warp; r < l_tok; r += 8) {
+        constexpr int EPL = HD / 32;
+        const int s = sm.best[r];
+        const bf16* pv = sm.vv + swz<HD>(r, lane * EPL);
+        const bf16* pa_ = sm.av + swz<HD>(s, lane * EPL);
+        float dot = 0.f, aa = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          const float x = bf2f(pv[e]), y = bf2f(pa_[e]);
+          dot = fmaf(x, y, dot);
+          aa = fmaf(y, y, aa);
+        }
+        dot = warp_sum(dot);
+        aa = warp_sum(aa);
+        if (lane == 0) {
+          const float sv = __fdiv_rn(dot, __fmul_rn(fmaxf(sm.nv[r], 1e-8f), fmaxf(sqrtf(aa), 1e-8f)));
+          const float bs = sm.bsk[r];
+          sm.score[r] = __fmul_rn(sm.rel[r], 1.0f - fminf(fmaxf(bs, 0.f), 1.f));
+          sm.mrg[r] = (bs >= SIM_K) && (sv >= SIM_V);
+        }
+      }
+      __syncthreads();
+      // ---- merge: running means of the matched slots (:112-123)
+      if (warp == 0) {
+        int base = 0;
+        for (int j0 = 0; j0 < CC; j0 += 32) {
+          const int j = j0 + lane;
+          const bool mm = j < l_tok && sm.mrg[j];
+          const unsigned bal = __ballot_sync(0xffffffffu, mm);
+          if (mm) sm.mlist[base + __popc(bal & ((1u << lane) - 1))] = j;
+          base += __popc(bal);
+        }
+        if (lane == 0) sm.n_merged = base;
+      }
+      __syncthreads();
+      const int n_m = sm.n_merged;
+      if (n_m > 0) {
+        for (int s = warp; s < S; s += 8) {
+          int cnt = 0;
+          for (int q = 0; q < n_m; ++q) cnt += sm.best[sm.mlist[q]] == s;
+          if (cnt == 0) continue;
+          constexpr int EPL = HD / 32;
+          float ks[EPL], vs[EPL];
+          float ps = 0.f;
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) ks[e] = vs[e] = 0.f;
+          for (int q = 0; q < n_m; ++q) {
+            const int j = sm.mlist[q];
+            if (sm.best[j] != s) continue;
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) {
+              ks[e] = __fadd_rn(ks[e], bf2f(sm.kr[swz<HD>(j, lane * EPL + e)]));
+              vs[e] = __fadd_rn(vs[e], bf2f(sm.vv[swz<HD>(j, lane * EPL + e)]));
+            }
+            ps = __fadd_rn(ps, sm.pos[j]);
+          }
+          const float ms = sm.mass[s];
+          const float nm = __fadd_rn(ms, (float)cnt);
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) {
+            const int d = lane * EPL + e;
+            const float ka = __fadd_rn(__fmul_rn(ms, bf2f(sm.ak[swz<HD>(s, d)])), ks[e]);
+            const float va = __fadd_rn(__fmul_rn(ms, bf2f(sm.av[swz<HD>(s, d)])), vs[e]);
+            sm.ak[swz<HD>(s, d)] = __float2bfloat16_rn(__fdiv_rn(ka, nm));
+            sm.av[swz<HD>(s, d)] = __float2bfloat16_rn(__fdiv_rn(va, nm));
+          }
+          __syncwarp();
+          const float aa = row_sumsq<HD>(sm.ak, s, lane);
+          if (lane == 0) {
+            sm.pm[s] = __fdiv_rn(__fadd_rn(__fmul_rn(ms, sm.pm[s]), ps), nm);
+            sm.mass[s] = nm;
+            sm.na[s] = sqrtf(aa);
+          }
+        }
+        __syncthreads();
+      }
+      // ---- diversity eviction (:125-152)
+      {
+        float acc[16][4];
+        gemm_nt<HD>(acc, sm.ak, r0, sm.ak, lane);
+        const float na0 = fmaxf(sm.na[r0 + g], 1e-12f), na1 = fmaxf(sm.na[r0 + g + 8], 1e-12f);
+        float m0 = neg_inf(), m1 = neg_inf();
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int col = n * 8 + 2 * t4 + q;
+            const float nb = fmaxf(sm.na[col], 1e-12f);
+            float p0 = __fdiv_rn(acc[n][q], __fmul_rn(na0, nb));
+            float p1 = __fdiv_rn(acc[n][2 + q], __fmul_rn(na1, nb));
+            if (col == r0 + g) p0 = -1.0f;
+            if (col == r0 + g + 8) p1 = -1.0f;
+            m0 = fmaxf(m0, p0);
+            m1 = fmaxf(m1, p1);
+          }
+        }
+        m0 = quad_max(m0);
+        m1 = quad_max(m1);
+        if (t4 == 0) {
+          sm.keep[r0 + g] = __fmul_rn(sm.util[r0 + g], 1.0f - fminf(fmaxf(m0, 0.f), 0.98f));
+          sm.keep[r0 + g + 8] = __fmul_rn(sm.util[r0 + g + 8], 1.0f - fminf(fmaxf(m1, 0.f), 0.98f));
+        }
+      }
+      for (int j = tid; j < CC; j += NT) sm.wgt[j] = sm.mrg[j] ? -1e9f : sm.score[j];
+      __syncthreads();
+      const int k_cand = min(l_tok, S);
+      if (warp == 0) warp_topk(sm.wgt, l_tok, k_cand, true, -1e8f, sm.tops, sm.topv, sm.selA, lane, a.status);
+      if (warp == 1) warp_topk(sm.keep, S, k_cand, false, neg_inf(), sm.bots, sm.botv, sm.selB, lane, a.status);
+      __syncthreads();
+      for (int i = warp; i < k_cand; i += 8) {
+        const float tv = sm.topv[i];
+        if (!((tv > sm.botv[i]) && (tv > -1e8f))) continue;  // :135
+        const int j = sm.tops[i], s = sm.bots[i];
+        constexpr int EPL = HD / 32;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          sm.ak[swz<HD>(s, lane * EPL + e)] = sm.kr[swz<HD>(j, lane * EPL + e)];
+          sm.av[swz<HD>(s, lane * EPL + e)] = sm.vv[swz<HD>(j, lane * EPL + e)];
+        }
+        if (lane == 0) {
+          sm.pm[s] = sm.pos[j];
+          sm.mass[s] = 1.f;
+          sm.util[s] = sm.rel[j];
+          sm.ins[j] = 1;
+        }
+      }
+      __syncthreads();
+      // ---- Gershgorin-normalised delta rule into M_res (:154-162)
+      for (int j = tid; j < CC; j += NT)
+        sm.wgt[j] = (j < l_tok && !sm.mrg[j] && !sm.ins[j]) ? sm.beta[j] : 0.f;
+      __syncthreads();
+      float bsafe0, bsafe1;
+      {
+        float acc[16][4];
+        gemm_nt<HD>(acc, sm.kr, r0, sm.kr, lane);
+        const float nk0 = fmaxf(sm.nk[r0 + g], 1e-12f), nk1 = fmaxf(sm.nk[r0 + g + 8], 1e-12f);
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int col = n * 8 + 2 * t4 + q;
+            const float nb = fmaxf(sm.nk[col], 1e-12f);
+            const float w = sm.wgt[col];
+            s0 = fmaf(fabsf(__fdiv_rn(acc[n][q], __fmul_rn(nk0, nb))), w, s0);
+            s1 = fmaf(fabsf(__fdiv_rn(acc[n][2 + q], __fmul_rn(nk1, nb))), w, s1);
+          }
+        }
+        s0 = fmaxf(quad_sum(s0), 1.0f);
+        s1 = fmaxf(quad_sum(s1), 1.0f);
+        bsafe0 = __fdiv_rn(sm.wgt[r0 + g], s0);
+        bsafe1 = __fdiv_rn(sm.wgt[r0 + g + 8], s1);
+      }
+      // M split into two bf16 terms, stored [d_in][d_out] in x1 (hi) and x2 (lo)
+      if (m_owner) {
+#pragma unroll
+        for (int n = 0; n < HD / 8; ++n) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int row = r0 + g + (q >> 1) * 8, col = n * 8 + 2 * t4 + (q & 1);
+            const bf16 hi = __float2bfloat16_rn(mr[n][q]);
+            sm.x1[swz<HD>(row, col)] = hi;
+            sm.x2[swz<HD>(row, col)] = __float2bfloat16_rn(mr[n][q] - bf2f(hi));
+          }
+        }
+      }
+      __syncthreads();
+      float err[HD / 8][4];
+      {
+#pragma unroll
+        for (int n = 0; n < HD / 8; ++n) err[n][0] = err[n][1] = err[n][2] = err[n][3] = 0.f;
+        gemm_nn<HD>(err, sm.kr, r0, sm.x1, lane);
+        gemm_nn<HD>(err, sm.kr, r0, sm.x2, lane);
+        const float nk0 = fmaxf(sm.nk[r0 + g], 1e-12f), nk1 = fmaxf(sm.nk[r0 + g + 8], 1e-12f);
+#pragma unroll
+        for (int n = 0; n < HD / 8; ++n) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int row = r0 + g + (q >> 1) * 8, col = n * 8 + 2 * t4 + (q & 1);
+            const float nk = q < 2 ? nk0 : nk1;
+            const float bs = q < 2 ? bsafe0 : bsafe1;
+            const float vpred = __fdiv_rn(err[n][q], nk);
+            const float e = __fmul_rn(bf2f(sm.vv[swz<HD>(row, col)]) - vpred, bs);
+            err[n][q] = __fdiv_rn(e, nk);  // E = err / |k| so that kr^T E = k^T err
+          }
+        }
+      }
+      __syncthreads();  // every warp is done reading the M split
+#pragma unroll
+      for (int n = 0; n < HD / 8; ++n) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int row = r0 + g + (q >> 1) * 8, col = n * 8 + 2 * t4 + (q & 1);
+          const bf16 hi = __float2bfloat16_rn(err[n][q]);
+          sm.x1[swz<HD>(row, col)] = hi;
+          sm.x2[swz<HD>(row, col)] = __float2bfloat16_rn(err[n][q] - bf2f(hi));
+        }
+      }
+      __syncthreads();
+      if (m_owner) {
+#pragma unroll
+        for (int n = 0; n < HD / 8; ++n) {
+          mr[n][0] = __fmul_rn(mr[n][0], gam); mr[n][1] = __fmul_rn(mr[n][1], gam);
+          mr[n][2] = __fmul_rn(mr[n][2], gam); mr[n][3] = __fmul_rn(mr[n][3], gam);
+        }
+        gemm_tn<HD>(mr, sm.kr, r0, sm.x1, lane);
+        gemm_tn<HD>(mr, sm.kr, r0, sm.x2, lane);
+      }
+      __syncthreads();
+    }
+
+    // ---- state the attention of a later chunk reads: RoPE(ak, pm), av, mass, act, M_res
+    compute_kread();
+    __syncthreads();
+    if (a.snap_ak_rope) {
+      const int64_t sn = (int64_t)c * a.snap_cap + a.snap0 + st;
+      s2g_rows<HD>(reinterpret_cast<bf16*>(a.snap_ak_rope) + sn * S * HD, sm.x2);
+      s2g_rows<HD>(reinterpret_cast<bf16*>(a.snap_av) + sn * S * HD, sm.av);
+      for (int s = tid; s < S; s += NT) {
+        a.snap_mass[sn * S + s] = sm.mass[s];
+        a.snap_act[sn * S + s] = sm.act[s];
+      }
+      if (m_owner) {
+        float* gm = a.snap_m + sn * HD * HD;
+#pragma unroll
+        for (int n = 0; n < HD / 8; ++n) {
+          *reinterpret_cast<float2*>(gm + (r0 + g) * HD + n * 8 + 2 * t4) = make_float2(mr[n][0], mr[n][1]);
+          *reinterpret_cast<float2*>(gm + (r0 + g + 8) * HD + n * 8 + 2 * t4) = make_float2(mr[n][2], mr[n][3]);
+        }
+      }
+    }
+  }
+
+  // ---- write the bank back
+  s2g_rows<HD>(g_ak, sm.ak);
+  s2g_rows<HD>(g_av, sm.av);
+  if (a.ak_rope) s2g_rows<HD>(reinterpret_cast<bf16*>(a.ak_rope) + (int64_t)c * S * HD, sm.x2);
+  for (int s = tid; s < S; s += NT) {
+    a.mass[(int64_t)c * S + s] = sm.mass[s];
+    a.util[(int64_t)c * S + s] = sm.util[s];
+    a.pm[(int64_t)c * S + s] = sm.pm[s];
+    a.act[(int64_t)c * S + s] = sm.act[s];
+  }
+  if (m_owner) {
+#pragma unroll
+    for (int n = 0; n < HD / 8; ++n) {
+      *reinterpret_cast<float2*>(g_m + (r0 + g) * HD + n * 8 + 2 * t4) = make_float2(mr[n][0], mr[n][1]);
+      *reinterpret_cast<float2*>(g_m + (r0 + g + 8) * HD + n * 8 + 2 * t4) = make_float2(mr[n][2], mr[n][3]);
+    }
+  }
+  if (tid == 0) a.n_filled[c] = n_filled;
+}
+
+template <int HD>
+int launch(const bolt3_consolidate_args& a, cudaStream_t s) {
+  const size_t smem = sizeof(Smem<HD>);
+  // the attribute is per function and per device; setting it again is harmless
+  if (cudaFuncSetAttribute(consolidate_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return BOLT3_ERR_CUDA;
+  consolidate_kernel<HD><<<a.n_chains, NT, smem, s>>>(a);
+  return cudaGetLastError() == cudaSuccess ? BOLT3_OK : BOLT3_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" int bolt3_consolidate(const bolt3_consolidate_args* a, void* stream) {
+  if (!a || !a->ak || !a->av || !a->mass || !a->util || !a->pm || !a->act || !a->m_res ||
+      !a->n_filled || !a->kr || !a->kp || !a->v || !a->beta || !a->kappa || !a->gamma || !a->inv_freq)
+    return BOLT3_ERR_ARG;
+  if (a->n_chains <= 0 || a->hkv <= 0 || a->n_steps < 0) return BOLT3_ERR_SHAPE;
+  if (a->chunk_len <= 0 || a->chunk_len > CC || a->skip0 < 0 || a->skip0 >= a->chunk_len)
+    return BOLT3_ERR_SHAPE;
+  if (a->snap_ak_rope && (!a->snap_av || !a->snap_mass || !a->snap_act || !a->snap_m ||
+                          a->snap0 < 0 || a->snap0 + a->n_steps > a->snap_cap))
+    return BOLT3_ERR_CAPACITY;
+  if (a->n_steps > 0 &&
+      a->token0 + (int64_t)(a->n_steps - 1) * a->step_tokens + a->chunk_len > a->chain_tokens)
+    return BOLT3_ERR_CAPACITY;
+  const uintptr_t al = (uintptr_t)a->ak | (uintptr_t)a->av | (uintptr_t)a->kr | (uintptr_t)a->kp |
+                       (uintptr_t)a->v | (uintptr_t)a->ak_rope | (uintptr_t)a->snap_ak_rope |
+                       (uintptr_t)a->snap_av | (uintptr_t)a->m_res | (uintptr_t)a->snap_m;
+  if (al & 15) return BOLT3_ERR_ALIGN;
+  if (a->n_steps == 0) return BOLT3_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (a->HD == 128) return launch<128>(*a, s);
+  if (a->HD == 64) return launch<64>(*a, s);
+  return BOLT3_ERR_SHAPE;
+}

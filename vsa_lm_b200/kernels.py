@@ -1,0 +1,144 @@
+"""Torch-facing wrappers of the Bolt-3 C-ABI: check devices, dtypes and contiguity, pass raw pointers
+and the current CUDA stream. PyTorch only provides device memory and streams here; every kernel is
+in libbolt3.so. Nothing here falls back to a CPU or PyTorch implementation.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+S_SLOTS = 128
+CHUNK = 128
+N_SINKS = 4
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _need(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor (the Bolt-3 path has no CPU implementation)")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def n_consolidations(T: int, C: int = CHUNK) -> int:
+    """Consolidations Bolt3Attn.forward runs for T tokens (vsa_lm/config/bolt3.py:262)."""
+    full = T // C
+    return max(0, full - 2) if T % C == 0 else max(0, full - 1)
+
+
+def prep(proj: torch.Tensor, *, B: int, T: int, H: int, HKV: int, HD: int, inv_freq: torch.Tensor,
+         eps: float, q_norm_w: torch.Tensor | None, k_norm_w: torch.Tensor | None, pos0: int,
+         q_raw: torch.Tensor, q_rope: torch.Tensor, eta: torch.Tensor, k_raw: torch.Tensor,
+         k_rope: torch.Tensor, v: torch.Tensor, beta: torch.Tensor,
+         q_head_stride: int, q_t_off: int, k_head_stride: int, k_t_off: int) -> None:
+    """RMSNorm/RoPE/gates from the fused projection output into head-major buffers (bolt3_prep)."""
+    lib = _lib.load()
+    _need(proj, torch.bfloat16, "proj")
+    for name, t in (("q_raw", q_raw), ("q_rope", q_rope), ("k_raw", k_raw), ("k_rope", k_rope), ("v", v)):
+        _need(t, torch.bfloat16, name)
+    for name, t in (("eta", eta), ("beta", beta), ("inv_freq", inv_freq)):
+        _need(t, torch.float32, name)
+    a = _lib.PrepArgs(
+        proj=proj.data_ptr(), ld=proj.stride(0), B=B, T=T, H=H, HKV=HKV, HD=HD,
+        q_norm_w=_ptr(q_norm_w), k_norm_w=_ptr(k_norm_w), eps=eps, inv_freq=inv_freq.data_ptr(),
+        pos0=pos0, q_raw=q_raw.data_ptr(), q_rope=q_rope.data_ptr(), q_head_stride=q_head_stride,
+        q_t_off=q_t_off, eta=eta.data_ptr(), eta_head_stride=q_head_stride, eta_t_off=q_t_off,
+        k_raw=k_raw.data_ptr(), k_rope=k_rope.data_ptr(), v=v.data_ptr(), k_head_stride=k_head_stride,
+        k_t_off=k_t_off, beta=beta.data_ptr(), beta_head_stride=k_head_stride, beta_t_off=k_t_off)
+    _lib.check(lib.bolt3_prep(ctypes.byref(a), _stream()), "bolt3_prep")
+
+
+def consolidate(*, n_chains: int, hkv: int, HD: int, bank: dict, init_blank: bool,
+                kr: torch.Tensor, kp: torch.Tensor, v: torch.Tensor, beta: torch.Tensor,
+                chain_tokens: int, token0: int, step_tokens: int, skip0: int, chunk_len: int,
+                pos0: int, n_steps: int, kappa: torch.Tensor, gamma: torch.Tensor,
+                inv_freq: torch.Tensor, snaps: dict | None = None, snap0: int = 0,
+                status: torch.Tensor | None = None) -> None:
+    """Run n_steps consolidations on every chain (bolt3_consolidate). `bank` holds the state
+    tensors ak, av, ak_rope (bf16 [chains,S,HD]), mass, util, pm (fp32 [chains,S]), act (uint8),
+    m_res (fp32 [chains,HD,HD]) and n_filled (int32 [chains]); they are updated in place."""
+    lib = _lib.load()
+    snaps = snaps or {}
+    a = _lib.ConsolidateArgs(
+        n_chains=n_chains, hkv=hkv, HD=HD,
+        ak=bank["ak"].data_ptr(), av=bank["av"].data_ptr(), ak_rope=_ptr(bank.get("ak_rope")),
+        mass=bank["mass"].data_ptr(), util=bank["util"].data_ptr(), pm=bank["pm"].data_ptr(),
+        act=bank["act"].data_ptr(), m_res=bank["m_res"].data_ptr(), n_filled=bank["n_filled"].data_ptr(),
+        init_blank=int(init_blank), kr=kr.data_ptr(), kp=kp.data_ptr(), v=v.data_ptr(), beta=beta.data_ptr(),
+        chain_tokens=chain_tokens, token0=token0, step_tokens=step_tokens, skip0=skip0,
+        chunk_len=chunk_len, pos0=pos0, n_steps=n_steps, kappa=kappa.data_ptr(), gamma=gamma.data_ptr(),
+        inv_freq=inv_freq.data_ptr(),
+        snap_ak_rope=_ptr(snaps.get("ak_rope")), snap_av=_ptr(snaps.get("av")),
+        snap_mass=_ptr(snaps.get("mass")), snap_act=_ptr(snaps.get("act")), snap_m=_ptr(snaps.get("m")),
+        snap_cap=int(snaps["ak_rope"].shape[1]) if snaps else 0, snap0=snap0, status=_ptr(status))
+    _lib.check(lib.bolt3_consolidate(ctypes.byref(a), _stream()), "bolt3_consolidate")
+
+
+def attend_decode(*, n_chains: int, hkv: int, G: int, HD: int, q_rope: torch.Tensor, q_raw: torch.Tensor,
+                  eta: torch.Tensor, Tq: int, seg0_k: torch.Tensor, seg0_v: torch.Tensor,
+                  seg0_chain_tokens: int, seg0_len: int, seg1_k: torch.Tensor, seg1_v: torch.Tensor,
+                  seg1_chain_tokens: int, seg1_len: int, len_before: int,
+                  sinks: tuple | None, bank: dict | None, kappa: torch.Tensor, coef: torch.Tensor,
+                  res_w: torch.Tensor, eps: float, y: torch.Tensor) -> None:
+    """Attention of Tq new tokens over sinks, the current bank and the two-chunk window."""
+    lib = _lib.load()
+    a = _lib.AttendArgs(
+        n_chains=n_chains, hkv=hkv, G=G, HD=HD, q_rope=q_rope.data_ptr(), q_raw=q_raw.data_ptr(),
+        eta=eta.data_ptr(), Tq=Tq, prefill=0,
+        seg0_k=seg0_k.data_ptr(), seg0_v=seg0_v.data_ptr(), seg0_chain_tokens=seg0_chain_tokens,
+        seg0_len=seg0_len, seg1_k=seg1_k.data_ptr(), seg1_v=seg1_v.data_ptr(),
+        seg1_chain_tokens=seg1_chain_tokens, seg1_len=seg1_len, len_before=len_before,
+        sink_k=_ptr(sinks[0]) if sinks else None, sink_v=_ptr(sinks[1]) if sinks else None,
+        sink_chain_tokens=N_SINKS, has_sinks=int(sinks is not None),
+        bank_ak_rope=_ptr(bank["ak_rope"]) if bank else None, bank_av=_ptr(bank["av"]) if bank else None,
+        bank_mass=_ptr(bank["mass"]) if bank else None, bank_act=_ptr(bank["act"]) if bank else None,
+        bank_m=_ptr(bank["m_res"]) if bank else None, bank_cap=1, has_bank=int(bank is not None),
+        kappa=kappa.data_ptr(), coef=coef.data_ptr(), res_w=res_w.data_ptr(), eps=eps,
+        y=y.data_ptr(), y_tokens=Tq)
+    _lib.check(lib.bolt3_attend(ctypes.byref(a), _stream()), "bolt3_attend")
+
+
+def prefill_workspace_bytes(n_chains: int, T: int, HD: int) -> int:
+    return int(_lib.load().bolt3_prefill_workspace_size(n_chains, T, HD))
+
+
+def prefill(*, B: int, T: int, H: int, HKV: int, HD: int, q_rope, q_raw, eta, k_raw, k_rope, v, beta,
+            kappa, gamma, coef, inv_freq, res_w, eps: float, workspace: torch.Tensor, bank: dict,
+            y: torch.Tensor, status: torch.Tensor | None = None) -> None:
+    """Phases B + C of Bolt3Attn.forward on prepared q/k/v (bolt3_prefill_fwd)."""
+    lib = _lib.load()
+    a = _lib.PrefillArgs(
+        B=B, T=T, H=H, HKV=HKV, HD=HD, q_rope=q_rope.data_ptr(), q_raw=q_raw.data_ptr(),
+        eta=eta.data_ptr(), k_raw=k_raw.data_ptr(), k_rope=k_rope.data_ptr(), v=v.data_ptr(),
+        beta=beta.data_ptr(), kappa=kappa.data_ptr(), gamma=gamma.data_ptr(), coef=coef.data_ptr(),
+        inv_freq=inv_freq.data_ptr(), res_w=res_w.data_ptr(), eps=eps,
+        workspace=workspace.data_ptr(), workspace_bytes=workspace.numel() * workspace.element_size(),
+        ak=bank["ak"].data_ptr(), av=bank["av"].data_ptr(), ak_rope=_ptr(bank.get("ak_rope")),
+        mass=bank["mass"].data_ptr(), util=bank["util"].data_ptr(), pm=bank["pm"].data_ptr(),
+        act=bank["act"].data_ptr(), m_res=bank["m_res"].data_ptr(), n_filled=bank["n_filled"].data_ptr(),
+        y=y.data_ptr(), status=_ptr(status))
+    _lib.check(lib.bolt3_prefill_fwd(ctypes.byref(a), _stream()), "bolt3_prefill_fwd")
+
+
+def new_bank(n_chains: int, HD: int, device, S: int = S_SLOTS) -> dict:
+    """Uninitialised bank tensors (the consolidation kernel initialises them with init_blank)."""
+    bf = dict(dtype=torch.bfloat16, device=device)
+    f32 = dict(dtype=torch.float32, device=device)
+    return dict(ak=torch.empty(n_chains, S, HD, **bf), av=torch.empty(n_chains, S, HD, **bf),
+                ak_rope=torch.empty(n_chains, S, HD, **bf), mass=torch.empty(n_chains, S, **f32),
+                util=torch.empty(n_chains, S, **f32), pm=torch.empty(n_chains, S, **f32),
+                act=torch.zeros(n_chains, S, dtype=torch.uint8, device=device),
+                m_res=torch.zeros(n_chains, HD, HD, **f32),
+                n_filled=torch.zeros(n_chains, dtype=torch.int32, device=device))
