@@ -54,6 +54,27 @@ def near_threshold(rec: dict) -> torch.Tensor:
     return (nk | nv).any(dim=-1)
 
 
+def near_tie_chains(rec: dict, rel: float = 1e-6) -> torch.Tensor:
+    """Chains whose ranking keys (eviction candidates, slot keep values, fill scores) contain
+    distinct values closer than `rel` (relative): their order is decided by rounding noise and the
+    CPU reference's own result depends on its reduction order."""
+    def close_pairs(v):  # v: [chains, k] sorted
+        a, b = v[:, :-1], v[:, 1:]
+        d = (a - b).abs()
+        return ((d > 0) & (d <= rel * torch.maximum(a.abs(), b.abs()))).any(dim=-1)
+
+    if rec.get("kind") == "full":
+        top, bot = rec["top_vals"], rec["bot_vals"]
+        real = top > -1e8
+        flag = close_pairs(torch.where(real, top, torch.full_like(top, -1e30)))
+        flag |= close_pairs(bot)
+        d = (top - bot).abs()
+        flag |= (real & (d > 0) & (d <= rel * bot.abs())).any(dim=-1)
+        return flag
+    sc = torch.sort(rec["score"], dim=-1, descending=True).values
+    return close_pairs(sc)
+
+
 def inputs(shape: str, B: int, T: int, dup, seed: int = 1, device="cuda"):
     cfg = layer_cfg(shape)
     x = make_input(B, T, cfg["dim"], dup=dup, seed=seed)

@@ -7,7 +7,7 @@ except for chains where a cosine lies within 1e-3 of the 0.88 / 0.80 thresholds,
 import pytest
 import torch
 
-from helpers import (BF16, STATE_RTOL, bf16_module, inputs, near_threshold, oracle_cfg_of,
+from helpers import (BF16, STATE_RTOL, bf16_module, inputs, near_threshold, near_tie_chains, oracle_cfg_of,
                      oracle_params, output_close)
 from oracle import LayerDecoderOracle, forward, gamma_delta, project, rope_at
 from vsa_lm_b200 import Bolt3Decoder, Bolt3LayerState
@@ -38,14 +38,22 @@ def test_prep_matches_oracle(shape):
     oc = oracle_cfg_of(m, cfg)
     qr, kr, vo, bo, eo = project(oracle_params(m), oc, x_cpu, BF16)
     pos = torch.arange(T, dtype=torch.float32)
-    qp, kp = rope_at(qr, pos, oc["inv_freq"], BF16), rope_at(kr, pos, oc["inv_freq"], BF16)
-    for name, got, ref in (("q_raw", q_raw, qr), ("q_rope", q_rope, qp), ("k_raw", k_raw, kr),
-                           ("k_rope", k_rope, kp), ("v", v, vo), ("beta", beta, bo), ("eta", eta, eo)):
+    # projections: equal up to the GEMM's accumulation order: one bf16 ulp of the projection, which
+    # the qk RMSNorm scale can stretch to two ulps of its output
+    for name, got, ref in (("q_raw", q_raw, qr), ("k_raw", k_raw, kr), ("v", v, vo), ("beta", beta, bo),
+                           ("eta", eta, eo)):
         ref = ref.reshape(got.shape)
-        torch.testing.assert_close(got.float().cpu(), ref, rtol=1.6e-2, atol=2e-3, msg=name)
-        # all but a handful of elements are bit-identical (GEMM accumulation order aside)
-        same = (got.float().cpu() == ref).float().mean().item()
+        g = got.float().cpu()
+        err = (g - ref).abs()
+        worst = int(err.argmax())
+        assert (err <= 1.6e-2 * ref.abs() + 2e-4).all(), \
+            f"{name}: max |diff| {err.max().item():.3e} at {worst}: got {g.flatten()[worst].item()} ref {ref.flatten()[worst].item()}"
+        same = (g == ref).float().mean().item()
         assert same > 0.98, f"{name}: only {same:.4f} identical"
+    # RoPE in the storage dtype: bit-exact given the same input
+    for name, got, src in (("q_rope", q_rope, q_raw), ("k_rope", k_rope, k_raw)):
+        ref = rope_at(src.float().cpu(), pos, oc["inv_freq"], BF16)
+        assert torch.equal(got.float().cpu(), ref), f"{name} differs from RoPE of the same input"
 
 
 def _oracle_run(shape, B, T, dup, seed=0):
@@ -82,9 +90,17 @@ def test_consolidation_teacher_forced(shape, B, T, dup):
                                         n_filled=0 if pre is None else pre["n_filled"])
         ak, av, mass, util, pmv, act, m_res, n_f = out
         assert n_f == post["n_filled"]
-        skipc = near_threshold(rec[i])
-        flips += int(skipc.sum())
-        ok = ~skipc
+        near = near_threshold(rec[i]) | near_tie_chains(rec[i])
+        flips += int(near.sum())
+        ok = ~near
+        if rec[i]["kind"] == "fill":
+            # the fill's slot order follows the score ranking: compare slots sorted by token position
+            order_g, order_r = torch.argsort(pmv.cpu(), dim=-1), torch.argsort(post["pm"], dim=-1)
+            take = lambda t, o: torch.gather(t, 1, o) if t.dim() == 2 else torch.gather(t, 1, o.unsqueeze(-1).expand_as(t))
+            ak, av, mass, util, pmv, act = (take(t.cpu(), order_g) for t in (ak, av, mass, util, pmv, act))
+            post = dict(post)
+            for k in ("ak", "av", "mass", "util", "pm", "act"):
+                post[k] = take(post[k], order_r)
         assert torch.equal(act.cpu()[ok], post["act"][ok]), f"act @ {i}"
         assert torch.equal(mass.cpu()[ok], post["mass"][ok]), f"mass (merge/evict decisions) @ {i}"
         torch.testing.assert_close(pmv.cpu()[ok], post["pm"][ok], rtol=STATE_RTOL, atol=1e-3, msg=f"pm @ {i}")
@@ -93,9 +109,9 @@ def test_consolidation_teacher_forced(shape, B, T, dup):
         torch.testing.assert_close(av.float().cpu()[ok], post["av"][ok], rtol=8e-3, atol=1e-6, msg=f"av @ {i}")
         ref_m = post["m_res"][ok]
         scale = ref_m.abs().amax(dim=(-1, -2), keepdim=True).clamp_min(1e-30)
-        err = ((m_res.cpu()[ok] - ref_m).abs() / scale).max().item()
+        err = ((m_res.cpu()[ok] - ref_m).abs() / scale).max().item() if ok.any() else 0.0
         assert err < STATE_RTOL, f"M_res @ {i}: max error {err:.2e} of the chain's max |M|"
-    print(f"near-threshold chains skipped: {flips}")
+    print(f"near-threshold / near-tie chains excluded: {flips}")
 
 
 @pytest.mark.parametrize("shape,B,T,dup", [
@@ -139,5 +155,7 @@ def test_decoder_matches_oracle(shape, prompt, n_dec):
     flips = sum(int(near_threshold(r).sum()) for r in dec.record)
     assert flips == 0
     output_close(torch.cat(outs, 1), torch.cat(refs, 1), "decoder step outputs")
+    # free-running state: the GPU's own bf16 projections feed it, so it is held to the output
+    # tolerance; the 1e-4 state bound is checked teacher-forced in test_consolidation_teacher_forced
     scale = dec.m_res.abs().max().clamp_min(1e-30)
-    assert ((m_res.cpu() - dec.m_res).abs().max() / scale).item() < STATE_RTOL
+    assert ((m_res.cpu() - dec.m_res).abs().max() / scale).item() < 1e-2

@@ -51,15 +51,13 @@ B3_DEV void load_rows(bf16* s, const bf16* g, int rows, int rows_valid) {
   }
 }
 
-// one key block: s = q k^T * scale (+ bias), mask, online-softmax update, o += p v
+// Scores of one key block for the warp's 16 rows: s = q k^T * scale (+ bias), masked to -inf.
 template <int HD, int NK>
-B3_DEV void attend_block(float (&o)[HD / 8][4], float (&mrow)[2], float (&lrow)[2],
-                         const uint32_t (&qa)[HD / 16][4], const bf16* ks, const bf16* vs,
+B3_DEV void block_scores(float (&s)[NK / 8][4], const uint32_t (&qa)[HD / 16][4], const bf16* ks,
                          const float* bias, int nvalid, bool causal, int kbase, int lim0, int lim1,
                          int lane) {
-  constexpr float scale = HD == 128 ? 0.08838834764831845f : 0.125f;
+  constexpr float scale = HD == 128 ? 0.08838834764831845f : 0.125f;  // fp32(HD ** -0.5)
   const int t4 = lane & 3;
-  float s[NK / 8][4];
 #pragma unroll
   for (int n = 0; n < NK / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
 #pragma unroll
@@ -72,7 +70,6 @@ B3_DEV void attend_block(float (&o)[HD / 8][4], float (&mrow)[2], float (&lrow)[
       mma16816(s[2 * np + 1], qa[kt], b[2], b[3]);
     }
   }
-  float bm0 = neg_inf(), bm1 = neg_inf();
 #pragma unroll
   for (int n = 0; n < NK / 8; ++n) {
 #pragma unroll
@@ -83,33 +80,57 @@ B3_DEV void attend_block(float (&o)[HD / 8][4], float (&mrow)[2], float (&lrow)[
       const bool vis = col < nvalid && (!causal || kbase + col <= (q < 2 ? lim0 : lim1));
       s[n][q] = vis ? x : neg_inf();
     }
+  }
+}
+
+// Pass 1: running row max and sum of exp over one block.
+template <int HD, int NK>
+B3_DEV void block_stats(float (&mrow)[2], float (&lrow)[2], const uint32_t (&qa)[HD / 16][4],
+                        const bf16* ks, const float* bias, int nvalid, bool causal, int kbase, int lim0,
+                        int lim1, int lane) {
+  float s[NK / 8][4];
+  block_scores<HD, NK>(s, qa, ks, bias, nvalid, causal, kbase, lim0, lim1, lane);
+  float bm0 = neg_inf(), bm1 = neg_inf();
+#pragma unroll
+  for (int n = 0; n < NK / 8; ++n) {
     bm0 = fmaxf(bm0, fmaxf(s[n][0], s[n][1]));
     bm1 = fmaxf(bm1, fmaxf(s[n][2], s[n][3]));
   }
   bm0 = quad_max(bm0);
   bm1 = quad_max(bm1);
   const float mn0 = fmaxf(mrow[0], bm0), mn1 = fmaxf(mrow[1], bm1);
-  const float c0 = mn0 == neg_inf() ? 1.f : expf(mrow[0] - mn0);
-  const float c1 = mn1 == neg_inf() ? 1.f : expf(mrow[1] - mn1);
   float ps0 = 0.f, ps1 = 0.f;
+  if (mn0 != neg_inf()) {
 #pragma unroll
-  for (int n = 0; n < NK / 8; ++n) {
-    s[n][0] = mn0 == neg_inf() ? 0.f : expf(s[n][0] - mn0);
-    s[n][1] = mn0 == neg_inf() ? 0.f : expf(s[n][1] - mn0);
-    s[n][2] = mn1 == neg_inf() ? 0.f : expf(s[n][2] - mn1);
-    s[n][3] = mn1 == neg_inf() ? 0.f : expf(s[n][3] - mn1);
-    ps0 += s[n][0] + s[n][1];
-    ps1 += s[n][2] + s[n][3];
+    for (int n = 0; n < NK / 8; ++n) ps0 += expf(s[n][0] - mn0) + expf(s[n][1] - mn0);
+  }
+  if (mn1 != neg_inf()) {
+#pragma unroll
+    for (int n = 0; n < NK / 8; ++n) ps1 += expf(s[n][2] - mn1) + expf(s[n][3] - mn1);
   }
   ps0 = quad_sum(ps0);
   ps1 = quad_sum(ps1);
-  lrow[0] = lrow[0] * c0 + ps0;
-  lrow[1] = lrow[1] * c1 + ps1;
+  lrow[0] = (mn0 == neg_inf() ? 0.f : lrow[0] * expf(mrow[0] - mn0)) + ps0;
+  lrow[1] = (mn1 == neg_inf() ? 0.f : lrow[1] * expf(mrow[1] - mn1)) + ps1;
   mrow[0] = mn0;
   mrow[1] = mn1;
+}
+
+// Pass 2: p = bf16(exp(s - max) / sum) exactly as the reference normalises before its bf16 cast
+// (F.softmax(...).to(dtype), bolt3.py:249), then o += p v.
+template <int HD, int NK>
+B3_DEV void block_pv(float (&o)[HD / 8][4], const float (&mrow)[2], const float (&lrow)[2],
+                     const uint32_t (&qa)[HD / 16][4], const bf16* ks, const bf16* vs, const float* bias,
+                     int nvalid, bool causal, int kbase, int lim0, int lim1, int lane) {
+  float s[NK / 8][4];
+  block_scores<HD, NK>(s, qa, ks, bias, nvalid, causal, kbase, lim0, lim1, lane);
 #pragma unroll
-  for (int n = 0; n < HD / 8; ++n) {
-    o[n][0] *= c0; o[n][1] *= c0; o[n][2] *= c1; o[n][3] *= c1;
+  for (int n = 0; n < NK / 8; ++n) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float m = mrow[q >> 1], l = lrow[q >> 1];
+      s[n][q] = s[n][q] == neg_inf() ? 0.f : __fdiv_rn(expf(s[n][q] - m), l);
+    }
   }
   uint32_t pk[NK / 16][4];
 #pragma unroll
@@ -219,11 +240,13 @@ __global__ void __launch_bounds__(NT, 1) attend_kernel(bolt3_attend_args a) {
     jb.n = min(KB, L1 - j * KB); jb.kind = 3; jb.kbase = L0 + j * KB; jb.slot0 = 0;
     return jb;
   };
+  // step j < n_jobs: statistics pass (keys only); step j >= n_jobs: P@V pass (keys and values)
   auto issue = [&](int j, int buf) {
-    const Job jb = job_at(j);
+    const bool pv = j >= n_jobs;
+    const Job jb = job_at(pv ? j - n_jobs : j);
     const int rows = jb.kind == 0 ? 16 : KB;
     load_rows<HD>(sm.k + buf * KB * HD, jb.k, rows, jb.n);
-    load_rows<HD>(sm.v + buf * KB * HD, jb.v, rows, jb.n);
+    if (pv) load_rows<HD>(sm.v + buf * KB * HD, jb.v, rows, jb.n);
     if (jb.kind == 1) {
       for (int i = tid; i < KB; i += NT) {
         const int s_ = jb.slot0 + i;
@@ -266,8 +289,9 @@ __global__ void __launch_bounds__(NT, 1) attend_kernel(bolt3_attend_args a) {
   int imax = 0;
   for (int r = r0; r < min(r0 + 16, n_rows); ++r) { int gg, ii; row_head_tok(r, gg, ii); imax = max(imax, ii); }
 
-  for (int j = 0; j < n_jobs; ++j) {
-    if (j + 1 < n_jobs) {
+  const int n_steps = 2 * n_jobs;
+  for (int j = 0; j < n_steps; ++j) {
+    if (j + 1 < n_steps) {
       issue(j + 1, (j + 1) & 1);
       cp_async_commit();
       cp_async_wait<1>();
@@ -280,27 +304,30 @@ __global__ void __launch_bounds__(NT, 1) attend_kernel(bolt3_attend_args a) {
       for (int kt = 0; kt < HD / 16; ++kt)
         ldsm_x4(qa[kt], sm.q + swz<HD>(r0 + (lane & 15), kt * 16 + (lane >> 4) * 8));
     }
-    const Job jb = job_at(j);
+    const bool pv = j >= n_jobs;
+    const Job jb = job_at(pv ? j - n_jobs : j);
     const int buf = j & 1;
     const bool skip = !warp_active || (jb.kind == 3 && jb.kbase > n_before + imax);
     if (!skip) {
-      if (jb.kind == 0)
-        attend_block<HD, 16>(o, mrow, lrow, qa, sm.k + buf * KB * HD, sm.v + buf * KB * HD, nullptr,
-                             jb.n, false, 0, lim0, lim1, lane);
-      else
-        attend_block<HD, KB>(o, mrow, lrow, qa, sm.k + buf * KB * HD, sm.v + buf * KB * HD,
-                             jb.kind == 1 ? sm.bias[buf] : nullptr, jb.n, jb.kind == 3, jb.kbase,
-                             lim0, lim1, lane);
+      const bf16* kt_ = sm.k + buf * KB * HD;
+      const bf16* vt_ = sm.v + buf * KB * HD;
+      const float* bs = jb.kind == 1 ? sm.bias[buf] : nullptr;
+      if (!pv) {
+        if (jb.kind == 0) block_stats<HD, 16>(mrow, lrow, qa, kt_, nullptr, jb.n, false, 0, lim0, lim1, lane);
+        else block_stats<HD, KB>(mrow, lrow, qa, kt_, bs, jb.n, jb.kind == 3, jb.kbase, lim0, lim1, lane);
+      } else {
+        if (jb.kind == 0) block_pv<HD, 16>(o, mrow, lrow, qa, kt_, vt_, nullptr, jb.n, false, 0, lim0, lim1, lane);
+        else block_pv<HD, KB>(o, mrow, lrow, qa, kt_, vt_, bs, jb.n, jb.kind == 3, jb.kbase, lim0, lim1, lane);
+      }
     }
     __syncthreads();
   }
 
-  // ---- P@V result rounded to the storage dtype
-  const float il0 = 1.0f / lrow[0], il1 = 1.0f / lrow[1];
+  // ---- P@V result rounded to the storage dtype (the probabilities were normalised already)
 #pragma unroll
   for (int n = 0; n < HD / 8; ++n) {
-    o[n][0] = rbf(__fmul_rn(o[n][0], il0)); o[n][1] = rbf(__fmul_rn(o[n][1], il0));
-    o[n][2] = rbf(__fmul_rn(o[n][2], il1)); o[n][3] = rbf(__fmul_rn(o[n][3], il1));
+    o[n][0] = rbf(o[n][0]); o[n][1] = rbf(o[n][1]);
+    o[n][2] = rbf(o[n][2]); o[n][3] = rbf(o[n][3]);
   }
 
   if (has_bank) {

@@ -361,21 +361,27 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
 
     const bool full = n_filled >= S;
     if (n_filled == 0) {
-      // ---- first fill: score = unbiased var(normalize(v)) (bolt3.py:180)
+      // ---- first fill: score = unbiased var(normalize(v)) (bolt3.py:180). The normalised values
+      // are fp32 as in the reference; mean and variance accumulate in fp64 (the CPU reference's
+      // variance reduction is exact to fp32 rounding given its inputs, which this reproduces).
       for (int r = warp; r < l_tok; r += 8) {
         constexpr int EPL = HD / 32;
         const bf16* p = sm.vv + swz<HD>(r, lane * EPL);
-        const float inv = fmaxf(sm.nv[r], 1e-12f);
-        float xs[EPL], sum = 0.f;
+        const float den = fmaxf(sm.nv[r], 1e-12f);
+        float xs[EPL];
+        double sum = 0.0;
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) { xs[e] = __fdiv_rn(bf2f(p[e]), inv); sum += xs[e]; }
-        const float mean = __fdiv_rn(warp_sum(sum), (float)HD);
-        float sq = 0.f;
+        for (int e = 0; e < EPL; ++e) { xs[e] = __fdiv_rn(bf2f(p[e]), den); sum += (double)xs[e]; }
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) { const float d = xs[e] - mean; sq = fmaf(d, d, sq); }
-        sq = warp_sum(sq);
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        const double mean = sum / HD;
+        double sq = 0.0;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) { const double d = (double)xs[e] - mean; sq += d * d; }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
         if (lane == 0) {
-          sm.score[r] = __fdiv_rn(sq, (float)(HD - 1));
+          sm.score[r] = (float)(sq / (HD - 1));
           sm.rel[r] = 0.15f;  // initial utility of the very first fill (:181)
         }
       }
