@@ -1,0 +1,411 @@
+"""Bolt-3 hot-path benchmark: prefill tok/s and decode tok/s on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+
+One process per GPU (launched by torch.distributed.run for N > 1). Prefill is weak-scaled: every
+rank runs its own configs[1] workload (8 x 8192 tokens, Qwen3-4B shape); decode shards the 256
+sequences of configs[2] across ranks. Inputs are seeded synthetic tensors; weights are seeded
+random values of the Bolt3Attn parameter set. Rank 0 prints one JSON line.
+
+`--impl reference` times the reference algorithm's CPU implementation (the oracle port of
+vsa_lm/config/bolt3.py, fp32, all host threads) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+from vsa_lm_b200.roofline import decode_step_bytes, prefill_flops  # noqa: E402
+from vsa_lm_b200.workloads import layer_cfg, make_input, make_params  # noqa: E402
+
+METRIC = "Bolt3 prefill tok/s + decode tok/s, Qwen3-4B shape, 1-8 B200, % roofline"
+SHAPE = "qwen3_4b"
+PREFILL_B, PREFILL_T, DUP = 8, 8192, 0.3
+DEC_SEQ, DEC_PROMPT, DEC_STEPS = 256, 4096, 512
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def profile_traffic():
+    """Per-launch DRAM bytes of kernels captured with ncu (profiles/traffic.json), if present."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    return json.load(open(p)) if os.path.exists(p) else {}
+
+
+class Clocks:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.out = index, None, None
+
+    def __enter__(self):
+        try:
+            self.out = open(os.path.join("/tmp", f"bolt3_clocks_{os.getpid()}.csv"), "w+")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.out, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+
+    def summary(self):
+        if self.proc is None or self.out is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.out.seek(0)
+        rows = [r.split(",") for r in self.out.read().strip().splitlines() if r.strip()]
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[0]))
+                mx = float(r[1])
+                for n, v in zip(names, r[3:7]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def timed(fn, steps: int, warmup: int, world: int, stream=None):
+    """Run fn() warmup + steps times; return max-over-ranks seconds of the `steps` timed calls."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t = torch.tensor([s.elapsed_time(e) / 1e3], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def build_layer(device):
+    from vsa_lm_b200 import Bolt3Attn
+
+    cfg = layer_cfg(SHAPE)
+    m = Bolt3Attn(cfg)
+    m.load_state_dict(make_params(cfg, 0))
+    return cfg, m.to(device=device, dtype=torch.bfloat16).eval()
+
+
+def phase_times(m, x, reps: int = 3):
+    """CUDA-event time of each phase of one prefill (same launches as forward, timed one by one)."""
+    from vsa_lm_b200 import kernels as K
+
+    b, T, D = x.shape
+    H, HKV, HD = m.H, m.HKV, m.HD
+    dev = x.device
+    f = m.fused(dev)
+    c = f.consts
+    bf = dict(dtype=torch.bfloat16, device=dev)
+    q_raw, q_rope = torch.empty(b * H, T, HD, **bf), torch.empty(b * H, T, HD, **bf)
+    k_raw, k_rope, v = (torch.empty(b * HKV, T, HD, **bf) for _ in range(3))
+    beta = torch.empty(b * HKV, T, dtype=torch.float32, device=dev)
+    eta = torch.empty(b * H, T, dtype=torch.float32, device=dev)
+    ws = torch.empty(max(1, K.prefill_workspace_bytes(b * HKV, T, HD)), dtype=torch.uint8, device=dev)
+    bank = K.new_bank(b * HKV, HD, dev)
+    y = torch.empty(b, T, H, HD, **bf)
+    x2 = x.reshape(b * T, D)
+    proj = m.project(x2, f)
+    lib = K._lib.load()
+    import ctypes
+
+    from vsa_lm_b200 import _lib
+
+    def prep():
+        K.prep(proj, B=b, T=T, H=H, HKV=HKV, HD=HD, inv_freq=c["inv_freq"], eps=m.eps, q_norm_w=c["qn"],
+               k_norm_w=c["kn"], pos0=0, q_raw=q_raw, q_rope=q_rope, eta=eta, k_raw=k_raw, k_rope=k_rope,
+               v=v, beta=beta, q_head_stride=T, q_t_off=0, k_head_stride=T, k_t_off=0)
+
+    n_cons = K.n_consolidations(T)
+    snap = {}
+    off = 0
+
+    def carve(nbytes):
+        nonlocal off
+        t = ws[off:off + nbytes]
+        off = (off + nbytes + 255) // 256 * 256
+        return t
+
+    ns = b * HKV * n_cons
+    snap["ak_rope"] = carve(ns * 128 * HD * 2).view(torch.bfloat16).view(b * HKV, n_cons, 128, HD)
+    snap["av"] = carve(ns * 128 * HD * 2).view(torch.bfloat16).view(b * HKV, n_cons, 128, HD)
+    snap["mass"] = carve(ns * 128 * 4).view(torch.float32)
+    snap["act"] = carve(ns * 128)
+    snap["m"] = carve(ns * HD * HD * 4).view(torch.float32)
+
+    def scan():
+        K.consolidate(n_chains=b * HKV, hkv=HKV, HD=HD, bank=bank, init_blank=True, kr=k_raw, kp=k_rope, v=v,
+                      beta=beta, chain_tokens=T, token0=0, step_tokens=128, skip0=4, chunk_len=128, pos0=0,
+                      n_steps=n_cons, kappa=c["kappa"], gamma=c["gamma"], inv_freq=c["inv_freq"], snaps=snap)
+
+    def attend():
+        a = _lib.AttendArgs(
+            n_chains=b * HKV, hkv=HKV, G=H // HKV, HD=HD, q_rope=q_rope.data_ptr(), q_raw=q_raw.data_ptr(),
+            eta=eta.data_ptr(), Tq=T, prefill=1, seg0_k=k_rope.data_ptr(), seg0_v=v.data_ptr(),
+            seg0_chain_tokens=T, seg1_k=k_rope.data_ptr(), seg1_v=v.data_ptr(), seg1_chain_tokens=T,
+            bank_ak_rope=snap["ak_rope"].data_ptr(), bank_av=snap["av"].data_ptr(),
+            bank_mass=snap["mass"].data_ptr(), bank_act=snap["act"].data_ptr(), bank_m=snap["m"].data_ptr(),
+            bank_cap=n_cons, kappa=c["kappa"].data_ptr(), coef=c["coef"].data_ptr(),
+            res_w=c["res_w"].data_ptr(), eps=m.eps, y=y.data_ptr(), y_tokens=T)
+        _lib.check(lib.bolt3_attend(ctypes.byref(a), torch.cuda.current_stream().cuda_stream), "attend")
+
+    phases = {
+        "proj_in": lambda: m.project(x2, f),
+        "prep": prep,
+        "consolidate": scan,
+        "attend": attend,
+        "proj_out": lambda: torch.nn.functional.linear(y.view(b, T, H * HD), f.w_out),
+    }
+    out = {}
+    for name, fn in phases.items():
+        fn()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(reps):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        out[name] = s.elapsed_time(e) / 1e3 / reps
+    return out
+
+
+def run_native(args, rank, world, local):
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    hbm, tf_burst, tf_sus, peak_kind = peaks()
+    cfg, m = build_layer(dev)
+    D, H, HKV, HD = cfg["dim"], m.H, m.HKV, m.HD
+    B, T = args.batch, args.seq
+    x = make_input(B, T, D, dup=DUP, seed=1 + rank, device=dev, dtype=torch.bfloat16)
+
+    def step():
+        m(x)
+
+    with Clocks(local) as clk:
+        t_prefill = timed(step, args.steps, args.warmup, world)
+    clocks = clk.summary()
+    tok = B * T
+    value = world * tok * args.steps / t_prefill
+    flops = prefill_flops(B, T, D, H, HKV, HD)
+
+    # per-phase times and the dominant kernel's roofline
+    ph = phase_times(m, x)
+    traffic = profile_traffic()
+    ours = {"prep": None, "consolidate": "consolidate", "attend": "attend"}
+    phase_rl = {}
+    for name, t in ph.items():
+        if name in ("proj_in", "proj_out", "attend", "consolidate"):
+            ach = flops[name] / t / 1e12
+            phase_rl[name] = {"ms": t * 1e3, "bound": "tensor", "achieved": ach, "unit": "TFLOP/s",
+                              "frac": ach / tf_burst}
+        else:  # prep: HBM-bound elementwise
+            nbytes = tok * ((H * HD + 2 * HKV * HD + HKV + H) * 2 + (2 * H * HD + 3 * HKV * HD) * 2 + (H + HKV) * 4)
+            ach = nbytes / t / 1e9
+            phase_rl[name] = {"ms": t * 1e3, "bound": "hbm", "achieved": ach, "unit": "GB/s", "frac": ach / hbm}
+    own = {k: v for k, v in ph.items() if k in ("prep", "consolidate", "attend")}
+    dom = max(own, key=own.get)
+    rl = dict(phase_rl[dom])
+    rl.pop("ms")
+    rl["kernel"] = dom
+    rl["peak"] = tf_burst if rl["bound"] == "tensor" else hbm
+    rl["peak_source"] = peak_kind
+    rl["traffic"] = traffic.get(dom)
+    step_rl = flops["total"] / (t_prefill / args.steps) / 1e12
+
+    # end-to-end through the public module: pinned host input in, host output back, every step
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(B, T, D, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        xd = xh.to(dev, non_blocking=True)
+        yh.copy_(m(xd), non_blocking=True)
+
+    t_e2e = timed(e2e_step, max(1, args.steps // 2), 1, world)
+    e2e_value = world * tok * max(1, args.steps // 2) / t_e2e
+
+    decode = None if args.no_decode else run_decode(args, rank, world, dev, m, cfg, hbm)
+    cpu = cpu_baseline(args) if (rank == 0 and world == 1 and not args.no_cpu) else None
+    res = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_prefill / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"configs[1]: Bolt3Attn prefill, Qwen3-4B shape (D2560 H32/8 HD128 theta1e6 "
+                               f"qk_norm), {B} x {T} tokens per GPU, 30% near-duplicates, seeded random weights",
+                   "global_batch": B * world, "seq_len": T, "parallelism": f"dp{world} (sequence batches)",
+                   "l2": "inputs and intermediates larger than L2 (x alone 335 MB)"},
+        "roofline": rl,
+        "prefill_step_roofline": {"bound": "tensor", "achieved": step_rl, "peak": tf_burst, "unit": "TFLOP/s",
+                                  "frac": step_rl / tf_burst, "flops_per_token": flops["total"] / tok},
+        "phases": phase_rl,
+        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": xh.numel() * 2,
+                "d2h_bytes_per_step": yh.numel() * 2},
+        "gpu_launches": 3 * args.steps,
+        "clocks": clocks,
+        "decode": decode,
+        "cpu_baseline": cpu,
+    }
+    return res
+
+
+def run_decode(args, rank, world, dev, m, cfg, hbm):
+    """one Bolt-3 layer, 256 sequences (sharded), 4096-token prefill, then decode steps."""
+    from vsa_lm_b200 import Bolt3Decoder, Bolt3LayerState
+
+    n_seq = DEC_SEQ // world
+    D = cfg["dim"]
+    st = Bolt3LayerState(m, n_seq, dev)
+    m_res = torch.zeros(n_seq, m.HKV, m.HD, m.HD, device=dev)
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    for s in range(0, DEC_PROMPT, 128):
+        h = torch.randn(n_seq, 128, D, generator=g, device=dev).to(torch.bfloat16)
+        Bolt3Decoder.layer_step(m, st, h, s, m_res)
+    steps = DEC_STEPS
+    toks = torch.randn(steps + args.warmup, n_seq, 1, D, generator=g, device=dev).to(torch.bfloat16)
+    pos = [DEC_PROMPT]
+    i = [0]
+
+    def one():
+        Bolt3Decoder.layer_step(m, st, toks[i[0]], pos[0], m_res)
+        pos[0] += 1
+        i[0] += 1
+
+    for _ in range(args.warmup):
+        one()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        one()
+    e.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([s.elapsed_time(e) / 1e3], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t = float(t.item())
+    nb = decode_step_bytes(n_seq, D, m.H, m.HKV, m.HD)
+    ach = nb["total"] * steps / t / 1e9
+    ach_core = nb["state"] * steps / t / 1e9
+    return {"value": world * n_seq * steps / t, "unit": "tok/s", "steps": steps, "seqs_per_gpu": n_seq,
+            "prompt": DEC_PROMPT, "ms_per_step": t / steps * 1e3,
+            "workload": "configs[2]: one Bolt-3 layer step (projections, attention, o_proj, consolidation "
+                        "every 128 steps), 256 sequences after a 4096-token prefill",
+            "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                         "bytes_per_step": nb["total"], "state_only_frac": ach_core / hbm}}
+
+
+def cpu_baseline(args):
+    """The reference algorithm on the host cores (oracle port, fp32), bounded sample of configs[1]."""
+    from oracle import Store, forward, oracle_cfg
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = layer_cfg(SHAPE)
+    P = make_params(cfg, 0)
+    oc = oracle_cfg(cfg)
+    T = args.cpu_tokens
+    x = make_input(1, T, cfg["dim"], dup=DUP, seed=1)
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        forward(P, oc, x, Store("fp32"))
+        n += 1
+        if time.perf_counter() - t0 > args.cpu_seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": n * T / dt, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"configs[1] shape, 1 x {T} tokens, fp32, {n} forward(s) in {dt:.1f} s"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    cpu = cpu_baseline(args)
+    return {"metric": METRIC, "impl": "reference", "value": cpu["value"], "unit": "tok/s", "n_gpus": world,
+            "steps": 1, "warmup": 0, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "configs[1] shape prefill on the host cores (reference algorithm, CPU "
+                                   "PyTorch port)", "global_batch": 1, "seq_len": args.cpu_tokens,
+                       "parallelism": "host threads"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": cpu["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-tokens", type=int, default=2048)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--batch", type=int, default=PREFILL_B, help="prefill sequences per GPU (profiling cases)")
+    ap.add_argument("--seq", type=int, default=PREFILL_T, help="prefill tokens per sequence (profiling cases)")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        # the CPU reference runs on rank 0 only; the other ranks exit without work
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    if world > 1:
+        from datetime import timedelta
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    try:
+        res = run_native(args, rank, world, local)
+        if rank == 0 and res is not None:
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
