@@ -141,6 +141,20 @@ typedef struct bolt3_prefill_args {
 } bolt3_prefill_args;
 int bolt3_prefill_fwd(const bolt3_prefill_args* a, void* stream);
 
+/* ---- bolt3_prefill_fwd without a caller-provided workspace. No counterpart in the reference.
+ * For hosts that cannot allocate device memory on their hot path (an engine that pools all of HBM
+ * itself, a C-ABI host without a device allocator, a loop that cannot afford cudaMalloc's implicit
+ * device synchronisation). The snapshot workspace is a fixed BOLT3_NOALLOC_SCRATCH_BYTES array
+ * inside the library, reserved on every GPU that loads it until the process exits; `workspace` and
+ * `workspace_bytes` of the arguments are ignored. Work needing more than that returns
+ * BOLT3_ERR_CAPACITY (32 MiB covers 254 chain-consolidations at HD = 128: e.g. one Qwen3-4B-shape
+ * sequence of up to 4224 tokens, or configs[0] whole). The first call on a device looks up the
+ * array's device address with that device current; make it before any stream capture. Calls share
+ * the array: two calls that overlap on the GPU (different streams, or different host threads)
+ * race and must be ordered by the caller. Allocates nothing (no cudaMalloc / cudaFree). */
+#define BOLT3_NOALLOC_SCRATCH_BYTES (32u << 20)
+int bolt3_prefill_fwd_noalloc(const bolt3_prefill_args* a, void* stream);
+
 /* ---- utilities */
 int bolt3_abi_version(void);
 const char* bolt3_status_string(int status);

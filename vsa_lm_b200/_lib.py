@@ -86,11 +86,15 @@ SIGNATURES = {
     "bolt3_consolidate": ([ctypes.POINTER(ConsolidateArgs), _P], _I),
     "bolt3_attend": ([ctypes.POINTER(AttendArgs), _P], _I),
     "bolt3_prefill_fwd": ([ctypes.POINTER(PrefillArgs), _P], _I),
+    "bolt3_prefill_fwd_noalloc": ([ctypes.POINTER(PrefillArgs), _P], _I),
     "bolt3_prefill_workspace_size": ([_I, _I64, _I], _SZ),
     "bolt3_abi_version": ([], _I),
     "bolt3_status_string": ([_I], ctypes.c_char_p),
     "bolt3_topk_order_host": ([_P, _I, _I, _I, _P], _I),
 }
+
+# Fixed scratch of bolt3_prefill_fwd_noalloc (BOLT3_NOALLOC_SCRATCH_BYTES in include/bolt3.h)
+NOALLOC_SCRATCH_BYTES = 32 << 20
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libbolt3.so")
 _lib = None

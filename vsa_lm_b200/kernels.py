@@ -132,6 +132,29 @@ def prefill(*, B: int, T: int, H: int, HKV: int, HD: int, q_rope, q_raw, eta, k_
     _lib.check(lib.bolt3_prefill_fwd(ctypes.byref(a), _stream()), "bolt3_prefill_fwd")
 
 
+def prefill_noalloc(*, B: int, T: int, H: int, HKV: int, HD: int, q_rope, q_raw, eta, k_raw, k_rope, v, beta,
+                    kappa, gamma, coef, inv_freq, res_w, eps: float, bank: dict, y: torch.Tensor,
+                    status: torch.Tensor | None = None) -> None:
+    """Phases B + C like `prefill`, with the snapshot workspace taken from the library's fixed
+    per-GPU array instead of the caller (bolt3_prefill_fwd_noalloc). For hosts that cannot allocate
+    device memory on their hot path; the work must fit in `_lib.NOALLOC_SCRATCH_BYTES`."""
+    lib = _lib.load()
+    need = prefill_workspace_bytes(B * HKV, T, HD)
+    if need > _lib.NOALLOC_SCRATCH_BYTES:
+        raise ValueError(f"prefill of {B} x {T} tokens needs {need} bytes of scratch; the no-alloc entry point "
+                         f"has a fixed {_lib.NOALLOC_SCRATCH_BYTES} bytes (use `prefill` with a workspace)")
+    a = _lib.PrefillArgs(
+        B=B, T=T, H=H, HKV=HKV, HD=HD, q_rope=q_rope.data_ptr(), q_raw=q_raw.data_ptr(),
+        eta=eta.data_ptr(), k_raw=k_raw.data_ptr(), k_rope=k_rope.data_ptr(), v=v.data_ptr(),
+        beta=beta.data_ptr(), kappa=kappa.data_ptr(), gamma=gamma.data_ptr(), coef=coef.data_ptr(),
+        inv_freq=inv_freq.data_ptr(), res_w=res_w.data_ptr(), eps=eps, workspace=None, workspace_bytes=0,
+        ak=bank["ak"].data_ptr(), av=bank["av"].data_ptr(), ak_rope=_ptr(bank.get("ak_rope")),
+        mass=bank["mass"].data_ptr(), util=bank["util"].data_ptr(), pm=bank["pm"].data_ptr(),
+        act=bank["act"].data_ptr(), m_res=bank["m_res"].data_ptr(), n_filled=bank["n_filled"].data_ptr(),
+        y=y.data_ptr(), status=_ptr(status))
+    _lib.check(lib.bolt3_prefill_fwd_noalloc(ctypes.byref(a), _stream()), "bolt3_prefill_fwd_noalloc")
+
+
 def new_bank(n_chains: int, HD: int, device, S: int = S_SLOTS) -> dict:
     """Uninitialised bank tensors (the consolidation kernel initialises them with init_blank)."""
     bf = dict(dtype=torch.bfloat16, device=device)
