@@ -139,6 +139,7 @@ def phase_times(m, x, reps: int = 3):
     k_raw, k_rope, v = (torch.empty(b * HKV, T, HD, **bf) for _ in range(3))
     beta = torch.empty(b * HKV, T, dtype=torch.float32, device=dev)
     eta = torch.empty(b * H, T, dtype=torch.float32, device=dev)
+    q_l2 = torch.empty(b * H, T, dtype=torch.float32, device=dev)
     ws = torch.empty(max(1, K.prefill_workspace_bytes(b * HKV, T, HD)), dtype=torch.uint8, device=dev)
     bank = K.new_bank(b * HKV, HD, dev)
     y = torch.empty(b, T, H, HD, **bf)
@@ -152,7 +153,7 @@ def phase_times(m, x, reps: int = 3):
     def prep():
         K.prep(proj, B=b, T=T, H=H, HKV=HKV, HD=HD, inv_freq=c["inv_freq"], eps=m.eps, q_norm_w=c["qn"],
                k_norm_w=c["kn"], pos0=0, q_raw=q_raw, q_rope=q_rope, eta=eta, k_raw=k_raw, k_rope=k_rope,
-               v=v, beta=beta, q_head_stride=T, q_t_off=0, k_head_stride=T, k_t_off=0)
+               v=v, beta=beta, q_head_stride=T, q_t_off=0, k_head_stride=T, k_t_off=0, q_l2=q_l2)
 
     n_cons = K.n_consolidations(T)
     snap = {}
@@ -184,7 +185,7 @@ def phase_times(m, x, reps: int = 3):
             bank_ak_rope=snap["ak_rope"].data_ptr(), bank_av=snap["av"].data_ptr(),
             bank_mass=snap["mass"].data_ptr(), bank_act=snap["act"].data_ptr(), bank_m=snap["m"].data_ptr(),
             bank_cap=n_cons, kappa=c["kappa"].data_ptr(), coef=c["coef"].data_ptr(),
-            res_w=c["res_w"].data_ptr(), eps=m.eps, y=y.data_ptr(), y_tokens=T)
+            res_w=c["res_w"].data_ptr(), eps=m.eps, y=y.data_ptr(), y_tokens=T, q_l2=q_l2.data_ptr())
         _lib.check(lib.bolt3_attend(ctypes.byref(a), torch.cuda.current_stream().cuda_stream), "attend")
 
     phases = {

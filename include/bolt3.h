@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define BOLT3_ABI_VERSION 1
+#define BOLT3_ABI_VERSION 3
 
 enum bolt3_status {
   BOLT3_OK = 0,
@@ -55,6 +55,7 @@ typedef struct bolt3_prep_args {
   float* eta; int64_t eta_head_stride; int64_t eta_t_off;
   void* k_raw; void* k_rope; void* v; int64_t k_head_stride; int64_t k_t_off;
   float* beta; int64_t beta_head_stride; int64_t beta_t_off;
+  float* q_l2;                        /* optional: |q_raw| per (head, token), laid out like eta */
 } bolt3_prep_args;
 int bolt3_prep(const bolt3_prep_args* a, void* stream);
 
@@ -68,7 +69,9 @@ int bolt3_prep(const bolt3_prep_args* a, void* stream);
  * arrays (init_blank = 1 starts from the empty bank of bolt3.py:83-92). After each step the
  * state the attention reads is optionally written to snapshot slot snap0 + i:
  *   snap_ak_rope, snap_av [chains][snap_cap][S][HD] bf16; snap_mass [chains][snap_cap][S] fp32;
- *   snap_act [chains][snap_cap][S] uint8; snap_m [chains][snap_cap][HD][HD] fp32.
+ *   snap_act [chains][snap_cap][S] uint8; snap_m [chains][snap_cap] x HD*HD*4 bytes: M_res split
+ *   into bf16 hi and lo terms, each the 128-byte-swizzled MN-major tensor-core operand image
+ *   [HD/64 column blocks][HD rows d][64 columns e] that bolt3_attend copies as is.
  * `ak_rope` (optional) receives RoPE(ak, pm) of the final bank. `status` (optional, device int)
  * is OR-ed with 1 when a kernel-side bounds check of the tie-order emulation fires. */
 typedef struct bolt3_consolidate_args {
@@ -80,7 +83,7 @@ typedef struct bolt3_consolidate_args {
   int64_t chain_tokens;               /* tokens between chains in kr / kp / v / beta */
   int64_t token0; int64_t step_tokens; int skip0; int chunk_len; int64_t pos0; int n_steps;
   const float* kappa; const float* gamma; const float* inv_freq;   /* [hkv], [hkv], [HD/2] */
-  void* snap_ak_rope; void* snap_av; float* snap_mass; uint8_t* snap_act; float* snap_m;
+  void* snap_ak_rope; void* snap_av; float* snap_mass; uint8_t* snap_act; void* snap_m;
   int64_t snap_cap; int64_t snap0;
   int32_t* status;
 } bolt3_consolidate_args;
@@ -98,7 +101,10 @@ int bolt3_consolidate(const bolt3_consolidate_args* a, void* stream);
  *   prefill = 1: block r is chunk r of a sequence of Tq tokens held in k_rope / v (Tk = Tq);
  *     segment 0 = chunk r-1, segment 1 = chunk r, sinks = tokens 0..3, bank = snapshot r-2.
  *   prefill = 0: one query block (Tq <= 128 new tokens); segment pointers, lengths, sinks and the
- *     bank (snapshot slot 0 of the snap_* arrays) are given explicitly. */
+ *     bank (slot 0 of [chains][bank_cap] arrays) are given explicitly.
+ * bank_m: prefill = 1 reads the split bf16 image bolt3_consolidate writes to snap_m; prefill = 0
+ * reads M_res itself, fp32 [chains][HD][HD]. q_l2 (optional, [B*H][Tq] fp32) holds |q_raw| per row
+ * as bolt3_prep writes it; without it the kernel computes the norms. */
 typedef struct bolt3_attend_args {
   int n_chains, hkv, G, HD;
   const void* q_rope; const void* q_raw; const float* eta; int64_t Tq;
@@ -110,11 +116,13 @@ typedef struct bolt3_attend_args {
   const void* sink_k; const void* sink_v; int64_t sink_chain_tokens; int has_sinks;
   /* attractor bank: [chains][snap_cap][S]... as written by bolt3_consolidate */
   const void* bank_ak_rope; const void* bank_av; const float* bank_mass; const uint8_t* bank_act;
-  const float* bank_m; int64_t bank_cap; int has_bank;
+  const void* bank_m; int64_t bank_cap; int has_bank;
   const float* kappa;                  /* [hkv] */
   const float* coef;                   /* [hkv]: (1 - gamma) / sqrt(HD), fp32 */
   const float* res_w; float eps;       /* res_norm weight [HD] (fp32), eps */
   void* y; int64_t y_tokens;           /* bf16 [B][y_tokens][H][HD]; row of query token t: t */
+  int32_t* status;                     /* optional device int: OR-ed with 2 if a bounded wait expired */
+  const float* q_l2;                   /* optional |q_raw| per row, [B*H][Tq] */
 } bolt3_attend_args;
 int bolt3_attend(const bolt3_attend_args* a, void* stream);
 
@@ -138,6 +146,7 @@ typedef struct bolt3_prefill_args {
   float* m_res; int32_t* n_filled;
   void* y;                            /* bf16 [B][T][H][HD] */
   int32_t* status;
+  const float* q_l2;                  /* optional |q_raw| per row from bolt3_prep, [B*H][T] */
 } bolt3_prefill_args;
 int bolt3_prefill_fwd(const bolt3_prefill_args* a, void* stream);
 

@@ -29,6 +29,7 @@ class PrepArgs(ctypes.Structure):
         ("eta", _P), ("eta_head_stride", _I64), ("eta_t_off", _I64),
         ("k_raw", _P), ("k_rope", _P), ("v", _P), ("k_head_stride", _I64), ("k_t_off", _I64),
         ("beta", _P), ("beta_head_stride", _I64), ("beta_t_off", _I64),
+        ("q_l2", _P),
     ]
 
 
@@ -62,6 +63,8 @@ class AttendArgs(ctypes.Structure):
         ("bank_cap", _I64), ("has_bank", _I),
         ("kappa", _P), ("coef", _P), ("res_w", _P), ("eps", _F),
         ("y", _P), ("y_tokens", _I64),
+        ("status", _P),
+        ("q_l2", _P),
     ]
 
 
@@ -77,6 +80,7 @@ class PrefillArgs(ctypes.Structure):
         ("m_res", _P), ("n_filled", _P),
         ("y", _P),
         ("status", _P),
+        ("q_l2", _P),
     ]
 
 
@@ -117,7 +121,7 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = argt
             fn.restype = rest
-        if lib.bolt3_abi_version() != 1:
+        if lib.bolt3_abi_version() != 3:
             raise RuntimeError("libbolt3.so ABI version mismatch; rebuild with `python -m vsa_lm_b200.build`")
         _lib = lib
         return lib

@@ -222,16 +222,18 @@ class Bolt3Attn(nn.Module):
         v = torch.empty_like(k_raw)
         beta = torch.empty(b * HKV, T, dtype=torch.float32, device=dev)
         eta = torch.empty(b * H, T, dtype=torch.float32, device=dev)
+        q_l2 = torch.empty(b * H, T, dtype=torch.float32, device=dev)
         K.prep(proj, B=b, T=T, H=H, HKV=HKV, HD=HD, inv_freq=c["inv_freq"], eps=self.eps,
                q_norm_w=c["qn"], k_norm_w=c["kn"], pos0=0, q_raw=q_raw, q_rope=q_rope, eta=eta,
                k_raw=k_raw, k_rope=k_rope, v=v, beta=beta, q_head_stride=T, q_t_off=0,
-               k_head_stride=T, k_t_off=0)
+               k_head_stride=T, k_t_off=0, q_l2=q_l2)
         ws = torch.empty(max(1, K.prefill_workspace_bytes(b * HKV, T, HD)), dtype=torch.uint8, device=dev)
         bank = K.new_bank(b * HKV, HD, dev)
         y = torch.empty(b, T, H, HD, **bf)
         K.prefill(B=b, T=T, H=H, HKV=HKV, HD=HD, q_rope=q_rope, q_raw=q_raw, eta=eta, k_raw=k_raw,
                   k_rope=k_rope, v=v, beta=beta, kappa=c["kappa"], gamma=c["gamma"], coef=c["coef"],
-                  inv_freq=c["inv_freq"], res_w=c["res_w"], eps=self.eps, workspace=ws, bank=bank, y=y)
+                  inv_freq=c["inv_freq"], res_w=c["res_w"], eps=self.eps, workspace=ws, bank=bank, y=y,
+                  q_l2=q_l2)
         out = F.linear(y.view(b, T, H * HD), f.w_out)
         return out.to(x.dtype)
 
@@ -381,11 +383,12 @@ class Bolt3Decoder:
         q_raw = torch.empty(b * H, t, HD, **bf)
         q_rope = torch.empty_like(q_raw)
         eta = torch.empty(b * H, t, dtype=torch.float32, device=dev)
+        q_l2 = torch.empty(b * H, t, dtype=torch.float32, device=dev)
         k_off = st.cur_slot * C + st.cur_len
         K.prep(proj, B=b, T=t, H=H, HKV=HKV, HD=HD, inv_freq=c["inv_freq"], eps=ly.eps, q_norm_w=c["qn"],
                k_norm_w=c["kn"], pos0=pos_start, q_raw=q_raw, q_rope=q_rope, eta=eta, k_raw=st.ring_kr,
                k_rope=st.ring_kp, v=st.ring_v, beta=st.ring_b, q_head_stride=t, q_t_off=0,
-               k_head_stride=2 * C, k_t_off=k_off)
+               k_head_stride=2 * C, k_t_off=k_off, q_l2=q_l2)
         has_prev = st.prev_slot >= 0
         p0 = st.prev_slot * C if has_prev else 0
         c0 = st.cur_slot * C
@@ -401,7 +404,7 @@ class Bolt3Decoder:
             seg1_k=st.ring_kp[:, c0:], seg1_v=st.ring_v[:, c0:], seg1_chain_tokens=2 * C,
             seg1_len=st.cur_len + t, len_before=st.cur_len,
             sinks=(st.sink_k, st.sink_v) if st.sinks_set else None, bank=bank, kappa=c["kappa"],
-            coef=c["coef"], res_w=c["res_w"], eps=ly.eps, y=y)
+            coef=c["coef"], res_w=c["res_w"], eps=ly.eps, y=y, q_l2=q_l2)
         out = F.linear(y.view(b, t, H * HD), f.w_out)
         st.cur_len += t
         if st.cur_len >= C:                                                   # bolt3.py:406-425

@@ -86,7 +86,7 @@ extern "C" int bolt3_prefill_fwd(const bolt3_prefill_args* a, void* stream) {
     c.snap_ak_rope = ws + L.ak_rope; c.snap_av = ws + L.av;
     c.snap_mass = reinterpret_cast<float*>(ws + L.mass);
     c.snap_act = reinterpret_cast<uint8_t*>(ws + L.act);
-    c.snap_m = reinterpret_cast<float*>(ws + L.m);
+    c.snap_m = ws + L.m;
     c.snap_cap = n_cons; c.snap0 = 0;
     c.status = a->status;
     const int rc = bolt3_consolidate(&c, stream);
@@ -102,10 +102,12 @@ extern "C" int bolt3_prefill_fwd(const bolt3_prefill_args* a, void* stream) {
     t.bank_ak_rope = ws + L.ak_rope; t.bank_av = ws + L.av;
     t.bank_mass = reinterpret_cast<const float*>(ws + L.mass);
     t.bank_act = reinterpret_cast<const uint8_t*>(ws + L.act);
-    t.bank_m = reinterpret_cast<const float*>(ws + L.m);
+    t.bank_m = ws + L.m;
     t.bank_cap = n_cons;
   }
   t.kappa = a->kappa; t.coef = a->coef; t.res_w = a->res_w; t.eps = a->eps;
   t.y = a->y; t.y_tokens = a->T;
+  t.status = a->status;
+  t.q_l2 = a->q_l2;
   return bolt3_attend(&t, stream);
 }

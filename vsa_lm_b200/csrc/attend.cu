@@ -1,18 +1,28 @@
-// Phase C: three-field softmax attention with the fused M_res read-out epilogue.
+// Phase C: three-field softmax attention with the fused M_res read-out, on tcgen05 + TMEM.
 //
-// One CTA = one 128-row query tile of one chain: rows are (query head g, token i) pairs of the same
-// KV head, so every key/value block loaded into shared memory serves all G query heads of the
-// group (the reference materialises G copies with repeat_kv, surgery.py:96-100). Keys are visited
-// block by block with an online (running-max) softmax:
-//   [4 sinks] [S attractors: RoPE'd at their mean position, + kappa*log(mass), -inf if inactive]
-//   [previous chunk] [current chunk, causal]                (vsa_lm/config/bolt3.py:219-249)
-// The epilogue reads M_res out for the same rows (bolt3.py:251-256):
-//   y = bf16( bf16(P@V) + bf16( eta * RMSNorm_w( q_raw @ (M_hi + M_lo) / |q_raw| * (1-gamma)/sqrt(HD) ) ) )
-// with M split into two bf16 terms for the tensor cores.
+// One CTA owns a 128-row query tile: prefill = 128 tokens of one query head; decode = the (head g,
+// token) pairs of one KV head. Its scores against all keys stay resident in tensor memory, so the
+// softmax is exact in one sweep of MMAs:
+//   TMEM columns [0,128) attractors, [128,256) previous chunk, [256,384) current chunk (fp32 S);
+//   [384, 384+HD) the P@V accumulator O. P (bf16, two per column) is written back over S in
+//   columns [0,192) and is the A operand of the P@V MMAs; the M_res read-out accumulates into
+//   columns [192, 192+HD) once the softmax has consumed them.
+// Keys: [4 sinks] [S attractors: RoPE'd at their mean position, + kappa*log(mass), -inf if inactive]
+// [previous chunk] [current chunk, causal] (vsa_lm/config/bolt3.py:219-249). The 4 sink scores are
+// computed on the CUDA cores; everything else is tcgen05.mma with bf16 operands in 128-byte swizzled
+// shared memory and fp32 accumulation. Probabilities are normalised before their bf16 cast exactly
+// as the reference does (F.softmax(...).to(dtype), bolt3.py:249). The epilogue reads M_res out
+// (bolt3.py:251-256): y = bf16( bf16(P@V) + bf16( eta * RMSNorm_w( q_raw @ (M_hi + M_lo) / |q_raw|
+// * (1-gamma)/sqrt(HD) ) ) ), with M split into two bf16 terms.
+//
+// Warps 0-3 own one query row per thread (TMEM lane = row) for the softmax and the epilogue;
+// warps 4-7 load V, q_raw and M_res while the softmax runs. Thread 0 issues the MMAs.
 #include "../../include/bolt3.h"
 #include "common.cuh"
+#include "tc5.cuh"
 
 #include <algorithm>
+#include <type_traits>
 
 namespace {
 
@@ -21,156 +31,55 @@ using namespace b3;
 constexpr int S = 128;
 constexpr int CC = 128;
 constexpr int NT = 256;
-constexpr int KB = 64;  // keys per block
+constexpr uint32_t kWaitIters = 1u << 24;
+constexpr uint32_t kColO = 384, kColR = 192;
 
 template <int HD>
-struct Smem {
-  bf16 q[128 * HD];        // q_rope tile; q_raw tile in the epilogue
-  bf16 k[2 * KB * HD];     // double-buffered key blocks; M_hi [HD][HD] in the epilogue
-  bf16 v[2 * KB * HD];     // double-buffered value blocks; M_lo in the epilogue
-  float bias[2][KB];
-  float qn[128];
+struct __align__(1024) Smem {
+  unsigned char q[HD / 64][16384];        // q_rope tile, then the q_raw tile (K-major SW128)
+  unsigned char kv[3][HD / 64][16384];    // K tiles of attractors / prev / cur, then their V tiles
+  unsigned char m[2][HD / 64][HD * 128];  // M_res hi / lo (MN-major B): rows = input dim d, N blocks of e
+  bf16 sink_k[4][HD];
+  bf16 sink_v[4][HD];
+  float sink_vf[4][HD];     // sink values in fp32 for the epilogue
+  float sink_s[128][4];     // scaled sink scores per query row
+  float res_w[HD];
+  float bias[S];
+  uint64_t bar_s, bar_o;
+  uint32_t tbase;
+  int err;
 };
 
-struct Job {
-  const bf16* k;
-  const bf16* v;
-  int n;        // valid keys in this block
-  int kind;     // 0 sinks, 1 attractors, 2 previous chunk, 3 current chunk (causal)
-  int kbase;    // window position of the block's first key (kinds 2, 3)
-  int slot0;    // first attractor slot (kind 1)
-};
-
+// 16-byte-chunk cp.async of 128 rows of an [*][HD] bf16 array into a SW128 tile; rows at or beyond
+// `valid` are zero-filled. Threads t, t + nthreads, ... take part.
 template <int HD>
-B3_DEV void load_rows(bf16* s, const bf16* g, int rows, int rows_valid) {
+B3_DEV void load_tile(unsigned char (*dst)[16384], const bf16* src, int valid, int t, int nthreads) {
   constexpr int CPR = HD / 8;
-  for (int i = threadIdx.x; i < rows * CPR; i += NT) {
+  for (int i = t; i < 128 * CPR; i += nthreads) {
     const int r = i / CPR, ch = i % CPR;
-    const bool ok = r < rows_valid;
-    cp_async16(s + swz<HD>(r, ch * 8), ok ? g + (int64_t)r * HD + ch * 8 : g, ok);
-  }
-}
-
-// Scores of one key block for the warp's 16 rows: s = q k^T * scale (+ bias), masked to -inf.
-template <int HD, int NK>
-B3_DEV void block_scores(float (&s)[NK / 8][4], const uint32_t (&qa)[HD / 16][4], const bf16* ks,
-                         const float* bias, int nvalid, bool causal, int kbase, int lim0, int lim1,
-                         int lane) {
-  constexpr float scale = HD == 128 ? 0.08838834764831845f : 0.125f;  // fp32(HD ** -0.5)
-  const int t4 = lane & 3;
-#pragma unroll
-  for (int n = 0; n < NK / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
-#pragma unroll
-  for (int kt = 0; kt < HD / 16; ++kt) {
-#pragma unroll
-    for (int np = 0; np < NK / 16; ++np) {
-      uint32_t b[4];
-      ldsm_x4(b, ks + swz<HD>(np * 16 + (lane & 7) + (lane >> 4) * 8, kt * 16 + ((lane >> 3) & 1) * 8));
-      mma16816(s[2 * np], qa[kt], b[0], b[1]);
-      mma16816(s[2 * np + 1], qa[kt], b[2], b[3]);
-    }
-  }
-#pragma unroll
-  for (int n = 0; n < NK / 8; ++n) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int col = n * 8 + 2 * t4 + (q & 1);
-      float x = __fmul_rn(s[n][q], scale);
-      if (bias) x = __fadd_rn(x, bias[col]);
-      const bool vis = col < nvalid && (!causal || kbase + col <= (q < 2 ? lim0 : lim1));
-      s[n][q] = vis ? x : neg_inf();
-    }
-  }
-}
-
-// Pass 1: running row max and sum of exp over one block.
-template <int HD, int NK>
-B3_DEV void block_stats(float (&mrow)[2], float (&lrow)[2], const uint32_t (&qa)[HD / 16][4],
-                        const bf16* ks, const float* bias, int nvalid, bool causal, int kbase, int lim0,
-                        int lim1, int lane) {
-  float s[NK / 8][4];
-  block_scores<HD, NK>(s, qa, ks, bias, nvalid, causal, kbase, lim0, lim1, lane);
-  float bm0 = neg_inf(), bm1 = neg_inf();
-#pragma unroll
-  for (int n = 0; n < NK / 8; ++n) {
-    bm0 = fmaxf(bm0, fmaxf(s[n][0], s[n][1]));
-    bm1 = fmaxf(bm1, fmaxf(s[n][2], s[n][3]));
-  }
-  bm0 = quad_max(bm0);
-  bm1 = quad_max(bm1);
-  const float mn0 = fmaxf(mrow[0], bm0), mn1 = fmaxf(mrow[1], bm1);
-  float ps0 = 0.f, ps1 = 0.f;
-  if (mn0 != neg_inf()) {
-#pragma unroll
-    for (int n = 0; n < NK / 8; ++n) ps0 += expf(s[n][0] - mn0) + expf(s[n][1] - mn0);
-  }
-  if (mn1 != neg_inf()) {
-#pragma unroll
-    for (int n = 0; n < NK / 8; ++n) ps1 += expf(s[n][2] - mn1) + expf(s[n][3] - mn1);
-  }
-  ps0 = quad_sum(ps0);
-  ps1 = quad_sum(ps1);
-  lrow[0] = (mn0 == neg_inf() ? 0.f : lrow[0] * expf(mrow[0] - mn0)) + ps0;
-  lrow[1] = (mn1 == neg_inf() ? 0.f : lrow[1] * expf(mrow[1] - mn1)) + ps1;
-  mrow[0] = mn0;
-  mrow[1] = mn1;
-}
-
-// Pass 2: p = bf16(exp(s - max) / sum) exactly as the reference normalises before its bf16 cast
-// (F.softmax(...).to(dtype), bolt3.py:249), then o += p v.
-template <int HD, int NK>
-B3_DEV void block_pv(float (&o)[HD / 8][4], const float (&mrow)[2], const float (&lrow)[2],
-                     const uint32_t (&qa)[HD / 16][4], const bf16* ks, const bf16* vs, const float* bias,
-                     int nvalid, bool causal, int kbase, int lim0, int lim1, int lane) {
-  float s[NK / 8][4];
-  block_scores<HD, NK>(s, qa, ks, bias, nvalid, causal, kbase, lim0, lim1, lane);
-#pragma unroll
-  for (int n = 0; n < NK / 8; ++n) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float m = mrow[q >> 1], l = lrow[q >> 1];
-      s[n][q] = s[n][q] == neg_inf() ? 0.f : __fdiv_rn(expf(s[n][q] - m), l);
-    }
-  }
-  uint32_t pk[NK / 16][4];
-#pragma unroll
-  for (int kt = 0; kt < NK / 16; ++kt) {
-    pk[kt][0] = pack_bf16(s[2 * kt][0], s[2 * kt][1]);
-    pk[kt][1] = pack_bf16(s[2 * kt][2], s[2 * kt][3]);
-    pk[kt][2] = pack_bf16(s[2 * kt + 1][0], s[2 * kt + 1][1]);
-    pk[kt][3] = pack_bf16(s[2 * kt + 1][2], s[2 * kt + 1][3]);
-  }
-#pragma unroll
-  for (int kt = 0; kt < NK / 16; ++kt) {
-#pragma unroll
-    for (int np = 0; np < HD / 16; ++np) {
-      uint32_t b[4];
-      ldsm_x4_t(b, vs + swz<HD>(kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, np * 16 + (lane >> 4) * 8));
-      mma16816(o[2 * np], pk[kt], b[0], b[1]);
-      mma16816(o[2 * np + 1], pk[kt], b[2], b[3]);
-    }
+    const bool ok = r < valid;
+    unsigned char* d = dst[ch >> 3] + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
+    cp_async16(d, ok ? src + (int64_t)r * HD + ch * 8 : src, ok);
   }
 }
 
 template <int HD>
-__global__ void __launch_bounds__(NT, 1) attend_kernel(bolt3_attend_args a) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  Smem<HD>& sm = *reinterpret_cast<Smem<HD>*>(smem_raw);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g8 = lane >> 2, t4 = lane & 3;
-  const int r0 = warp * 16;
-  const int c = blockIdx.z;
-  const int blk = blockIdx.x;
+__global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_args a) {
+  extern __shared__ unsigned char smem_raw[];
+  Smem<HD>& sm = *reinterpret_cast<Smem<HD>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5;
   const int G = a.G;
+  const int g_fast = blockIdx.x;  // head group within the KV head: the G CTAs of one chain-chunk run
+  const int blk = blockIdx.y;     // together and share K/V through L2
+  const int c = blockIdx.z;
   const int kvh = c % a.hkv, b = c / a.hkv;
   const int H = a.hkv * G;
 
-  // ---- geometry of this tile
+  // ---- geometry
   const int ntok = (int)min((int64_t)128, a.Tq - (int64_t)blk * 128);
-  const int gn = a.prefill ? 1 : max(1, min(G, 128 / max(ntok, 1)));
-  const int g0 = blockIdx.y * gn;
-  const int ng = min(gn, G - g0);
-  const int n_rows = ng * ntok;
+  const int gn = a.prefill ? 1 : max(1, min(G, 128 / ntok));
+  const int g0 = g_fast * gn;
+  const int n_rows = min(gn, G - g0) * ntok;
   int L0, L1, len_before;
   const bf16 *k0, *v0, *k1, *v1, *sk = nullptr, *sv = nullptr;
   bool has_sinks, has_bank;
@@ -203,236 +112,369 @@ __global__ void __launch_bounds__(NT, 1) attend_kernel(bolt3_attend_args a) {
       sv = reinterpret_cast<const bf16*>(a.sink_v) + (int64_t)c * a.sink_chain_tokens * HD;
     }
   }
-  const int n_before = L0 + len_before;
-  const int64_t bofs = ((int64_t)c * a.bank_cap + bank_idx);
+  const int64_t bofs = (int64_t)c * a.bank_cap + bank_idx;
   const bf16* bk = has_bank ? reinterpret_cast<const bf16*>(a.bank_ak_rope) + bofs * S * HD : nullptr;
   const bf16* bv = has_bank ? reinterpret_cast<const bf16*>(a.bank_av) + bofs * S * HD : nullptr;
-  const float* bmass = has_bank ? a.bank_mass + bofs * S : nullptr;
-  const uint8_t* bact = has_bank ? a.bank_act + bofs * S : nullptr;
-  const float kappa = a.kappa[kvh];
+  const bool seg_on[3] = {has_bank, L0 > 0, L1 > 0};
+  const int seg_len[3] = {S, L0, L1};
+  const bf16* seg_k[3] = {bk, k0, k1};
+  const bf16* seg_v[3] = {bv, v0, v1};
 
-  const int n_sink_jobs = has_sinks ? 1 : 0;
-  const int n_attr_jobs = has_bank ? S / KB : 0;
-  const int n_seg0_jobs = (L0 + KB - 1) / KB;
-  const int n_seg1_jobs = (L1 + KB - 1) / KB;
-  const int n_jobs = n_sink_jobs + n_attr_jobs + n_seg0_jobs + n_seg1_jobs;
-
-  auto job_at = [&](int j) {
-    Job jb;
-    if (j < n_sink_jobs) {
-      jb.k = sk; jb.v = sv; jb.n = 4; jb.kind = 0; jb.kbase = 0; jb.slot0 = 0;
-      return jb;
-    }
-    j -= n_sink_jobs;
-    if (j < n_attr_jobs) {
-      jb.k = bk + (int64_t)j * KB * HD; jb.v = bv + (int64_t)j * KB * HD; jb.n = KB; jb.kind = 1;
-      jb.kbase = 0; jb.slot0 = j * KB;
-      return jb;
-    }
-    j -= n_attr_jobs;
-    if (j < n_seg0_jobs) {
-      jb.k = k0 + (int64_t)j * KB * HD; jb.v = v0 + (int64_t)j * KB * HD;
-      jb.n = min(KB, L0 - j * KB); jb.kind = 2; jb.kbase = j * KB; jb.slot0 = 0;
-      return jb;
-    }
-    j -= n_seg0_jobs;
-    jb.k = k1 + (int64_t)j * KB * HD; jb.v = v1 + (int64_t)j * KB * HD;
-    jb.n = min(KB, L1 - j * KB); jb.kind = 3; jb.kbase = L0 + j * KB; jb.slot0 = 0;
-    return jb;
+  auto row_tok = [&](int r, int& g, int& i) {
+    g = g0 + r / ntok;
+    i = r % ntok;
   };
-  // step j < n_jobs: statistics pass (keys only); step j >= n_jobs: P@V pass (keys and values)
-  auto issue = [&](int j, int buf) {
-    const bool pv = j >= n_jobs;
-    const Job jb = job_at(pv ? j - n_jobs : j);
-    const int rows = jb.kind == 0 ? 16 : KB;
-    load_rows<HD>(sm.k + buf * KB * HD, jb.k, rows, jb.n);
-    if (pv) load_rows<HD>(sm.v + buf * KB * HD, jb.v, rows, jb.n);
-    if (jb.kind == 1) {
-      for (int i = tid; i < KB; i += NT) {
-        const int s_ = jb.slot0 + i;
-        sm.bias[buf][i] = bact[s_] ? __fmul_rn(kappa, logf(fmaxf(bmass[s_], 1.0f))) : neg_inf();
-      }
-    }
+  auto q_row_ptr = [&](const void* base, int r) {
+    int g, i;
+    row_tok(r < n_rows ? r : 0, g, i);
+    return reinterpret_cast<const bf16*>(base) + (((int64_t)c * G + g) * a.Tq + (int64_t)blk * 128 + i) * HD;
   };
 
-  // ---- query tile (q_rope) and its A fragments
-  auto row_head_tok = [&](int r, int& g, int& i) {
-    g = g0 + r / max(ntok, 1);
-    i = r % max(ntok, 1);
-  };
+  // ---- stage 1: Q (q_rope), K tiles, sinks, attractor bias
   {
     constexpr int CPR = HD / 8;
     for (int i = tid; i < 128 * CPR; i += NT) {
       const int r = i / CPR, ch = i % CPR;
-      const bool ok = r < n_rows;
-      int g, ti;
-      row_head_tok(ok ? r : 0, g, ti);
-      const int64_t tq = (int64_t)blk * 128 + ti;
-      const bf16* src = reinterpret_cast<const bf16*>(a.q_rope) + (((int64_t)c * G + g) * a.Tq + tq) * HD + ch * 8;
-      cp_async16(sm.q + swz<HD>(r, ch * 8), ok ? src : reinterpret_cast<const bf16*>(a.q_rope), ok);
+      unsigned char* d = sm.q[ch >> 3] + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
+      cp_async16(d, q_row_ptr(a.q_rope, r) + ch * 8, r < n_rows);
     }
-  }
-  if (n_jobs > 0) issue(0, 0);
-  cp_async_commit();
-
-  float o[HD / 8][4];
-#pragma unroll
-  for (int n = 0; n < HD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-  float mrow[2] = {neg_inf(), neg_inf()}, lrow[2] = {0.f, 0.f};
-  uint32_t qa[HD / 16][4];
-  const bool warp_active = r0 < n_rows;
-  int gA, iA, gB, iB;
-  row_head_tok(min(r0 + g8, max(n_rows - 1, 0)), gA, iA);
-  row_head_tok(min(r0 + g8 + 8, max(n_rows - 1, 0)), gB, iB);
-  const int lim0 = n_before + iA, lim1 = n_before + iB;
-  // largest token index among this warp's rows (for skipping fully masked causal blocks)
-  int imax = 0;
-  for (int r = r0; r < min(r0 + 16, n_rows); ++r) { int gg, ii; row_head_tok(r, gg, ii); imax = max(imax, ii); }
-
-  const int n_steps = 2 * n_jobs;
-  for (int j = 0; j < n_steps; ++j) {
-    if (j + 1 < n_steps) {
-      issue(j + 1, (j + 1) & 1);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    if (j == 0 && warp_active) {
-#pragma unroll
-      for (int kt = 0; kt < HD / 16; ++kt)
-        ldsm_x4(qa[kt], sm.q + swz<HD>(r0 + (lane & 15), kt * 16 + (lane >> 4) * 8));
-    }
-    const bool pv = j >= n_jobs;
-    const Job jb = job_at(pv ? j - n_jobs : j);
-    const int buf = j & 1;
-    const bool skip = !warp_active || (jb.kind == 3 && jb.kbase > n_before + imax);
-    if (!skip) {
-      const bf16* kt_ = sm.k + buf * KB * HD;
-      const bf16* vt_ = sm.v + buf * KB * HD;
-      const float* bs = jb.kind == 1 ? sm.bias[buf] : nullptr;
-      if (!pv) {
-        if (jb.kind == 0) block_stats<HD, 16>(mrow, lrow, qa, kt_, nullptr, jb.n, false, 0, lim0, lim1, lane);
-        else block_stats<HD, KB>(mrow, lrow, qa, kt_, bs, jb.n, jb.kind == 3, jb.kbase, lim0, lim1, lane);
-      } else {
-        if (jb.kind == 0) block_pv<HD, 16>(o, mrow, lrow, qa, kt_, vt_, nullptr, jb.n, false, 0, lim0, lim1, lane);
-        else block_pv<HD, KB>(o, mrow, lrow, qa, kt_, vt_, bs, jb.n, jb.kind == 3, jb.kbase, lim0, lim1, lane);
+    for (int s = 0; s < 3; ++s)
+      if (seg_on[s]) load_tile<HD>(sm.kv[s], seg_k[s], seg_len[s], tid, NT);
+    if (has_sinks) {
+      for (int i = tid; i < 4 * HD / 8; i += NT) {
+        cp_async16(&sm.sink_k[0][0] + i * 8, sk + i * 8, true);
+        cp_async16(&sm.sink_v[0][0] + i * 8, sv + i * 8, true);
       }
     }
-    __syncthreads();
+    cp_async_commit();
+    if (has_bank)
+      for (int i = tid; i < HD; i += NT) sm.res_w[i] = a.res_w[i];
+    if (has_bank) {
+      const float kappa = a.kappa[kvh];
+      for (int s = tid; s < S; s += NT)
+        sm.bias[s] = a.bank_act[bofs * S + s] ? __fmul_rn(kappa, logf(fmaxf(a.bank_mass[bofs * S + s], 1.0f)))
+                                              : neg_inf();
+    }
   }
-
-  // ---- P@V result rounded to the storage dtype (the probabilities were normalised already)
-#pragma unroll
-  for (int n = 0; n < HD / 8; ++n) {
-    o[n][0] = rbf(o[n][0]); o[n][1] = rbf(o[n][1]);
-    o[n][2] = rbf(o[n][2]); o[n][3] = rbf(o[n][3]);
+  if (warp == 0) {
+    tc5::tmem_alloc(&sm.tbase, 512);
+    tc5::tmem_relinquish();
   }
+  if (tid == 0) {
+    tc5::mbar_init(&sm.bar_s, 1);
+    tc5::mbar_init(&sm.bar_o, 1);
+    tc5::mbar_fence_init();
+    sm.err = 0;
+  }
+  cp_async_wait<0>();
+  asm volatile("fence.proxy.async.shared::cta;\n" ::);
+  tc5::fence_before_sync();
+  __syncthreads();
+  tc5::fence_after_sync();
+  const uint32_t tb = sm.tbase;
 
-  if (has_bank) {
-    // ---- M_res read-out epilogue: q_raw tile, M split, normalise, RMSNorm, eta gate
-    const float* gm = a.bank_m + bofs * HD * HD;
-    {
-      constexpr int CPR = HD / 8;
-      for (int i = tid; i < 128 * CPR; i += NT) {
-        const int r = i / CPR, ch = i % CPR;
-        const bool ok = r < n_rows;
-        int g, ti;
-        row_head_tok(ok ? r : 0, g, ti);
-        const int64_t tq = (int64_t)blk * 128 + ti;
-        const bf16* src = reinterpret_cast<const bf16*>(a.q_raw) + (((int64_t)c * G + g) * a.Tq + tq) * HD + ch * 8;
-        cp_async16(sm.q + swz<HD>(r, ch * 8), ok ? src : reinterpret_cast<const bf16*>(a.q_raw), ok);
+  // ---- stage 2: S = Q K^T for every present segment
+  constexpr uint32_t kIdS = tc5::idesc_bf16(128, 128, false, false);
+  if (tid == 0) {
+    const uint32_t qa = tc5::smem_u32(sm.q[0]);
+    for (int s = 0; s < 3; ++s) {
+      if (!seg_on[s]) continue;
+      const uint32_t ka = tc5::smem_u32(sm.kv[s][0]);
+      for (int ks = 0; ks < HD / 16; ++ks) {
+        const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
+        tc5::mma_ss(tb + s * 128, tc5::sdesc(qa + off, 16, 1024), tc5::sdesc(ka + off, 16, 1024), kIdS, ks > 0);
       }
+    }
+    tc5::commit(&sm.bar_s);
+  }
+
+  constexpr float scale = HD == 128 ? 0.08838834764831845f : 0.125f;  // fp32(HD ** -0.5)
+  float p_sink[4] = {0.f, 0.f, 0.f, 0.f};
+  if (warp < 4) {
+    // ================= row warps: softmax
+    const int r = tid;
+    int gr, ir;
+    row_tok(min(r, max(n_rows - 1, 0)), gr, ir);
+    const int lim1 = len_before + ir;  // current-chunk key j is visible iff j <= lim1
+    asm volatile("bar.sync 1, 256;\n" ::);  // sink scores are in shared memory
+    float s_sink[4] = {neg_inf(), neg_inf(), neg_inf(), neg_inf()};
+    if (has_sinks) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s_sink[j] = sm.sink_s[r][j];
+    }
+    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
+    const bool ok = tc5::mbar_wait(&sm.bar_s, 0, kWaitIters);
+    if (!ok) sm.err = 1;
+    tc5::fence_after_sync();
+    // score of column `col` of segment SEG after scale, bias and masks (SEG is compile-time, so
+    // the segment parameters stay in registers)
+    const float* bias = sm.bias;
+    auto row_pass = [&](auto seg_tag, auto&& body) {
+      constexpr int SEG = decltype(seg_tag)::value;
+      const int lim = SEG == 1 ? L0 - 1 : (SEG == 2 ? min(L1 - 1, lim1) : S - 1);
+      for (int c0 = 0; c0 < 128; c0 += 32) {
+        uint32_t v[32];
+        tc5::ld32(tb + lane_off + SEG * 128 + c0, v);
+        tc5::ld_wait();
+        float x[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float sc = __fmul_rn(__uint_as_float(v[j]), scale);
+          if (SEG == 0) x[j] = __fadd_rn(sc, bias[c0 + j]);
+          else x[j] = (c0 + j <= lim) ? sc : neg_inf();
+        }
+        body(c0, x);
+      }
+    };
+    auto for_each_seg = [&](auto&& body) {
+      if (seg_on[0]) row_pass(std::integral_constant<int, 0>{}, [&](int c0, float (&x)[32]) { body(0, c0, x); });
+      if (seg_on[1]) row_pass(std::integral_constant<int, 1>{}, [&](int c0, float (&x)[32]) { body(1, c0, x); });
+      if (seg_on[2]) row_pass(std::integral_constant<int, 2>{}, [&](int c0, float (&x)[32]) { body(2, c0, x); });
+    };
+    // pass 1: row max
+    float mx = fmaxf(fmaxf(s_sink[0], s_sink[1]), fmaxf(s_sink[2], s_sink[3]));
+    if (ok) {
+      for_each_seg([&](int, int, float (&x)[32]) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, x[j]);
+      });
+    }
+    // pass 2: row sum of exp(x - max) (exp2 of the scaled difference: only the sum's value is
+    // needed here, at fp32 accuracy)
+    constexpr float kLog2e = 1.4426950408889634f;
+    float sum = 0.f;
+    float e_sink[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      e_sink[j] = s_sink[j] == neg_inf() ? 0.f : expf(s_sink[j] - mx);
+      sum += e_sink[j];
+    }
+    if (ok) {
+      float part[4] = {0.f, 0.f, 0.f, 0.f};
+      for_each_seg([&](int, int, float (&x)[32]) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) part[j & 3] += exp2f(__fmul_rn(x[j] - mx, kLog2e));
+      });
+      sum += (part[0] + part[1]) + (part[2] + part[3]);
+    }
+    // pass 3: p = bf16(exp(x - max) * (1 / sum)), two per column, into TMEM columns [0, 192).
+    // exp via exp2 of (x - max) * log2(e): within ~1e-6 relative of exp, so the bf16 cast of p
+    // matches the reference's except for values within that distance of a rounding boundary.
+    const float inv_sum = 1.0f / sum;
+    if (ok) {
+      for_each_seg([&](int s, int c0, float (&x)[32]) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float e0 = exp2f(__fmul_rn(x[2 * j] - mx, kLog2e));
+          const float e1 = exp2f(__fmul_rn(x[2 * j + 1] - mx, kLog2e));
+          pk[j] = pack_bf16(__fmul_rn(e0, inv_sum), __fmul_rn(e1, inv_sum));
+        }
+        tc5::st16(tb + lane_off + (uint32_t)((s * 128 + c0) >> 1), pk);
+      });
+      tc5::st_wait();
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) p_sink[j] = rbf(__fmul_rn(e_sink[j], inv_sum));
+    tc5::fence_before_sync();
+  } else {
+    // ================= helper warps: M_res operand, sink scores, then (after the S MMAs) V and q_raw
+    const int ht = tid - 128;
+    if (has_bank && a.prefill) {
+      // the consolidation scan wrote the split, swizzled operand image: copy it as is
+      const unsigned char* img = reinterpret_cast<const unsigned char*>(a.bank_m) + bofs * (int64_t)HD * HD * 4;
+      for (int i = ht; i < HD * HD / 4; i += 128) cp_async16(&sm.m[0][0][0] + i * 16, img + i * 16, true);
       cp_async_commit();
-      for (int i = tid; i < HD * HD / 4; i += NT) {
-        const int d = (i * 4) / HD, e = (i * 4) % HD;
-        const float4 m4 = *reinterpret_cast<const float4*>(gm + (int64_t)d * HD + e);
-        const float mv[4] = {m4.x, m4.y, m4.z, m4.w};
+    } else if (has_bank) {
+      // M_res [d][e] fp32 row-major: split into bf16 hi/lo in the MN-major operand layout (rows d,
+      // 64-column blocks of e); coalesced float4 loads, eight in flight per thread
+      const float4* gm = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.bank_m) + bofs * HD * HD);
+      constexpr int N4 = HD * HD / 4;
+      for (int i0 = ht; i0 < N4; i0 += 128 * 8) {
+        float4 mv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mv[u] = i0 + u * 128 < N4 ? gm[i0 + u * 128] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int i = i0 + u * 128;
+          if (i >= N4) break;
+          const int d = (i * 4) / HD, e = (i * 4) % HD;
+          const float v4[4] = {mv[u].x, mv[u].y, mv[u].z, mv[u].w};
+          uint32_t hi[2], lo[2];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const bf16 h0 = __float2bfloat16_rn(v4[2 * q]), h1 = __float2bfloat16_rn(v4[2 * q + 1]);
+            hi[q] = pack_bf16(bf2f(h0), bf2f(h1));
+            lo[q] = pack_bf16(v4[2 * q] - bf2f(h0), v4[2 * q + 1] - bf2f(h1));
+          }
+          const uint32_t off = tc5::sw128_off(d, e & 63);
+          *reinterpret_cast<uint2*>(sm.m[0][e >> 6] + off) = make_uint2(hi[0], hi[1]);
+          *reinterpret_cast<uint2*>(sm.m[1][e >> 6] + off) = make_uint2(lo[0], lo[1]);
+        }
+      }
+    }
+    if (has_sinks) {
+      // scaled sink scores of row ht, and the sink values in fp32
+      const int r = ht;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int ch = 0; ch < HD / 8; ++ch) {
+        const uint4 qv = *reinterpret_cast<const uint4*>(sm.q[ch >> 3] + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
+        const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const bf16 hi = __float2bfloat16_rn(mv[u]);
-          sm.k[swz<HD>(d, e + u)] = hi;
-          sm.v[swz<HD>(d, e + u)] = __float2bfloat16_rn(mv[u] - bf2f(hi));
+          const float2 qf = unpack_bf16(qw[u]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 kf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sm.sink_k[j][ch * 8 + 2 * u]));
+            acc[j] = fmaf(qf.x, kf.x, acc[j]);
+            acc[j] = fmaf(qf.y, kf.y, acc[j]);
+          }
         }
       }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sm.sink_s[r][j] = __fmul_rn(acc[j], scale);
+      for (int i = ht; i < 4 * HD; i += 128) sm.sink_vf[i / HD][i % HD] = bf2f(sm.sink_v[i / HD][i % HD]);
+    }
+    asm volatile("bar.sync 2, 128;\n" ::);   // every helper is done reading Q
+    asm volatile("bar.arrive 1, 256;\n" ::); // sink scores ready for the row warps
+    const bool ok = tc5::mbar_wait(&sm.bar_s, 0, kWaitIters);
+    if (!ok) sm.err = 1;
+    tc5::fence_after_sync();
+    if (ok) {
+      for (int s = 0; s < 3; ++s)
+        if (seg_on[s]) load_tile<HD>(sm.kv[s], seg_v[s], seg_len[s], ht, 128);
+      if (has_bank) {
+        constexpr int CPR = HD / 8;
+        for (int i = ht; i < 128 * CPR; i += 128) {
+          const int r = i / CPR, ch = i % CPR;
+          unsigned char* d = sm.q[ch >> 3] + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
+          cp_async16(d, q_row_ptr(a.q_raw, r) + ch * 8, r < n_rows);
+        }
+      }
+      cp_async_commit();
       cp_async_wait<0>();
-      __syncthreads();
     }
-    for (int r = warp * 16; r < warp * 16 + 16; ++r) {
-      constexpr int EPL = HD / 32;
-      const bf16* p = sm.q + swz<HD>(r, lane * EPL);
-      float acc = 0.f;
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) { const float x = bf2f(p[e]); acc = fmaf(x, x, acc); }
-      acc = warp_sum(acc);
-      if (lane == 0) sm.qn[r] = sqrtf(acc);
+    asm volatile("fence.proxy.async.shared::cta;\n" ::);
+    tc5::fence_before_sync();
+  }
+  __syncthreads();
+  tc5::fence_after_sync();
+  const bool ok_all = sm.err == 0;
+
+  // ---- stage 3: O = P V; R = q_raw (M_hi + M_lo)
+  if (tid == 0 && ok_all) {
+    constexpr uint32_t kIdO = tc5::idesc_bf16(128, HD, false, true);
+    bool first = true;
+    for (int s = 0; s < 3; ++s) {
+      if (!seg_on[s]) continue;
+      const uint32_t va = tc5::smem_u32(sm.kv[s][0]);
+      for (int ks = 0; ks < 8; ++ks) {
+        tc5::mma_ts(tb + kColO, tb + (uint32_t)(s * 64 + ks * 8), tc5::sdesc(va + ks * 2048, 16384, 1024), kIdO,
+                    first ? 0u : 1u);
+        first = false;
+      }
     }
-    __syncwarp();
-    if (warp_active) {
-      float ym[HD / 8][4];
-#pragma unroll
-      for (int n = 0; n < HD / 8; ++n) ym[n][0] = ym[n][1] = ym[n][2] = ym[n][3] = 0.f;
-#pragma unroll
-      for (int kt = 0; kt < HD / 16; ++kt) {
-        uint32_t qr[4];
-        ldsm_x4(qr, sm.q + swz<HD>(r0 + (lane & 15), kt * 16 + (lane >> 4) * 8));
-#pragma unroll
-        for (int np = 0; np < HD / 16; ++np) {
-          uint32_t bb[4];
-          ldsm_x4_t(bb, sm.k + swz<HD>(kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, np * 16 + (lane >> 4) * 8));
-          mma16816(ym[2 * np], qr, bb[0], bb[1]);
-          mma16816(ym[2 * np + 1], qr, bb[2], bb[3]);
-          ldsm_x4_t(bb, sm.v + swz<HD>(kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, np * 16 + (lane >> 4) * 8));
-          mma16816(ym[2 * np], qr, bb[0], bb[1]);
-          mma16816(ym[2 * np + 1], qr, bb[2], bb[3]);
+    if (has_bank) {
+      constexpr uint32_t kIdR = tc5::idesc_bf16(128, HD, false, true);
+      const uint32_t qa = tc5::smem_u32(sm.q[0]);
+      for (int hl = 0; hl < 2; ++hl) {
+        const uint32_t ma = tc5::smem_u32(sm.m[hl][0]);
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          const uint32_t qo = (ks >> 2) * 16384 + (ks & 3) * 32;
+          tc5::mma_ss(tb + kColR, tc5::sdesc(qa + qo, 16, 1024), tc5::sdesc(ma + ks * 2048, HD * 128, 1024), kIdR,
+                      (hl | ks) ? 1u : 0u);
         }
       }
-      const float coef = a.coef[kvh];
-      const float qn0 = fmaxf(sm.qn[r0 + g8], 1e-12f), qn1 = fmaxf(sm.qn[r0 + g8 + 8], 1e-12f);
-      float ss0 = 0.f, ss1 = 0.f;
-#pragma unroll
-      for (int n = 0; n < HD / 8; ++n) {
-        ym[n][0] = __fmul_rn(__fdiv_rn(ym[n][0], qn0), coef);
-        ym[n][1] = __fmul_rn(__fdiv_rn(ym[n][1], qn0), coef);
-        ym[n][2] = __fmul_rn(__fdiv_rn(ym[n][2], qn1), coef);
-        ym[n][3] = __fmul_rn(__fdiv_rn(ym[n][3], qn1), coef);
-        ss0 = fmaf(ym[n][0], ym[n][0], fmaf(ym[n][1], ym[n][1], ss0));
-        ss1 = fmaf(ym[n][2], ym[n][2], fmaf(ym[n][3], ym[n][3], ss1));
-      }
-      ss0 = quad_sum(ss0);
-      ss1 = quad_sum(ss1);
-      const float rs0 = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss0, (float)HD), a.eps));
-      const float rs1 = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss1, (float)HD), a.eps));
-      const float* eta = a.eta;
-      const float e0 = eta[((int64_t)c * G + gA) * a.Tq + (int64_t)blk * 128 + iA];
-      const float e1 = eta[((int64_t)c * G + gB) * a.Tq + (int64_t)blk * 128 + iB];
-#pragma unroll
-      for (int n = 0; n < HD / 8; ++n) {
-        const int col = n * 8 + 2 * t4;
-        const float w0 = a.res_w[col], w1 = a.res_w[col + 1];
-        o[n][0] = rbf(__fadd_rn(o[n][0], rbf(__fmul_rn(e0, __fmul_rn(__fmul_rn(ym[n][0], rs0), w0)))));
-        o[n][1] = rbf(__fadd_rn(o[n][1], rbf(__fmul_rn(e0, __fmul_rn(__fmul_rn(ym[n][1], rs0), w1)))));
-        o[n][2] = rbf(__fadd_rn(o[n][2], rbf(__fmul_rn(e1, __fmul_rn(__fmul_rn(ym[n][2], rs1), w0)))));
-        o[n][3] = rbf(__fadd_rn(o[n][3], rbf(__fmul_rn(e1, __fmul_rn(__fmul_rn(ym[n][3], rs1), w1)))));
-      }
     }
+    tc5::commit(&sm.bar_o);
   }
 
-  // ---- store y [B][y_tokens][H][HD]
-  if (warp_active) {
-    bf16* y = reinterpret_cast<bf16*>(a.y);
-    const int rA = r0 + g8, rB = r0 + g8 + 8;
-    const int64_t tA = (int64_t)blk * 128 + iA, tB = (int64_t)blk * 128 + iB;
-    bf16* yA = y + (((int64_t)b * a.y_tokens + tA) * H + kvh * G + gA) * HD;
-    bf16* yB = y + (((int64_t)b * a.y_tokens + tB) * H + kvh * G + gB) * HD;
+  if (warp < 4) {
+    // ================= epilogue: one output row per thread
+    const int r = tid;
+    int gr, ir;
+    row_tok(min(r, max(n_rows - 1, 0)), gr, ir);
+    float qn = 0.f;
+    if (has_bank && a.q_l2 != nullptr) {
+      qn = a.q_l2[((int64_t)c * G + gr) * a.Tq + (int64_t)blk * 128 + ir];
+    } else if (has_bank) {
+      float acc = 0.f;
+      for (int ch = 0; ch < HD / 8; ++ch) {
+        const uint4 qv = *reinterpret_cast<const uint4*>(sm.q[ch >> 3] + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
+        const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
-    for (int n = 0; n < HD / 8; ++n) {
-      const int col = n * 8 + 2 * t4;
-      if (rA < n_rows) *reinterpret_cast<uint32_t*>(yA + col) = pack_bf16(o[n][0], o[n][1]);
-      if (rB < n_rows) *reinterpret_cast<uint32_t*>(yB + col) = pack_bf16(o[n][2], o[n][3]);
+        for (int u = 0; u < 4; ++u) {
+          const float2 f = unpack_bf16(qw[u]);
+          acc = fmaf(f.x, f.x, fmaf(f.y, f.y, acc));
+        }
+      }
+      qn = sqrtf(acc);
     }
+    const bool ok = ok_all && tc5::mbar_wait(&sm.bar_o, 0, kWaitIters);
+    if (!ok && ok_all) sm.err = 1;
+    tc5::fence_after_sync();
+    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
+    float rs = 0.f, inv_qn = 0.f, coef = 0.f, eta = 0.f;
+    if (ok && has_bank) {
+      inv_qn = 1.0f / fmaxf(qn, 1e-12f);
+      coef = a.coef[kvh];
+      eta = a.eta[((int64_t)c * G + gr) * a.Tq + (int64_t)blk * 128 + ir];
+      float ss = 0.f;
+      for (int c0 = 0; c0 < HD; c0 += 32) {
+        uint32_t v[32];
+        tc5::ld32(tb + lane_off + kColR + c0, v);
+        tc5::ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float ym = __fmul_rn(__fmul_rn(__uint_as_float(v[j]), inv_qn), coef);
+          ss = fmaf(ym, ym, ss);
+        }
+      }
+      rs = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)HD), a.eps));
+    }
+    if (ok) {
+      bf16* yrow = reinterpret_cast<bf16*>(a.y) +
+                   (((int64_t)b * a.y_tokens + (int64_t)blk * 128 + ir) * H + kvh * G + gr) * HD;
+      for (int c0 = 0; c0 < HD; c0 += 32) {
+        uint32_t vo[32], vr[32];
+        tc5::ld32(tb + lane_off + kColO + c0, vo);
+        if (has_bank) tc5::ld32(tb + lane_off + kColR + c0, vr);
+        tc5::ld_wait();
+        uint32_t packed[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          float o2[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int col = c0 + j + u;
+            float o = __uint_as_float(vo[j + u]);
+            if (has_sinks) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) o = fmaf(p_sink[q], sm.sink_vf[q][col], o);
+            }
+            o = rbf(o);
+            if (has_bank) {
+              const float ym = __fmul_rn(__fmul_rn(__uint_as_float(vr[j + u]), inv_qn), coef);
+              o = rbf(__fadd_rn(o, rbf(__fmul_rn(eta, __fmul_rn(__fmul_rn(ym, rs), sm.res_w[col])))));
+            }
+            o2[u] = o;
+          }
+          packed[j >> 1] = pack_bf16(o2[0], o2[1]);
+        }
+        if (r < n_rows) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(yrow + c0 + q * 8) =
+                make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+        }
+      }
+    }
+    tc5::fence_before_sync();
   }
+  __syncthreads();
+  tc5::fence_after_sync();
+  if (warp == 0) tc5::tmem_dealloc(tb, 512);
+  if (tid == 0 && sm.err && a.status) atomicOr(a.status, 2);
 }
 
 }  // namespace
@@ -460,30 +502,30 @@ extern "C" int bolt3_attend(const bolt3_attend_args* a, void* stream) {
   const uintptr_t al = (uintptr_t)a->q_rope | (uintptr_t)a->q_raw | (uintptr_t)a->seg0_k | (uintptr_t)a->seg0_v |
                        (uintptr_t)a->seg1_k | (uintptr_t)a->seg1_v | (uintptr_t)a->sink_k |
                        (uintptr_t)a->sink_v | (uintptr_t)a->bank_ak_rope | (uintptr_t)a->bank_av |
-                       (uintptr_t)a->bank_m;
+                       (uintptr_t)a->bank_m | (uintptr_t)a->y;
   if (al & 15) return BOLT3_ERR_ALIGN;
   cudaStream_t s = (cudaStream_t)stream;
   dim3 grid;
   if (a->prefill) {
-    grid = dim3((unsigned)((a->Tq + 127) / 128), (unsigned)a->G, (unsigned)a->n_chains);
+    grid = dim3((unsigned)a->G, (unsigned)((a->Tq + 127) / 128), (unsigned)a->n_chains);
   } else {
     const int gn = (int)std::max<int64_t>(1, std::min<int64_t>(a->G, 128 / a->Tq));
-    grid = dim3(1, (unsigned)((a->G + gn - 1) / gn), (unsigned)a->n_chains);
+    grid = dim3((unsigned)((a->G + gn - 1) / gn), 1, (unsigned)a->n_chains);
   }
-  int rc;
+  // Each CTA allocates all 512 TMEM columns, so the shared-memory request keeps one CTA per SM.
+  constexpr size_t kMinSmem = 120 * 1024;
   if (a->HD == 128) {
-    const size_t smem = sizeof(Smem<128>);
-    if (cudaFuncSetAttribute(attend_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    const size_t smem = std::max(sizeof(Smem<128>) + 1024, kMinSmem);
+    if (cudaFuncSetAttribute(attend_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return BOLT3_ERR_CUDA;
-    attend_kernel<128><<<grid, NT, smem, s>>>(*a);
+    attend_tc_kernel<128><<<grid, NT, smem, s>>>(*a);
   } else if (a->HD == 64) {
-    const size_t smem = sizeof(Smem<64>);
-    if (cudaFuncSetAttribute(attend_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    const size_t smem = std::max(sizeof(Smem<64>) + 1024, kMinSmem);
+    if (cudaFuncSetAttribute(attend_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return BOLT3_ERR_CUDA;
-    attend_kernel<64><<<grid, NT, smem, s>>>(*a);
+    attend_tc_kernel<64><<<grid, NT, smem, s>>>(*a);
   } else {
     return BOLT3_ERR_SHAPE;
   }
-  rc = cudaGetLastError() == cudaSuccess ? BOLT3_OK : BOLT3_ERR_CUDA;
-  return rc;
+  return cudaGetLastError() == cudaSuccess ? BOLT3_OK : BOLT3_ERR_CUDA;
 }

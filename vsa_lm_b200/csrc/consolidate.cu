@@ -743,11 +743,20 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
         a.snap_act[sn * S + s] = sm.act[s];
       }
       if (m_owner) {
-        float* gm = a.snap_m + sn * HD * HD;
+        // M_res as the attention's read-out operand: bf16 hi and lo terms, each an MN-major
+        // 128-byte-swizzled image [e / 64][d][64] (see attend.cu)
+        unsigned char* img = reinterpret_cast<unsigned char*>(a.snap_m) + sn * (int64_t)HD * HD * 4;
 #pragma unroll
         for (int n = 0; n < HD / 8; ++n) {
-          *reinterpret_cast<float2*>(gm + (r0 + g) * HD + n * 8 + 2 * t4) = make_float2(mr[n][0], mr[n][1]);
-          *reinterpret_cast<float2*>(gm + (r0 + g + 8) * HD + n * 8 + 2 * t4) = make_float2(mr[n][2], mr[n][3]);
+#pragma unroll
+          for (int hrow = 0; hrow < 2; ++hrow) {
+            const int d = r0 + g + hrow * 8, e = n * 8 + 2 * t4;
+            const float m0 = mr[n][2 * hrow], m1 = mr[n][2 * hrow + 1];
+            const bf16 h0 = __float2bfloat16_rn(m0), h1 = __float2bfloat16_rn(m1);
+            const int64_t off = (int64_t)(e >> 6) * HD * 128 + d * 128 + ((((e & 63) >> 3) ^ (d & 7)) << 4) + (e & 7) * 2;
+            *reinterpret_cast<uint32_t*>(img + off) = pack_bf16(bf2f(h0), bf2f(h1));
+            *reinterpret_cast<uint32_t*>(img + (int64_t)HD * HD * 2 + off) = pack_bf16(m0 - bf2f(h0), m1 - bf2f(h1));
+          }
         }
       }
     }

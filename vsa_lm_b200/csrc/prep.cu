@@ -61,6 +61,7 @@ __global__ void __launch_bounds__(256) prep_kernel(bolt3_prep_args a) {
       continue;
     }
     const float* nw = kind == 0 ? a.q_norm_w : a.k_norm_w;
+    float l2 = 0.f;  // |q_raw| of the stored (bf16) row, for the M_res read-out
     if (nw != nullptr) {
       float ss = 0.f;
 #pragma unroll
@@ -72,6 +73,12 @@ __global__ void __launch_bounds__(256) prep_kernel(bolt3_prep_args a) {
         x0[e] = rbf(__fmul_rn(__fmul_rn(x0[e], r_), nw[lane * E + e]));
         x1[e] = rbf(__fmul_rn(__fmul_rn(x1[e], r_), nw[HD / 2 + lane * E + e]));
       }
+    }
+    if (kind == 0 && a.q_l2 != nullptr) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) l2 = fmaf(rbf(x0[e]), rbf(x0[e]), fmaf(rbf(x1[e]), rbf(x1[e]), l2));
+      l2 = warp_sum(l2);
+      if (lane == 0) a.q_l2[((int64_t)b * a.H + head) * a.eta_head_stride + a.eta_t_off + t] = sqrtf(l2);
     }
     bf16* draw = reinterpret_cast<bf16*>(kind == 0 ? a.q_raw : a.k_raw) + off;
     bf16* drope = reinterpret_cast<bf16*>(kind == 0 ? a.q_rope : a.k_rope) + off;

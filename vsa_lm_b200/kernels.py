@@ -42,8 +42,10 @@ def prep(proj: torch.Tensor, *, B: int, T: int, H: int, HKV: int, HD: int, inv_f
          eps: float, q_norm_w: torch.Tensor | None, k_norm_w: torch.Tensor | None, pos0: int,
          q_raw: torch.Tensor, q_rope: torch.Tensor, eta: torch.Tensor, k_raw: torch.Tensor,
          k_rope: torch.Tensor, v: torch.Tensor, beta: torch.Tensor,
-         q_head_stride: int, q_t_off: int, k_head_stride: int, k_t_off: int) -> None:
-    """RMSNorm/RoPE/gates from the fused projection output into head-major buffers (bolt3_prep)."""
+         q_head_stride: int, q_t_off: int, k_head_stride: int, k_t_off: int,
+         q_l2: torch.Tensor | None = None) -> None:
+    """RMSNorm/RoPE/gates from the fused projection output into head-major buffers (bolt3_prep);
+    `q_l2` (optional, laid out like eta) receives |q_raw| per row."""
     lib = _lib.load()
     _need(proj, torch.bfloat16, "proj")
     for name, t in (("q_raw", q_raw), ("q_rope", q_rope), ("k_raw", k_raw), ("k_rope", k_rope), ("v", v)):
@@ -56,7 +58,8 @@ def prep(proj: torch.Tensor, *, B: int, T: int, H: int, HKV: int, HD: int, inv_f
         pos0=pos0, q_raw=q_raw.data_ptr(), q_rope=q_rope.data_ptr(), q_head_stride=q_head_stride,
         q_t_off=q_t_off, eta=eta.data_ptr(), eta_head_stride=q_head_stride, eta_t_off=q_t_off,
         k_raw=k_raw.data_ptr(), k_rope=k_rope.data_ptr(), v=v.data_ptr(), k_head_stride=k_head_stride,
-        k_t_off=k_t_off, beta=beta.data_ptr(), beta_head_stride=k_head_stride, beta_t_off=k_t_off)
+        k_t_off=k_t_off, beta=beta.data_ptr(), beta_head_stride=k_head_stride, beta_t_off=k_t_off,
+        q_l2=_ptr(q_l2))
     _lib.check(lib.bolt3_prep(ctypes.byref(a), _stream()), "bolt3_prep")
 
 
@@ -91,7 +94,7 @@ def attend_decode(*, n_chains: int, hkv: int, G: int, HD: int, q_rope: torch.Ten
                   seg0_chain_tokens: int, seg0_len: int, seg1_k: torch.Tensor, seg1_v: torch.Tensor,
                   seg1_chain_tokens: int, seg1_len: int, len_before: int,
                   sinks: tuple | None, bank: dict | None, kappa: torch.Tensor, coef: torch.Tensor,
-                  res_w: torch.Tensor, eps: float, y: torch.Tensor) -> None:
+                  res_w: torch.Tensor, eps: float, y: torch.Tensor, q_l2: torch.Tensor | None = None) -> None:
     """Attention of Tq new tokens over sinks, the current bank and the two-chunk window."""
     lib = _lib.load()
     a = _lib.AttendArgs(
@@ -106,7 +109,7 @@ def attend_decode(*, n_chains: int, hkv: int, G: int, HD: int, q_rope: torch.Ten
         bank_mass=_ptr(bank["mass"]) if bank else None, bank_act=_ptr(bank["act"]) if bank else None,
         bank_m=_ptr(bank["m_res"]) if bank else None, bank_cap=1, has_bank=int(bank is not None),
         kappa=kappa.data_ptr(), coef=coef.data_ptr(), res_w=res_w.data_ptr(), eps=eps,
-        y=y.data_ptr(), y_tokens=Tq)
+        y=y.data_ptr(), y_tokens=Tq, q_l2=_ptr(q_l2))
     _lib.check(lib.bolt3_attend(ctypes.byref(a), _stream()), "bolt3_attend")
 
 
@@ -116,7 +119,7 @@ def prefill_workspace_bytes(n_chains: int, T: int, HD: int) -> int:
 
 def prefill(*, B: int, T: int, H: int, HKV: int, HD: int, q_rope, q_raw, eta, k_raw, k_rope, v, beta,
             kappa, gamma, coef, inv_freq, res_w, eps: float, workspace: torch.Tensor, bank: dict,
-            y: torch.Tensor, status: torch.Tensor | None = None) -> None:
+            y: torch.Tensor, status: torch.Tensor | None = None, q_l2: torch.Tensor | None = None) -> None:
     """Phases B + C of Bolt3Attn.forward on prepared q/k/v (bolt3_prefill_fwd)."""
     lib = _lib.load()
     a = _lib.PrefillArgs(
@@ -128,13 +131,13 @@ def prefill(*, B: int, T: int, H: int, HKV: int, HD: int, q_rope, q_raw, eta, k_
         ak=bank["ak"].data_ptr(), av=bank["av"].data_ptr(), ak_rope=_ptr(bank.get("ak_rope")),
         mass=bank["mass"].data_ptr(), util=bank["util"].data_ptr(), pm=bank["pm"].data_ptr(),
         act=bank["act"].data_ptr(), m_res=bank["m_res"].data_ptr(), n_filled=bank["n_filled"].data_ptr(),
-        y=y.data_ptr(), status=_ptr(status))
+        y=y.data_ptr(), status=_ptr(status), q_l2=_ptr(q_l2))
     _lib.check(lib.bolt3_prefill_fwd(ctypes.byref(a), _stream()), "bolt3_prefill_fwd")
 
 
 def prefill_noalloc(*, B: int, T: int, H: int, HKV: int, HD: int, q_rope, q_raw, eta, k_raw, k_rope, v, beta,
                     kappa, gamma, coef, inv_freq, res_w, eps: float, bank: dict, y: torch.Tensor,
-                    status: torch.Tensor | None = None) -> None:
+                    status: torch.Tensor | None = None, q_l2: torch.Tensor | None = None) -> None:
     """Phases B + C like `prefill`, with the snapshot workspace taken from the library's fixed
     per-GPU array instead of the caller (bolt3_prefill_fwd_noalloc). For hosts that cannot allocate
     device memory on their hot path; the work must fit in `_lib.NOALLOC_SCRATCH_BYTES`."""
@@ -151,7 +154,7 @@ def prefill_noalloc(*, B: int, T: int, H: int, HKV: int, HD: int, q_rope, q_raw,
         ak=bank["ak"].data_ptr(), av=bank["av"].data_ptr(), ak_rope=_ptr(bank.get("ak_rope")),
         mass=bank["mass"].data_ptr(), util=bank["util"].data_ptr(), pm=bank["pm"].data_ptr(),
         act=bank["act"].data_ptr(), m_res=bank["m_res"].data_ptr(), n_filled=bank["n_filled"].data_ptr(),
-        y=y.data_ptr(), status=_ptr(status))
+        y=y.data_ptr(), status=_ptr(status), q_l2=_ptr(q_l2))
     _lib.check(lib.bolt3_prefill_fwd_noalloc(ctypes.byref(a), _stream()), "bolt3_prefill_fwd_noalloc")
 
 
