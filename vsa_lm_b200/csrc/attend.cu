@@ -15,8 +15,9 @@
 // (bolt3.py:251-256): y = bf16( bf16(P@V) + bf16( eta * RMSNorm_w( q_raw @ (M_hi + M_lo) / |q_raw|
 // * (1-gamma)/sqrt(HD) ) ) ), with M split into two bf16 terms.
 //
-// Warps 0-3 own one query row per thread (TMEM lane = row) for the softmax and the epilogue;
-// warps 4-7 load V, q_raw and M_res while the softmax runs. Thread 0 issues the MMAs.
+// Both warpgroups handle every query row (TMEM lane = row), each on half of the columns, and swap
+// row max / sum / RMS partials through shared memory. Warpgroup 1 also stages the M_res operand,
+// the sink scores, and V / q_raw behind the consumed K tiles. Thread 0 issues the MMAs.
 #include "../../include/bolt3.h"
 #include "common.cuh"
 #include "tc5.cuh"
@@ -44,6 +45,8 @@ struct __align__(1024) Smem {
   float sink_vf[4][HD];     // sink values in fp32 for the epilogue
   float sink_s[128][4];     // scaled sink scores per query row
   float res_w[HD];
+  float red_max[2][128];    // per-row partial results exchanged between the two warpgroups
+  float red_sum[2][128];
   float bias[S];
   uint64_t bar_s, bar_o;
   uint32_t tbase;
@@ -189,108 +192,29 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
   }
 
   constexpr float scale = HD == 128 ? 0.08838834764831845f : 0.125f;  // fp32(HD ** -0.5)
-  float p_sink[4] = {0.f, 0.f, 0.f, 0.f};
-  if (warp < 4) {
-    // ================= row warps: softmax
-    const int r = tid;
-    int gr, ir;
-    row_tok(min(r, max(n_rows - 1, 0)), gr, ir);
-    const int lim1 = len_before + ir;  // current-chunk key j is visible iff j <= lim1
-    asm volatile("bar.sync 1, 256;\n" ::);  // sink scores are in shared memory
-    float s_sink[4] = {neg_inf(), neg_inf(), neg_inf(), neg_inf()};
-    if (has_sinks) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) s_sink[j] = sm.sink_s[r][j];
-    }
-    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
-    const bool ok = tc5::mbar_wait(&sm.bar_s, 0, kWaitIters);
-    if (!ok) sm.err = 1;
-    tc5::fence_after_sync();
-    // score of column `col` of segment SEG after scale, bias and masks (SEG is compile-time, so
-    // the segment parameters stay in registers)
-    const float* bias = sm.bias;
-    auto row_pass = [&](auto seg_tag, auto&& body) {
-      constexpr int SEG = decltype(seg_tag)::value;
-      const int lim = SEG == 1 ? L0 - 1 : (SEG == 2 ? min(L1 - 1, lim1) : S - 1);
-      for (int c0 = 0; c0 < 128; c0 += 32) {
-        uint32_t v[32];
-        tc5::ld32(tb + lane_off + SEG * 128 + c0, v);
-        tc5::ld_wait();
-        float x[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float sc = __fmul_rn(__uint_as_float(v[j]), scale);
-          if (SEG == 0) x[j] = __fadd_rn(sc, bias[c0 + j]);
-          else x[j] = (c0 + j <= lim) ? sc : neg_inf();
-        }
-        body(c0, x);
-      }
-    };
-    auto for_each_seg = [&](auto&& body) {
-      if (seg_on[0]) row_pass(std::integral_constant<int, 0>{}, [&](int c0, float (&x)[32]) { body(0, c0, x); });
-      if (seg_on[1]) row_pass(std::integral_constant<int, 1>{}, [&](int c0, float (&x)[32]) { body(1, c0, x); });
-      if (seg_on[2]) row_pass(std::integral_constant<int, 2>{}, [&](int c0, float (&x)[32]) { body(2, c0, x); });
-    };
-    // pass 1: row max
-    float mx = fmaxf(fmaxf(s_sink[0], s_sink[1]), fmaxf(s_sink[2], s_sink[3]));
-    if (ok) {
-      for_each_seg([&](int, int, float (&x)[32]) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, x[j]);
-      });
-    }
-    // pass 2: row sum of exp(x - max) (exp2 of the scaled difference: only the sum's value is
-    // needed here, at fp32 accuracy)
-    constexpr float kLog2e = 1.4426950408889634f;
-    float sum = 0.f;
-    float e_sink[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      e_sink[j] = s_sink[j] == neg_inf() ? 0.f : expf(s_sink[j] - mx);
-      sum += e_sink[j];
-    }
-    if (ok) {
-      float part[4] = {0.f, 0.f, 0.f, 0.f};
-      for_each_seg([&](int, int, float (&x)[32]) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) part[j & 3] += exp2f(__fmul_rn(x[j] - mx, kLog2e));
-      });
-      sum += (part[0] + part[1]) + (part[2] + part[3]);
-    }
-    // pass 3: p = bf16(exp(x - max) * (1 / sum)), two per column, into TMEM columns [0, 192).
-    // exp via exp2 of (x - max) * log2(e): within ~1e-6 relative of exp, so the bf16 cast of p
-    // matches the reference's except for values within that distance of a rounding boundary.
-    const float inv_sum = 1.0f / sum;
-    if (ok) {
-      for_each_seg([&](int s, int c0, float (&x)[32]) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float e0 = exp2f(__fmul_rn(x[2 * j] - mx, kLog2e));
-          const float e1 = exp2f(__fmul_rn(x[2 * j + 1] - mx, kLog2e));
-          pk[j] = pack_bf16(__fmul_rn(e0, inv_sum), __fmul_rn(e1, inv_sum));
-        }
-        tc5::st16(tb + lane_off + (uint32_t)((s * 128 + c0) >> 1), pk);
-      });
-      tc5::st_wait();
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) p_sink[j] = rbf(__fmul_rn(e_sink[j], inv_sum));
-    tc5::fence_before_sync();
-  } else {
-    // ================= helper warps: M_res operand, sink scores, then (after the S MMAs) V and q_raw
-    const int ht = tid - 128;
+  constexpr float kLog2e = 1.4426950408889634f;
+  // Both warpgroups work on every query row r (= TMEM lane): warpgroup wg takes columns
+  // [wg*64, wg*64+64) of each key segment and [wg*HD/2, (wg+1)*HD/2) of the output.
+  const int wg = warp >> 2;
+  const int r = tid & 127;
+  const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+  int gr, ir;
+  row_tok(min(r, max(n_rows - 1, 0)), gr, ir);
+  const int lim1 = len_before + ir;  // current-chunk key j is visible iff j <= lim1
+
+  if (wg == 1) {
+    // ---- warpgroup 1 prologue: the M_res operand and the sink scores
     if (has_bank && a.prefill) {
       // the consolidation scan wrote the split, swizzled operand image: copy it as is
       const unsigned char* img = reinterpret_cast<const unsigned char*>(a.bank_m) + bofs * (int64_t)HD * HD * 4;
-      for (int i = ht; i < HD * HD / 4; i += 128) cp_async16(&sm.m[0][0][0] + i * 16, img + i * 16, true);
+      for (int i = r; i < HD * HD / 4; i += 128) cp_async16(&sm.m[0][0][0] + i * 16, img + i * 16, true);
       cp_async_commit();
     } else if (has_bank) {
       // M_res [d][e] fp32 row-major: split into bf16 hi/lo in the MN-major operand layout (rows d,
       // 64-column blocks of e); coalesced float4 loads, eight in flight per thread
       const float4* gm = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.bank_m) + bofs * HD * HD);
       constexpr int N4 = HD * HD / 4;
-      for (int i0 = ht; i0 < N4; i0 += 128 * 8) {
+      for (int i0 = r; i0 < N4; i0 += 128 * 8) {
         float4 mv[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) mv[u] = i0 + u * 128 < N4 ? gm[i0 + u * 128] : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -314,8 +238,6 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
       }
     }
     if (has_sinks) {
-      // scaled sink scores of row ht, and the sink values in fp32
-      const int r = ht;
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
       for (int ch = 0; ch < HD / 8; ++ch) {
         const uint4 qv = *reinterpret_cast<const uint4*>(sm.q[ch >> 3] + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
@@ -333,30 +255,128 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
       }
 #pragma unroll
       for (int j = 0; j < 4; ++j) sm.sink_s[r][j] = __fmul_rn(acc[j], scale);
-      for (int i = ht; i < 4 * HD; i += 128) sm.sink_vf[i / HD][i % HD] = bf2f(sm.sink_v[i / HD][i % HD]);
+      for (int i = r; i < 4 * HD; i += 128) sm.sink_vf[i / HD][i % HD] = bf2f(sm.sink_v[i / HD][i % HD]);
     }
-    asm volatile("bar.sync 2, 128;\n" ::);   // every helper is done reading Q
-    asm volatile("bar.arrive 1, 256;\n" ::); // sink scores ready for the row warps
-    const bool ok = tc5::mbar_wait(&sm.bar_s, 0, kWaitIters);
-    if (!ok) sm.err = 1;
-    tc5::fence_after_sync();
-    if (ok) {
-      for (int s = 0; s < 3; ++s)
-        if (seg_on[s]) load_tile<HD>(sm.kv[s], seg_v[s], seg_len[s], ht, 128);
-      if (has_bank) {
-        constexpr int CPR = HD / 8;
-        for (int i = ht; i < 128 * CPR; i += 128) {
-          const int r = i / CPR, ch = i % CPR;
-          unsigned char* d = sm.q[ch >> 3] + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
-          cp_async16(d, q_row_ptr(a.q_raw, r) + ch * 8, r < n_rows);
-        }
-      }
-      cp_async_commit();
-      cp_async_wait<0>();
-    }
-    asm volatile("fence.proxy.async.shared::cta;\n" ::);
-    tc5::fence_before_sync();
+    asm volatile("bar.sync 2, 128;\n" ::);   // warpgroup 1 is done reading Q
+    asm volatile("bar.arrive 1, 256;\n" ::); // sink scores are ready
+  } else {
+    asm volatile("bar.sync 1, 256;\n" ::);
   }
+  float s_sink[4] = {neg_inf(), neg_inf(), neg_inf(), neg_inf()};
+  if (has_sinks) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s_sink[j] = sm.sink_s[r][j];
+  }
+  const bool ok = tc5::mbar_wait(&sm.bar_s, 0, kWaitIters);
+  if (!ok) sm.err = 1;
+  tc5::fence_after_sync();
+  if (wg == 1 && ok) {
+    // K tiles are consumed: stream V (and q_raw for the read-out) in behind them
+    for (int s2 = 0; s2 < 3; ++s2)
+      if (seg_on[s2]) load_tile<HD>(sm.kv[s2], seg_v[s2], seg_len[s2], r, 128);
+    if (has_bank) {
+      constexpr int CPR = HD / 8;
+      for (int i = r; i < 128 * CPR; i += 128) {
+        const int rr = i / CPR, ch = i % CPR;
+        unsigned char* d = sm.q[ch >> 3] + rr * 128 + (((ch & 7) ^ (rr & 7)) << 4);
+        cp_async16(d, q_row_ptr(a.q_raw, rr) + ch * 8, rr < n_rows);
+      }
+    }
+    cp_async_commit();
+  }
+
+  // ---- softmax over this warpgroup's half of every segment
+  const float* bias = sm.bias;
+  auto row_pass = [&](auto seg_tag, auto&& body) {
+    constexpr int SEG = decltype(seg_tag)::value;
+    const int lim = SEG == 1 ? L0 - 1 : (SEG == 2 ? min(L1 - 1, lim1) : S - 1);
+    for (int c0 = wg * 64; c0 < wg * 64 + 64; c0 += 32) {
+      uint32_t v[32];
+      tc5::ld32(tb + lane_off + SEG * 128 + c0, v);
+      tc5::ld_wait();
+      float x[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float sc = __fmul_rn(__uint_as_float(v[j]), scale);
+        if (SEG == 0) x[j] = __fadd_rn(sc, bias[c0 + j]);
+        else x[j] = (c0 + j <= lim) ? sc : neg_inf();
+      }
+      body(c0, x);
+    }
+  };
+  auto for_each_seg = [&](auto&& body) {
+    if (seg_on[0]) row_pass(std::integral_constant<int, 0>{}, [&](int c0, float (&x)[32]) { body(0, c0, x); });
+    if (seg_on[1]) row_pass(std::integral_constant<int, 1>{}, [&](int c0, float (&x)[32]) { body(1, c0, x); });
+    if (seg_on[2]) row_pass(std::integral_constant<int, 2>{}, [&](int c0, float (&x)[32]) { body(2, c0, x); });
+  };
+  // pass 1: row max (the sinks are counted by warpgroup 0)
+  float mx = wg == 0 ? fmaxf(fmaxf(s_sink[0], s_sink[1]), fmaxf(s_sink[2], s_sink[3])) : neg_inf();
+  if (ok) {
+    for_each_seg([&](int, int, float (&x)[32]) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) mx = fmaxf(mx, x[j]);
+    });
+  }
+  sm.red_max[wg][r] = mx;
+  asm volatile("bar.sync 3, 256;\n" ::);
+  mx = fmaxf(sm.red_max[0][r], sm.red_max[1][r]);
+  // pass 2: row sum of exp(x - max); exp via exp2 of (x - max) * log2(e), within ~1e-6 relative
+  float e_sink[4];
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    e_sink[j] = s_sink[j] == neg_inf() ? 0.f : expf(s_sink[j] - mx);
+    if (wg == 0) sum += e_sink[j];
+  }
+  if (ok) {
+    float part[4] = {0.f, 0.f, 0.f, 0.f};
+    for_each_seg([&](int, int, float (&x)[32]) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) part[j & 3] += exp2f(__fmul_rn(x[j] - mx, kLog2e));
+    });
+    sum += (part[0] + part[1]) + (part[2] + part[3]);
+  }
+  sm.red_sum[wg][r] = sum;
+  asm volatile("bar.sync 3, 256;\n" ::);
+  sum = sm.red_sum[0][r] + sm.red_sum[1][r];
+  // pass 3: p = bf16(exp(x - max) * (1 / sum)), two per column, into TMEM columns [0, 192); the
+  // bf16 cast matches the reference's except within ~1e-6 of a rounding boundary. P of segment s
+  // lands on score columns of earlier segments that either warpgroup may still be reading, so each
+  // segment's P is written only after both warpgroups have read that segment's scores.
+  const float inv_sum = 1.0f / sum;
+  auto p_pass = [&](auto seg_tag) {
+    constexpr int SEG = decltype(seg_tag)::value;
+    uint32_t pk[2][16];
+    int half = 0;
+    if (ok) {
+      row_pass(seg_tag, [&](int, float (&x)[32]) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float e0 = exp2f(__fmul_rn(x[2 * j] - mx, kLog2e));
+          const float e1 = exp2f(__fmul_rn(x[2 * j + 1] - mx, kLog2e));
+          pk[half][j] = pack_bf16(__fmul_rn(e0, inv_sum), __fmul_rn(e1, inv_sum));
+        }
+        ++half;
+      });
+    }
+    asm volatile("bar.sync 3, 256;\n" ::);
+    if (ok) {
+      tc5::st16(tb + lane_off + (uint32_t)(SEG * 64 + wg * 32), pk[0]);
+      tc5::st16(tb + lane_off + (uint32_t)(SEG * 64 + wg * 32 + 16), pk[1]);
+    }
+  };
+  if (seg_on[0]) p_pass(std::integral_constant<int, 0>{});
+  if (seg_on[1]) p_pass(std::integral_constant<int, 1>{});
+  if (seg_on[2]) p_pass(std::integral_constant<int, 2>{});
+  if (ok) tc5::st_wait();
+  float p_sink[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) p_sink[j] = rbf(__fmul_rn(e_sink[j], inv_sum));
+  if (wg == 1) {
+    cp_async_wait<0>();
+    asm volatile("fence.proxy.async.shared::cta;\n" ::);
+  }
+  tc5::fence_before_sync();
   __syncthreads();
   tc5::fence_after_sync();
   const bool ok_all = sm.err == 0;
@@ -365,11 +385,11 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
   if (tid == 0 && ok_all) {
     constexpr uint32_t kIdO = tc5::idesc_bf16(128, HD, false, true);
     bool first = true;
-    for (int s = 0; s < 3; ++s) {
-      if (!seg_on[s]) continue;
-      const uint32_t va = tc5::smem_u32(sm.kv[s][0]);
+    for (int s2 = 0; s2 < 3; ++s2) {
+      if (!seg_on[s2]) continue;
+      const uint32_t va = tc5::smem_u32(sm.kv[s2][0]);
       for (int ks = 0; ks < 8; ++ks) {
-        tc5::mma_ts(tb + kColO, tb + (uint32_t)(s * 64 + ks * 8), tc5::sdesc(va + ks * 2048, 16384, 1024), kIdO,
+        tc5::mma_ts(tb + kColO, tb + (uint32_t)(s2 * 64 + ks * 8), tc5::sdesc(va + ks * 2048, 16384, 1024), kIdO,
                     first ? 0u : 1u);
         first = false;
       }
@@ -389,11 +409,10 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
     tc5::commit(&sm.bar_o);
   }
 
-  if (warp < 4) {
-    // ================= epilogue: one output row per thread
-    const int r = tid;
-    int gr, ir;
-    row_tok(min(r, max(n_rows - 1, 0)), gr, ir);
+  // ---- epilogue: warpgroup wg writes columns [wg*HD/2, (wg+1)*HD/2) of row r
+  {
+    constexpr int HALF = HD / 2;
+    const int cbeg = wg * HALF;
     float qn = 0.f;
     if (has_bank && a.q_l2 != nullptr) {
       qn = a.q_l2[((int64_t)c * G + gr) * a.Tq + (int64_t)blk * 128 + ir];
@@ -410,17 +429,15 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
       }
       qn = sqrtf(acc);
     }
-    const bool ok = ok_all && tc5::mbar_wait(&sm.bar_o, 0, kWaitIters);
-    if (!ok && ok_all) sm.err = 1;
+    const float eta = has_bank ? a.eta[((int64_t)c * G + gr) * a.Tq + (int64_t)blk * 128 + ir] : 0.f;
+    const float coef = has_bank ? a.coef[kvh] : 0.f;
+    const bool ok2 = ok_all && tc5::mbar_wait(&sm.bar_o, 0, kWaitIters);
+    if (!ok2 && ok_all) sm.err = 1;
     tc5::fence_after_sync();
-    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
-    float rs = 0.f, inv_qn = 0.f, coef = 0.f, eta = 0.f;
-    if (ok && has_bank) {
-      inv_qn = 1.0f / fmaxf(qn, 1e-12f);
-      coef = a.coef[kvh];
-      eta = a.eta[((int64_t)c * G + gr) * a.Tq + (int64_t)blk * 128 + ir];
-      float ss = 0.f;
-      for (int c0 = 0; c0 < HD; c0 += 32) {
+    const float inv_qn = 1.0f / fmaxf(qn, 1e-12f);
+    float ss = 0.f;
+    if (ok2 && has_bank) {
+      for (int c0 = cbeg; c0 < cbeg + HALF; c0 += 32) {
         uint32_t v[32];
         tc5::ld32(tb + lane_off + kColR + c0, v);
         tc5::ld_wait();
@@ -430,12 +447,14 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
           ss = fmaf(ym, ym, ss);
         }
       }
-      rs = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)HD), a.eps));
     }
-    if (ok) {
+    sm.red_max[wg][r] = ss;
+    asm volatile("bar.sync 3, 256;\n" ::);
+    const float rs = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(sm.red_max[0][r] + sm.red_max[1][r], (float)HD), a.eps));
+    if (ok2) {
       bf16* yrow = reinterpret_cast<bf16*>(a.y) +
                    (((int64_t)b * a.y_tokens + (int64_t)blk * 128 + ir) * H + kvh * G + gr) * HD;
-      for (int c0 = 0; c0 < HD; c0 += 32) {
+      for (int c0 = cbeg; c0 < cbeg + HALF; c0 += 32) {
         uint32_t vo[32], vr[32];
         tc5::ld32(tb + lane_off + kColO + c0, vo);
         if (has_bank) tc5::ld32(tb + lane_off + kColR + c0, vr);
