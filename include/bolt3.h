@@ -68,10 +68,13 @@ int bolt3_prep(const bolt3_prep_args* a, void* stream);
  * whose RoPE position is pos0 + token index. The bank is read from / written back to the state
  * arrays (init_blank = 1 starts from the empty bank of bolt3.py:83-92). After each step the
  * state the attention reads is optionally written to snapshot slot snap0 + i:
- *   snap_ak_rope, snap_av [chains][snap_cap][S][HD] bf16; snap_mass [chains][snap_cap][S] fp32;
- *   snap_act [chains][snap_cap][S] uint8; snap_m [chains][snap_cap] x HD*HD*4 bytes: M_res split
- *   into bf16 hi and lo terms, each the 128-byte-swizzled MN-major tensor-core operand image
- *   [HD/64 column blocks][HD rows d][64 columns e] that bolt3_attend copies as is.
+ *   snap_ak_rope, snap_av [chains][snap_cap] x S*HD*2 bytes; snap_mass [chains][snap_cap][S] fp32;
+ *   snap_act [chains][snap_cap][S] uint8; snap_m [chains][snap_cap] x HD*HD*4 bytes.
+ *   The bf16 snapshots are tensor-core operand images that bolt3_attend copies as is: a tile of
+ *   R rows x HD columns is HD/64 blocks of [R rows][64 columns], each row 128 bytes whose 16-byte
+ *   chunk c sits at chunk c ^ (row & 7). ak_rope and av: R = S rows of slots. snap_m: M_res split
+ *   into bf16 hi then lo terms, each an image with R = HD rows d and columns e. The final bank
+ *   (ak, av, ak_rope, m_res) is written in the plain row-major layouts listed at the top.
  * `ak_rope` (optional) receives RoPE(ak, pm) of the final bank. `status` (optional, device int)
  * is OR-ed with 1 when a kernel-side bounds check of the tie-order emulation fires. */
 typedef struct bolt3_consolidate_args {

@@ -75,6 +75,24 @@ def near_tie_chains(rec: dict, rel: float = 1e-6) -> torch.Tensor:
     return close_pairs(sc)
 
 
+def ambiguous(rec: dict) -> bool:
+    """A consolidation whose decisions depend on rounding noise: a cosine within NEAR of a merge
+    threshold, or ranking keys within 1e-6 relative of each other (first-fill variance scores of
+    near-zero-mean values tie at the fp32 ulp level; their order then follows the CPU's reduction
+    order, and any later exact-tie break between those slots follows that order)."""
+    return bool(near_threshold(rec).any() or near_tie_chains(rec).any())
+
+
+def bank_multiset(mass: torch.Tensor, pm: torch.Tensor, act: torch.Tensor):
+    """Slot-order-free view of a bank: per chain, the sorted (pm, mass) of the active slots."""
+    out = []
+    for c in range(mass.shape[0]):
+        a = act[c].bool()
+        key = torch.stack([pm[c][a].double(), mass[c][a].double()], dim=-1)
+        out.append(key[torch.argsort(key[:, 0] * 1e6 + key[:, 1])])
+    return out
+
+
 def inputs(shape: str, B: int, T: int, dup, seed: int = 1, device="cuda"):
     cfg = layer_cfg(shape)
     x = make_input(B, T, cfg["dim"], dup=dup, seed=seed)

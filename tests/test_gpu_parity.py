@@ -7,8 +7,8 @@ except for chains where a cosine lies within 1e-3 of the 0.88 / 0.80 thresholds,
 import pytest
 import torch
 
-from helpers import (BF16, STATE_RTOL, bf16_module, inputs, near_threshold, near_tie_chains, oracle_cfg_of,
-                     oracle_params, output_close)
+from helpers import (ATOL_RMS, BF16, RTOL, STATE_RTOL, ambiguous, bank_multiset, bf16_module, inputs,
+                     near_threshold, near_tie_chains, oracle_cfg_of, oracle_params, output_close)
 from oracle import LayerDecoderOracle, forward, gamma_delta, project, rope_at
 from vsa_lm_b200 import Bolt3Decoder, Bolt3LayerState
 from vsa_lm_b200 import kernels as K
@@ -122,12 +122,24 @@ def test_consolidation_teacher_forced(shape, B, T, dup):
     ("tiny", 1, 257, 0.0), ("tiny", 3, 300, 0.0), ("tiny", 1, 1, 0.0),
 ])
 def test_forward_matches_oracle(shape, B, T, dup):
+    """Free-running forward. Outputs must match chunk by chunk; a chunk may deviate only after a
+    consolidation whose decisions the oracle records as rounding-ambiguous (the strict per-step
+    checks are the teacher-forced tests)."""
     cfg, m, P, oc, x_cpu, x, y_ref, rec, snaps = _oracle_run(shape, B, T, dup)
-    y = m(x)
+    y = m(x).float().cpu()
     torch.cuda.synchronize()
-    flips = sum(int(near_threshold(r).sum()) for r in rec)
-    assert flips == 0, f"{flips} near-threshold decisions in this seeded case; pick another seed"
-    output_close(y, y_ref, "Bolt3Attn.forward")
+    rms = y_ref.pow(2).mean().sqrt().item()
+    bad_chunk = None
+    for r in range(0, (T + C - 1) // C):
+        yg, yr = y[:, r * C:(r + 1) * C], y_ref[:, r * C:(r + 1) * C]
+        if ((yg - yr).abs() > RTOL * yr.abs() + ATOL_RMS * rms).any():
+            bad_chunk = r
+            break
+    if bad_chunk is not None:
+        # chunk r reads the bank after consolidation r-2: some consolidation <= r-2 must be ambiguous
+        assert bad_chunk >= 2 and any(ambiguous(rec[i]) for i in range(bad_chunk - 1)), \
+            f"chunk {bad_chunk} deviates with no rounding-ambiguous decision before it"
+        print(f"outputs agree up to chunk {bad_chunk}; a rounding-ambiguous decision precedes it")
 
 
 def test_forward_is_deterministic():
@@ -138,6 +150,9 @@ def test_forward_is_deterministic():
 
 @pytest.mark.parametrize("shape,prompt,n_dec", [("tiny", 300, 150), ("qwen3_4b", 512, 140)])
 def test_decoder_matches_oracle(shape, prompt, n_dec):
+    """Free-running decoder (prefill slices + single-token steps). Outputs must match until the
+    native bank stops being the same set of slots as the oracle's, and that may only happen at a
+    consolidation the oracle records as rounding-ambiguous."""
     cfg = layer_cfg(shape)
     B = 2
     m = bf16_module(cfg, 0)
@@ -148,14 +163,69 @@ def test_decoder_matches_oracle(shape, prompt, n_dec):
     m_res = torch.zeros(B, m.HKV, m.HD, m.HD, device="cuda")
     steps = [(s, min(128, prompt - s)) for s in range(0, prompt, 128)] + [(prompt + i, 1) for i in range(n_dec)]
     outs, refs = [], []
+    diverged = False
     for pos, n in steps:
         h = x[:, pos:pos + n]
-        outs.append(Bolt3Decoder.layer_step(m, st, h.cuda(), pos, m_res).float().cpu())
-        refs.append(dec.step(h.float(), pos))
-    flips = sum(int(near_threshold(r).sum()) for r in dec.record)
-    assert flips == 0
-    output_close(torch.cat(outs, 1), torch.cat(refs, 1), "decoder step outputs")
-    # free-running state: the GPU's own bf16 projections feed it, so it is held to the output
-    # tolerance; the 1e-4 state bound is checked teacher-forced in test_consolidation_teacher_forced
-    scale = dec.m_res.abs().max().clamp_min(1e-30)
-    assert ((m_res.cpu() - dec.m_res).abs().max() / scale).item() < 1e-2
+        n_rec = len(dec.record)
+        got = Bolt3Decoder.layer_step(m, st, h.cuda(), pos, m_res).float().cpu()
+        ref = dec.step(h.float(), pos)
+        outs.append(got)
+        refs.append(ref)
+        if len(dec.record) > n_rec:
+            torch.cuda.synchronize()
+            mine = bank_multiset(st.bank["mass"].cpu(), st.bank["pm"].cpu(), st.bank["act"].cpu())
+            theirs = bank_multiset(dec.sc["mass"], dec.sc["pm"], dec.sc["act"])
+            same = all(a.shape == b.shape and torch.allclose(a, b, rtol=1e-5, atol=1e-3) for a, b in zip(mine, theirs))
+            if not same:
+                assert any(ambiguous(r) for r in dec.record), \
+                    f"bank diverged at position {pos} with no rounding-ambiguous decision"
+                diverged = True
+                break
+    assert len(outs) >= (prompt + 127) // 128, "must cover at least the prefill"
+    output_close(torch.cat(outs[:-1] if diverged else outs, 1), torch.cat(refs[:-1] if diverged else refs, 1),
+                 "decoder step outputs")
+    if not diverged:
+        # free-running state: the GPU's own bf16 projections feed it, so it is held to the output
+        # tolerance; the 1e-4 state bound is checked teacher-forced in test_consolidation_teacher_forced
+        scale = dec.m_res.abs().max().clamp_min(1e-30)
+        assert ((m_res.cpu() - dec.m_res).abs().max() / scale).item() < 1e-2
+
+
+@pytest.mark.parametrize("shape,B,T,dup", [("config0", 1, 1024, "chunks"), ("qwen3_4b", 2, 1024, 0.3),
+                                           ("tiny", 2, 900, 0.3)])
+def test_attention_teacher_forced(shape, B, T, dup):
+    """The attention kernel fed the oracle's exact bank (snapshot r-2), sinks and window for every
+    chunk r reproduces the oracle's attention output of that chunk (strict: no decision involved)."""
+    cfg, m, P, oc, x_cpu, x, y_ref, rec, snaps = _oracle_run(shape, B, T, dup)
+    qr, kr, vo, bo, eo = project(P, oc, x_cpu, BF16)
+    pos = torch.arange(T, dtype=torch.float32)
+    qp, kp = rope_at(qr, pos, oc["inv_freq"], BF16), rope_at(kr, pos, oc["inv_freq"], BF16)
+    _, yh_ref = forward(P, oc, x_cpu, BF16, return_y_heads=True)      # [b, H, T, HD]
+    H, HKV, HD, G = m.H, m.HKV, m.HD, m.G
+    f = m.fused("cuda")
+    c = f.consts
+    cu = lambda t, dt=torch.bfloat16: t.to(device="cuda", dtype=dt).contiguous()
+    q_rope_all, q_raw_all = cu(qp.reshape(B * H, T, HD)), cu(qr.reshape(B * H, T, HD))
+    k_all, v_all = cu(kp.reshape(B * HKV, T, HD)), cu(vo.reshape(B * HKV, T, HD))
+    eta_all = cu(eo.reshape(B * H, T), torch.float32)
+    worst = 0.0
+    for r in range(2, (T + C - 1) // C):
+        s0, e0 = r * C, min(T, (r + 1) * C)
+        tq = e0 - s0
+        bank = snaps[r - 2]
+        ak_rope = rope_at(bank["ak"].view(B, HKV, 128, HD), bank["pm"].view(B, HKV, 128), oc["inv_freq"], BF16)
+        b = dict(ak_rope=cu(ak_rope.reshape(B * HKV, 128, HD)), av=cu(bank["av"]), mass=cu(bank["mass"], torch.float32),
+                 act=cu(bank["act"], torch.uint8), m_res=cu(bank["m_res"], torch.float32))
+        y = torch.empty(B, tq, H, HD, dtype=torch.bfloat16, device="cuda")
+        K.attend_decode(n_chains=B * HKV, hkv=HKV, G=G, HD=HD, q_rope=q_rope_all[:, s0:e0].contiguous(),
+                        q_raw=q_raw_all[:, s0:e0].contiguous(), eta=eta_all[:, s0:e0].contiguous(), Tq=tq,
+                        seg0_k=k_all[:, s0 - C:s0].contiguous(), seg0_v=v_all[:, s0 - C:s0].contiguous(),
+                        seg0_chain_tokens=C, seg0_len=C, seg1_k=k_all[:, s0:e0].contiguous(),
+                        seg1_v=v_all[:, s0:e0].contiguous(), seg1_chain_tokens=tq, seg1_len=tq, len_before=0,
+                        sinks=(k_all[:, :4].contiguous(), v_all[:, :4].contiguous()), bank=b,
+                        kappa=c["kappa"], coef=c["coef"], res_w=c["res_w"], eps=m.eps, y=y)
+        got = y.float().cpu().permute(0, 2, 1, 3)
+        ref = yh_ref[:, :, s0:e0]
+        info = output_close(got, ref, f"attention of chunk {r}")
+        worst = max(worst, info["max_rel_rms"])
+    print(f"worst chunk error {worst:.3e} of RMS")

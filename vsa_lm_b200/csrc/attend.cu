@@ -53,6 +53,14 @@ struct __align__(1024) Smem {
   int err;
 };
 
+// Contiguous 16-byte-chunk copy of a tile that is already a SW128 operand image (the snapshots
+// written by the consolidation scan).
+template <int HD>
+B3_DEV void copy_image(unsigned char (*dst)[16384], const bf16* src, int t, int nthreads) {
+  const unsigned char* s = reinterpret_cast<const unsigned char*>(src);
+  for (int i = t; i < 128 * HD * 2 / 16; i += nthreads) cp_async16(&dst[0][0] + i * 16, s + i * 16, true);
+}
+
 // 16-byte-chunk cp.async of 128 rows of an [*][HD] bf16 array into a SW128 tile; rows at or beyond
 // `valid` are zero-filled. Threads t, t + nthreads, ... take part.
 template <int HD>
@@ -141,8 +149,11 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
       unsigned char* d = sm.q[ch >> 3] + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
       cp_async16(d, q_row_ptr(a.q_rope, r) + ch * 8, r < n_rows);
     }
-    for (int s = 0; s < 3; ++s)
-      if (seg_on[s]) load_tile<HD>(sm.kv[s], seg_k[s], seg_len[s], tid, NT);
+    for (int s = 0; s < 3; ++s) {
+      if (!seg_on[s]) continue;
+      if (s == 0 && a.prefill) copy_image<HD>(sm.kv[0], seg_k[0], tid, NT);
+      else load_tile<HD>(sm.kv[s], seg_k[s], seg_len[s], tid, NT);
+    }
     if (has_sinks) {
       for (int i = tid; i < 4 * HD / 8; i += NT) {
         cp_async16(&sm.sink_k[0][0] + i * 8, sk + i * 8, true);
@@ -272,8 +283,11 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
   tc5::fence_after_sync();
   if (wg == 1 && ok) {
     // K tiles are consumed: stream V (and q_raw for the read-out) in behind them
-    for (int s2 = 0; s2 < 3; ++s2)
-      if (seg_on[s2]) load_tile<HD>(sm.kv[s2], seg_v[s2], seg_len[s2], r, 128);
+    for (int s2 = 0; s2 < 3; ++s2) {
+      if (!seg_on[s2]) continue;
+      if (s2 == 0 && a.prefill) copy_image<HD>(sm.kv[0], seg_v[0], r, 128);
+      else load_tile<HD>(sm.kv[s2], seg_v[s2], seg_len[s2], r, 128);
+    }
     if (has_bank) {
       constexpr int CPR = HD / 8;
       for (int i = r; i < 128 * CPR; i += 128) {

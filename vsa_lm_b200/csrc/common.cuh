@@ -48,12 +48,13 @@ B3_DEV float quad_max(float v) {
   return v;
 }
 
-// ---- swizzled [rows][COLS] bf16 tiles in shared memory: the 16-byte chunk index of each row is
-// XOR-ed with (row & 7) so that ldmatrix row reads of 8 consecutive rows hit distinct banks.
+// ---- swizzled [128][COLS] bf16 tiles in shared memory, in the 128-byte-swizzle layout the tensor
+// cores read: COLS / 64 blocks of [128 rows][64 columns]; within a 128-byte row the 16-byte chunk
+// index is XOR-ed with (row & 7), so ldmatrix reads of 8 consecutive rows hit distinct banks.
 template <int COLS>
 B3_DEV int swz(int r, int c) {
-  static_assert(COLS % 64 == 0, "swizzled tiles need >= 8 chunks per row");
-  return r * COLS + ((((c >> 3) ^ (r & 7))) << 3) + (c & 7);
+  static_assert(COLS % 64 == 0, "swizzled tiles are made of 64-column blocks");
+  return (c >> 6) * (128 * 64) + r * 64 + (((((c >> 3) & 7) ^ (r & 7))) << 3) + (c & 7);
 }
 
 // ---- legacy warp-level tensor-core MMA (m16n8k16, bf16 in, fp32 accumulate)

@@ -35,8 +35,8 @@ struct Smem {
   bf16 vv[CC * HD];
   bf16 x1[128 * HD];   // kp, then M_hi, then E_hi
   bf16 x2[128 * HD];   // RoPE(ak, pm), then M_lo, then E_lo
-  float mass[S], util[S], pm[S], keep[S], na[S], bias[S], botv[S];
-  float rel[CC], score[CC], bsk[CC], beta[CC], nk[CC], nv[CC], pos[CC], wgt[CC], topv[CC];
+  float mass[S], util[S], pm[S], keep[S], na[S], rna[S], bias[S], botv[S];
+  float rel[CC], score[CC], bsk[CC], beta[CC], nk[CC], rnk[CC], nv[CC], pos[CC], wgt[CC], topv[CC];
   int best[CC], tops[CC], bots[S], mlist[CC];
   unsigned char act[S], mrg[CC], ins[CC];
   int n_merged;
@@ -66,6 +66,13 @@ B3_DEV void s2g_rows(bf16* g, const bf16* s) {
   }
 }
 
+// Bulk (TMA engine) copy of `bytes` contiguous bytes of shared memory to global memory.
+B3_DEV void bulk_s2g(void* gdst, const void* ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(gdst),
+               "r"((uint32_t)__cvta_generic_to_shared(ssrc)), "r"(bytes)
+               : "memory");
+}
+
 // squared L2 norm of row r of a swizzled tile (whole warp)
 template <int HD>
 B3_DEV float row_sumsq(const bf16* s, int r, int lane) {
@@ -78,6 +85,27 @@ B3_DEV float row_sumsq(const bf16* s, int r, int lane) {
     acc = fmaf(x, x, acc);
   }
   return warp_sum(acc);
+}
+
+// Sum over one half of the 16-byte chunks of row r of x*y (swizzling only permutes chunks within a
+// row, so the two halves of a row together cover it exactly once).
+template <int HD>
+B3_DEV float half_row_dot(const bf16* x, const bf16* y, int r, int half) {
+  constexpr int CPR = HD / 8;
+  float acc = 0.f;
+#pragma unroll
+  for (int ch = half * CPR / 2; ch < (half + 1) * CPR / 2; ++ch) {
+    const int off = (ch >> 3) * (128 * 64) + r * 64 + (ch & 7) * 8;  // physical chunk ch of row r
+    const uint4 a = *reinterpret_cast<const uint4*>(x + off);
+    const uint4 b = *reinterpret_cast<const uint4*>(y + off);
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float2 fa = unpack_bf16(aw[u]), fb = unpack_bf16(bw[u]);
+      acc = fmaf(fa.x, fb.x, fmaf(fa.y, fb.y, acc));
+    }
+  }
+  return acc;
 }
 
 // ------------------------------------------------------------------------------------------
@@ -338,6 +366,14 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
     g2s_rows<HD>(sm.vv, g_v + t_begin * HD, l_tok);
     if (n_filled > 0) g2s_rows<HD>(sm.x1, g_kp + t_begin * HD, l_tok);
     cp_async_commit();
+    if (tid == 0 && st + 1 < a.n_steps) {
+      // pull the next chunk into L2 while this step computes
+      const int64_t nb = a.token0 + (int64_t)(st + 1) * a.step_tokens;
+      const uint32_t bytes = (uint32_t)a.chunk_len * HD * 2;
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(g_kr + nb * HD), "r"(bytes));
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(g_kp + nb * HD), "r"(bytes));
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(g_v + nb * HD), "r"(bytes));
+    }
     for (int j = tid; j < CC; j += NT) {
       sm.beta[j] = j < l_tok ? g_beta[t_begin + j] : 0.f;
       sm.pos[j] = (float)(a.pos0 + t_begin + j);
@@ -347,14 +383,22 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
     for (int s = tid; s < S; s += NT) sm.util[s] = __fmul_rn(sm.util[s], GAMMA_U);  // :94
     cp_async_wait<0>();
     __syncthreads();
-    for (int r = warp; r < 128; r += 8) {
-      const float kk = row_sumsq<HD>(sm.kr, r, lane);
-      const float vv2 = row_sumsq<HD>(sm.vv, r, lane);
-      const float aa = row_sumsq<HD>(sm.ak, r, lane);
-      if (lane == 0) {
+    {
+      // row norms of the chunk keys / values and of the slot keys: two threads per row
+      const int r = tid >> 1, half = tid & 1;
+      float kk = half_row_dot<HD>(sm.kr, sm.kr, r, half);
+      float vv2 = half_row_dot<HD>(sm.vv, sm.vv, r, half);
+      float aa = half_row_dot<HD>(sm.ak, sm.ak, r, half);
+      kk += __shfl_xor_sync(0xffffffffu, kk, 1);
+      vv2 += __shfl_xor_sync(0xffffffffu, vv2, 1);
+      aa += __shfl_xor_sync(0xffffffffu, aa, 1);
+      if (half == 0) {
         sm.nk[r] = sqrtf(kk);
         sm.nv[r] = sqrtf(vv2);
         sm.na[r] = sqrtf(aa);
+        // F.normalize divides by max(|x|, 1e-12); the contractions multiply by the reciprocal
+        sm.rnk[r] = 1.0f / fmaxf(sm.nk[r], 1e-12f);
+        sm.rna[r] = 1.0f / fmaxf(sm.na[r], 1e-12f);
       }
     }
     __syncthreads();
@@ -420,14 +464,13 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
           s0 += acc[n][0] + acc[n][1];
           s1 += acc[n][2] + acc[n][3];
         }
-        s0 = quad_sum(s0);
-        s1 = quad_sum(s1);
+        const float i0 = 1.0f / quad_sum(s0), i1 = 1.0f / quad_sum(s1);
 #pragma unroll
         for (int kt = 0; kt < 8; ++kt) {
-          pa[kt][0] = pack_bf16(__fdiv_rn(acc[2 * kt][0], s0), __fdiv_rn(acc[2 * kt][1], s0));
-          pa[kt][1] = pack_bf16(__fdiv_rn(acc[2 * kt][2], s1), __fdiv_rn(acc[2 * kt][3], s1));
-          pa[kt][2] = pack_bf16(__fdiv_rn(acc[2 * kt + 1][0], s0), __fdiv_rn(acc[2 * kt + 1][1], s0));
-          pa[kt][3] = pack_bf16(__fdiv_rn(acc[2 * kt + 1][2], s1), __fdiv_rn(acc[2 * kt + 1][3], s1));
+          pa[kt][0] = pack_bf16(__fmul_rn(acc[2 * kt][0], i0), __fmul_rn(acc[2 * kt][1], i0));
+          pa[kt][1] = pack_bf16(__fmul_rn(acc[2 * kt][2], i1), __fmul_rn(acc[2 * kt][3], i1));
+          pa[kt][2] = pack_bf16(__fmul_rn(acc[2 * kt + 1][0], i0), __fmul_rn(acc[2 * kt + 1][1], i0));
+          pa[kt][3] = pack_bf16(__fmul_rn(acc[2 * kt + 1][2], i1), __fmul_rn(acc[2 * kt + 1][3], i1));
         }
       }
       {
@@ -439,8 +482,9 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
 #pragma unroll
         for (int n = 0; n < HD / 8; ++n) {
           const int col = n * 8 + 2 * t4;
-          const float v00 = bf2f(sm.vv[swz<HD>(r0 + g, col)]), v01 = bf2f(sm.vv[swz<HD>(r0 + g, col + 1)]);
-          const float v10 = bf2f(sm.vv[swz<HD>(r0 + g + 8, col)]), v11 = bf2f(sm.vv[swz<HD>(r0 + g + 8, col + 1)]);
+          const float2 va = unpack_bf16(*reinterpret_cast<const uint32_t*>(&sm.vv[swz<HD>(r0 + g, col)]));
+          const float2 vb = unpack_bf16(*reinterpret_cast<const uint32_t*>(&sm.vv[swz<HD>(r0 + g + 8, col)]));
+          const float v00 = va.x, v01 = va.y, v10 = vb.x, v11 = vb.y;
           float d;
           d = v00 - acc2[n][0]; e0 = fmaf(d, d, e0);
           d = v01 - acc2[n][1]; e0 = fmaf(d, d, e0);
@@ -458,7 +502,7 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
       {
         float acc[16][4];
         gemm_nt<HD>(acc, sm.kr, r0, sm.ak, lane);
-        const float nk0 = fmaxf(sm.nk[r0 + g], 1e-12f), nk1 = fmaxf(sm.nk[r0 + g + 8], 1e-12f);
+        const float rk0 = sm.rnk[r0 + g], rk1 = sm.rnk[r0 + g + 8];
         float b0 = neg_inf(), b1 = neg_inf();
         int i0 = 0x7fffffff, i1 = 0x7fffffff;
 #pragma unroll
@@ -466,9 +510,9 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
 #pragma unroll
           for (int q = 0; q < 2; ++q) {
             const int col = n * 8 + 2 * t4 + q;
-            const float na = fmaxf(sm.na[col], 1e-12f);
-            float c0 = __fdiv_rn(acc[n][q], __fmul_rn(nk0, na));
-            float c1 = __fdiv_rn(acc[n][2 + q], __fmul_rn(nk1, na));
+            const float ra = sm.rna[col];
+            float c0 = __fmul_rn(acc[n][q], __fmul_rn(rk0, ra));
+            float c1 = __fmul_rn(acc[n][2 + q], __fmul_rn(rk1, ra));
             if (!full && !sm.act[col]) { c0 = 0.f; c1 = 0.f; }
             if (c0 > b0) { b0 = c0; i0 = col; }
             if (c1 > b1) { b1 = c1; i1 = col; }
@@ -519,22 +563,31 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
       n_filled += m;
       __syncthreads();
     } else {
-      // ---- sim_v, score, merge mask (:107-110)
-      for (int r = warp; r < l_tok; r += 8) {
-        constexpr int EPL = HD / 32;
-        const int s = sm.best[r];
-        const bf16* pv = sm.vv + swz<HD>(r, lane * EPL);
-        const bf16* pa_ = sm.av + swz<HD>(s, lane * EPL);
+      // ---- sim_v, score, merge mask (:107-110): two threads per row
+      {
+        const int r = tid >> 1, half = tid & 1;
+        const int sb = sm.best[r];
         float dot = 0.f, aa = 0.f;
+        if (r < l_tok) {
+          constexpr int CPR = HD / 8;
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) {
-          const float x = bf2f(pv[e]), y = bf2f(pa_[e]);
-          dot = fmaf(x, y, dot);
-          aa = fmaf(y, y, aa);
+          for (int h = 0; h < CPR / 2; ++h) {
+            // logical chunk ch of row r sits at physical chunk ch ^ (row & 7) of that row
+            const int ch = half * CPR / 2 + h;
+            const uint4 a4 = *reinterpret_cast<const uint4*>(&sm.vv[swz<HD>(r, ch * 8)]);
+            const uint4 b4 = *reinterpret_cast<const uint4*>(&sm.av[swz<HD>(sb, ch * 8)]);
+            const uint32_t aw[4] = {a4.x, a4.y, a4.z, a4.w}, bw[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float2 fa = unpack_bf16(aw[u]), fb = unpack_bf16(bw[u]);
+              dot = fmaf(fa.x, fb.x, fmaf(fa.y, fb.y, dot));
+              aa = fmaf(fb.x, fb.x, fmaf(fb.y, fb.y, aa));
+            }
+          }
         }
-        dot = warp_sum(dot);
-        aa = warp_sum(aa);
-        if (lane == 0) {
+        dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+        aa += __shfl_xor_sync(0xffffffffu, aa, 1);
+        if (half == 0 && r < l_tok) {
           const float sv = __fdiv_rn(dot, __fmul_rn(fmaxf(sm.nv[r], 1e-8f), fmaxf(sqrtf(aa), 1e-8f)));
           const float bs = sm.bsk[r];
           sm.score[r] = __fmul_rn(sm.rel[r], 1.0f - fminf(fmaxf(bs, 0.f), 1.f));
@@ -592,6 +645,7 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
             sm.pm[s] = __fdiv_rn(__fadd_rn(__fmul_rn(ms, sm.pm[s]), ps), nm);
             sm.mass[s] = nm;
             sm.na[s] = sqrtf(aa);
+            sm.rna[s] = 1.0f / fmaxf(sm.na[s], 1e-12f);
           }
         }
         __syncthreads();
@@ -600,16 +654,17 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
       {
         float acc[16][4];
         gemm_nt<HD>(acc, sm.ak, r0, sm.ak, lane);
-        const float na0 = fmaxf(sm.na[r0 + g], 1e-12f), na1 = fmaxf(sm.na[r0 + g + 8], 1e-12f);
+        const float ra0 = sm.rna[r0 + g], ra1 = sm.rna[r0 + g + 8];
         float m0 = neg_inf(), m1 = neg_inf();
 #pragma unroll
         for (int n = 0; n < 16; ++n) {
 #pragma unroll
           for (int q = 0; q < 2; ++q) {
             const int col = n * 8 + 2 * t4 + q;
-            const float nb = fmaxf(sm.na[col], 1e-12f);
-            float p0 = __fdiv_rn(acc[n][q], __fmul_rn(na0, nb));
-            float p1 = __fdiv_rn(acc[n][2 + q], __fmul_rn(na1, nb));
+            // (ra_s * ra_s') is symmetric, so equal cosines of a mutual pair stay bit-identical
+            const float rb = sm.rna[col];
+            float p0 = __fmul_rn(acc[n][q], __fmul_rn(ra0, rb));
+            float p1 = __fmul_rn(acc[n][2 + q], __fmul_rn(ra1, rb));
             if (col == r0 + g) p0 = -1.0f;
             if (col == r0 + g + 8) p1 = -1.0f;
             m0 = fmaxf(m0, p0);
@@ -655,17 +710,17 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
       {
         float acc[16][4];
         gemm_nt<HD>(acc, sm.kr, r0, sm.kr, lane);
-        const float nk0 = fmaxf(sm.nk[r0 + g], 1e-12f), nk1 = fmaxf(sm.nk[r0 + g + 8], 1e-12f);
+        const float rk0 = sm.rnk[r0 + g], rk1 = sm.rnk[r0 + g + 8];
         float s0 = 0.f, s1 = 0.f;
 #pragma unroll
         for (int n = 0; n < 16; ++n) {
 #pragma unroll
           for (int q = 0; q < 2; ++q) {
             const int col = n * 8 + 2 * t4 + q;
-            const float nb = fmaxf(sm.nk[col], 1e-12f);
+            const float rb = sm.rnk[col];
             const float w = sm.wgt[col];
-            s0 = fmaf(fabsf(__fdiv_rn(acc[n][q], __fmul_rn(nk0, nb))), w, s0);
-            s1 = fmaf(fabsf(__fdiv_rn(acc[n][2 + q], __fmul_rn(nk1, nb))), w, s1);
+            s0 = fmaf(fabsf(__fmul_rn(acc[n][q], __fmul_rn(rk0, rb))), w, s0);
+            s1 = fmaf(fabsf(__fmul_rn(acc[n][2 + q], __fmul_rn(rk1, rb))), w, s1);
           }
         }
         s0 = fmaxf(quad_sum(s0), 1.0f);
@@ -693,17 +748,19 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
         for (int n = 0; n < HD / 8; ++n) err[n][0] = err[n][1] = err[n][2] = err[n][3] = 0.f;
         gemm_nn<HD>(err, sm.kr, r0, sm.x1, lane);
         gemm_nn<HD>(err, sm.kr, r0, sm.x2, lane);
-        const float nk0 = fmaxf(sm.nk[r0 + g], 1e-12f), nk1 = fmaxf(sm.nk[r0 + g + 8], 1e-12f);
+        const float rk0 = sm.rnk[r0 + g], rk1 = sm.rnk[r0 + g + 8];
 #pragma unroll
         for (int n = 0; n < HD / 8; ++n) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int row = r0 + g + (q >> 1) * 8, col = n * 8 + 2 * t4 + (q & 1);
-            const float nk = q < 2 ? nk0 : nk1;
-            const float bs = q < 2 ? bsafe0 : bsafe1;
-            const float vpred = __fdiv_rn(err[n][q], nk);
-            const float e = __fmul_rn(bf2f(sm.vv[swz<HD>(row, col)]) - vpred, bs);
-            err[n][q] = __fdiv_rn(e, nk);  // E = err / |k| so that kr^T E = k^T err
+          for (int hr = 0; hr < 2; ++hr) {
+            const int row = r0 + g + hr * 8, col = n * 8 + 2 * t4;
+            const float rk = hr ? rk1 : rk0;
+            const float bs = hr ? bsafe1 : bsafe0;
+            const float2 vv = unpack_bf16(*reinterpret_cast<const uint32_t*>(&sm.vv[swz<HD>(row, col)]));
+            const float e0 = __fmul_rn(vv.x - __fmul_rn(err[n][2 * hr], rk), bs);
+            const float e1 = __fmul_rn(vv.y - __fmul_rn(err[n][2 * hr + 1], rk), bs);
+            err[n][2 * hr] = __fmul_rn(e0, rk);  // E = err / |k| so that kr^T E = k^T err
+            err[n][2 * hr + 1] = __fmul_rn(e1, rk);
           }
         }
       }
@@ -731,34 +788,43 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
       __syncthreads();
     }
 
-    // ---- state the attention of a later chunk reads: RoPE(ak, pm), av, mass, act, M_res
+    // ---- state the attention of a later chunk reads: RoPE(ak, pm), av, mass, act, M_res. The
+    // shared-memory tiles already have the operand layout the attention's tensor cores read, so
+    // the snapshot is a handful of bulk copies: k_read (x2), av, M_hi (rebuilt in x1), M_lo (kr).
     compute_kread();
+    if (a.snap_ak_rope && m_owner) {
+#pragma unroll
+      for (int n = 0; n < HD / 8; ++n) {
+#pragma unroll
+        for (int hrow = 0; hrow < 2; ++hrow) {
+          const int d = r0 + g + hrow * 8, e = n * 8 + 2 * t4;
+          const float m0 = mr[n][2 * hrow], m1 = mr[n][2 * hrow + 1];
+          const bf16 h0 = __float2bfloat16_rn(m0), h1 = __float2bfloat16_rn(m1);
+          *reinterpret_cast<uint32_t*>(&sm.x1[swz<HD>(d, e)]) = pack_bf16(bf2f(h0), bf2f(h1));
+          *reinterpret_cast<uint32_t*>(&sm.kr[swz<HD>(d, e)]) = pack_bf16(m0 - bf2f(h0), m1 - bf2f(h1));
+        }
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
     __syncthreads();
     if (a.snap_ak_rope) {
       const int64_t sn = (int64_t)c * a.snap_cap + a.snap0 + st;
-      s2g_rows<HD>(reinterpret_cast<bf16*>(a.snap_ak_rope) + sn * S * HD, sm.x2);
-      s2g_rows<HD>(reinterpret_cast<bf16*>(a.snap_av) + sn * S * HD, sm.av);
+      constexpr uint32_t kTile = 128 * HD * 2;
+      if (tid == 0) {
+        unsigned char* gm = reinterpret_cast<unsigned char*>(a.snap_m) + sn * (int64_t)HD * HD * 4;
+        bulk_s2g(reinterpret_cast<unsigned char*>(a.snap_ak_rope) + sn * kTile, sm.x2, kTile);
+        bulk_s2g(reinterpret_cast<unsigned char*>(a.snap_av) + sn * kTile, sm.av, kTile);
+        bulk_s2g(gm, sm.x1, (uint32_t)HD * HD * 2);
+        bulk_s2g(gm + (int64_t)HD * HD * 2, sm.kr, (uint32_t)HD * HD * 2);
+        asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+      }
       for (int s = tid; s < S; s += NT) {
         a.snap_mass[sn * S + s] = sm.mass[s];
         a.snap_act[sn * S + s] = sm.act[s];
       }
-      if (m_owner) {
-        // M_res as the attention's read-out operand: bf16 hi and lo terms, each an MN-major
-        // 128-byte-swizzled image [e / 64][d][64] (see attend.cu)
-        unsigned char* img = reinterpret_cast<unsigned char*>(a.snap_m) + sn * (int64_t)HD * HD * 4;
-#pragma unroll
-        for (int n = 0; n < HD / 8; ++n) {
-#pragma unroll
-          for (int hrow = 0; hrow < 2; ++hrow) {
-            const int d = r0 + g + hrow * 8, e = n * 8 + 2 * t4;
-            const float m0 = mr[n][2 * hrow], m1 = mr[n][2 * hrow + 1];
-            const bf16 h0 = __float2bfloat16_rn(m0), h1 = __float2bfloat16_rn(m1);
-            const int64_t off = (int64_t)(e >> 6) * HD * 128 + d * 128 + ((((e & 63) >> 3) ^ (d & 7)) << 4) + (e & 7) * 2;
-            *reinterpret_cast<uint32_t*>(img + off) = pack_bf16(bf2f(h0), bf2f(h1));
-            *reinterpret_cast<uint32_t*>(img + (int64_t)HD * HD * 2 + off) = pack_bf16(m0 - bf2f(h0), m1 - bf2f(h1));
-          }
-        }
-      }
+      // the next step overwrites these tiles: wait until the copies have read them
+      if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+      __syncthreads();
     }
   }
 
@@ -779,7 +845,10 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
       *reinterpret_cast<float2*>(g_m + (r0 + g + 8) * HD + n * 8 + 2 * t4) = make_float2(mr[n][2], mr[n][3]);
     }
   }
-  if (tid == 0) a.n_filled[c] = n_filled;
+  if (tid == 0) {
+    a.n_filled[c] = n_filled;
+    asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");  // snapshot copies have landed
+  }
 }
 
 template <int HD>
