@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define BOLT3_ABI_VERSION 3
+#define BOLT3_ABI_VERSION 4
 
 enum bolt3_status {
   BOLT3_OK = 0,
@@ -126,6 +126,8 @@ typedef struct bolt3_attend_args {
   void* y; int64_t y_tokens;           /* bf16 [B][y_tokens][H][HD]; row of query token t: t */
   int32_t* status;                     /* optional device int: OR-ed with 2 if a bounded wait expired */
   const float* q_l2;                   /* optional |q_raw| per row, [B*H][Tq] */
+  int64_t blk_begin, blk_count;        /* prefill: query blocks [blk_begin, blk_begin + blk_count)
+                                          (blk_count = 0: every block) */
 } bolt3_attend_args;
 int bolt3_attend(const bolt3_attend_args* a, void* stream);
 

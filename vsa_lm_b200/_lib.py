@@ -65,6 +65,7 @@ class AttendArgs(ctypes.Structure):
         ("y", _P), ("y_tokens", _I64),
         ("status", _P),
         ("q_l2", _P),
+        ("blk_begin", _I64), ("blk_count", _I64),
     ]
 
 
@@ -121,7 +122,7 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = argt
             fn.restype = rest
-        if lib.bolt3_abi_version() != 3:
+        if lib.bolt3_abi_version() != 4:
             raise RuntimeError("libbolt3.so ABI version mismatch; rebuild with `python -m vsa_lm_b200.build`")
         _lib = lib
         return lib

@@ -175,10 +175,15 @@ class Bolt3Attn(nn.Module):
             bf = dict(dtype=torch.bfloat16, device=device)
             ws = [self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, self.beta_proj.weight,
                   self.eta_proj.weight]
-            f.w_in = torch.cat([w.detach().to(**bf) for w in ws], dim=0).contiguous()
+            # rows padded to a multiple of 8 so every projection row starts on a 16-byte boundary
+            n_in = sum(w.shape[0] for w in ws)
+            pad = (-n_in) % 8
+            f.w_in = torch.cat([w.detach().to(**bf) for w in ws] + [torch.zeros(pad, ws[0].shape[1], **bf)],
+                               dim=0).contiguous()
             parts = [b.detach().to(**bf) if b is not None else torch.zeros(w.shape[0], **bf)
                      for w, b in zip(ws[:3], (self.q_proj.bias, self.k_proj.bias, self.v_proj.bias))]
-            parts += [self.beta_proj.bias.detach().to(**bf), self.eta_proj.bias.detach().to(**bf)]
+            parts += [self.beta_proj.bias.detach().to(**bf), self.eta_proj.bias.detach().to(**bf),
+                      torch.zeros(pad, **bf)]
             f.b_in = torch.cat(parts).contiguous()
             f.w_out = self.o_proj.weight.detach().to(**bf).contiguous()
             gam = self.gamma_delta().detach()
@@ -230,12 +235,64 @@ class Bolt3Attn(nn.Module):
         ws = torch.empty(max(1, K.prefill_workspace_bytes(b * HKV, T, HD)), dtype=torch.uint8, device=dev)
         bank = K.new_bank(b * HKV, HD, dev)
         y = torch.empty(b, T, H, HD, **bf)
-        K.prefill(B=b, T=T, H=H, HKV=HKV, HD=HD, q_rope=q_rope, q_raw=q_raw, eta=eta, k_raw=k_raw,
-                  k_rope=k_rope, v=v, beta=beta, kappa=c["kappa"], gamma=c["gamma"], coef=c["coef"],
-                  inv_freq=c["inv_freq"], res_w=c["res_w"], eps=self.eps, workspace=ws, bank=bank, y=y,
-                  q_l2=q_l2)
+        self._scan_and_attend(b, T, q_rope=q_rope, q_raw=q_raw, eta=eta, k_raw=k_raw, k_rope=k_rope, v=v,
+                              beta=beta, q_l2=q_l2, ws=ws, bank=bank, y=y, consts=c)
         out = F.linear(y.view(b, T, H * HD), f.w_out)
         return out.to(x.dtype)
+
+    # scan steps per segment when the consolidation scan overlaps the attention
+    SCAN_SEGMENT = 8
+
+    def _aux_stream(self, device) -> torch.cuda.Stream:
+        cache = self.__dict__.setdefault("_streams", {})
+        key = str(device)
+        if key not in cache:
+            cache[key] = torch.cuda.Stream(device=device)
+        return cache[key]
+
+    def _scan_and_attend(self, b, T, *, q_rope, q_raw, eta, k_raw, k_rope, v, beta, q_l2, ws, bank, y, consts):
+        """Phases B and C of the forward (bolt3.py:210-273), overlapped on two streams.
+
+        The consolidation scan is sequential per chain and fills only b*HKV SMs, so it runs on a
+        side stream in segments of SCAN_SEGMENT steps while the main stream runs the attention of
+        every chunk whose snapshot (consolidation r - 2) is already written."""
+        H, HKV, HD, G = self.H, self.HKV, self.HD, self.G
+        c = consts
+        n_chunks = (T + self.C - 1) // self.C
+        n_cons = K.n_consolidations(T)
+        att = dict(n_chains=b * HKV, hkv=HKV, G=G, HD=HD, T=T, q_rope=q_rope, q_raw=q_raw, eta=eta,
+                   k_rope=k_rope, v=v, n_cons=n_cons, kappa=c["kappa"], coef=c["coef"], res_w=c["res_w"],
+                   eps=self.eps, y=y, q_l2=q_l2)
+        if n_cons == 0:
+            K.attend_prefill(snaps=None, **att)
+            return
+        snaps = K.snapshot_views(ws, b * HKV, n_cons, HD)
+        main = torch.cuda.current_stream(q_rope.device)
+        aux = self._aux_stream(q_rope.device)
+        ready = torch.cuda.Event()
+        ready.record(main)
+        aux.wait_event(ready)
+        seg = self.SCAN_SEGMENT
+        done = []
+        with torch.cuda.stream(aux):
+            for s0 in range(0, n_cons, seg):
+                n = min(seg, n_cons - s0)
+                K.consolidate(n_chains=b * HKV, hkv=HKV, HD=HD, bank=bank, init_blank=s0 == 0, kr=k_raw, kp=k_rope,
+                              v=v, beta=beta, chain_tokens=T, token0=s0 * self.C, step_tokens=self.C,
+                              skip0=N_SINKS if s0 == 0 else 0, chunk_len=self.C, pos0=0, n_steps=n,
+                              kappa=c["kappa"], gamma=c["gamma"], inv_freq=c["inv_freq"], snaps=snaps, snap0=s0)
+                ev = torch.cuda.Event()
+                ev.record(aux)
+                done.append((s0 + n, ev))
+        # chunks 0 and 1 read no bank
+        K.attend_prefill(snaps=snaps, blk_begin=0, blk_count=min(2, n_chunks), **att)
+        blk = 2
+        for end, ev in done:
+            main.wait_event(ev)
+            last = n_chunks if end == n_cons else end + 2
+            if last > blk:
+                K.attend_prefill(snaps=snaps, blk_begin=blk, blk_count=last - blk, **att)
+                blk = last
 
     # ---- one consolidation on reference-format tensors (bolt3.py:68-192), natively
     @torch.no_grad()

@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
   const int tid = threadIdx.x, warp = tid >> 5;
   const int G = a.G;
   const int g_fast = blockIdx.x;  // head group within the KV head: the G CTAs of one chain-chunk run
-  const int blk = blockIdx.y;     // together and share K/V through L2
+  const int blk = (int)a.blk_begin + blockIdx.y;  // together and share K/V through L2
   const int c = blockIdx.z;
   const int kvh = c % a.hkv, b = c / a.hkv;
   const int H = a.hkv * G;
@@ -540,7 +540,10 @@ extern "C" int bolt3_attend(const bolt3_attend_args* a, void* stream) {
   cudaStream_t s = (cudaStream_t)stream;
   dim3 grid;
   if (a->prefill) {
-    grid = dim3((unsigned)a->G, (unsigned)((a->Tq + 127) / 128), (unsigned)a->n_chains);
+    const int64_t n_blk = (a->Tq + 127) / 128;
+    const int64_t count = a->blk_count > 0 ? a->blk_count : n_blk - a->blk_begin;
+    if (a->blk_begin < 0 || count <= 0 || a->blk_begin + count > n_blk) return BOLT3_ERR_SHAPE;
+    grid = dim3((unsigned)a->G, (unsigned)count, (unsigned)a->n_chains);
   } else {
     const int gn = (int)std::max<int64_t>(1, std::min<int64_t>(a->G, 128 / a->Tq));
     grid = dim3((unsigned)((a->G + gn - 1) / gn), 1, (unsigned)a->n_chains);

@@ -5,8 +5,9 @@
 // product and the sum rounded to bf16), beta = sigmoid(beta_proj x) and eta = tanh(eta_proj x)
 // (bolt3.py:198-199) computed from the bf16 logits and rounded to bf16.
 //
-// HBM-bound elementwise work: one CTA per token, one warp per head row; a lane owns the element
-// pairs (i, i + HD/2) that rotate-half RoPE couples, so no cross-lane exchange is needed.
+// HBM-bound elementwise work with 16-byte loads and stores: a head row of HD values is handled by
+// HD/8 lanes, each owning 8 consecutive elements; the lane holding elements i and the lane holding
+// i + HD/2 (the pair rotate-half RoPE couples) swap values with one shuffle.
 #include "../../include/bolt3.h"
 #include "common.cuh"
 
@@ -15,83 +16,130 @@ namespace {
 using namespace b3;
 
 template <int HD>
-__global__ void __launch_bounds__(256) prep_kernel(bolt3_prep_args a) {
-  constexpr int E = HD / 64;  // elements per lane in each half
-  const int tok = blockIdx.x;           // b * T + t
+__global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
+  constexpr int LPR = HD / 8;          // lanes per head row
+  constexpr int RPW = 32 / LPR;        // rows per warp pass
+  constexpr int HALF = LPR / 2;        // lane offset between the RoPE partners
+  const int tok = blockIdx.x;          // b * T + t
   const int b = tok / a.T, t = tok % a.T;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane / LPR, l = lane % LPR;   // row slot within the warp, lane within the row
   const bf16* row = reinterpret_cast<const bf16*>(a.proj) + (int64_t)tok * a.ld;
   const float pos = (float)(a.pos0 + t);
+  const bool first = l < HALF;         // holds elements of the first half
 
-  // cos/sin of this lane's frequencies (shared by every head of the token)
-  float cs[E], sn[E];
+  // cos/sin of the HD/2 frequencies, once per token, shared by every head through shared memory
+  __shared__ float s_cos[HD / 2], s_sin[HD / 2];
+  for (int i = threadIdx.x; i < HD / 2; i += blockDim.x) {
+    float sv, cv;
+    sincosf(__fmul_rn(pos, a.inv_freq[i]), &sv, &cv);
+    s_cos[i] = rbf(cv);
+    s_sin[i] = rbf(sv);
+  }
+  __syncthreads();
+  float cs[8], sn[8];
 #pragma unroll
-  for (int e = 0; e < E; ++e) {
-    const float ang = __fmul_rn(pos, a.inv_freq[lane * E + e]);
-    float s, c;
-    sincosf(ang, &s, &c);
-    cs[e] = rbf(c);
-    sn[e] = rbf(s);
+  for (int e = 0; e < 8; ++e) {
+    const int fi = (l % HALF) * 8 + e;  // frequency index: element index mod HD/2
+    cs[e] = s_cos[fi];
+    sn[e] = s_sin[fi];
   }
 
   const int n_rows = a.H + 2 * a.HKV;
-  for (int r = warp; r < n_rows; r += 8) {
-    const bf16* src;
-    int kind, head;  // 0 = q, 1 = k, 2 = v
-    if (r < a.H) { kind = 0; head = r; src = row + (int64_t)head * HD; }
-    else if (r < a.H + a.HKV) { kind = 1; head = r - a.H; src = row + (int64_t)(a.H + head) * HD; }
-    else { kind = 2; head = r - a.H - a.HKV; src = row + (int64_t)(a.H + a.HKV + head) * HD; }
-    float x0[E], x1[E];
+  // issue the loads of up to kPre passes before any use, so each lane keeps several 16-byte loads
+  // in flight (this kernel is bound by HBM latency x bytes in flight)
+  constexpr int kPre = 4;
+  uint4 pre[kPre];
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-      x0[e] = bf2f(src[lane * E + e]);
-      x1[e] = bf2f(src[HD / 2 + lane * E + e]);
+  for (int p = 0; p < kPre; ++p) {
+    const int r = warp * RPW + p * 8 * RPW + sub;
+    pre[p] = make_uint4(0, 0, 0, 0);
+    if (r < n_rows) pre[p] = *reinterpret_cast<const uint4*>(row + (int64_t)r * HD + l * 8);
+  }
+  int pass = 0;
+  for (int r0 = warp * RPW; r0 < n_rows; r0 += 8 * RPW, ++pass) {
+    const int r = r0 + sub;
+    const bool live = r < n_rows;
+    int kind = 2, head = 0;  // 0 = q, 1 = k, 2 = v
+    if (live) {
+      if (r < a.H) { kind = 0; head = r; }
+      else if (r < a.H + a.HKV) { kind = 1; head = r - a.H; }
+      else { kind = 2; head = r - a.H - a.HKV; }
+    }
+    float x[8];
+    {
+      uint4 u = make_uint4(0, 0, 0, 0);
+      if (pass < kPre) {
+#pragma unroll
+        for (int p = 0; p < kPre; ++p)
+          if (p == pass) u = pre[p];
+      } else if (live) {
+        u = *reinterpret_cast<const uint4*>(row + (int64_t)r * HD + l * 8);
+      }
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = unpack_bf16(w[q]);
+        x[2 * q] = f.x;
+        x[2 * q + 1] = f.y;
+      }
     }
     const int nh = kind == 0 ? a.H : a.HKV;
     const int64_t hs = kind == 0 ? a.q_head_stride : a.k_head_stride;
     const int64_t to = kind == 0 ? a.q_t_off : a.k_t_off;
-    const int64_t off = (((int64_t)b * nh + head) * hs + to + t) * HD;
-    if (kind == 2) {
-      bf16* dst = reinterpret_cast<bf16*>(a.v) + off;
+    const int64_t off = (((int64_t)b * nh + head) * hs + to + t) * HD + l * 8;
+    // per-row reductions stay inside the LPR lanes of the row
+    auto row_sum = [&](float v) {
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        dst[lane * E + e] = __float2bfloat16_rn(x0[e]);
-        dst[HD / 2 + lane * E + e] = __float2bfloat16_rn(x1[e]);
-      }
+      for (int o = LPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      return v;
+    };
+    const float* nw = kind == 0 ? a.q_norm_w : a.k_norm_w;
+    // all lanes take part in the shuffles below, whatever their row's kind
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
+    ss = row_sum(ss);
+    if (kind != 2 && nw != nullptr) {
+      const float rr = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)HD), a.eps));
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = rbf(__fmul_rn(__fmul_rn(x[e], rr), nw[l * 8 + e]));
+    }
+    float l2 = 0.f;  // |q_raw| of the stored (bf16) row, for the M_res read-out
+#pragma unroll
+    for (int e = 0; e < 8; ++e) l2 = fmaf(x[e], x[e], l2);
+    l2 = row_sum(l2);
+    // RoPE partner values (element i <-> i + HD/2)
+    float y[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = __shfl_xor_sync(0xffffffffu, x[e], HALF);
+    if (!live) continue;
+    uint32_t raw[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) raw[q] = pack_bf16(x[2 * q], x[2 * q + 1]);
+    if (kind == 2) {
+      *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(a.v) + off) = make_uint4(raw[0], raw[1], raw[2], raw[3]);
       continue;
     }
-    const float* nw = kind == 0 ? a.q_norm_w : a.k_norm_w;
-    float l2 = 0.f;  // |q_raw| of the stored (bf16) row, for the M_res read-out
-    if (nw != nullptr) {
-      float ss = 0.f;
+    if (kind == 0 && a.q_l2 != nullptr && l == 0)
+      a.q_l2[((int64_t)b * a.H + head) * a.eta_head_stride + a.eta_t_off + t] = sqrtf(l2);
+    uint32_t rot[4];
 #pragma unroll
-      for (int e = 0; e < E; ++e) ss += x0[e] * x0[e] + x1[e] * x1[e];
-      ss = warp_sum(ss);
-      const float r_ = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)HD), a.eps));
+    for (int q = 0; q < 4; ++q) {
+      float o2[2];
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        x0[e] = rbf(__fmul_rn(__fmul_rn(x0[e], r_), nw[lane * E + e]));
-        x1[e] = rbf(__fmul_rn(__fmul_rn(x1[e], r_), nw[HD / 2 + lane * E + e]));
+      for (int u = 0; u < 2; ++u) {
+        const int e = 2 * q + u;
+        // rotate_half: the first half pairs with -x[i + HD/2], the second half with x[i - HD/2]
+        const float partner = first ? -y[e] : y[e];
+        o2[u] = rbf(__fadd_rn(rbf(__fmul_rn(x[e], cs[e])), rbf(__fmul_rn(partner, sn[e]))));
       }
+      rot[q] = pack_bf16(o2[0], o2[1]);
     }
-    if (kind == 0 && a.q_l2 != nullptr) {
-#pragma unroll
-      for (int e = 0; e < E; ++e) l2 = fmaf(rbf(x0[e]), rbf(x0[e]), fmaf(rbf(x1[e]), rbf(x1[e]), l2));
-      l2 = warp_sum(l2);
-      if (lane == 0) a.q_l2[((int64_t)b * a.H + head) * a.eta_head_stride + a.eta_t_off + t] = sqrtf(l2);
-    }
-    bf16* draw = reinterpret_cast<bf16*>(kind == 0 ? a.q_raw : a.k_raw) + off;
-    bf16* drope = reinterpret_cast<bf16*>(kind == 0 ? a.q_rope : a.k_rope) + off;
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      draw[lane * E + e] = __float2bfloat16_rn(x0[e]);
-      draw[HD / 2 + lane * E + e] = __float2bfloat16_rn(x1[e]);
-      // rotate_half: first half pairs with -x1, second half with x0
-      const float r0 = rbf(__fadd_rn(rbf(__fmul_rn(x0[e], cs[e])), rbf(__fmul_rn(-x1[e], sn[e]))));
-      const float r1 = rbf(__fadd_rn(rbf(__fmul_rn(x1[e], cs[e])), rbf(__fmul_rn(x0[e], sn[e]))));
-      drope[lane * E + e] = __float2bfloat16_rn(r0);
-      drope[HD / 2 + lane * E + e] = __float2bfloat16_rn(r1);
-    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(kind == 0 ? a.q_raw : a.k_raw) + off) =
+        make_uint4(raw[0], raw[1], raw[2], raw[3]);
+    *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(kind == 0 ? a.q_rope : a.k_rope) + off) =
+        make_uint4(rot[0], rot[1], rot[2], rot[3]);
   }
 
   // gates: HKV beta logits then H eta logits
@@ -119,6 +167,10 @@ extern "C" int bolt3_prep(const bolt3_prep_args* a, void* stream) {
   if (a->q_head_stride < a->q_t_off + a->T || a->k_head_stride < a->k_t_off + a->T ||
       a->beta_head_stride < a->beta_t_off + a->T || a->eta_head_stride < a->eta_t_off + a->T)
     return BOLT3_ERR_CAPACITY;
+  // 16-byte vector access: rows of proj, and every output row, start on 16-byte boundaries
+  const uintptr_t al = (uintptr_t)a->proj | (uintptr_t)a->q_raw | (uintptr_t)a->q_rope | (uintptr_t)a->k_raw |
+                       (uintptr_t)a->k_rope | (uintptr_t)a->v;
+  if ((al & 15) || (a->ld % 8)) return BOLT3_ERR_ALIGN;
   const int64_t n_tok = (int64_t)a->B * a->T;
   if (n_tok > 0x7fffffff) return BOLT3_ERR_SHAPE;
   cudaStream_t s = (cudaStream_t)stream;

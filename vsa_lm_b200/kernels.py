@@ -117,6 +117,42 @@ def prefill_workspace_bytes(n_chains: int, T: int, HD: int) -> int:
     return int(_lib.load().bolt3_prefill_workspace_size(n_chains, T, HD))
 
 
+def snapshot_views(ws: torch.Tensor, n_chains: int, n_cons: int, HD: int, S: int = S_SLOTS) -> dict:
+    """Views of a prefill workspace as the consolidation snapshots, at the offsets
+    bolt3_prefill_fwd uses: ak_rope / av images, mass, act, and the split M_res image."""
+    ns = n_chains * n_cons
+    off = 0
+    views = {}
+    for name, nbytes in (("ak_rope", ns * S * HD * 2), ("av", ns * S * HD * 2), ("mass", ns * S * 4),
+                         ("act", ns * S), ("m", ns * HD * HD * 4)):
+        views[name] = ws[off:off + nbytes]
+        off = (off + nbytes + 255) // 256 * 256
+    views["ak_rope"] = views["ak_rope"].view(torch.bfloat16).view(n_chains, n_cons, S, HD)
+    views["av"] = views["av"].view(torch.bfloat16).view(n_chains, n_cons, S, HD)
+    views["mass"] = views["mass"].view(torch.float32)
+    views["m"] = views["m"].view(torch.float32)
+    return views
+
+
+def attend_prefill(*, n_chains: int, hkv: int, G: int, HD: int, T: int, q_rope, q_raw, eta, k_rope, v,
+                   snaps: dict | None, n_cons: int, kappa, coef, res_w, eps: float, y: torch.Tensor,
+                   blk_begin: int = 0, blk_count: int = 0, q_l2=None, status=None) -> None:
+    """Attention of prefill query blocks [blk_begin, blk_begin + blk_count) (bolt3_attend, prefill
+    mode): chunk r reads snapshot r - 2 of the consolidation scan."""
+    lib = _lib.load()
+    sn = snaps or {}
+    a = _lib.AttendArgs(
+        n_chains=n_chains, hkv=hkv, G=G, HD=HD, q_rope=q_rope.data_ptr(), q_raw=q_raw.data_ptr(),
+        eta=eta.data_ptr(), Tq=T, prefill=1, seg0_k=k_rope.data_ptr(), seg0_v=v.data_ptr(),
+        seg0_chain_tokens=T, seg1_k=k_rope.data_ptr(), seg1_v=v.data_ptr(), seg1_chain_tokens=T,
+        bank_ak_rope=_ptr(sn.get("ak_rope")), bank_av=_ptr(sn.get("av")), bank_mass=_ptr(sn.get("mass")),
+        bank_act=_ptr(sn.get("act")), bank_m=_ptr(sn.get("m")), bank_cap=n_cons,
+        kappa=kappa.data_ptr(), coef=coef.data_ptr(), res_w=res_w.data_ptr(), eps=eps,
+        y=y.data_ptr(), y_tokens=T, status=_ptr(status), q_l2=_ptr(q_l2), blk_begin=blk_begin,
+        blk_count=blk_count)
+    _lib.check(lib.bolt3_attend(ctypes.byref(a), _stream()), "bolt3_attend")
+
+
 def prefill(*, B: int, T: int, H: int, HKV: int, HD: int, q_rope, q_raw, eta, k_raw, k_rope, v, beta,
             kappa, gamma, coef, inv_freq, res_w, eps: float, workspace: torch.Tensor, bank: dict,
             y: torch.Tensor, status: torch.Tensor | None = None, q_l2: torch.Tensor | None = None) -> None:
