@@ -152,7 +152,7 @@ def phase_times(m, x, reps: int = 3):
 
     def prep():
         K.prep(proj, B=b, T=T, H=H, HKV=HKV, HD=HD, inv_freq=c["inv_freq"], eps=m.eps, q_norm_w=c["qn"],
-               k_norm_w=c["kn"], pos0=0, q_raw=q_raw, q_rope=q_rope, eta=eta, k_raw=k_raw, k_rope=k_rope,
+               k_norm_w=c["kn"], pos0=0, cols=f.cols, q_raw=q_raw, q_rope=q_rope, eta=eta, k_raw=k_raw, k_rope=k_rope,
                v=v, beta=beta, q_head_stride=T, q_t_off=0, k_head_stride=T, k_t_off=0, q_l2=q_l2)
 
     n_cons = K.n_consolidations(T)

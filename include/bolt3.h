@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define BOLT3_ABI_VERSION 4
+#define BOLT3_ABI_VERSION 5
 
 enum bolt3_status {
   BOLT3_OK = 0,
@@ -39,8 +39,10 @@ enum bolt3_status {
 /* ---- Phase A epilogue: per-head RMSNorm (optional), RoPE, beta = sigmoid, eta = tanh.
  * Replaces Bolt3Attn.head_qkv + rope + gates (vsa_lm/config/bolt3.py:59-66, 196-199;
  * vsa_lm/surgery.py:43-53, 80-93) and the same lines of Bolt3Decoder.step (bolt3.py:346-350).
- * Input `proj` is the output of ONE fused projection GEMM, token-major [B*T][ld] with columns
- * [q (H*HD) | k (HKV*HD) | v (HKV*HD) | beta logits (HKV) | eta logits (H)].
+ * Input `proj` is a token-major projection output [B*T][ld] (ld a multiple of 8, 16-byte aligned).
+ * `parts` selects what it holds: bit 0 = q (H*HD columns at q_col) and eta logits (H at eta_col);
+ * bit 1 = k and v (HKV*HD each at k_col, v_col) and beta logits (HKV at beta_col). The q and k/v
+ * column blocks must start on multiples of 8.
  * Output element (b, head, t) of a head-major array lives at
  *   ((b * n_heads + head) * head_stride + t_off + t) * HD      (q_*: n_heads = H, k/v: HKV). */
 typedef struct bolt3_prep_args {
@@ -56,6 +58,8 @@ typedef struct bolt3_prep_args {
   void* k_raw; void* k_rope; void* v; int64_t k_head_stride; int64_t k_t_off;
   float* beta; int64_t beta_head_stride; int64_t beta_t_off;
   float* q_l2;                        /* optional: |q_raw| per (head, token), laid out like eta */
+  int parts;                          /* 1 = q/eta, 2 = k/v/beta, 3 = both */
+  int64_t q_col, k_col, v_col, beta_col, eta_col;
 } bolt3_prep_args;
 int bolt3_prep(const bolt3_prep_args* a, void* stream);
 

@@ -24,7 +24,7 @@ def test_library_exports_every_declared_symbol():
     for n in names:
         assert hasattr(lib, n), f"{n} declared in include/bolt3.h but not exported"
         assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
-    assert lib.bolt3_abi_version() == 4
+    assert lib.bolt3_abi_version() == 5
     assert lib.bolt3_status_string(0) == b"ok"
     assert b"shape" in lib.bolt3_status_string(2)
 
@@ -44,6 +44,31 @@ def test_entry_points_reject_bad_arguments_without_a_gpu():
     a = _lib.ConsolidateArgs()
     assert lib.bolt3_consolidate(ctypes.byref(a), None) == 1      # null state pointers
     assert lib.bolt3_prefill_workspace_size(4, 1024, 96) == 0      # unsupported head dim
+
+
+def test_prep_validates_parts_and_columns_without_a_gpu():
+    """Fake (never dereferenced) 16-byte-aligned addresses: every case returns before a launch."""
+    lib = _lib.load()
+    fake = 1 << 20
+
+    def args(**kw):
+        a = _lib.PrepArgs(proj=fake, ld=1024, B=1, T=4, H=4, HKV=2, HD=64, inv_freq=fake, eps=1e-6,
+                          q_raw=fake, q_rope=fake, eta=fake, k_raw=fake, k_rope=fake, v=fake, beta=fake,
+                          q_head_stride=4, k_head_stride=4, eta_head_stride=4, beta_head_stride=4, parts=2,
+                          k_col=0, v_col=128, beta_col=256)
+        for k, v in kw.items():
+            setattr(a, k, v)
+        return lib.bolt3_prep(ctypes.byref(a), None)
+
+    assert args(parts=0) == 1 and args(parts=4) == 1                  # BOLT3_ERR_ARG
+    assert args(k_raw=0) == 1                                         # k/v/beta outputs required
+    assert args(parts=1, q_col=0, eta_col=1020, q_raw=0) == 1         # q/eta outputs required
+    cap = 4                                                           # BOLT3_ERR_CAPACITY
+    assert args(v_col=1000) == cap                                    # section runs past the row
+    assert args(k_col=4) == 3                                         # BOLT3_ERR_ALIGN: section start
+    assert args(parts=1, q_col=0, eta_col=1022) == cap                # eta logits past the row
+    assert args(k_head_stride=3) == cap                               # T does not fit the buffer
+    assert args(ld=1020) == 3                                         # BOLT3_ERR_ALIGN: row stride
 
 
 def test_workspace_size_formula():

@@ -18,8 +18,10 @@ pytestmark = pytest.mark.gpu
 C = 128
 
 
-@pytest.mark.parametrize("shape", ["config0", "qwen3_4b"])
-def test_prep_matches_oracle(shape):
+@pytest.mark.parametrize("shape,split", [("config0", False), ("qwen3_4b", False), ("qwen3_4b", True)])
+def test_prep_matches_oracle(shape, split):
+    """Fused projection with one prep call (the decoder's form), or the k/v/beta and q/eta row blocks
+    as two GEMMs with one prep call each (the prefill's form)."""
     B, T = 2, 300
     cfg, x_cpu, x = inputs(shape, B, T, 0.0)
     m = bf16_module(cfg, 0)
@@ -32,9 +34,15 @@ def test_prep_matches_oracle(shape):
     k_raw, k_rope, v = (torch.empty(B * HKV, T, HD, **bf) for _ in range(3))
     beta = torch.empty(B * HKV, T, dtype=torch.float32, device="cuda")
     eta = torch.empty(B * H, T, dtype=torch.float32, device="cuda")
-    K.prep(proj, B=B, T=T, H=H, HKV=HKV, HD=HD, inv_freq=c["inv_freq"], eps=m.eps, q_norm_w=c["qn"],
-           k_norm_w=c["kn"], pos0=0, q_raw=q_raw, q_rope=q_rope, eta=eta, k_raw=k_raw, k_rope=k_rope, v=v,
-           beta=beta, q_head_stride=T, q_t_off=0, k_head_stride=T, k_t_off=0)
+    common = dict(B=B, T=T, H=H, HKV=HKV, HD=HD, inv_freq=c["inv_freq"], eps=m.eps, q_norm_w=c["qn"],
+                  k_norm_w=c["kn"], pos0=0, q_head_stride=T, q_t_off=0, k_head_stride=T, k_t_off=0)
+    if split:
+        x2 = x.reshape(B * T, -1)
+        K.prep(m.project(x2, f, "kv"), cols=f.cols_kv, parts=2, k_raw=k_raw, k_rope=k_rope, v=v, beta=beta, **common)
+        K.prep(m.project(x2, f, "q"), cols=f.cols_q, parts=1, q_raw=q_raw, q_rope=q_rope, eta=eta, **common)
+    else:
+        K.prep(proj, cols=f.cols, q_raw=q_raw, q_rope=q_rope, eta=eta, k_raw=k_raw, k_rope=k_rope, v=v, beta=beta,
+               **common)
     oc = oracle_cfg_of(m, cfg)
     qr, kr, vo, bo, eo = project(oracle_params(m), oc, x_cpu, BF16)
     pos = torch.arange(T, dtype=torch.float32)

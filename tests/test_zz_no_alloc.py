@@ -28,7 +28,8 @@ def _prepared(m, x):
              v=torch.empty(b * HKV, T, HD, **bf), beta=torch.empty(b * HKV, T, device=x.device),
              eta=torch.empty(b * H, T, device=x.device), q_l2=torch.empty(b * H, T, device=x.device))
     K.prep(m.project(x.reshape(b * T, D), f), B=b, T=T, H=H, HKV=HKV, HD=HD, inv_freq=c["inv_freq"], eps=m.eps,
-           q_norm_w=c["qn"], k_norm_w=c["kn"], pos0=0, q_head_stride=T, q_t_off=0, k_head_stride=T, k_t_off=0, **t)
+           q_norm_w=c["qn"], k_norm_w=c["kn"], pos0=0, cols=f.cols, q_head_stride=T, q_t_off=0, k_head_stride=T,
+           k_t_off=0, **t)
     t.update(kappa=c["kappa"], gamma=c["gamma"], coef=c["coef"], inv_freq=c["inv_freq"], res_w=c["res_w"],
              eps=m.eps, B=b, T=T, H=H, HKV=HKV, HD=HD)
     return t

@@ -30,6 +30,8 @@ class PrepArgs(ctypes.Structure):
         ("k_raw", _P), ("k_rope", _P), ("v", _P), ("k_head_stride", _I64), ("k_t_off", _I64),
         ("beta", _P), ("beta_head_stride", _I64), ("beta_t_off", _I64),
         ("q_l2", _P),
+        ("parts", _I),
+        ("q_col", _I64), ("k_col", _I64), ("v_col", _I64), ("beta_col", _I64), ("eta_col", _I64),
     ]
 
 
@@ -122,7 +124,7 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = argt
             fn.restype = rest
-        if lib.bolt3_abi_version() != 4:
+        if lib.bolt3_abi_version() != 5:
             raise RuntimeError("libbolt3.so ABI version mismatch; rebuild with `python -m vsa_lm_b200.build`")
         _lib = lib
         return lib

@@ -175,16 +175,34 @@ class Bolt3Attn(nn.Module):
             bf = dict(dtype=torch.bfloat16, device=device)
             ws = [self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, self.beta_proj.weight,
                   self.eta_proj.weight]
-            # rows padded to a multiple of 8 so every projection row starts on a 16-byte boundary
-            n_in = sum(w.shape[0] for w in ws)
-            pad = (-n_in) % 8
-            f.w_in = torch.cat([w.detach().to(**bf) for w in ws] + [torch.zeros(pad, ws[0].shape[1], **bf)],
-                               dim=0).contiguous()
-            parts = [b.detach().to(**bf) if b is not None else torch.zeros(w.shape[0], **bf)
-                     for w, b in zip(ws[:3], (self.q_proj.bias, self.k_proj.bias, self.v_proj.bias))]
-            parts += [self.beta_proj.bias.detach().to(**bf), self.eta_proj.bias.detach().to(**bf),
-                      torch.zeros(pad, **bf)]
-            f.b_in = torch.cat(parts).contiguous()
+            # One fused input projection with row blocks [k | v | beta | pad | q | eta | pad]: the first
+            # n_kv rows (the k/v/beta GEMM the consolidation scan waits on) and the rest (q/eta) are
+            # also usable as two separate GEMMs. Blocks start on multiples of 8 rows, so every
+            # section of a projection row is 16-byte aligned.
+            H, HKV, HD = self.H, self.HKV, self.HD
+            r8 = lambda n: (n + 7) // 8 * 8
+            n_kv = r8(2 * HKV * HD + HKV)
+            n_all = n_kv + r8(H * HD + H)
+            bias = lambda b, n: b.detach().to(**bf) if b is not None else torch.zeros(n, **bf)
+            blocks_w = [self.k_proj.weight, self.v_proj.weight, self.beta_proj.weight]
+            blocks_b = [bias(self.k_proj.bias, HKV * HD), bias(self.v_proj.bias, HKV * HD), bias(self.beta_proj.bias, HKV)]
+            D = self.q_proj.weight.shape[1]
+            w = torch.zeros(n_all, D, **bf)
+            bvec = torch.zeros(n_all, **bf)
+            r = 0
+            for wt, bt in zip(blocks_w, blocks_b):
+                w[r:r + wt.shape[0]] = wt.detach().to(**bf)
+                bvec[r:r + wt.shape[0]] = bt
+                r += wt.shape[0]
+            w[n_kv:n_kv + H * HD] = self.q_proj.weight.detach().to(**bf)
+            bvec[n_kv:n_kv + H * HD] = bias(self.q_proj.bias, H * HD)
+            w[n_kv + H * HD:n_kv + H * HD + H] = self.eta_proj.weight.detach().to(**bf)
+            bvec[n_kv + H * HD:n_kv + H * HD + H] = bias(self.eta_proj.bias, H)
+            f.w_in, f.b_in = w, bvec
+            f.n_kv = n_kv
+            f.cols = dict(k_col=0, v_col=HKV * HD, beta_col=2 * HKV * HD, q_col=n_kv, eta_col=n_kv + H * HD)
+            f.cols_kv = dict(k_col=0, v_col=HKV * HD, beta_col=2 * HKV * HD)
+            f.cols_q = dict(q_col=0, eta_col=H * HD)
             f.w_out = self.o_proj.weight.detach().to(**bf).contiguous()
             gam = self.gamma_delta().detach()
             f.consts = dict(
@@ -199,8 +217,13 @@ class Bolt3Attn(nn.Module):
         f.key = key
         return f
 
-    def project(self, x2d: torch.Tensor, f) -> torch.Tensor:
-        """Fused q/k/v/beta/eta projection GEMM (cuBLAS via torch): [n_tok, D] -> [n_tok, N] bf16."""
+    def project(self, x2d: torch.Tensor, f, part: str = "all") -> torch.Tensor:
+        """Input projection GEMM (cuBLAS via torch): [n_tok, D] -> [n_tok, N] bf16. part = "all"
+        (columns per f.cols), "kv" (f.cols_kv) or "q" (f.cols_q)."""
+        if part == "kv":
+            return F.linear(x2d, f.w_in[:f.n_kv], f.b_in[:f.n_kv])
+        if part == "q":
+            return F.linear(x2d, f.w_in[f.n_kv:], f.b_in[f.n_kv:])
         return F.linear(x2d, f.w_in, f.b_in)
 
     # ---- forward (bolt3.py:194-276)
@@ -218,7 +241,7 @@ class Bolt3Attn(nn.Module):
         dev = x.device
         f = self.fused(dev)
         c = f.consts
-        proj = self.project(x.reshape(b * T, D).to(torch.bfloat16), f)
+        x2 = x.reshape(b * T, D).to(torch.bfloat16)
         bf = dict(dtype=torch.bfloat16, device=dev)
         q_raw = torch.empty(b * H, T, HD, **bf)
         q_rope = torch.empty_like(q_raw)
@@ -228,15 +251,21 @@ class Bolt3Attn(nn.Module):
         beta = torch.empty(b * HKV, T, dtype=torch.float32, device=dev)
         eta = torch.empty(b * H, T, dtype=torch.float32, device=dev)
         q_l2 = torch.empty(b * H, T, dtype=torch.float32, device=dev)
-        K.prep(proj, B=b, T=T, H=H, HKV=HKV, HD=HD, inv_freq=c["inv_freq"], eps=self.eps,
-               q_norm_w=c["qn"], k_norm_w=c["kn"], pos0=0, q_raw=q_raw, q_rope=q_rope, eta=eta,
-               k_raw=k_raw, k_rope=k_rope, v=v, beta=beta, q_head_stride=T, q_t_off=0,
-               k_head_stride=T, k_t_off=0, q_l2=q_l2)
+        common = dict(B=b, T=T, H=H, HKV=HKV, HD=HD, inv_freq=c["inv_freq"], eps=self.eps, q_norm_w=c["qn"],
+                      k_norm_w=c["kn"], pos0=0)
+        # k/v/beta first: the consolidation scan waits only on them
+        K.prep(self.project(x2, f, "kv"), cols=f.cols_kv, parts=2, k_raw=k_raw, k_rope=k_rope, v=v, beta=beta,
+               k_head_stride=T, k_t_off=0, **common)
         ws = torch.empty(max(1, K.prefill_workspace_bytes(b * HKV, T, HD)), dtype=torch.uint8, device=dev)
         bank = K.new_bank(b * HKV, HD, dev)
         y = torch.empty(b, T, H, HD, **bf)
+
+        def prep_q():
+            K.prep(self.project(x2, f, "q"), cols=f.cols_q, parts=1, q_raw=q_raw, q_rope=q_rope, eta=eta,
+                   q_head_stride=T, q_t_off=0, q_l2=q_l2, **common)
+
         self._scan_and_attend(b, T, q_rope=q_rope, q_raw=q_raw, eta=eta, k_raw=k_raw, k_rope=k_rope, v=v,
-                              beta=beta, q_l2=q_l2, ws=ws, bank=bank, y=y, consts=c)
+                              beta=beta, q_l2=q_l2, ws=ws, bank=bank, y=y, consts=c, before_attend=prep_q)
         out = F.linear(y.view(b, T, H * HD), f.w_out)
         return out.to(x.dtype)
 
@@ -250,7 +279,8 @@ class Bolt3Attn(nn.Module):
             cache[key] = torch.cuda.Stream(device=device)
         return cache[key]
 
-    def _scan_and_attend(self, b, T, *, q_rope, q_raw, eta, k_raw, k_rope, v, beta, q_l2, ws, bank, y, consts):
+    def _scan_and_attend(self, b, T, *, q_rope, q_raw, eta, k_raw, k_rope, v, beta, q_l2, ws, bank, y, consts,
+                         before_attend=None):
         """Phases B and C of the forward (bolt3.py:210-273), overlapped on two streams.
 
         The consolidation scan is sequential per chain and fills only b*HKV SMs, so it runs on a
@@ -264,6 +294,8 @@ class Bolt3Attn(nn.Module):
                    k_rope=k_rope, v=v, n_cons=n_cons, kappa=c["kappa"], coef=c["coef"], res_w=c["res_w"],
                    eps=self.eps, y=y, q_l2=q_l2)
         if n_cons == 0:
+            if before_attend is not None:
+                before_attend()
             K.attend_prefill(snaps=None, **att)
             return
         snaps = K.snapshot_views(ws, b * HKV, n_cons, HD)
@@ -284,6 +316,8 @@ class Bolt3Attn(nn.Module):
                 ev = torch.cuda.Event()
                 ev.record(aux)
                 done.append((s0 + n, ev))
+        if before_attend is not None:   # the q projection runs while the scan starts
+            before_attend()
         # chunks 0 and 1 read no bank
         K.attend_prefill(snaps=snaps, blk_begin=0, blk_count=min(2, n_chunks), **att)
         blk = 2
@@ -443,8 +477,8 @@ class Bolt3Decoder:
         q_l2 = torch.empty(b * H, t, dtype=torch.float32, device=dev)
         k_off = st.cur_slot * C + st.cur_len
         K.prep(proj, B=b, T=t, H=H, HKV=HKV, HD=HD, inv_freq=c["inv_freq"], eps=ly.eps, q_norm_w=c["qn"],
-               k_norm_w=c["kn"], pos0=pos_start, q_raw=q_raw, q_rope=q_rope, eta=eta, k_raw=st.ring_kr,
-               k_rope=st.ring_kp, v=st.ring_v, beta=st.ring_b, q_head_stride=t, q_t_off=0,
+               k_norm_w=c["kn"], pos0=pos_start, cols=f.cols, parts=3, q_raw=q_raw, q_rope=q_rope, eta=eta,
+               k_raw=st.ring_kr, k_rope=st.ring_kp, v=st.ring_v, beta=st.ring_b, q_head_stride=t, q_t_off=0,
                k_head_stride=2 * C, k_t_off=k_off, q_l2=q_l2)
         has_prev = st.prev_slot >= 0
         p0 = st.prev_slot * C if has_prev else 0

@@ -45,7 +45,16 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
     sn[e] = s_sin[fi];
   }
 
-  const int n_rows = a.H + 2 * a.HKV;
+  // head rows this call handles: [0, H) q when parts & 1, then HKV k and HKV v rows when parts & 2
+  const bool do_q = a.parts & 1, do_kv = (a.parts & 2) != 0;
+  const int n_rows = (do_q ? a.H : 0) + (do_kv ? 2 * a.HKV : 0);
+  auto row_col = [&](int r, int& kind, int& head) -> int64_t {
+    if (do_q && r < a.H) { kind = 0; head = r; return a.q_col + (int64_t)head * HD; }
+    const int rk = r - (do_q ? a.H : 0);
+    if (rk < a.HKV) { kind = 1; head = rk; return a.k_col + (int64_t)head * HD; }
+    kind = 2; head = rk - a.HKV;
+    return a.v_col + (int64_t)head * HD;
+  };
   // issue the loads of up to kPre passes before any use, so each lane keeps several 16-byte loads
   // in flight (this kernel is bound by HBM latency x bytes in flight)
   constexpr int kPre = 4;
@@ -54,18 +63,16 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
   for (int p = 0; p < kPre; ++p) {
     const int r = warp * RPW + p * 8 * RPW + sub;
     pre[p] = make_uint4(0, 0, 0, 0);
-    if (r < n_rows) pre[p] = *reinterpret_cast<const uint4*>(row + (int64_t)r * HD + l * 8);
+    int kd, hd_;
+    if (r < n_rows) pre[p] = *reinterpret_cast<const uint4*>(row + row_col(r, kd, hd_) + l * 8);
   }
   int pass = 0;
   for (int r0 = warp * RPW; r0 < n_rows; r0 += 8 * RPW, ++pass) {
     const int r = r0 + sub;
     const bool live = r < n_rows;
     int kind = 2, head = 0;  // 0 = q, 1 = k, 2 = v
-    if (live) {
-      if (r < a.H) { kind = 0; head = r; }
-      else if (r < a.H + a.HKV) { kind = 1; head = r - a.H; }
-      else { kind = 2; head = r - a.H - a.HKV; }
-    }
+    int64_t col = 0;
+    if (live) col = row_col(r, kind, head);
     float x[8];
     {
       uint4 u = make_uint4(0, 0, 0, 0);
@@ -74,7 +81,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
         for (int p = 0; p < kPre; ++p)
           if (p == pass) u = pre[p];
       } else if (live) {
-        u = *reinterpret_cast<const uint4*>(row + (int64_t)r * HD + l * 8);
+        u = *reinterpret_cast<const uint4*>(row + col + l * 8);
       }
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -142,15 +149,15 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
         make_uint4(rot[0], rot[1], rot[2], rot[3]);
   }
 
-  // gates: HKV beta logits then H eta logits
-  const bf16* gl = row + (int64_t)(a.H + 2 * a.HKV) * HD;
-  for (int i = threadIdx.x; i < a.HKV + a.H; i += blockDim.x) {
-    const float z = bf2f(gl[i]);
-    if (i < a.HKV) {
-      const float s = rbf(1.0f / (1.0f + expf(-z)));
-      a.beta[((int64_t)b * a.HKV + i) * a.beta_head_stride + a.beta_t_off + t] = s;
+  // gates: HKV beta logits and H eta logits
+  const int n_gates = (do_kv ? a.HKV : 0) + (do_q ? a.H : 0);
+  for (int i = threadIdx.x; i < n_gates; i += blockDim.x) {
+    if (do_kv && i < a.HKV) {
+      const float z = bf2f(row[a.beta_col + i]);
+      a.beta[((int64_t)b * a.HKV + i) * a.beta_head_stride + a.beta_t_off + t] = rbf(1.0f / (1.0f + expf(-z)));
     } else {
-      const int h = i - a.HKV;
+      const int h = i - (do_kv ? a.HKV : 0);
+      const float z = bf2f(row[a.eta_col + h]);
       a.eta[((int64_t)b * a.H + h) * a.eta_head_stride + a.eta_t_off + t] = rbf(tanhf(z));
     }
   }
@@ -159,18 +166,28 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
 }  // namespace
 
 extern "C" int bolt3_prep(const bolt3_prep_args* a, void* stream) {
-  if (!a || !a->proj || !a->inv_freq || !a->q_raw || !a->q_rope || !a->k_raw || !a->k_rope || !a->v ||
-      !a->beta || !a->eta)
-    return BOLT3_ERR_ARG;
+  if (!a || !a->proj || !a->inv_freq) return BOLT3_ERR_ARG;
+  if (a->parts < 1 || a->parts > 3) return BOLT3_ERR_ARG;
+  if ((a->parts & 1) && (!a->q_raw || !a->q_rope || !a->eta)) return BOLT3_ERR_ARG;
+  if ((a->parts & 2) && (!a->k_raw || !a->k_rope || !a->v || !a->beta)) return BOLT3_ERR_ARG;
   if (a->B <= 0 || a->T <= 0 || a->H <= 0 || a->HKV <= 0 || a->H % a->HKV) return BOLT3_ERR_SHAPE;
-  if (a->ld < (int64_t)(a->H + 2 * a->HKV) * a->HD + a->HKV + a->H) return BOLT3_ERR_CAPACITY;
-  if (a->q_head_stride < a->q_t_off + a->T || a->k_head_stride < a->k_t_off + a->T ||
-      a->beta_head_stride < a->beta_t_off + a->T || a->eta_head_stride < a->eta_t_off + a->T)
+  if ((a->parts & 1) && (a->q_col < 0 || a->q_col + (int64_t)a->H * a->HD > a->ld || a->eta_col < 0 ||
+                         a->eta_col + a->H > a->ld))
+    return BOLT3_ERR_CAPACITY;
+  if ((a->parts & 2) && (a->k_col < 0 || a->k_col + (int64_t)a->HKV * a->HD > a->ld || a->v_col < 0 ||
+                         a->v_col + (int64_t)a->HKV * a->HD > a->ld || a->beta_col < 0 ||
+                         a->beta_col + a->HKV > a->ld))
+    return BOLT3_ERR_CAPACITY;
+  if ((a->parts & 1) && (a->q_head_stride < a->q_t_off + a->T || a->eta_head_stride < a->eta_t_off + a->T))
+    return BOLT3_ERR_CAPACITY;
+  if ((a->parts & 2) && (a->k_head_stride < a->k_t_off + a->T || a->beta_head_stride < a->beta_t_off + a->T))
     return BOLT3_ERR_CAPACITY;
   // 16-byte vector access: rows of proj, and every output row, start on 16-byte boundaries
-  const uintptr_t al = (uintptr_t)a->proj | (uintptr_t)a->q_raw | (uintptr_t)a->q_rope | (uintptr_t)a->k_raw |
-                       (uintptr_t)a->k_rope | (uintptr_t)a->v;
-  if ((al & 15) || (a->ld % 8)) return BOLT3_ERR_ALIGN;
+  const uintptr_t al = (uintptr_t)a->proj |
+                       ((a->parts & 1) ? ((uintptr_t)a->q_raw | (uintptr_t)a->q_rope) : 0) |
+                       ((a->parts & 2) ? ((uintptr_t)a->k_raw | (uintptr_t)a->k_rope | (uintptr_t)a->v) : 0);
+  const bool cols_ok = !((a->parts & 1) && a->q_col % 8) && !((a->parts & 2) && (a->k_col % 8 || a->v_col % 8));
+  if ((al & 15) || (a->ld % 8) || !cols_ok) return BOLT3_ERR_ALIGN;
   const int64_t n_tok = (int64_t)a->B * a->T;
   if (n_tok > 0x7fffffff) return BOLT3_ERR_SHAPE;
   cudaStream_t s = (cudaStream_t)stream;

@@ -40,26 +40,33 @@ def n_consolidations(T: int, C: int = CHUNK) -> int:
 
 def prep(proj: torch.Tensor, *, B: int, T: int, H: int, HKV: int, HD: int, inv_freq: torch.Tensor,
          eps: float, q_norm_w: torch.Tensor | None, k_norm_w: torch.Tensor | None, pos0: int,
-         q_raw: torch.Tensor, q_rope: torch.Tensor, eta: torch.Tensor, k_raw: torch.Tensor,
-         k_rope: torch.Tensor, v: torch.Tensor, beta: torch.Tensor,
-         q_head_stride: int, q_t_off: int, k_head_stride: int, k_t_off: int,
+         cols: dict, parts: int = 3, q_raw=None, q_rope=None, eta=None, k_raw=None, k_rope=None, v=None,
+         beta=None, q_head_stride: int = 0, q_t_off: int = 0, k_head_stride: int = 0, k_t_off: int = 0,
          q_l2: torch.Tensor | None = None) -> None:
-    """RMSNorm/RoPE/gates from the fused projection output into head-major buffers (bolt3_prep);
-    `q_l2` (optional, laid out like eta) receives |q_raw| per row."""
+    """RMSNorm/RoPE/gates from a projection output into head-major buffers (bolt3_prep). `cols` gives
+    the column offsets q_col, k_col, v_col, beta_col, eta_col of the sections in `proj`; `parts`
+    selects q/eta (1), k/v/beta (2) or both (3). `q_l2` (optional, laid out like eta) receives
+    |q_raw| per row."""
     lib = _lib.load()
     _need(proj, torch.bfloat16, "proj")
-    for name, t in (("q_raw", q_raw), ("q_rope", q_rope), ("k_raw", k_raw), ("k_rope", k_rope), ("v", v)):
-        _need(t, torch.bfloat16, name)
-    for name, t in (("eta", eta), ("beta", beta), ("inv_freq", inv_freq)):
-        _need(t, torch.float32, name)
+    outs = []
+    if parts & 1:
+        outs += [("q_raw", q_raw, torch.bfloat16), ("q_rope", q_rope, torch.bfloat16), ("eta", eta, torch.float32)]
+    if parts & 2:
+        outs += [("k_raw", k_raw, torch.bfloat16), ("k_rope", k_rope, torch.bfloat16), ("v", v, torch.bfloat16),
+                 ("beta", beta, torch.float32)]
+    for name, t, dt in outs:
+        _need(t, dt, name)
+    _need(inv_freq, torch.float32, "inv_freq")
     a = _lib.PrepArgs(
         proj=proj.data_ptr(), ld=proj.stride(0), B=B, T=T, H=H, HKV=HKV, HD=HD,
         q_norm_w=_ptr(q_norm_w), k_norm_w=_ptr(k_norm_w), eps=eps, inv_freq=inv_freq.data_ptr(),
-        pos0=pos0, q_raw=q_raw.data_ptr(), q_rope=q_rope.data_ptr(), q_head_stride=q_head_stride,
-        q_t_off=q_t_off, eta=eta.data_ptr(), eta_head_stride=q_head_stride, eta_t_off=q_t_off,
-        k_raw=k_raw.data_ptr(), k_rope=k_rope.data_ptr(), v=v.data_ptr(), k_head_stride=k_head_stride,
-        k_t_off=k_t_off, beta=beta.data_ptr(), beta_head_stride=k_head_stride, beta_t_off=k_t_off,
-        q_l2=_ptr(q_l2))
+        pos0=pos0, q_raw=_ptr(q_raw), q_rope=_ptr(q_rope), q_head_stride=q_head_stride,
+        q_t_off=q_t_off, eta=_ptr(eta), eta_head_stride=q_head_stride, eta_t_off=q_t_off,
+        k_raw=_ptr(k_raw), k_rope=_ptr(k_rope), v=_ptr(v), k_head_stride=k_head_stride,
+        k_t_off=k_t_off, beta=_ptr(beta), beta_head_stride=k_head_stride, beta_t_off=k_t_off,
+        q_l2=_ptr(q_l2), parts=parts, q_col=cols.get("q_col", 0), k_col=cols.get("k_col", 0),
+        v_col=cols.get("v_col", 0), beta_col=cols.get("beta_col", 0), eta_col=cols.get("eta_col", 0))
     _lib.check(lib.bolt3_prep(ctypes.byref(a), _stream()), "bolt3_prep")
 
 
