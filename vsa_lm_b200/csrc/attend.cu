@@ -8,21 +8,31 @@
 //   columns [0,192) and is the A operand of the P@V MMAs; the M_res read-out accumulates into
 //   columns [192, 192+HD) once the softmax has consumed them.
 // Keys: [4 sinks] [S attractors: RoPE'd at their mean position, + kappa*log(mass), -inf if inactive]
-// [previous chunk] [current chunk, causal] (vsa_lm/config/bolt3.py:219-249). The 4 sink scores are
-// computed on the CUDA cores; everything else is tcgen05.mma with bf16 operands in 128-byte swizzled
-// shared memory and fp32 accumulation. Probabilities are normalised before their bf16 cast exactly
+// [previous chunk] [current chunk, causal] (vsa_lm/config/bolt3.py:219-249). Every product is a
+// tcgen05.mma with bf16 operands in 128-byte swizzled shared memory and fp32 accumulation; the 4
+// sinks are a 16-row key tile (rows 4..15 zero and masked) whose scores land in TMEM columns
+// [384, 400) before O is written there, and whose probabilities (columns [320, 328)) add one K step
+// to the P@V product. Probabilities are normalised before their bf16 cast exactly
 // as the reference does (F.softmax(...).to(dtype), bolt3.py:249). The epilogue reads M_res out
 // (bolt3.py:251-256): y = bf16( bf16(P@V) + bf16( eta * RMSNorm_w( q_raw @ (M_hi + M_lo) / |q_raw|
 // * (1-gamma)/sqrt(HD) ) ) ), with M split into two bf16 terms.
 //
 // Both warpgroups handle every query row (TMEM lane = row), each on half of the columns, and swap
-// row max / sum / RMS partials through shared memory. Warpgroup 1 also stages the M_res operand,
-// the sink scores, and V / q_raw behind the consumed K tiles. Thread 0 issues the MMAs.
+// row max / sum / RMS partials through shared memory. Thread 0 issues the MMAs. Prefill tiles arrive
+// by TMA, issued by thread 0: Q and K tiles (3-D tensor maps, 128-byte swizzle, rows past the end of
+// a sequence zero-filled), the scan's snapshot images as plain bulk copies, and V / q_raw into the
+// K / Q tiles once the score MMAs have consumed them. Decode tiles (ring buffers) are gathered with
+// cp.async by every thread, and warpgroup 1 converts the fp32 M_res into the split operand.
 #include "../../include/bolt3.h"
 #include "common.cuh"
 #include "tc5.cuh"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
+#include <cstring>
+#include <mutex>
 #include <type_traits>
 
 namespace {
@@ -33,33 +43,24 @@ constexpr int S = 128;
 constexpr int CC = 128;
 constexpr int NT = 256;
 constexpr uint32_t kWaitIters = 1u << 24;
-constexpr uint32_t kColO = 384, kColR = 192;
+constexpr uint32_t kColO = 384, kColR = 192, kColPSink = 320;
 
 template <int HD>
 struct __align__(1024) Smem {
   unsigned char q[HD / 64][16384];        // q_rope tile, then the q_raw tile (K-major SW128)
   unsigned char kv[3][HD / 64][16384];    // K tiles of attractors / prev / cur, then their V tiles
   unsigned char m[2][HD / 64][HD * 128];  // M_res hi / lo (MN-major B): rows = input dim d, N blocks of e
-  bf16 sink_k[4][HD];
-  bf16 sink_v[4][HD];
-  float sink_vf[4][HD];     // sink values in fp32 for the epilogue
-  float sink_s[128][4];     // scaled sink scores per query row
+  unsigned char sink_k[HD / 64][2048];  // the 4 sink keys as a 16-row K-major tile, rows 4..15 zero
+  unsigned char sink_v[HD / 64][2048];  // the 4 sink values as the 16-key B tile of P@V
   float res_w[HD];
   float red_max[2][128];    // per-row partial results exchanged between the two warpgroups
   float red_sum[2][128];
   float bias[S];
   uint64_t bar_s, bar_o;
+  uint64_t bar_k, bar_v, bar_m;   // TMA completion: Q + K tiles, V + q_raw tiles, M_res image
   uint32_t tbase;
   int err;
 };
-
-// Contiguous 16-byte-chunk copy of a tile that is already a SW128 operand image (the snapshots
-// written by the consolidation scan).
-template <int HD>
-B3_DEV void copy_image(unsigned char (*dst)[16384], const bf16* src, int t, int nthreads) {
-  const unsigned char* s = reinterpret_cast<const unsigned char*>(src);
-  for (int i = t; i < 128 * HD * 2 / 16; i += nthreads) cp_async16(&dst[0][0] + i * 16, s + i * 16, true);
-}
 
 // 16-byte-chunk cp.async of 128 rows of an [*][HD] bf16 array into a SW128 tile; rows at or beyond
 // `valid` are zero-filled. Threads t, t + nthreads, ... take part.
@@ -74,8 +75,15 @@ B3_DEV void load_tile(unsigned char (*dst)[16384], const bf16* src, int valid, i
   }
 }
 
+// Tensor maps of the prefill operands: 3-D {HD, tokens, heads or chains}, box {64, 128, 1}, bf16,
+// 128-byte swizzle.
+struct __align__(64) AttendMaps {
+  CUtensorMap q_rope, q_raw, k0, v0, k1, v1;
+};
+
 template <int HD>
-__global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_args a) {
+__global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_args a,
+                                                          const __grid_constant__ AttendMaps tm) {
   extern __shared__ unsigned char smem_raw[];
   Smem<HD>& sm = *reinterpret_cast<Smem<HD>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -142,22 +150,54 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
   };
 
   // ---- stage 1: Q (q_rope), K tiles, sinks, attractor bias
+  const bool use_tma = a.prefill != 0;
+  constexpr uint32_t kTileBytes = 128 * HD * 2;
+  if (tid == 0) {
+    tc5::mbar_init(&sm.bar_s, 1);
+    tc5::mbar_init(&sm.bar_o, 1);
+    tc5::mbar_init(&sm.bar_k, 1);
+    tc5::mbar_init(&sm.bar_v, 1);
+    tc5::mbar_init(&sm.bar_m, 1);
+    tc5::mbar_fence_init();
+    sm.err = 0;
+    if (use_tma) {
+      const int zq = c * G + g0;
+      tc5::mbar_expect_tx(&sm.bar_k, kTileBytes * (1 + seg_on[0] + seg_on[1] + seg_on[2]));
+      for (int h2 = 0; h2 < HD / 64; ++h2) tc5::tma_load_3d(sm.q[h2], &tm.q_rope, h2 * 64, blk * 128, zq, &sm.bar_k);
+      if (seg_on[0]) tc5::bulk_load(sm.kv[0][0], seg_k[0], kTileBytes, &sm.bar_k);
+      if (seg_on[1])
+        for (int h2 = 0; h2 < HD / 64; ++h2) tc5::tma_load_3d(sm.kv[1][h2], &tm.k0, h2 * 64, (blk - 1) * 128, c, &sm.bar_k);
+      for (int h2 = 0; h2 < HD / 64; ++h2) tc5::tma_load_3d(sm.kv[2][h2], &tm.k1, h2 * 64, blk * 128, c, &sm.bar_k);
+      if (has_bank) {
+        tc5::mbar_expect_tx(&sm.bar_m, HD * HD * 4);
+        tc5::bulk_load(sm.m[0][0], reinterpret_cast<const unsigned char*>(a.bank_m) + bofs * (int64_t)HD * HD * 4,
+                       HD * HD * 4, &sm.bar_m);
+      }
+    }
+  }
   {
     constexpr int CPR = HD / 8;
-    for (int i = tid; i < 128 * CPR; i += NT) {
-      const int r = i / CPR, ch = i % CPR;
-      unsigned char* d = sm.q[ch >> 3] + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
-      cp_async16(d, q_row_ptr(a.q_rope, r) + ch * 8, r < n_rows);
-    }
-    for (int s = 0; s < 3; ++s) {
-      if (!seg_on[s]) continue;
-      if (s == 0 && a.prefill) copy_image<HD>(sm.kv[0], seg_k[0], tid, NT);
-      else load_tile<HD>(sm.kv[s], seg_k[s], seg_len[s], tid, NT);
+    if (!use_tma) {
+      for (int i = tid; i < 128 * CPR; i += NT) {
+        const int r = i / CPR, ch = i % CPR;
+        unsigned char* d = sm.q[ch >> 3] + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
+        cp_async16(d, q_row_ptr(a.q_rope, r) + ch * 8, r < n_rows);
+      }
+      for (int s = 0; s < 3; ++s)
+        if (seg_on[s]) load_tile<HD>(sm.kv[s], seg_k[s], seg_len[s], tid, NT);
     }
     if (has_sinks) {
-      for (int i = tid; i < 4 * HD / 8; i += NT) {
-        cp_async16(&sm.sink_k[0][0] + i * 8, sk + i * 8, true);
-        cp_async16(&sm.sink_v[0][0] + i * 8, sv + i * 8, true);
+      constexpr int CPR = HD / 8;
+      for (int i = tid; i < 16 * CPR; i += NT) {
+        const int rr = i / CPR, ch = i % CPR;
+        const uint32_t off = (ch >> 3) * 2048 + rr * 128 + (((ch & 7) ^ (rr & 7)) << 4);
+        if (rr < 4) {
+          cp_async16(&sm.sink_k[0][0] + off, sk + rr * HD + ch * 8, true);
+          cp_async16(&sm.sink_v[0][0] + off, sv + rr * HD + ch * 8, true);
+        } else {
+          *reinterpret_cast<uint4*>(&sm.sink_k[0][0] + off) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(&sm.sink_v[0][0] + off) = make_uint4(0, 0, 0, 0);
+        }
       }
     }
     cp_async_commit();
@@ -174,12 +214,6 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
     tc5::tmem_alloc(&sm.tbase, 512);
     tc5::tmem_relinquish();
   }
-  if (tid == 0) {
-    tc5::mbar_init(&sm.bar_s, 1);
-    tc5::mbar_init(&sm.bar_o, 1);
-    tc5::mbar_fence_init();
-    sm.err = 0;
-  }
   cp_async_wait<0>();
   asm volatile("fence.proxy.async.shared::cta;\n" ::);
   tc5::fence_before_sync();
@@ -189,14 +223,28 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
 
   // ---- stage 2: S = Q K^T for every present segment
   constexpr uint32_t kIdS = tc5::idesc_bf16(128, 128, false, false);
+  // thread 0 tracks which TMA groups it has seen complete, so that it never leaves with copies in flight
+  bool seen_k = !use_tma, seen_v = true, seen_m = !(use_tma && has_bank);
+  if (tid == 0 && !seen_k) {
+    seen_k = tc5::mbar_wait(&sm.bar_k, 0, kWaitIters);
+    if (!seen_k) sm.err = 1;
+  }
   if (tid == 0) {
     const uint32_t qa = tc5::smem_u32(sm.q[0]);
     for (int s = 0; s < 3; ++s) {
-      if (!seg_on[s]) continue;
+      if (!seg_on[s] || !seen_k) continue;
       const uint32_t ka = tc5::smem_u32(sm.kv[s][0]);
       for (int ks = 0; ks < HD / 16; ++ks) {
         const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
         tc5::mma_ss(tb + s * 128, tc5::sdesc(qa + off, 16, 1024), tc5::sdesc(ka + off, 16, 1024), kIdS, ks > 0);
+      }
+    }
+    if (has_sinks && seen_k) {
+      constexpr uint32_t kIdSink = tc5::idesc_bf16(128, 16, false, false);
+      const uint32_t sa = tc5::smem_u32(sm.sink_k[0]);
+      for (int ks = 0; ks < HD / 16; ++ks) {
+        const uint32_t qo = (ks >> 2) * 16384 + (ks & 3) * 32, so = (ks >> 2) * 2048 + (ks & 3) * 32;
+        tc5::mma_ss(tb + kColO, tc5::sdesc(qa + qo, 16, 1024), tc5::sdesc(sa + so, 16, 1024), kIdSink, ks > 0);
       }
     }
     tc5::commit(&sm.bar_s);
@@ -214,13 +262,8 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
   const int lim1 = len_before + ir;  // current-chunk key j is visible iff j <= lim1
 
   if (wg == 1) {
-    // ---- warpgroup 1 prologue: the M_res operand and the sink scores
-    if (has_bank && a.prefill) {
-      // the consolidation scan wrote the split, swizzled operand image: copy it as is
-      const unsigned char* img = reinterpret_cast<const unsigned char*>(a.bank_m) + bofs * (int64_t)HD * HD * 4;
-      for (int i = r; i < HD * HD / 4; i += 128) cp_async16(&sm.m[0][0][0] + i * 16, img + i * 16, true);
-      cp_async_commit();
-    } else if (has_bank) {
+    // ---- warpgroup 1 prologue (decode): the M_res operand
+    if (has_bank && !use_tma) {
       // M_res [d][e] fp32 row-major: split into bf16 hi/lo in the MN-major operand layout (rows d,
       // 64-column blocks of e); coalesced float4 loads, eight in flight per thread
       const float4* gm = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.bank_m) + bofs * HD * HD);
@@ -248,46 +291,24 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
         }
       }
     }
-    if (has_sinks) {
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int ch = 0; ch < HD / 8; ++ch) {
-        const uint4 qv = *reinterpret_cast<const uint4*>(sm.q[ch >> 3] + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
-        const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float2 qf = unpack_bf16(qw[u]);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 kf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sm.sink_k[j][ch * 8 + 2 * u]));
-            acc[j] = fmaf(qf.x, kf.x, acc[j]);
-            acc[j] = fmaf(qf.y, kf.y, acc[j]);
-          }
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) sm.sink_s[r][j] = __fmul_rn(acc[j], scale);
-      for (int i = r; i < 4 * HD; i += 128) sm.sink_vf[i / HD][i % HD] = bf2f(sm.sink_v[i / HD][i % HD]);
-    }
-    asm volatile("bar.sync 2, 128;\n" ::);   // warpgroup 1 is done reading Q
-    asm volatile("bar.arrive 1, 256;\n" ::); // sink scores are ready
-  } else {
-    asm volatile("bar.sync 1, 256;\n" ::);
-  }
-  float s_sink[4] = {neg_inf(), neg_inf(), neg_inf(), neg_inf()};
-  if (has_sinks) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) s_sink[j] = sm.sink_s[r][j];
   }
   const bool ok = tc5::mbar_wait(&sm.bar_s, 0, kWaitIters);
   if (!ok) sm.err = 1;
   tc5::fence_after_sync();
-  if (wg == 1 && ok) {
-    // K tiles are consumed: stream V (and q_raw for the read-out) in behind them
-    for (int s2 = 0; s2 < 3; ++s2) {
-      if (!seg_on[s2]) continue;
-      if (s2 == 0 && a.prefill) copy_image<HD>(sm.kv[0], seg_v[0], r, 128);
-      else load_tile<HD>(sm.kv[s2], seg_v[s2], seg_len[s2], r, 128);
-    }
+  // K tiles are consumed: stream V (and q_raw for the read-out) in behind them
+  if (use_tma && tid == 0 && ok && seen_k) {
+    seen_v = false;
+    tc5::mbar_expect_tx(&sm.bar_v, kTileBytes * (seg_on[0] + seg_on[1] + seg_on[2] + has_bank));
+    if (seg_on[0]) tc5::bulk_load(sm.kv[0][0], seg_v[0], kTileBytes, &sm.bar_v);
+    if (seg_on[1])
+      for (int h2 = 0; h2 < HD / 64; ++h2) tc5::tma_load_3d(sm.kv[1][h2], &tm.v0, h2 * 64, (blk - 1) * 128, c, &sm.bar_v);
+    for (int h2 = 0; h2 < HD / 64; ++h2) tc5::tma_load_3d(sm.kv[2][h2], &tm.v1, h2 * 64, blk * 128, c, &sm.bar_v);
+    if (has_bank)
+      for (int h2 = 0; h2 < HD / 64; ++h2) tc5::tma_load_3d(sm.q[h2], &tm.q_raw, h2 * 64, blk * 128, c * G + g0, &sm.bar_v);
+  }
+  if (!use_tma && wg == 1 && ok) {
+    for (int s2 = 0; s2 < 3; ++s2)
+      if (seg_on[s2]) load_tile<HD>(sm.kv[s2], seg_v[s2], seg_len[s2], r, 128);
     if (has_bank) {
       constexpr int CPR = HD / 8;
       for (int i = r; i < 128 * CPR; i += 128) {
@@ -323,36 +344,46 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
     if (seg_on[1]) row_pass(std::integral_constant<int, 1>{}, [&](int c0, float (&x)[32]) { body(1, c0, x); });
     if (seg_on[2]) row_pass(std::integral_constant<int, 2>{}, [&](int c0, float (&x)[32]) { body(2, c0, x); });
   };
-  // pass 1: row max (the sinks are counted by warpgroup 0)
-  float mx = wg == 0 ? fmaxf(fmaxf(s_sink[0], s_sink[1]), fmaxf(s_sink[2], s_sink[3])) : neg_inf();
-  if (ok) {
-    for_each_seg([&](int, int, float (&x)[32]) {
+  // statistics pass: row max and sum of exp(x - max) in one sweep, the sum rescaled whenever a
+  // 32-column block raises the max; exp via exp2 of (x - max) * log2(e), within ~1e-6 relative.
+  // Warpgroup 0 also counts the sinks (scores in TMEM columns [384, 388)).
+  float mx = neg_inf(), sum = 0.f;
+  auto stats = [&](const float (&x)[32]) {
+    float cm = x[0];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) mx = fmaxf(mx, x[j]);
-    });
-  }
-  sm.red_max[wg][r] = mx;
-  asm volatile("bar.sync 3, 256;\n" ::);
-  mx = fmaxf(sm.red_max[0][r], sm.red_max[1][r]);
-  // pass 2: row sum of exp(x - max); exp via exp2 of (x - max) * log2(e), within ~1e-6 relative
-  float e_sink[4];
-  float sum = 0.f;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    e_sink[j] = s_sink[j] == neg_inf() ? 0.f : expf(s_sink[j] - mx);
-    if (wg == 0) sum += e_sink[j];
-  }
-  if (ok) {
+    for (int j = 1; j < 32; ++j) cm = fmaxf(cm, x[j]);
+    if (cm == neg_inf()) return;
+    if (cm > mx) {
+      sum = __fmul_rn(sum, exp2f(__fmul_rn(mx - cm, kLog2e)));
+      mx = cm;
+    }
     float part[4] = {0.f, 0.f, 0.f, 0.f};
-    for_each_seg([&](int, int, float (&x)[32]) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) part[j & 3] += exp2f(__fmul_rn(x[j] - mx, kLog2e));
-    });
+    for (int j = 0; j < 32; ++j) part[j & 3] += exp2f(__fmul_rn(x[j] - mx, kLog2e));
     sum += (part[0] + part[1]) + (part[2] + part[3]);
+  };
+  float s_sink[4] = {neg_inf(), neg_inf(), neg_inf(), neg_inf()};
+  if (ok && has_sinks && wg == 0) {
+    uint32_t v[32];
+    tc5::ld32(tb + lane_off + kColO, v);
+    tc5::ld_wait();
+    float x[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = neg_inf();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x[j] = s_sink[j] = __fmul_rn(__uint_as_float(v[j]), scale);
+    stats(x);
   }
+  if (ok) for_each_seg([&](int, int, float (&x)[32]) { stats(x); });
+  sm.red_max[wg][r] = mx;
   sm.red_sum[wg][r] = sum;
   asm volatile("bar.sync 3, 256;\n" ::);
-  sum = sm.red_sum[0][r] + sm.red_sum[1][r];
+  {
+    const float m0 = sm.red_max[0][r], m1 = sm.red_max[1][r];
+    mx = fmaxf(m0, m1);
+    sum = __fmul_rn(sm.red_sum[0][r], exp2f(__fmul_rn(m0 - mx, kLog2e))) +
+          __fmul_rn(sm.red_sum[1][r], exp2f(__fmul_rn(m1 - mx, kLog2e)));
+  }
   // pass 3: p = bf16(exp(x - max) * (1 / sum)), two per column, into TMEM columns [0, 192); the
   // bf16 cast matches the reference's except within ~1e-6 of a rounding boundary. P of segment s
   // lands on score columns of earlier segments that either warpgroup may still be reading, so each
@@ -382,13 +413,31 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
   if (seg_on[0]) p_pass(std::integral_constant<int, 0>{});
   if (seg_on[1]) p_pass(std::integral_constant<int, 1>{});
   if (seg_on[2]) p_pass(std::integral_constant<int, 2>{});
-  if (ok) tc5::st_wait();
-  float p_sink[4];
+  if (ok && has_sinks && wg == 0) {
+    // sink probabilities, two per column, into columns [320, 328) (every score there has been read)
+    uint32_t pk[16];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) p_sink[j] = rbf(__fmul_rn(e_sink[j], inv_sum));
-  if (wg == 1) {
+    for (int j = 0; j < 16; ++j) pk[j] = 0u;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float e0 = exp2f(__fmul_rn(s_sink[2 * j] - mx, kLog2e));
+      const float e1 = exp2f(__fmul_rn(s_sink[2 * j + 1] - mx, kLog2e));
+      pk[j] = pack_bf16(__fmul_rn(e0, inv_sum), __fmul_rn(e1, inv_sum));
+    }
+    tc5::st16(tb + lane_off + kColPSink, pk);
+  }
+  if (ok) tc5::st_wait();
+  if (wg == 1 && !use_tma) {
     cp_async_wait<0>();
     asm volatile("fence.proxy.async.shared::cta;\n" ::);
+  }
+  if (tid == 0 && !seen_v) {
+    seen_v = tc5::mbar_wait(&sm.bar_v, 0, kWaitIters);
+    if (!seen_v) sm.err = 1;
+  }
+  if (tid == 0 && !seen_m) {
+    seen_m = tc5::mbar_wait(&sm.bar_m, 0, kWaitIters);
+    if (!seen_m) sm.err = 1;
   }
   tc5::fence_before_sync();
   __syncthreads();
@@ -407,6 +456,11 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
                     first ? 0u : 1u);
         first = false;
       }
+    }
+    if (has_sinks) {
+      tc5::mma_ts(tb + kColO, tb + kColPSink, tc5::sdesc(tc5::smem_u32(sm.sink_v[0]), 2048, 1024), kIdO,
+                  first ? 0u : 1u);
+      first = false;
     }
     if (has_bank) {
       constexpr uint32_t kIdR = tc5::idesc_bf16(128, HD, false, true);
@@ -430,7 +484,7 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
     float qn = 0.f;
     if (has_bank && a.q_l2 != nullptr) {
       qn = a.q_l2[((int64_t)c * G + gr) * a.Tq + (int64_t)blk * 128 + ir];
-    } else if (has_bank) {
+    } else if (has_bank && (!use_tma || tc5::mbar_wait(&sm.bar_v, 0, kWaitIters))) {
       float acc = 0.f;
       for (int ch = 0; ch < HD / 8; ++ch) {
         const uint4 qv = *reinterpret_cast<const uint4*>(sm.q[ch >> 3] + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
@@ -480,12 +534,7 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int col = c0 + j + u;
-            float o = __uint_as_float(vo[j + u]);
-            if (has_sinks) {
-#pragma unroll
-              for (int q = 0; q < 4; ++q) o = fmaf(p_sink[q], sm.sink_vf[q][col], o);
-            }
-            o = rbf(o);
+            float o = rbf(__uint_as_float(vo[j + u]));
             if (has_bank) {
               const float ym = __fmul_rn(__fmul_rn(__uint_as_float(vr[j + u]), inv_qn), coef);
               o = rbf(__fadd_rn(o, rbf(__fmul_rn(eta, __fmul_rn(__fmul_rn(ym, rs), sm.res_w[col])))));
@@ -506,11 +555,43 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
   }
   __syncthreads();
   tc5::fence_after_sync();
+  if (tid == 0) {
+    // copies still in flight after a timed-out wait: give them one more bounded wait before leaving
+    if (!seen_k) tc5::mbar_wait(&sm.bar_k, 0, kWaitIters);
+    if (!seen_v) tc5::mbar_wait(&sm.bar_v, 0, kWaitIters);
+    if (!seen_m) tc5::mbar_wait(&sm.bar_m, 0, kWaitIters);
+  }
   if (warp == 0) tc5::tmem_dealloc(tb, 512);
   if (tid == 0 && sm.err && a.status) atomicOr(a.status, 2);
 }
 
 }  // namespace
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// [slices][tokens][hd] bf16, box {64, 128, 1}, 128-byte swizzle; rows past `tokens` read as zero.
+static bool encode_rows(CUtensorMap* m, const void* base, int hd, int64_t tokens, int64_t slices) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)hd, (cuuint64_t)tokens, (cuuint64_t)slices};
+  const cuuint64_t strides[2] = {(cuuint64_t)hd * 2, (cuuint64_t)tokens * hd * 2};
+  const cuuint32_t box[3] = {64, 128, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 extern "C" int bolt3_attend(const bolt3_attend_args* a, void* stream) {
   if (!a || !a->q_rope || !a->q_raw || !a->eta || !a->y || !a->kappa || !a->seg0_k || !a->seg0_v ||
@@ -548,18 +629,30 @@ extern "C" int bolt3_attend(const bolt3_attend_args* a, void* stream) {
     const int gn = (int)std::max<int64_t>(1, std::min<int64_t>(a->G, 128 / a->Tq));
     grid = dim3((unsigned)((a->G + gn - 1) / gn), 1, (unsigned)a->n_chains);
   }
+  AttendMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  if (a->prefill) {
+    const int64_t nq = (int64_t)a->n_chains * a->G;
+    if (!encode_rows(&maps.q_rope, a->q_rope, (int)a->HD, a->Tq, nq) ||
+        !encode_rows(&maps.q_raw, a->q_raw, (int)a->HD, a->Tq, nq) ||
+        !encode_rows(&maps.k0, a->seg0_k, (int)a->HD, a->seg0_chain_tokens, a->n_chains) ||
+        !encode_rows(&maps.v0, a->seg0_v, (int)a->HD, a->seg0_chain_tokens, a->n_chains) ||
+        !encode_rows(&maps.k1, a->seg1_k, (int)a->HD, a->seg1_chain_tokens, a->n_chains) ||
+        !encode_rows(&maps.v1, a->seg1_v, (int)a->HD, a->seg1_chain_tokens, a->n_chains))
+      return BOLT3_ERR_CUDA;
+  }
   // Each CTA allocates all 512 TMEM columns, so the shared-memory request keeps one CTA per SM.
   constexpr size_t kMinSmem = 120 * 1024;
   if (a->HD == 128) {
     const size_t smem = std::max(sizeof(Smem<128>) + 1024, kMinSmem);
     if (cudaFuncSetAttribute(attend_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return BOLT3_ERR_CUDA;
-    attend_tc_kernel<128><<<grid, NT, smem, s>>>(*a);
+    attend_tc_kernel<128><<<grid, NT, smem, s>>>(*a, maps);
   } else if (a->HD == 64) {
     const size_t smem = std::max(sizeof(Smem<64>) + 1024, kMinSmem);
     if (cudaFuncSetAttribute(attend_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return BOLT3_ERR_CUDA;
-    attend_tc_kernel<64><<<grid, NT, smem, s>>>(*a);
+    attend_tc_kernel<64><<<grid, NT, smem, s>>>(*a, maps);
   } else {
     return BOLT3_ERR_SHAPE;
   }
