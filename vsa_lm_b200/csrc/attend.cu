@@ -17,8 +17,8 @@
 // (bolt3.py:251-256): y = bf16( bf16(P@V) + bf16( eta * RMSNorm_w( q_raw @ (M_hi + M_lo) / |q_raw|
 // * (1-gamma)/sqrt(HD) ) ) ), with M split into two bf16 terms.
 //
-// Both warpgroups handle every query row (TMEM lane = row), each on half of the columns, and swap
-// row max / sum / RMS partials through shared memory. Thread 0 issues the MMAs. Prefill tiles arrive
+// All four warpgroups handle every query row (TMEM lane = row), each on a quarter of the columns,
+// and swap row max / sum / RMS partials through shared memory. Thread 0 issues the MMAs. Prefill tiles arrive
 // by TMA, issued by thread 0: Q and K tiles (3-D tensor maps, 128-byte swizzle, rows past the end of
 // a sequence zero-filled), the scan's snapshot images as plain bulk copies, and V / q_raw into the
 // K / Q tiles once the score MMAs have consumed them. Decode tiles (ring buffers) are gathered with
@@ -41,7 +41,10 @@ using namespace b3;
 
 constexpr int S = 128;
 constexpr int CC = 128;
-constexpr int NT = 256;
+constexpr int NT = 512;
+constexpr int NWG = NT / 128;  // warpgroups; each covers all 128 query rows (TMEM lanes)
+constexpr int CW = 128 / NWG;  // score columns per segment handled by one warpgroup
+static_assert(CW == 32, "one 32-column TMEM chunk per segment and warpgroup");
 constexpr uint32_t kWaitIters = 1u << 24;
 constexpr uint32_t kColO = 384, kColR = 192, kColPSink = 320;
 
@@ -53,8 +56,8 @@ struct __align__(1024) Smem {
   unsigned char sink_k[HD / 64][2048];  // the 4 sink keys as a 16-row K-major tile, rows 4..15 zero
   unsigned char sink_v[HD / 64][2048];  // the 4 sink values as the 16-key B tile of P@V
   float res_w[HD];
-  float red_max[2][128];    // per-row partial results exchanged between the two warpgroups
-  float red_sum[2][128];
+  float red_max[NWG][128];  // per-row partial results exchanged between the warpgroups
+  float red_sum[NWG][128];
   float bias[S];
   uint64_t bar_s, bar_o;
   uint64_t bar_k, bar_v, bar_m;   // TMA completion: Q + K tiles, V + q_raw tiles, M_res image
@@ -252,8 +255,8 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
 
   constexpr float scale = HD == 128 ? 0.08838834764831845f : 0.125f;  // fp32(HD ** -0.5)
   constexpr float kLog2e = 1.4426950408889634f;
-  // Both warpgroups work on every query row r (= TMEM lane): warpgroup wg takes columns
-  // [wg*64, wg*64+64) of each key segment and [wg*HD/2, (wg+1)*HD/2) of the output.
+  // Every warpgroup works on every query row r (= TMEM lane): warpgroup wg takes columns
+  // [wg*CW, wg*CW+CW) of each key segment and [wg*HD/NWG, (wg+1)*HD/NWG) of the output.
   const int wg = warp >> 2;
   const int r = tid & 127;
   const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
@@ -322,45 +325,57 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
 
   // ---- softmax over this warpgroup's half of every segment
   const float* bias = sm.bias;
-  auto row_pass = [&](auto seg_tag, auto&& body) {
+  // the 32 scores of this warpgroup in segment SEG: scaled, attractor bias added, masked keys -inf
+  auto load_scores = [&](auto seg_tag, float (&x)[32]) {
     constexpr int SEG = decltype(seg_tag)::value;
     const int lim = SEG == 1 ? L0 - 1 : (SEG == 2 ? min(L1 - 1, lim1) : S - 1);
-    for (int c0 = wg * 64; c0 < wg * 64 + 64; c0 += 32) {
-      uint32_t v[32];
-      tc5::ld32(tb + lane_off + SEG * 128 + c0, v);
-      tc5::ld_wait();
-      float x[32];
+    const int c0 = wg * CW;
+    uint32_t v[32];
+    tc5::ld32(tb + lane_off + SEG * 128 + c0, v);
+    tc5::ld_wait();
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float sc = __fmul_rn(__uint_as_float(v[j]), scale);
-        if (SEG == 0) x[j] = __fadd_rn(sc, bias[c0 + j]);
-        else x[j] = (c0 + j <= lim) ? sc : neg_inf();
-      }
-      body(c0, x);
+    for (int j = 0; j < 32; ++j) {
+      const float sc = __fmul_rn(__uint_as_float(v[j]), scale);
+      if (SEG == 0) x[j] = __fadd_rn(sc, bias[c0 + j]);
+      else x[j] = (c0 + j <= lim) ? sc : neg_inf();
     }
   };
-  auto for_each_seg = [&](auto&& body) {
-    if (seg_on[0]) row_pass(std::integral_constant<int, 0>{}, [&](int c0, float (&x)[32]) { body(0, c0, x); });
-    if (seg_on[1]) row_pass(std::integral_constant<int, 1>{}, [&](int c0, float (&x)[32]) { body(1, c0, x); });
-    if (seg_on[2]) row_pass(std::integral_constant<int, 2>{}, [&](int c0, float (&x)[32]) { body(2, c0, x); });
-  };
   // statistics pass: row max and sum of exp(x - max) in one sweep, the sum rescaled whenever a
-  // 32-column block raises the max; exp via exp2 of (x - max) * log2(e), within ~1e-6 relative.
-  // Warpgroup 0 also counts the sinks (scores in TMEM columns [384, 388)).
+  // block raises the running max; exp via exp2 of (x - max) * log2(e), within ~1e-6 relative. Each
+  // block's exp(x - running max) goes back to TMEM over its scores, with that running max kept in
+  // mrun, so the P pass only rescales. Warpgroup 0 also counts the sinks (TMEM columns [384, 388)).
   float mx = neg_inf(), sum = 0.f;
-  auto stats = [&](const float (&x)[32]) {
+  auto stats = [&](const float (&x)[32], uint32_t (&ev)[32]) {
     float cm = x[0];
 #pragma unroll
     for (int j = 1; j < 32; ++j) cm = fmaxf(cm, x[j]);
-    if (cm == neg_inf()) return;
+    if (cm == neg_inf()) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ev[j] = 0u;
+      return;
+    }
     if (cm > mx) {
       sum = __fmul_rn(sum, exp2f(__fmul_rn(mx - cm, kLog2e)));
       mx = cm;
     }
     float part[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < 32; ++j) part[j & 3] += exp2f(__fmul_rn(x[j] - mx, kLog2e));
+    for (int j = 0; j < 32; ++j) {
+      const float e = exp2f(__fmul_rn(x[j] - mx, kLog2e));
+      part[j & 3] += e;
+      ev[j] = __float_as_uint(e);
+    }
     sum += (part[0] + part[1]) + (part[2] + part[3]);
+  };
+  float mrun[3] = {neg_inf(), neg_inf(), neg_inf()};
+  auto stats_seg = [&](auto seg_tag) {
+    constexpr int SEG = decltype(seg_tag)::value;
+    float x[32];
+    uint32_t ev[32];
+    load_scores(seg_tag, x);
+    stats(x, ev);
+    mrun[SEG] = mx;
+    tc5::st32(tb + lane_off + SEG * 128 + wg * CW, ev);
   };
   float s_sink[4] = {neg_inf(), neg_inf(), neg_inf(), neg_inf()};
   if (ok && has_sinks && wg == 0) {
@@ -372,43 +387,45 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
     for (int j = 0; j < 32; ++j) x[j] = neg_inf();
 #pragma unroll
     for (int j = 0; j < 4; ++j) x[j] = s_sink[j] = __fmul_rn(__uint_as_float(v[j]), scale);
-    stats(x);
+    stats(x, v);
   }
-  if (ok) for_each_seg([&](int, int, float (&x)[32]) { stats(x); });
+  if (ok) {
+    if (seg_on[0]) stats_seg(std::integral_constant<int, 0>{});
+    if (seg_on[1]) stats_seg(std::integral_constant<int, 1>{});
+    if (seg_on[2]) stats_seg(std::integral_constant<int, 2>{});
+    tc5::st_wait();
+  }
   sm.red_max[wg][r] = mx;
   sm.red_sum[wg][r] = sum;
-  asm volatile("bar.sync 3, 256;\n" ::);
+  asm volatile("bar.sync 3, %0;\n" ::"n"(NT));
   {
-    const float m0 = sm.red_max[0][r], m1 = sm.red_max[1][r];
-    mx = fmaxf(m0, m1);
-    sum = __fmul_rn(sm.red_sum[0][r], exp2f(__fmul_rn(m0 - mx, kLog2e))) +
-          __fmul_rn(sm.red_sum[1][r], exp2f(__fmul_rn(m1 - mx, kLog2e)));
+    mx = sm.red_max[0][r];
+#pragma unroll
+    for (int w = 1; w < NWG; ++w) mx = fmaxf(mx, sm.red_max[w][r]);
+    sum = 0.f;
+#pragma unroll
+    for (int w = 0; w < NWG; ++w) sum += __fmul_rn(sm.red_sum[w][r], exp2f(__fmul_rn(sm.red_max[w][r] - mx, kLog2e)));
   }
-  // pass 3: p = bf16(exp(x - max) * (1 / sum)), two per column, into TMEM columns [0, 192); the
-  // bf16 cast matches the reference's except within ~1e-6 of a rounding boundary. P of segment s
-  // lands on score columns of earlier segments that either warpgroup may still be reading, so each
-  // segment's P is written only after both warpgroups have read that segment's scores.
+  // P pass: p = bf16(exp(x - max) * (1 / sum)) = bf16(e * exp(mrun - max) / sum) from the stored e,
+  // two per column, into TMEM columns [0, 192); the bf16 cast matches the reference's except within
+  // ~1e-6 of a rounding boundary. P of segment s lands on columns of earlier segments that another
+  // warpgroup may still be reading, so each segment's P is written only after every warpgroup has
+  // read that segment's values.
   const float inv_sum = 1.0f / sum;
   auto p_pass = [&](auto seg_tag) {
     constexpr int SEG = decltype(seg_tag)::value;
-    uint32_t pk[2][16];
-    int half = 0;
+    uint32_t pk[16];
     if (ok) {
-      row_pass(seg_tag, [&](int, float (&x)[32]) {
+      uint32_t v[32];
+      tc5::ld32(tb + lane_off + SEG * 128 + wg * CW, v);
+      tc5::ld_wait();
+      const float f = __fmul_rn(exp2f(__fmul_rn(mrun[SEG] - mx, kLog2e)), inv_sum);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float e0 = exp2f(__fmul_rn(x[2 * j] - mx, kLog2e));
-          const float e1 = exp2f(__fmul_rn(x[2 * j + 1] - mx, kLog2e));
-          pk[half][j] = pack_bf16(__fmul_rn(e0, inv_sum), __fmul_rn(e1, inv_sum));
-        }
-        ++half;
-      });
+      for (int j = 0; j < 16; ++j)
+        pk[j] = pack_bf16(__fmul_rn(__uint_as_float(v[2 * j]), f), __fmul_rn(__uint_as_float(v[2 * j + 1]), f));
     }
-    asm volatile("bar.sync 3, 256;\n" ::);
-    if (ok) {
-      tc5::st16(tb + lane_off + (uint32_t)(SEG * 64 + wg * 32), pk[0]);
-      tc5::st16(tb + lane_off + (uint32_t)(SEG * 64 + wg * 32 + 16), pk[1]);
-    }
+    asm volatile("bar.sync 3, %0;\n" ::"n"(NT));
+    if (ok) tc5::st16(tb + lane_off + (uint32_t)(SEG * 64 + wg * (CW / 2)), pk);
   };
   if (seg_on[0]) p_pass(std::integral_constant<int, 0>{});
   if (seg_on[1]) p_pass(std::integral_constant<int, 1>{});
@@ -477,10 +494,11 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
     tc5::commit(&sm.bar_o);
   }
 
-  // ---- epilogue: warpgroup wg writes columns [wg*HD/2, (wg+1)*HD/2) of row r
+  // ---- epilogue: warpgroup wg writes columns [wg*EW, (wg+1)*EW) of row r, EC at a time
   {
-    constexpr int HALF = HD / 2;
-    const int cbeg = wg * HALF;
+    constexpr int EW = HD / NWG;
+    constexpr int EC = EW < 32 ? EW : 32;
+    const int cbeg = wg * EW;
     float qn = 0.f;
     if (has_bank && a.q_l2 != nullptr) {
       qn = a.q_l2[((int64_t)c * G + gr) * a.Tq + (int64_t)blk * 128 + ir];
@@ -505,31 +523,34 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
     const float inv_qn = 1.0f / fmaxf(qn, 1e-12f);
     float ss = 0.f;
     if (ok2 && has_bank) {
-      for (int c0 = cbeg; c0 < cbeg + HALF; c0 += 32) {
-        uint32_t v[32];
-        tc5::ld32(tb + lane_off + kColR + c0, v);
+      for (int c0 = cbeg; c0 < cbeg + EW; c0 += EC) {
+        uint32_t v[EC];
+        tc5::ld_cols(tb + lane_off + kColR + c0, v);
         tc5::ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
+        for (int j = 0; j < EC; ++j) {
           const float ym = __fmul_rn(__fmul_rn(__uint_as_float(v[j]), inv_qn), coef);
           ss = fmaf(ym, ym, ss);
         }
       }
     }
     sm.red_max[wg][r] = ss;
-    asm volatile("bar.sync 3, 256;\n" ::);
-    const float rs = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(sm.red_max[0][r] + sm.red_max[1][r], (float)HD), a.eps));
+    asm volatile("bar.sync 3, %0;\n" ::"n"(NT));
+    float ss_all = 0.f;
+#pragma unroll
+    for (int w = 0; w < NWG; ++w) ss_all += sm.red_max[w][r];
+    const float rs = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss_all, (float)HD), a.eps));
     if (ok2) {
       bf16* yrow = reinterpret_cast<bf16*>(a.y) +
                    (((int64_t)b * a.y_tokens + (int64_t)blk * 128 + ir) * H + kvh * G + gr) * HD;
-      for (int c0 = cbeg; c0 < cbeg + HALF; c0 += 32) {
-        uint32_t vo[32], vr[32];
-        tc5::ld32(tb + lane_off + kColO + c0, vo);
-        if (has_bank) tc5::ld32(tb + lane_off + kColR + c0, vr);
+      for (int c0 = cbeg; c0 < cbeg + EW; c0 += EC) {
+        uint32_t vo[EC], vr[EC];
+        tc5::ld_cols(tb + lane_off + kColO + c0, vo);
+        if (has_bank) tc5::ld_cols(tb + lane_off + kColR + c0, vr);
         tc5::ld_wait();
-        uint32_t packed[16];
+        uint32_t packed[EC / 2];
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
+        for (int j = 0; j < EC; j += 2) {
           float o2[2];
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
@@ -545,7 +566,7 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
         }
         if (r < n_rows) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
+          for (int q = 0; q < EC / 8; ++q)
             *reinterpret_cast<uint4*>(yrow + c0 + q * 8) =
                 make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
         }
