@@ -270,13 +270,27 @@ class Bolt3Attn(nn.Module):
         return out.to(x.dtype)
 
     # scan steps per segment when the consolidation scan overlaps the attention
-    SCAN_SEGMENT = 8
+    # Scan segment lengths, front-loaded: the attention of bank-reading chunks cannot start before the
+    # q projection is done anyway, while every relaunch costs a bank reload and the slowest chain.
+    SCAN_SEGMENTS = (32, 12, 8, 6, 4)
+
+    def _scan_segments(self, n_cons: int):
+        """(first step, steps) of each scan launch; the last length repeats past the table."""
+        out, s0, i = [], 0, 0
+        while s0 < n_cons:
+            n = min(self.SCAN_SEGMENTS[min(i, len(self.SCAN_SEGMENTS) - 1)], n_cons - s0)
+            out.append((s0, n))
+            s0 += n
+            i += 1
+        return out
 
     def _aux_stream(self, device) -> torch.cuda.Stream:
         cache = self.__dict__.setdefault("_streams", {})
         key = str(device)
         if key not in cache:
-            cache[key] = torch.cuda.Stream(device=device)
+            # highest priority: each scan segment is on the critical path, and the block scheduler
+            # then hands it SMs as soon as attention CTAs retire instead of after the whole grid
+            cache[key] = torch.cuda.Stream(device=device, priority=-8)
         return cache[key]
 
     def _scan_and_attend(self, b, T, *, q_rope, q_raw, eta, k_raw, k_rope, v, beta, q_l2, ws, bank, y, consts,
@@ -284,7 +298,7 @@ class Bolt3Attn(nn.Module):
         """Phases B and C of the forward (bolt3.py:210-273), overlapped on two streams.
 
         The consolidation scan is sequential per chain and fills only b*HKV SMs, so it runs on a
-        side stream in segments of SCAN_SEGMENT steps while the main stream runs the attention of
+        side stream in segments (SCAN_SEGMENTS) while the main stream runs the attention of
         every chunk whose snapshot (consolidation r - 2) is already written."""
         H, HKV, HD, G = self.H, self.HKV, self.HD, self.G
         c = consts
@@ -304,11 +318,9 @@ class Bolt3Attn(nn.Module):
         ready = torch.cuda.Event()
         ready.record(main)
         aux.wait_event(ready)
-        seg = self.SCAN_SEGMENT
         done = []
         with torch.cuda.stream(aux):
-            for s0 in range(0, n_cons, seg):
-                n = min(seg, n_cons - s0)
+            for s0, n in self._scan_segments(n_cons):
                 K.consolidate(n_chains=b * HKV, hkv=HKV, HD=HD, bank=bank, init_blank=s0 == 0, kr=k_raw, kp=k_rope,
                               v=v, beta=beta, chain_tokens=T, token0=s0 * self.C, step_tokens=self.C,
                               skip0=N_SINKS if s0 == 0 else 0, chunk_len=self.C, pos0=0, n_steps=n,

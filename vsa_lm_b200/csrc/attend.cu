@@ -47,6 +47,14 @@ constexpr int CW = 128 / NWG;  // score columns per segment handled by one warpg
 static_assert(CW == 32, "one 32-column TMEM chunk per segment and warpgroup");
 constexpr uint32_t kWaitIters = 1u << 24;
 constexpr uint32_t kColO = 384, kColR = 192, kColPSink = 320;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// 2^x on the special-function unit (relative error ~2^-22; results below 2^-126 flush to zero)
+B3_DEV float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
 
 template <int HD>
 struct __align__(1024) Smem {
@@ -59,7 +67,7 @@ struct __align__(1024) Smem {
   float red_max[NWG][128];  // per-row partial results exchanged between the warpgroups
   float red_sum[NWG][128];
   float bias[S];
-  uint64_t bar_s, bar_o;
+  uint64_t bar_s, bar_o, bar_r;
   uint64_t bar_k, bar_v, bar_m;   // TMA completion: Q + K tiles, V + q_raw tiles, M_res image
   uint32_t tbase;
   int err;
@@ -158,6 +166,7 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
   if (tid == 0) {
     tc5::mbar_init(&sm.bar_s, 1);
     tc5::mbar_init(&sm.bar_o, 1);
+    tc5::mbar_init(&sm.bar_r, 1);
     tc5::mbar_init(&sm.bar_k, 1);
     tc5::mbar_init(&sm.bar_v, 1);
     tc5::mbar_init(&sm.bar_m, 1);
@@ -209,8 +218,9 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
     if (has_bank) {
       const float kappa = a.kappa[kvh];
       for (int s = tid; s < S; s += NT)
-        sm.bias[s] = a.bank_act[bofs * S + s] ? __fmul_rn(kappa, logf(fmaxf(a.bank_mass[bofs * S + s], 1.0f)))
-                                              : neg_inf();
+        sm.bias[s] = a.bank_act[bofs * S + s]
+                         ? __fmul_rn(__fmul_rn(kappa, logf(fmaxf(a.bank_mass[bofs * S + s], 1.0f))), kLog2e)
+                         : neg_inf();
     }
   }
   if (warp == 0) {
@@ -253,8 +263,6 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
     tc5::commit(&sm.bar_s);
   }
 
-  constexpr float scale = HD == 128 ? 0.08838834764831845f : 0.125f;  // fp32(HD ** -0.5)
-  constexpr float kLog2e = 1.4426950408889634f;
   // Every warpgroup works on every query row r (= TMEM lane): warpgroup wg takes columns
   // [wg*CW, wg*CW+CW) of each key segment and [wg*HD/NWG, (wg+1)*HD/NWG) of the output.
   const int wg = warp >> 2;
@@ -324,6 +332,9 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
   }
 
   // ---- softmax over this warpgroup's half of every segment
+  // The softmax runs in log2 units: t = S * (HD^-0.5 * log2 e) + bias * log2 e, p = 2^(t - max t) / sum,
+  // which differs from exp(s - max s) by ~|s| * 1e-7 relative.
+  constexpr float kScaleL2 = (float)((HD == 128 ? 0.08838834764831845 : 0.125) * 1.4426950408889634);
   const float* bias = sm.bias;
   // the 32 scores of this warpgroup in segment SEG: scaled, attractor bias added, masked keys -inf
   auto load_scores = [&](auto seg_tag, float (&x)[32]) {
@@ -335,15 +346,14 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
     tc5::ld_wait();
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      const float sc = __fmul_rn(__uint_as_float(v[j]), scale);
-      if (SEG == 0) x[j] = __fadd_rn(sc, bias[c0 + j]);
-      else x[j] = (c0 + j <= lim) ? sc : neg_inf();
+      if (SEG == 0) x[j] = fmaf(__uint_as_float(v[j]), kScaleL2, bias[c0 + j]);
+      else x[j] = (c0 + j <= lim) ? __fmul_rn(__uint_as_float(v[j]), kScaleL2) : neg_inf();
     }
   };
-  // statistics pass: row max and sum of exp(x - max) in one sweep, the sum rescaled whenever a
-  // block raises the running max; exp via exp2 of (x - max) * log2(e), within ~1e-6 relative. Each
-  // block's exp(x - running max) goes back to TMEM over its scores, with that running max kept in
-  // mrun, so the P pass only rescales. Warpgroup 0 also counts the sinks (TMEM columns [384, 388)).
+  // statistics pass: row max and sum of 2^(t - max) in one sweep, the sum rescaled whenever a block
+  // raises the running max. Each block's 2^(t - running max) goes back to TMEM over its scores, with
+  // that running max kept in mrun, so the P pass only rescales. Warpgroup 0 also counts the sinks
+  // (TMEM columns [384, 388)).
   float mx = neg_inf(), sum = 0.f;
   auto stats = [&](const float (&x)[32], uint32_t (&ev)[32]) {
     float cm = x[0];
@@ -355,13 +365,13 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
       return;
     }
     if (cm > mx) {
-      sum = __fmul_rn(sum, exp2f(__fmul_rn(mx - cm, kLog2e)));
+      sum = __fmul_rn(sum, ex2(mx - cm));
       mx = cm;
     }
     float part[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      const float e = exp2f(__fmul_rn(x[j] - mx, kLog2e));
+      const float e = ex2(x[j] - mx);
       part[j & 3] += e;
       ev[j] = __float_as_uint(e);
     }
@@ -386,7 +396,7 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
 #pragma unroll
     for (int j = 0; j < 32; ++j) x[j] = neg_inf();
 #pragma unroll
-    for (int j = 0; j < 4; ++j) x[j] = s_sink[j] = __fmul_rn(__uint_as_float(v[j]), scale);
+    for (int j = 0; j < 4; ++j) x[j] = s_sink[j] = __fmul_rn(__uint_as_float(v[j]), kScaleL2);
     stats(x, v);
   }
   if (ok) {
@@ -404,9 +414,9 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
     for (int w = 1; w < NWG; ++w) mx = fmaxf(mx, sm.red_max[w][r]);
     sum = 0.f;
 #pragma unroll
-    for (int w = 0; w < NWG; ++w) sum += __fmul_rn(sm.red_sum[w][r], exp2f(__fmul_rn(sm.red_max[w][r] - mx, kLog2e)));
+    for (int w = 0; w < NWG; ++w) sum += __fmul_rn(sm.red_sum[w][r], ex2(sm.red_max[w][r] - mx));
   }
-  // P pass: p = bf16(exp(x - max) * (1 / sum)) = bf16(e * exp(mrun - max) / sum) from the stored e,
+  // P pass: p = bf16(2^(t - max) * (1 / sum)) = bf16(e * 2^(mrun - max) / sum) from the stored e,
   // two per column, into TMEM columns [0, 192); the bf16 cast matches the reference's except within
   // ~1e-6 of a rounding boundary. P of segment s lands on columns of earlier segments that another
   // warpgroup may still be reading, so each segment's P is written only after every warpgroup has
@@ -419,7 +429,7 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
       uint32_t v[32];
       tc5::ld32(tb + lane_off + SEG * 128 + wg * CW, v);
       tc5::ld_wait();
-      const float f = __fmul_rn(exp2f(__fmul_rn(mrun[SEG] - mx, kLog2e)), inv_sum);
+      const float f = __fmul_rn(ex2(mrun[SEG] - mx), inv_sum);
 #pragma unroll
       for (int j = 0; j < 16; ++j)
         pk[j] = pack_bf16(__fmul_rn(__uint_as_float(v[2 * j]), f), __fmul_rn(__uint_as_float(v[2 * j + 1]), f));
@@ -437,8 +447,8 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
     for (int j = 0; j < 16; ++j) pk[j] = 0u;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      const float e0 = exp2f(__fmul_rn(s_sink[2 * j] - mx, kLog2e));
-      const float e1 = exp2f(__fmul_rn(s_sink[2 * j + 1] - mx, kLog2e));
+      const float e0 = ex2(s_sink[2 * j] - mx);
+      const float e1 = ex2(s_sink[2 * j + 1] - mx);
       pk[j] = pack_bf16(__fmul_rn(e0, inv_sum), __fmul_rn(e1, inv_sum));
     }
     tc5::st16(tb + lane_off + kColPSink, pk);
@@ -461,8 +471,21 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
   tc5::fence_after_sync();
   const bool ok_all = sm.err == 0;
 
-  // ---- stage 3: O = P V; R = q_raw (M_hi + M_lo)
+  // ---- stage 3: R = q_raw (M_hi + M_lo) first (the epilogue's RMS sweep overlaps P@V), then O = P V
   if (tid == 0 && ok_all) {
+    if (has_bank) {
+      constexpr uint32_t kIdR = tc5::idesc_bf16(128, HD, false, true);
+      const uint32_t qa = tc5::smem_u32(sm.q[0]);
+      for (int hl = 0; hl < 2; ++hl) {
+        const uint32_t ma = tc5::smem_u32(sm.m[hl][0]);
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          const uint32_t qo = (ks >> 2) * 16384 + (ks & 3) * 32;
+          tc5::mma_ss(tb + kColR, tc5::sdesc(qa + qo, 16, 1024), tc5::sdesc(ma + ks * 2048, HD * 128, 1024), kIdR,
+                      (hl | ks) ? 1u : 0u);
+        }
+      }
+      tc5::commit(&sm.bar_r);
+    }
     constexpr uint32_t kIdO = tc5::idesc_bf16(128, HD, false, true);
     bool first = true;
     for (int s2 = 0; s2 < 3; ++s2) {
@@ -478,18 +501,6 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
       tc5::mma_ts(tb + kColO, tb + kColPSink, tc5::sdesc(tc5::smem_u32(sm.sink_v[0]), 2048, 1024), kIdO,
                   first ? 0u : 1u);
       first = false;
-    }
-    if (has_bank) {
-      constexpr uint32_t kIdR = tc5::idesc_bf16(128, HD, false, true);
-      const uint32_t qa = tc5::smem_u32(sm.q[0]);
-      for (int hl = 0; hl < 2; ++hl) {
-        const uint32_t ma = tc5::smem_u32(sm.m[hl][0]);
-        for (int ks = 0; ks < HD / 16; ++ks) {
-          const uint32_t qo = (ks >> 2) * 16384 + (ks & 3) * 32;
-          tc5::mma_ss(tb + kColR, tc5::sdesc(qa + qo, 16, 1024), tc5::sdesc(ma + ks * 2048, HD * 128, 1024), kIdR,
-                      (hl | ks) ? 1u : 0u);
-        }
-      }
     }
     tc5::commit(&sm.bar_o);
   }
@@ -517,12 +528,12 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
     }
     const float eta = has_bank ? a.eta[((int64_t)c * G + gr) * a.Tq + (int64_t)blk * 128 + ir] : 0.f;
     const float coef = has_bank ? a.coef[kvh] : 0.f;
-    const bool ok2 = ok_all && tc5::mbar_wait(&sm.bar_o, 0, kWaitIters);
-    if (!ok2 && ok_all) sm.err = 1;
+    const bool ok_r = ok_all && (!has_bank || tc5::mbar_wait(&sm.bar_r, 0, kWaitIters));
+    if (!ok_r && ok_all) sm.err = 1;
     tc5::fence_after_sync();
     const float inv_qn = 1.0f / fmaxf(qn, 1e-12f);
     float ss = 0.f;
-    if (ok2 && has_bank) {
+    if (ok_r && has_bank) {
       for (int c0 = cbeg; c0 < cbeg + EW; c0 += EC) {
         uint32_t v[EC];
         tc5::ld_cols(tb + lane_off + kColR + c0, v);
@@ -540,6 +551,9 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
 #pragma unroll
     for (int w = 0; w < NWG; ++w) ss_all += sm.red_max[w][r];
     const float rs = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss_all, (float)HD), a.eps));
+    const bool ok2 = ok_r && tc5::mbar_wait(&sm.bar_o, 0, kWaitIters);
+    if (!ok2 && ok_r) sm.err = 1;
+    tc5::fence_after_sync();
     if (ok2) {
       bf16* yrow = reinterpret_cast<bf16*>(a.y) +
                    (((int64_t)b * a.y_tokens + (int64_t)blk * 128 + ir) * H + kvh * G + gr) * HD;

@@ -5,9 +5,10 @@
 // product and the sum rounded to bf16), beta = sigmoid(beta_proj x) and eta = tanh(eta_proj x)
 // (bolt3.py:198-199) computed from the bf16 logits and rounded to bf16.
 //
-// HBM-bound elementwise work with 16-byte loads and stores: a head row of HD values is handled by
-// HD/8 lanes, each owning 8 consecutive elements; the lane holding elements i and the lane holding
-// i + HD/2 (the pair rotate-half RoPE couples) swap values with one shuffle.
+// HBM-bound elementwise work with 16-byte loads and stores: a block takes 16 tokens and every head
+// row of them; a head row of HD values is handled by HD/8 lanes, each owning 8 consecutive elements;
+// the lane holding elements i and the lane holding i + HD/2 (the pair rotate-half RoPE couples) swap
+// values with one shuffle. cos/sin are computed once per (token, frequency) into shared memory.
 #include "../../include/bolt3.h"
 #include "common.cuh"
 
@@ -15,39 +16,34 @@ namespace {
 
 using namespace b3;
 
-template <int HD>
+template <int HD, int TB>
 __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
   constexpr int LPR = HD / 8;          // lanes per head row
   constexpr int RPW = 32 / LPR;        // rows per warp pass
   constexpr int HALF = LPR / 2;        // lane offset between the RoPE partners
-  const int tok = blockIdx.x;          // b * T + t
-  const int b = tok / a.T, t = tok % a.T;
+  constexpr int NW = 8;                // warps
+  const int64_t n_tok = (int64_t)a.B * a.T;
+  const int64_t tok0 = (int64_t)blockIdx.x * TB;  // this block's tokens: tok0 .. tok0 + ntb - 1
+  const int ntb = (int)min((int64_t)TB, n_tok - tok0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane / LPR, l = lane % LPR;   // row slot within the warp, lane within the row
-  const bf16* row = reinterpret_cast<const bf16*>(a.proj) + (int64_t)tok * a.ld;
-  const float pos = (float)(a.pos0 + t);
   const bool first = l < HALF;         // holds elements of the first half
 
-  // cos/sin of the HD/2 frequencies, once per token, shared by every head through shared memory
-  __shared__ float s_cos[HD / 2], s_sin[HD / 2];
-  for (int i = threadIdx.x; i < HD / 2; i += blockDim.x) {
+  // cos/sin of the HD/2 frequencies for each of the block's tokens, shared by all their heads
+  __shared__ float s_cos[TB][HD / 2], s_sin[TB][HD / 2];
+  for (int i = threadIdx.x; i < ntb * (HD / 2); i += blockDim.x) {
+    const int tl = i / (HD / 2), fi = i % (HD / 2);
+    const float pos = (float)(a.pos0 + (tok0 + tl) % a.T);
     float sv, cv;
-    sincosf(__fmul_rn(pos, a.inv_freq[i]), &sv, &cv);
-    s_cos[i] = rbf(cv);
-    s_sin[i] = rbf(sv);
-  }
-  __syncthreads();
-  float cs[8], sn[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const int fi = (l % HALF) * 8 + e;  // frequency index: element index mod HD/2
-    cs[e] = s_cos[fi];
-    sn[e] = s_sin[fi];
+    sincosf(__fmul_rn(pos, a.inv_freq[fi]), &sv, &cv);
+    s_cos[tl][fi] = rbf(cv);
+    s_sin[tl][fi] = rbf(sv);
   }
 
-  // head rows this call handles: [0, H) q when parts & 1, then HKV k and HKV v rows when parts & 2
+  // head rows per token: [0, H) q when parts & 1, then HKV k and HKV v rows when parts & 2
   const bool do_q = a.parts & 1, do_kv = (a.parts & 2) != 0;
   const int n_rows = (do_q ? a.H : 0) + (do_kv ? 2 * a.HKV : 0);
+  const int n_items = ntb * n_rows;    // (token, row) pairs; consecutive rows of a token are adjacent
   auto row_col = [&](int r, int& kind, int& head) -> int64_t {
     if (do_q && r < a.H) { kind = 0; head = r; return a.q_col + (int64_t)head * HD; }
     const int rk = r - (do_q ? a.H : 0);
@@ -55,34 +51,23 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
     kind = 2; head = rk - a.HKV;
     return a.v_col + (int64_t)head * HD;
   };
-  // issue the loads of up to kPre passes before any use, so each lane keeps several 16-byte loads
-  // in flight (this kernel is bound by HBM latency x bytes in flight)
-  constexpr int kPre = 4;
-  uint4 pre[kPre];
-#pragma unroll
-  for (int p = 0; p < kPre; ++p) {
-    const int r = warp * RPW + p * 8 * RPW + sub;
-    pre[p] = make_uint4(0, 0, 0, 0);
+  auto src = [&](int it) -> const uint4* {
+    const int tl = it / n_rows;
     int kd, hd_;
-    if (r < n_rows) pre[p] = *reinterpret_cast<const uint4*>(row + row_col(r, kd, hd_) + l * 8);
-  }
-  int pass = 0;
-  for (int r0 = warp * RPW; r0 < n_rows; r0 += 8 * RPW, ++pass) {
-    const int r = r0 + sub;
-    const bool live = r < n_rows;
+    const int64_t col = row_col(it - tl * n_rows, kd, hd_);
+    return reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(a.proj) + (tok0 + tl) * a.ld + col + l * 8);
+  };
+  // the row item a lane handles in warp pass `pass`
+  auto item = [&](int pass) { return warp * RPW + pass * NW * RPW + sub; };
+  auto process = [&](int it, const uint4 u) {
+    const bool live = it < n_items;
+    const int tl = live ? it / n_rows : 0;
+    const int64_t tok = tok0 + tl;
+    const int b = (int)(tok / a.T), t = (int)(tok % a.T);
     int kind = 2, head = 0;  // 0 = q, 1 = k, 2 = v
-    int64_t col = 0;
-    if (live) col = row_col(r, kind, head);
+    if (live) row_col(it - tl * n_rows, kind, head);
     float x[8];
     {
-      uint4 u = make_uint4(0, 0, 0, 0);
-      if (pass < kPre) {
-#pragma unroll
-        for (int p = 0; p < kPre; ++p)
-          if (p == pass) u = pre[p];
-      } else if (live) {
-        u = *reinterpret_cast<const uint4*>(row + col + l * 8);
-      }
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -120,26 +105,28 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
     float y[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) y[e] = __shfl_xor_sync(0xffffffffu, x[e], HALF);
-    if (!live) continue;
+    if (!live) return;
     uint32_t raw[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) raw[q] = pack_bf16(x[2 * q], x[2 * q + 1]);
     if (kind == 2) {
       *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(a.v) + off) = make_uint4(raw[0], raw[1], raw[2], raw[3]);
-      continue;
+      return;
     }
     if (kind == 0 && a.q_l2 != nullptr && l == 0)
       a.q_l2[((int64_t)b * a.H + head) * a.eta_head_stride + a.eta_t_off + t] = sqrtf(l2);
+    const float* cs = &s_cos[tl][(l % HALF) * 8];  // frequency index: element index mod HD/2
+    const float* sn = &s_sin[tl][(l % HALF) * 8];
     uint32_t rot[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       float o2[2];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int e = 2 * q + u;
+      for (int u2 = 0; u2 < 2; ++u2) {
+        const int e = 2 * q + u2;
         // rotate_half: the first half pairs with -x[i + HD/2], the second half with x[i - HD/2]
         const float partner = first ? -y[e] : y[e];
-        o2[u] = rbf(__fadd_rn(rbf(__fmul_rn(x[e], cs[e])), rbf(__fmul_rn(partner, sn[e]))));
+        o2[u2] = rbf(__fadd_rn(rbf(__fmul_rn(x[e], cs[e])), rbf(__fmul_rn(partner, sn[e]))));
       }
       rot[q] = pack_bf16(o2[0], o2[1]);
     }
@@ -147,16 +134,37 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
         make_uint4(raw[0], raw[1], raw[2], raw[3]);
     *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(kind == 0 ? a.q_rope : a.k_rope) + off) =
         make_uint4(rot[0], rot[1], rot[2], rot[3]);
+  };
+  // rolling prefetch: each lane keeps kPre 16-byte loads in flight (this kernel is bound by HBM
+  // latency x bytes in flight); the load for pass p + kPre is issued before pass p is processed
+  constexpr int kPre = 4;
+  auto fetch = [&](int it) { return it < n_items ? *src(it) : make_uint4(0, 0, 0, 0); };
+  uint4 buf[kPre];
+#pragma unroll
+  for (int p = 0; p < kPre; ++p) buf[p] = fetch(item(p));
+  __syncthreads();  // trig table
+  const int n_pass = (n_items + NW * RPW - 1) / (NW * RPW);
+  for (int p0 = 0; p0 < n_pass; p0 += kPre) {
+#pragma unroll
+    for (int p = 0; p < kPre; ++p) {
+      const uint4 u = buf[p];
+      buf[p] = fetch(item(p0 + kPre + p));
+      process(item(p0 + p), u);
+    }
   }
 
-  // gates: HKV beta logits and H eta logits
+  // gates: HKV beta logits and H eta logits per token
   const int n_gates = (do_kv ? a.HKV : 0) + (do_q ? a.H : 0);
-  for (int i = threadIdx.x; i < n_gates; i += blockDim.x) {
-    if (do_kv && i < a.HKV) {
-      const float z = bf2f(row[a.beta_col + i]);
-      a.beta[((int64_t)b * a.HKV + i) * a.beta_head_stride + a.beta_t_off + t] = rbf(1.0f / (1.0f + expf(-z)));
+  for (int i = threadIdx.x; i < ntb * n_gates; i += blockDim.x) {
+    const int tl = i / n_gates, gi = i % n_gates;
+    const int64_t tok = tok0 + tl;
+    const int b = (int)(tok / a.T), t = (int)(tok % a.T);
+    const bf16* row = reinterpret_cast<const bf16*>(a.proj) + tok * a.ld;
+    if (do_kv && gi < a.HKV) {
+      const float z = bf2f(row[a.beta_col + gi]);
+      a.beta[((int64_t)b * a.HKV + gi) * a.beta_head_stride + a.beta_t_off + t] = rbf(1.0f / (1.0f + expf(-z)));
     } else {
-      const int h = i - (do_kv ? a.HKV : 0);
+      const int h = gi - (do_kv ? a.HKV : 0);
       const float z = bf2f(row[a.eta_col + h]);
       a.eta[((int64_t)b * a.H + h) * a.eta_head_stride + a.eta_t_off + t] = rbf(tanhf(z));
     }
@@ -190,9 +198,13 @@ extern "C" int bolt3_prep(const bolt3_prep_args* a, void* stream) {
   if ((al & 15) || (a->ld % 8) || !cols_ok) return BOLT3_ERR_ALIGN;
   const int64_t n_tok = (int64_t)a->B * a->T;
   if (n_tok > 0x7fffffff) return BOLT3_ERR_SHAPE;
+  constexpr int TB = 16;  // tokens per block
+  const unsigned grid = (unsigned)((n_tok + TB - 1) / TB);
+  // (token, row) pairs per block must fit an int
+  if ((int64_t)TB * (a->H + 2 * a->HKV) > 0x7fffffff) return BOLT3_ERR_SHAPE;
   cudaStream_t s = (cudaStream_t)stream;
-  if (a->HD == 128) prep_kernel<128><<<(unsigned)n_tok, 256, 0, s>>>(*a);
-  else if (a->HD == 64) prep_kernel<64><<<(unsigned)n_tok, 256, 0, s>>>(*a);
+  if (a->HD == 128) prep_kernel<128, TB><<<grid, 256, 0, s>>>(*a);
+  else if (a->HD == 64) prep_kernel<64, TB><<<grid, 256, 0, s>>>(*a);
   else return BOLT3_ERR_SHAPE;
   return cudaGetLastError() == cudaSuccess ? BOLT3_OK : BOLT3_ERR_CUDA;
 }
