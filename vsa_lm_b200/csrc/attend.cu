@@ -562,21 +562,22 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
         tc5::ld_cols(tb + lane_off + kColO + c0, vo);
         if (has_bank) tc5::ld_cols(tb + lane_off + kColR + c0, vr);
         tc5::ld_wait();
+        // y = bf16(bf16(O) + bf16(eta * (ym * rs) * w)), every rounding done two columns at a time
         uint32_t packed[EC / 2];
 #pragma unroll
         for (int j = 0; j < EC; j += 2) {
-          float o2[2];
+          const float2 o = rbf2(__uint_as_float(vo[j]), __uint_as_float(vo[j + 1]), packed[j >> 1]);
+          if (has_bank) {
+            float t[2];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int col = c0 + j + u;
-            float o = rbf(__uint_as_float(vo[j + u]));
-            if (has_bank) {
+            for (int u = 0; u < 2; ++u) {
               const float ym = __fmul_rn(__fmul_rn(__uint_as_float(vr[j + u]), inv_qn), coef);
-              o = rbf(__fadd_rn(o, rbf(__fmul_rn(eta, __fmul_rn(__fmul_rn(ym, rs), sm.res_w[col])))));
+              t[u] = __fmul_rn(eta, __fmul_rn(__fmul_rn(ym, rs), sm.res_w[c0 + j + u]));
             }
-            o2[u] = o;
+            uint32_t tmp;
+            const float2 tr = rbf2(t[0], t[1], tmp);
+            packed[j >> 1] = pack_bf16(__fadd_rn(o.x, tr.x), __fadd_rn(o.y, tr.y));
           }
-          packed[j >> 1] = pack_bf16(o2[0], o2[1]);
         }
         if (r < n_rows) {
 #pragma unroll

@@ -21,8 +21,13 @@ B3_DEV uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 B3_DEV float2 unpack_bf16(uint32_t u) {
-  __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&u);
-  return __bfloat1622float2(v);
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+// Two roundings for the price of one conversion instruction: `packed` gets the bf16 pair, the
+// return value the same two values as floats.
+B3_DEV float2 rbf2(float lo, float hi, uint32_t& packed) {
+  packed = pack_bf16(lo, hi);
+  return unpack_bf16(packed);
 }
 
 // ---- warp reductions

@@ -92,10 +92,17 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
     ss = row_sum(ss);
+    // the stored row: the loaded bf16 values as they are, or their RMSNorm rounded to bf16
+    uint32_t raw[4] = {u.x, u.y, u.z, u.w};
     if (kind != 2 && nw != nullptr) {
       const float rr = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)HD), a.eps));
 #pragma unroll
-      for (int e = 0; e < 8; ++e) x[e] = rbf(__fmul_rn(__fmul_rn(x[e], rr), nw[l * 8 + e]));
+      for (int q = 0; q < 4; ++q) {
+        const float2 r2 = rbf2(__fmul_rn(__fmul_rn(x[2 * q], rr), nw[l * 8 + 2 * q]),
+                               __fmul_rn(__fmul_rn(x[2 * q + 1], rr), nw[l * 8 + 2 * q + 1]), raw[q]);
+        x[2 * q] = r2.x;
+        x[2 * q + 1] = r2.y;
+      }
     }
     float l2 = 0.f;  // |q_raw| of the stored (bf16) row, for the M_res read-out
 #pragma unroll
@@ -106,9 +113,6 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) y[e] = __shfl_xor_sync(0xffffffffu, x[e], HALF);
     if (!live) return;
-    uint32_t raw[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) raw[q] = pack_bf16(x[2 * q], x[2 * q + 1]);
     if (kind == 2) {
       *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(a.v) + off) = make_uint4(raw[0], raw[1], raw[2], raw[3]);
       return;
@@ -117,18 +121,17 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
       a.q_l2[((int64_t)b * a.H + head) * a.eta_head_stride + a.eta_t_off + t] = sqrtf(l2);
     const float* cs = &s_cos[tl][(l % HALF) * 8];  // frequency index: element index mod HD/2
     const float* sn = &s_sin[tl][(l % HALF) * 8];
+    // rope = bf16(bf16(x cos) + bf16(partner sin)), the roundings done two at a time;
+    // rotate_half: the first half pairs with -x[i + HD/2], the second half with x[i - HD/2]
     uint32_t rot[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      float o2[2];
-#pragma unroll
-      for (int u2 = 0; u2 < 2; ++u2) {
-        const int e = 2 * q + u2;
-        // rotate_half: the first half pairs with -x[i + HD/2], the second half with x[i - HD/2]
-        const float partner = first ? -y[e] : y[e];
-        o2[u2] = rbf(__fadd_rn(rbf(__fmul_rn(x[e], cs[e])), rbf(__fmul_rn(partner, sn[e]))));
-      }
-      rot[q] = pack_bf16(o2[0], o2[1]);
+      const int e0 = 2 * q, e1 = 2 * q + 1;
+      const float p0 = first ? -y[e0] : y[e0], p1 = first ? -y[e1] : y[e1];
+      uint32_t tmp;
+      const float2 xc = rbf2(__fmul_rn(x[e0], cs[e0]), __fmul_rn(x[e1], cs[e1]), tmp);
+      const float2 ps = rbf2(__fmul_rn(p0, sn[e0]), __fmul_rn(p1, sn[e1]), tmp);
+      rot[q] = pack_bf16(__fadd_rn(xc.x, ps.x), __fadd_rn(xc.y, ps.y));
     }
     *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(kind == 0 ? a.q_raw : a.k_raw) + off) =
         make_uint4(raw[0], raw[1], raw[2], raw[3]);
