@@ -12,11 +12,15 @@
 //   gram = |kr . kr^T| / (|kr| |kr|)      (:156-157)
 //   k^ M = kr . (M_hi + M_lo) / |kr|      (:159)   M split into two bf16 terms: ~2^-17 relative
 //   M   <- gamma M + kr^T . (E_hi + E_lo)  (:162)   E = err / |kr|, split the same way
-// Rankings use a warp bitonic sort; when it finds exactly equal keys the CPU torch.topk order is
-// reproduced with the emulation in stl_select.h (bolt3.py:133-134, 183).
+// Rankings count, per entry, the entries that sort before it (128 threads, one entry each); when
+// exactly equal keys decide the result the CPU torch.topk order is reproduced with the emulation in
+// stl_select.h (bolt3.py:133-134, 183).
 #include "../../include/bolt3.h"
 #include "common.cuh"
 #include "stl_select.h"
+
+#include <cstddef>
+#include <type_traits>
 
 namespace {
 
@@ -41,7 +45,10 @@ struct Smem {
   unsigned char act[S], mrg[CC], ins[CC];
   int n_merged;
   b3sel::KV selA[128], selB[128];
+  alignas(16) uint32_t keys[2][128];   // ranking scratch of the two thread groups (read as uint4)
 };
+static_assert(offsetof(Smem<128>, keys) % 16 == 0 && offsetof(Smem<64>, keys) % 16 == 0,
+              "group_rank reads the ranking keys 16 bytes at a time");
 
 // ------------------------------------------------------------------------------------------
 // shared-memory tile movement
@@ -88,14 +95,16 @@ B3_DEV float row_sumsq(const bf16* s, int r, int lane) {
 }
 
 // Sum over one half of the 16-byte chunks of row r of x*y (swizzling only permutes chunks within a
-// row, so the two halves of a row together cover it exactly once).
+// row, so the two halves of a row together cover it exactly once). Each row starts its sweep at a
+// different chunk, so the lanes of a warp (consecutive rows) read different shared-memory banks.
 template <int HD>
 B3_DEV float half_row_dot(const bf16* x, const bf16* y, int r, int half) {
-  constexpr int CPR = HD / 8;
+  constexpr int CPR = HD / 8, NH = CPR / 2;
   float acc = 0.f;
 #pragma unroll
-  for (int ch = half * CPR / 2; ch < (half + 1) * CPR / 2; ++ch) {
-    const int off = (ch >> 3) * (128 * 64) + r * 64 + (ch & 7) * 8;  // physical chunk ch of row r
+  for (int c = 0; c < NH; ++c) {
+    const int ch = half * NH + ((c + r) & (NH - 1));                  // physical chunk of row r
+    const int off = (ch >> 3) * (128 * 64) + r * 64 + (ch & 7) * 8;
     const uint4 a = *reinterpret_cast<const uint4*>(x + off);
     const uint4 b = *reinterpret_cast<const uint4*>(y + off);
     const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
@@ -180,87 +189,62 @@ B3_DEV void gemm_tn(float (&acc)[HD / 8][4], const bf16* A, int m0, const bf16* 
 }
 
 // ------------------------------------------------------------------------------------------
-// ranking: warp bitonic sort of up to 128 (value, index) entries, 4 per lane.
-// Sorted order: "largest" = descending value, else ascending; equal values by ascending index.
-// Entries with index >= n are padding and sort last. After sorting, if two adjacent entries that
-// can change the result are exactly equal (or a NaN is present) the CPU torch.topk order is
-// recomputed by lane 0 with the libstdc++-compatible emulation. Writes out_idx/out_val[0..k).
-B3_DEV void warp_topk(const float* vals, int n, int k, bool largest, float ignore_below,
-                      int* out_idx, float* out_val, b3sel::KV* buf, int lane, int32_t* status) {
-  uint64_t key[4];
-#pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const int i = lane * 4 + r;
-    uint32_t kv = 0xffffffffu;
-    if (i < n) {
-      const uint32_t f = fkey(vals[i]);
-      kv = largest ? ~f : f;
-      if (kv == 0xffffffffu) kv = 0xfffffffeu;
-    }
-    key[r] = ((uint64_t)kv << 32) | (uint32_t)i;
+// ranking of up to 128 (value, index) entries by 128 threads (t = 0..127 of a named-barrier group):
+// thread t counts the entries that sort before entry t. Sorted order: "largest" = descending value,
+// else ascending; equal values by ascending index; entries with index >= n are padding and sort
+// last. group_rank writes out_idx/out_val[0..k) in that order; group_resolve then checks whether
+// exactly equal values (or a NaN) decide any of the first `limit` positions and, if so, has thread 0
+// recompute the CPU torch.topk order with the libstdc++-compatible emulation. Equal values sit on
+// adjacent positions, so the order of ties never changes the value at a position, only the index.
+// `keys` is 128 words of shared scratch for the group.
+struct Rank {
+  int rank, eq_after;  // position of entry t; entries with the same value and a larger index
+  float v;
+};
+
+B3_DEV Rank group_rank(const float* vals, int n, int k, bool largest, int* out_idx, float* out_val,
+                       uint32_t* keys, int t, int bar_id) {
+  uint32_t kt = 0xffffffffu;
+  float vt = 0.f;
+  if (t < n) {
+    vt = vals[t];
+    // +0 and -0 compare equal: give them one key so that equal values have equal keys
+    const uint32_t f = fkey(vt == 0.f ? 0.f : vt);
+    kt = largest ? ~f : f;
+    if (kt == 0xffffffffu) kt = 0xfffffffeu;
   }
-  for (int kk = 2; kk <= 128; kk <<= 1) {
-    for (int j = kk >> 1; j > 0; j >>= 1) {
-      if (j >= 4) {
-        const int lj = j >> 2;
+  keys[t] = kt;
+  asm volatile("bar.sync %0, 128;\n" ::"r"(bar_id) : "memory");
+  int rank = 0, eq_after = 0;
+#pragma unroll 4
+  for (int j4 = 0; j4 < 128; j4 += 4) {
+    const uint4 kq = *reinterpret_cast<const uint4*>(keys + j4);
+    const uint32_t kk[4] = {kq.x, kq.y, kq.z, kq.w};
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          const int e = lane * 4 + r;
-          const uint64_t other = __shfl_xor_sync(0xffffffffu, key[r], lj);
-          const bool up = (e & kk) == 0;
-          const bool lower = (e & j) == 0;
-          const uint64_t mn = key[r] < other ? key[r] : other;
-          const uint64_t mx = key[r] < other ? other : key[r];
-          key[r] = (lower == up) ? mn : mx;
-        }
-      } else {
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          const int p = r ^ j;
-          if (p > r) {
-            const int e = lane * 4 + r;
-            const bool up = (e & kk) == 0;
-            const uint64_t a = key[r], b = key[p];
-            const bool sw = up ? (a > b) : (a < b);
-            if (sw) { key[r] = b; key[p] = a; }
-          }
-        }
-      }
+    for (int u = 0; u < 4; ++u) {
+      const int j = j4 + u;
+      rank += (kk[u] < kt) | ((kk[u] == kt) & (j < t));
+      eq_after += (kk[u] == kt) & (j > t);
     }
   }
-  // tie / NaN detection over the positions that decide the first k entries
-  bool tie = false;
-#pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const int i = lane * 4 + r;
-    const int idx = (int)(key[r] & 0xffffffffu);
-    uint64_t nxt = (r < 3) ? key[r + 1] : __shfl_down_sync(0xffffffffu, key[0], 1);
-    if (r == 3 && lane == 31) nxt = ~0ull;
-    const int nidx = (int)(nxt & 0xffffffffu);
-    if (i < n) {
-      const float v = vals[idx];
-      if (v != v) tie = true;
-      if (i < k && i + 1 < n) {
-        const float w = vals[nidx];
-        if (v == w && v >= ignore_below) tie = true;
-      }
-    }
+  if (rank < k) {
+    out_idx[rank] = t;
+    out_val[rank] = vt;
   }
-  tie = __any_sync(0xffffffffu, tie);
-  if (!tie) {
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int i = lane * 4 + r;
-      if (i < k) {
-        const int idx = (int)(key[r] & 0xffffffffu);
-        out_idx[i] = idx;
-        out_val[i] = vals[idx];
-      }
-    }
-    __syncwarp();
-    return;
-  }
-  if (lane == 0) {
+  return Rank{rank, eq_after, vt};
+}
+
+B3_DEV void group_resolve(const Rank& rk, int limit, float ignore_below, const float* vals, int n, int k, bool largest,
+                          int* out_idx, float* out_val, b3sel::KV* buf, int t, int bar_id, int32_t* status) {
+  const bool tie_t =
+      t < n && ((rk.v != rk.v) || (rk.rank < limit && rk.eq_after > 0 && rk.rank + 1 < n && rk.v >= ignore_below));
+  int any_tie;
+  asm volatile(
+      "{\n.reg .pred p, q;\nsetp.ne.u32 p, %2, 0;\nbar.red.or.pred q, %1, 128, p;\nselp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(any_tie)
+      : "r"(bar_id), "r"((uint32_t)tie_t)
+      : "memory");
+  if (any_tie && t == 0) {
     for (int i = 0; i < n; ++i) { buf[i].v = vals[i]; buf[i].i = i; }
     const int bad = b3sel::topk_order(buf, n, k, largest);
     if (bad && status) atomicOr(status, 1);
@@ -269,7 +253,14 @@ B3_DEV void warp_topk(const float* vals, int n, int k, bool largest, float ignor
       out_val[i] = buf[i].v;
     }
   }
-  __syncwarp();
+}
+
+// copy one row of EPL bf16 per lane (lane * EPL .. + EPL - 1 lie in one 16-byte chunk)
+template <int HD>
+B3_DEV void copy_row_part(bf16* dst, int sd, const bf16* src, int ss, int lane) {
+  constexpr int EPL = HD / 32;
+  using V = typename std::conditional<EPL == 4, uint2, uint32_t>::type;
+  *reinterpret_cast<V*>(dst + swz<HD>(sd, lane * EPL)) = *reinterpret_cast<const V*>(src + swz<HD>(ss, lane * EPL));
 }
 
 // ------------------------------------------------------------------------------------------
@@ -543,16 +534,15 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
     if (!full) {
       // ---- fill: the m best tokens take the next empty slots (:183-192)
       const int m = min(S - n_filled, l_tok);
-      if (warp == 0) warp_topk(sm.score, l_tok, m, true, neg_inf(), sm.tops, sm.topv, sm.selA, lane, a.status);
+      if (tid < 128) {
+        const Rank rk = group_rank(sm.score, l_tok, m, true, sm.tops, sm.topv, sm.keys[0], tid, 1);
+        group_resolve(rk, m, neg_inf(), sm.score, l_tok, m, true, sm.tops, sm.topv, sm.selA, tid, 1, a.status);
+      }
       __syncthreads();
       for (int i = warp; i < m; i += 8) {
         const int j = sm.tops[i], s = n_filled + i;
-        constexpr int EPL = HD / 32;
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) {
-          sm.ak[swz<HD>(s, lane * EPL + e)] = sm.kr[swz<HD>(j, lane * EPL + e)];
-          sm.av[swz<HD>(s, lane * EPL + e)] = sm.vv[swz<HD>(j, lane * EPL + e)];
-        }
+        copy_row_part<HD>(sm.ak, s, sm.kr, j, lane);
+        copy_row_part<HD>(sm.av, s, sm.vv, j, lane);
         if (lane == 0) {
           sm.pm[s] = sm.pos[j];
           sm.mass[s] = 1.f;
@@ -681,19 +671,26 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
       for (int j = tid; j < CC; j += NT) sm.wgt[j] = sm.mrg[j] ? -1e9f : sm.score[j];
       __syncthreads();
       const int k_cand = min(l_tok, S);
-      if (warp == 0) warp_topk(sm.wgt, l_tok, k_cand, true, -1e8f, sm.tops, sm.topv, sm.selA, lane, a.status);
-      if (warp == 1) warp_topk(sm.keep, S, k_cand, false, neg_inf(), sm.bots, sm.botv, sm.selB, lane, a.status);
+      // token candidates by weight (threads 0..127) and slots by keep value (128..255), both at once
+      const bool grp_a = tid < 128;
+      const Rank rk = grp_a ? group_rank(sm.wgt, l_tok, k_cand, true, sm.tops, sm.topv, sm.keys[0], tid, 1)
+                            : group_rank(sm.keep, S, k_cand, false, sm.bots, sm.botv, sm.keys[1], tid - 128, 2);
+      __syncthreads();
+      // replacements take a prefix of the pairs (weights descend, keep values ascend); ties can only
+      // matter inside it
+      const int n_rep = __syncthreads_count(tid < k_cand && sm.topv[tid] > sm.botv[tid] && sm.topv[tid] > -1e8f);
+      if (grp_a)
+        group_resolve(rk, n_rep, -1e8f, sm.wgt, l_tok, k_cand, true, sm.tops, sm.topv, sm.selA, tid, 1, a.status);
+      else
+        group_resolve(rk, n_rep, neg_inf(), sm.keep, S, k_cand, false, sm.bots, sm.botv, sm.selB, tid - 128, 2,
+                      a.status);
       __syncthreads();
       for (int i = warp; i < k_cand; i += 8) {
         const float tv = sm.topv[i];
         if (!((tv > sm.botv[i]) && (tv > -1e8f))) continue;  // :135
         const int j = sm.tops[i], s = sm.bots[i];
-        constexpr int EPL = HD / 32;
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) {
-          sm.ak[swz<HD>(s, lane * EPL + e)] = sm.kr[swz<HD>(j, lane * EPL + e)];
-          sm.av[swz<HD>(s, lane * EPL + e)] = sm.vv[swz<HD>(j, lane * EPL + e)];
-        }
+        copy_row_part<HD>(sm.ak, s, sm.kr, j, lane);
+        copy_row_part<HD>(sm.av, s, sm.vv, j, lane);
         if (lane == 0) {
           sm.pm[s] = sm.pos[j];
           sm.mass[s] = 1.f;
