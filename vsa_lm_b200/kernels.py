@@ -19,6 +19,20 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+# Kernel launches issued through this module (C-ABI calls that returned BOLT3_OK), for bench.py's
+# gpu_launches count.
+_launches = 0
+
+
+def launch_count() -> int:
+    return _launches
+
+
+def _count(n: int) -> None:
+    global _launches
+    _launches += n
+
+
 def _need(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
     if not t.is_cuda:
         raise RuntimeError(f"{name} must be a CUDA tensor (the Bolt-3 path has no CPU implementation)")
@@ -68,6 +82,7 @@ def prep(proj: torch.Tensor, *, B: int, T: int, H: int, HKV: int, HD: int, inv_f
         q_l2=_ptr(q_l2), parts=parts, q_col=cols.get("q_col", 0), k_col=cols.get("k_col", 0),
         v_col=cols.get("v_col", 0), beta_col=cols.get("beta_col", 0), eta_col=cols.get("eta_col", 0))
     _lib.check(lib.bolt3_prep(ctypes.byref(a), _stream()), "bolt3_prep")
+    _count(1)
 
 
 def consolidate(*, n_chains: int, hkv: int, HD: int, bank: dict, init_blank: bool,
@@ -94,6 +109,7 @@ def consolidate(*, n_chains: int, hkv: int, HD: int, bank: dict, init_blank: boo
         snap_mass=_ptr(snaps.get("mass")), snap_act=_ptr(snaps.get("act")), snap_m=_ptr(snaps.get("m")),
         snap_cap=int(snaps["ak_rope"].shape[1]) if snaps else 0, snap0=snap0, status=_ptr(status))
     _lib.check(lib.bolt3_consolidate(ctypes.byref(a), _stream()), "bolt3_consolidate")
+    _count(1 if a.n_steps > 0 else 0)
 
 
 def attend_decode(*, n_chains: int, hkv: int, G: int, HD: int, q_rope: torch.Tensor, q_raw: torch.Tensor,
@@ -118,6 +134,7 @@ def attend_decode(*, n_chains: int, hkv: int, G: int, HD: int, q_rope: torch.Ten
         kappa=kappa.data_ptr(), coef=coef.data_ptr(), res_w=res_w.data_ptr(), eps=eps,
         y=y.data_ptr(), y_tokens=Tq, q_l2=_ptr(q_l2))
     _lib.check(lib.bolt3_attend(ctypes.byref(a), _stream()), "bolt3_attend")
+    _count(1)
 
 
 def prefill_workspace_bytes(n_chains: int, T: int, HD: int) -> int:
@@ -158,6 +175,7 @@ def attend_prefill(*, n_chains: int, hkv: int, G: int, HD: int, T: int, q_rope, 
         y=y.data_ptr(), y_tokens=T, status=_ptr(status), q_l2=_ptr(q_l2), blk_begin=blk_begin,
         blk_count=blk_count)
     _lib.check(lib.bolt3_attend(ctypes.byref(a), _stream()), "bolt3_attend")
+    _count(1)
 
 
 def prefill(*, B: int, T: int, H: int, HKV: int, HD: int, q_rope, q_raw, eta, k_raw, k_rope, v, beta,
@@ -176,6 +194,7 @@ def prefill(*, B: int, T: int, H: int, HKV: int, HD: int, q_rope, q_raw, eta, k_
         act=bank["act"].data_ptr(), m_res=bank["m_res"].data_ptr(), n_filled=bank["n_filled"].data_ptr(),
         y=y.data_ptr(), status=_ptr(status), q_l2=_ptr(q_l2))
     _lib.check(lib.bolt3_prefill_fwd(ctypes.byref(a), _stream()), "bolt3_prefill_fwd")
+    _count(2)  # the scan, then the attention
 
 
 def prefill_noalloc(*, B: int, T: int, H: int, HKV: int, HD: int, q_rope, q_raw, eta, k_raw, k_rope, v, beta,
@@ -199,6 +218,7 @@ def prefill_noalloc(*, B: int, T: int, H: int, HKV: int, HD: int, q_rope, q_raw,
         act=bank["act"].data_ptr(), m_res=bank["m_res"].data_ptr(), n_filled=bank["n_filled"].data_ptr(),
         y=y.data_ptr(), status=_ptr(status), q_l2=_ptr(q_l2))
     _lib.check(lib.bolt3_prefill_fwd_noalloc(ctypes.byref(a), _stream()), "bolt3_prefill_fwd_noalloc")
+    _count(2)
 
 
 def new_bank(n_chains: int, HD: int, device, S: int = S_SLOTS) -> dict:
