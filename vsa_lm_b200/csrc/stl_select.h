@@ -11,8 +11,9 @@
 // This header re-implements those published algorithms step for step so that ties come out in the
 // same order, which matters for Bolt-3: at the first full-bank consolidation many attractor slots
 // carry identical `keep` scores (equal utility, mutual nearest neighbours), and which slot is
-// evicted first changes all later state. The CUDA kernels only call it when a fast bitonic sort
-// has found an exact tie; the CPU test `test_topk_tie_order` checks it against `torch.topk`.
+// evicted first changes all later state. The CUDA kernels only call it when their counting-rank
+// sort finds exactly equal values at a position that decides the result; the CPU test
+// `test_topk_tie_order` checks it against `torch.topk`.
 //
 // All routines are iterative (no recursion) and every loop index is bounds-checked: an index that
 // would leave [0, n) sets `*bad = 1` and the routine returns early instead of reading out of range.
