@@ -156,11 +156,13 @@ def test_forward_is_deterministic():
     assert torch.equal(m(x), m(x))
 
 
-@pytest.mark.parametrize("shape,prompt,n_dec", [("tiny", 300, 150), ("qwen3_4b", 512, 140)])
-def test_decoder_matches_oracle(shape, prompt, n_dec):
-    """Free-running decoder (prefill slices + single-token steps). Outputs must match until the
-    native bank stops being the same set of slots as the oracle's, and that may only happen at a
-    consolidation the oracle records as rounding-ambiguous."""
+@pytest.mark.parametrize("shape,prompt,n_dec,tps", [("tiny", 300, 150, 1), ("qwen3_4b", 512, 140, 1),
+                                                    ("qwen3_4b", 384, 136, 4)])
+def test_decoder_matches_oracle(shape, prompt, n_dec, tps):
+    """Free-running decoder (prefill slices + decode steps of `tps` tokens: G * tps <= 16 query rows
+    take the decode-step kernel). Outputs must match until the native bank stops being the same set
+    of slots as the oracle's, and that may only happen at a consolidation the oracle records as
+    rounding-ambiguous."""
     cfg = layer_cfg(shape)
     B = 2
     m = bf16_module(cfg, 0)
@@ -169,7 +171,8 @@ def test_decoder_matches_oracle(shape, prompt, n_dec):
     dec = LayerDecoderOracle(P, oc, B, BF16)
     st = Bolt3LayerState(m, B, "cuda")
     m_res = torch.zeros(B, m.HKV, m.HD, m.HD, device="cuda")
-    steps = [(s, min(128, prompt - s)) for s in range(0, prompt, 128)] + [(prompt + i, 1) for i in range(n_dec)]
+    steps = [(s, min(128, prompt - s)) for s in range(0, prompt, 128)] + \
+        [(prompt + i, tps) for i in range(0, n_dec, tps)]
     outs, refs = [], []
     diverged = False
     for pos, n in steps:

@@ -629,6 +629,9 @@ static bool encode_rows(CUtensorMap* m, const void* base, int hd, int64_t tokens
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// decode steps with few query rows per chain (attend_decode.cu)
+int b3_attend_decode_launch(const bolt3_attend_args* a, cudaStream_t s);
+
 extern "C" int bolt3_attend(const bolt3_attend_args* a, void* stream) {
   if (!a || !a->q_rope || !a->q_raw || !a->eta || !a->y || !a->kappa || !a->seg0_k || !a->seg0_v ||
       !a->seg1_k || !a->seg1_v)
@@ -655,6 +658,7 @@ extern "C" int bolt3_attend(const bolt3_attend_args* a, void* stream) {
                        (uintptr_t)a->bank_m | (uintptr_t)a->y;
   if (al & 15) return BOLT3_ERR_ALIGN;
   cudaStream_t s = (cudaStream_t)stream;
+  if (!a->prefill && (int64_t)a->G * a->Tq <= 16) return b3_attend_decode_launch(a, s);
   dim3 grid;
   if (a->prefill) {
     const int64_t n_blk = (a->Tq + 127) / 128;

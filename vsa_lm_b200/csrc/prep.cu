@@ -5,8 +5,8 @@
 // product and the sum rounded to bf16), beta = sigmoid(beta_proj x) and eta = tanh(eta_proj x)
 // (bolt3.py:198-199) computed from the bf16 logits and rounded to bf16.
 //
-// HBM-bound elementwise work with 16-byte loads and stores: a block takes 16 tokens and every head
-// row of them; a head row of HD values is handled by HD/8 lanes, each owning 8 consecutive elements;
+// HBM-bound elementwise work with 16-byte loads and stores: a block takes 16 tokens (1 for small
+// calls such as decode steps) and every head row of them; a head row of HD values is handled by HD/8 lanes, each owning 8 consecutive elements;
 // the lane holding elements i and the lane holding i + HD/2 (the pair rotate-half RoPE couples) swap
 // values with one shuffle. cos/sin are computed once per (token, frequency) into shared memory.
 #include "../../include/bolt3.h"
@@ -201,13 +201,16 @@ extern "C" int bolt3_prep(const bolt3_prep_args* a, void* stream) {
   if ((al & 15) || (a->ld % 8) || !cols_ok) return BOLT3_ERR_ALIGN;
   const int64_t n_tok = (int64_t)a->B * a->T;
   if (n_tok > 0x7fffffff) return BOLT3_ERR_SHAPE;
-  constexpr int TB = 16;  // tokens per block
-  const unsigned grid = (unsigned)((n_tok + TB - 1) / TB);
+  // 16 tokens per block when there are enough tokens to fill the GPU several times over (prefill);
+  // one token per block otherwise (decode steps), so that every SM gets work
+  const bool big = n_tok >= 16 * 1024;
+  const int tb = big ? 16 : 1;
+  const unsigned grid = (unsigned)((n_tok + tb - 1) / tb);
   // (token, row) pairs per block must fit an int
-  if ((int64_t)TB * (a->H + 2 * a->HKV) > 0x7fffffff) return BOLT3_ERR_SHAPE;
+  if ((int64_t)tb * (a->H + 2 * a->HKV) > 0x7fffffff) return BOLT3_ERR_SHAPE;
   cudaStream_t s = (cudaStream_t)stream;
-  if (a->HD == 128) prep_kernel<128, TB><<<grid, 256, 0, s>>>(*a);
-  else if (a->HD == 64) prep_kernel<64, TB><<<grid, 256, 0, s>>>(*a);
+  if (a->HD == 128) big ? prep_kernel<128, 16><<<grid, 256, 0, s>>>(*a) : prep_kernel<128, 1><<<grid, 256, 0, s>>>(*a);
+  else if (a->HD == 64) big ? prep_kernel<64, 16><<<grid, 256, 0, s>>>(*a) : prep_kernel<64, 1><<<grid, 256, 0, s>>>(*a);
   else return BOLT3_ERR_SHAPE;
   return cudaGetLastError() == cudaSuccess ? BOLT3_OK : BOLT3_ERR_CUDA;
 }
