@@ -18,6 +18,7 @@
 #include "../../include/bolt3.h"
 #include "common.cuh"
 #include "stl_select.h"
+#include "tc5.cuh"
 
 #include <cstddef>
 #include <type_traits>
@@ -46,6 +47,9 @@ struct Smem {
   int n_merged;
   b3sel::KV selA[128], selB[128];
   alignas(16) uint32_t keys[2][128];   // ranking scratch of the two thread groups (read as uint4)
+  unsigned char dirty[S];   // slots whose key or mean position changed this step
+  int dlist[S], n_dirty;
+  uint32_t tbase;           // tensor memory holding RoPE(ak, pm) between steps
 };
 static_assert(offsetof(Smem<128>, keys) % 16 == 0 && offsetof(Smem<64>, keys) % 16 == 0,
               "group_rank reads the ranking keys 16 bytes at a time");
@@ -323,24 +327,64 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
   }
   __syncthreads();
 
-  // RoPE(ak, pm) of the current bank into x2 (bolt3.py:17-20 in the storage dtype)
-  auto compute_kread = [&]() {
-    for (int i = tid; i < S * (HD / 2); i += NT) {
-      const int s = i / (HD / 2), d = i % (HD / 2);
-      const float ang = __fmul_rn(sm.pm[s], a.inv_freq[d]);
-      float sn, cs;
-      sincosf(ang, &sn, &cs);
-      cs = rbf(cs); sn = rbf(sn);
-      const float x0 = bf2f(sm.ak[swz<HD>(s, d)]);
-      const float x1 = bf2f(sm.ak[swz<HD>(s, d + HD / 2)]);
-      const float o0 = rbf(__fadd_rn(rbf(__fmul_rn(x0, cs)), rbf(__fmul_rn(-x1, sn))));
-      const float o1 = rbf(__fadd_rn(rbf(__fmul_rn(x1, cs)), rbf(__fmul_rn(x0, sn))));
-      sm.x2[swz<HD>(s, d)] = __float2bfloat16_rn(o0);
-      sm.x2[swz<HD>(s, d + HD / 2)] = __float2bfloat16_rn(o1);
+  // RoPE(ak, pm) of slots slot_of(0 .. n_slots-1) into x2 (bolt3.py:17-20 in the storage dtype: cos
+  // and sin rounded, every product and sum rounded), two frequencies per item so that each pair of
+  // roundings is one conversion
+  auto rope_slots = [&](int n_slots, auto slot_of) {
+    for (int i = tid; i < n_slots * (HD / 4); i += NT) {
+      const int s = slot_of(i / (HD / 4)), d = (i % (HD / 4)) * 2;
+      float sn0, cs0, sn1, cs1;
+      sincosf(__fmul_rn(sm.pm[s], a.inv_freq[d]), &sn0, &cs0);
+      sincosf(__fmul_rn(sm.pm[s], a.inv_freq[d + 1]), &sn1, &cs1);
+      uint32_t t;
+      const float2 cs = rbf2(cs0, cs1, t), sn = rbf2(sn0, sn1, t);
+      const float2 x0 = unpack_bf16(*reinterpret_cast<const uint32_t*>(&sm.ak[swz<HD>(s, d)]));
+      const float2 x1 = unpack_bf16(*reinterpret_cast<const uint32_t*>(&sm.ak[swz<HD>(s, d + HD / 2)]));
+      const float2 a0 = rbf2(__fmul_rn(x0.x, cs.x), __fmul_rn(x0.y, cs.y), t);
+      const float2 b0 = rbf2(__fmul_rn(-x1.x, sn.x), __fmul_rn(-x1.y, sn.y), t);
+      const float2 a1 = rbf2(__fmul_rn(x1.x, cs.x), __fmul_rn(x1.y, cs.y), t);
+      const float2 b1 = rbf2(__fmul_rn(x0.x, sn.x), __fmul_rn(x0.y, sn.y), t);
+      *reinterpret_cast<uint32_t*>(&sm.x2[swz<HD>(s, d)]) = pack_bf16(__fadd_rn(a0.x, b0.x), __fadd_rn(a0.y, b0.y));
+      *reinterpret_cast<uint32_t*>(&sm.x2[swz<HD>(s, d + HD / 2)]) =
+          pack_bf16(__fadd_rn(a1.x, b1.x), __fadd_rn(a1.y, b1.y));
     }
   };
-  compute_kread();
+  // x2 <-> tensor memory between steps (x2 is scratch inside a step): warp w moves row
+  // 32 * (w % 4) + lane (its TMEM lane), half w / 4 of the columns
+  constexpr int NW2 = HD / 4;  // 32-bit words per half row
+  const int x2_row = 32 * (warp & 3) + lane, x2_half = warp >> 2;
+  auto x2_taddr = [&]() { return sm.tbase + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(x2_half * NW2); };
+  auto x2_save = [&]() {
+    uint32_t w[NW2];
+#pragma unroll
+    for (int q = 0; q < NW2 / 4; ++q) {
+      const uint4 u = *reinterpret_cast<const uint4*>(&sm.x2[swz<HD>(x2_row, x2_half * (HD / 2) + q * 8)]);
+      w[4 * q] = u.x; w[4 * q + 1] = u.y; w[4 * q + 2] = u.z; w[4 * q + 3] = u.w;
+    }
+    if constexpr (NW2 == 32) tc5::st32(x2_taddr(), w);
+    else tc5::st16(x2_taddr(), w);
+    tc5::st_wait();
+  };
+  auto x2_restore = [&]() {
+    uint32_t w[NW2];
+    tc5::ld_cols(x2_taddr(), w);
+    tc5::ld_wait();
+#pragma unroll
+    for (int q = 0; q < NW2 / 4; ++q)
+      *reinterpret_cast<uint4*>(&sm.x2[swz<HD>(x2_row, x2_half * (HD / 2) + q * 8)]) =
+          make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  };
+  if (warp == 0) {
+    tc5::tmem_alloc(&sm.tbase, 64);
+    tc5::tmem_relinquish();
+  }
+  for (int s = tid; s < S; s += NT) sm.dirty[s] = 0;
+  tc5::fence_before_sync();
   __syncthreads();
+  tc5::fence_after_sync();
+  rope_slots(S, [](int i) { return i; });
+  __syncthreads();
+  x2_save();
 
   const bf16* g_kr = reinterpret_cast<const bf16*>(a.kr) + (int64_t)c * a.chain_tokens * HD;
   const bf16* g_kp = reinterpret_cast<const bf16*>(a.kp) + (int64_t)c * a.chain_tokens * HD;
@@ -548,6 +592,7 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
           sm.mass[s] = 1.f;
           sm.util[s] = sm.rel[j];
           sm.act[s] = 1;
+          sm.dirty[s] = 1;
         }
       }
       n_filled += m;
@@ -634,6 +679,7 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
           if (lane == 0) {
             sm.pm[s] = __fdiv_rn(__fadd_rn(__fmul_rn(ms, sm.pm[s]), ps), nm);
             sm.mass[s] = nm;
+            sm.dirty[s] = 1;
             sm.na[s] = sqrtf(aa);
             sm.rna[s] = 1.0f / fmaxf(sm.na[s], 1e-12f);
           }
@@ -696,6 +742,7 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
           sm.mass[s] = 1.f;
           sm.util[s] = sm.rel[j];
           sm.ins[j] = 1;
+          sm.dirty[s] = 1;
         }
       }
       __syncthreads();
@@ -788,7 +835,21 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
     // ---- state the attention of a later chunk reads: RoPE(ak, pm), av, mass, act, M_res. The
     // shared-memory tiles already have the operand layout the attention's tensor cores read, so
     // the snapshot is a handful of bulk copies: k_read (x2), av, M_hi (rebuilt in x1), M_lo (kr).
-    compute_kread();
+    // k_read: last step's, from tensor memory, with the slots this step changed recomputed.
+    x2_restore();
+    if (warp == 0) {
+      int base = 0;
+      for (int s0 = 0; s0 < S; s0 += 32) {
+        const bool dd = sm.dirty[s0 + lane] != 0;
+        const unsigned bal = __ballot_sync(0xffffffffu, dd);
+        if (dd) sm.dlist[base + __popc(bal & ((1u << lane) - 1))] = s0 + lane;
+        base += __popc(bal);
+        sm.dirty[s0 + lane] = 0;
+      }
+      if (lane == 0) sm.n_dirty = base;
+    }
+    __syncthreads();
+    rope_slots(sm.n_dirty, [&](int i) { return sm.dlist[i]; });
     if (a.snap_ak_rope && m_owner) {
 #pragma unroll
       for (int n = 0; n < HD / 8; ++n) {
@@ -804,6 +865,7 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
     }
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
     __syncthreads();
+    x2_save();
     if (a.snap_ak_rope) {
       const int64_t sn = (int64_t)c * a.snap_cap + a.snap0 + st;
       constexpr uint32_t kTile = 128 * HD * 2;
@@ -846,6 +908,10 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
     a.n_filled[c] = n_filled;
     asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");  // snapshot copies have landed
   }
+  tc5::fence_before_sync();
+  __syncthreads();
+  tc5::fence_after_sync();
+  if (warp == 0) tc5::tmem_dealloc(sm.tbase, 64);
 }
 
 template <int HD>
