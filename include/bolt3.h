@@ -80,7 +80,8 @@ int bolt3_prep(const bolt3_prep_args* a, void* stream);
  *   into bf16 hi then lo terms, each an image with R = HD rows d and columns e. The final bank
  *   (ak, av, ak_rope, m_res) is written in the plain row-major layouts listed at the top.
  * `ak_rope` (optional) receives RoPE(ak, pm) of the final bank. `status` (optional, device int)
- * is OR-ed with 1 when a kernel-side bounds check of the tie-order emulation fires. */
+ * is OR-ed with 1 when a kernel-side bounds check of the tie-order emulation fires, and with 4 when
+ * a bounded wait for a tensor-core product expired. */
 typedef struct bolt3_consolidate_args {
   int n_chains, hkv, HD;
   void* ak; void* av; void* ak_rope;

@@ -1,20 +1,22 @@
 // Phase B: the sequential attractor-bank / M_res consolidation scan.
 //
 // One CTA (8 warps) owns one chain (sequence b, KV head h) for all of its consolidation steps, so
-// the bank never leaves the SM between steps: ak / av live in shared memory, M_res lives in the
-// registers of warps 0..HD/16-1 as the accumulator fragments of its own update GEMM. Every
-// contraction of _consolidate_functional (vsa_lm/config/bolt3.py:68-192) is a 128 x 128 x HD
-// tensor-core product with bf16 operands, fp32 accumulation:
+// the bank never leaves the SM between steps: ak / av live in shared memory, M_res (fp32) lives in
+// tensor memory as the accumulator of its own update. Every contraction of _consolidate_functional
+// (vsa_lm/config/bolt3.py:68-192) is a tcgen05.mma over 128-byte-swizzled shared-memory tiles with
+// bf16 operands and fp32 accumulation in tensor memory:
 //   sc   = kp . RoPE(ak, pm)^T            (:97-100, :169-171)   exact bf16 products
-//   v^   = softmax(sc).bf16 @ av          (:101, :172)
+//   v^   = softmax(sc).bf16 @ av          (:101, :172)          P written to tensor memory
 //   cos  = kr . ak^T / (|kr| |ak|)        (:104-106, :175-176)
 //   pair = ak . ak^T / (|ak| |ak|)        (:128-130)
 //   gram = |kr . kr^T| / (|kr| |kr|)      (:156-157)
 //   k^ M = kr . (M_hi + M_lo) / |kr|      (:159)   M split into two bf16 terms: ~2^-17 relative
 //   M   <- gamma M + kr^T . (E_hi + E_lo)  (:162)   E = err / |kr|, split the same way
-// Rankings count, per entry, the entries that sort before it (128 threads, one entry each); when
-// exactly equal keys decide the result the CPU torch.topk order is reproduced with the emulation in
-// stl_select.h (bolt3.py:133-134, 183).
+// Thread 0 issues the MMAs; the row-wise work that follows each one (softmax, argmax, maxima, sums,
+// the error rows) reads tensor-memory lanes, one thread per row and column half. Rankings count,
+// per entry, the entries that sort before it (128 threads, one entry each); when exactly equal keys
+// decide the result the CPU torch.topk order is reproduced with the emulation in stl_select.h
+// (bolt3.py:133-134, 183).
 #include "../../include/bolt3.h"
 #include "common.cuh"
 #include "stl_select.h"
@@ -33,15 +35,18 @@ constexpr int NT = 256;  // threads per CTA
 constexpr float SIM_K = 0.88f, SIM_V = 0.80f, GAMMA_U = 0.995f;  // bolt3.py:31
 
 template <int HD>
-struct Smem {
-  bf16 ak[S * HD];
+struct __align__(1024) Smem {
+  bf16 ak[S * HD];     // every tile: 128 rows, 128-byte-swizzled blocks of 64 columns (tcgen05 operands)
   bf16 av[S * HD];
   bf16 kr[CC * HD];
   bf16 vv[CC * HD];
   bf16 x1[128 * HD];   // kp, then M_hi, then E_hi
   bf16 x2[128 * HD];   // RoPE(ak, pm), then M_lo, then E_lo
+  bf16 zpad[HD == 64 ? 128 * 64 : 8];  // HD = 64: zero rows 64..127 of the M update's A operand
   float mass[S], util[S], pm[S], keep[S], na[S], rna[S], bias[S], botv[S];
-  float rel[CC], score[CC], bsk[CC], beta[CC], nk[CC], rnk[CC], nv[CC], pos[CC], wgt[CC], topv[CC];
+  float rel[CC], score[CC], bsk[CC], beta[CC], nk[CC], rnk[CC], nv[CC], pos[CC], wgt[CC], topv[CC], bsafe[CC];
+  float red[2][128], red2[2][128];  // per-row partial results of the two column halves
+  int redi[2][128];
   int best[CC], tops[CC], bots[S], mlist[CC];
   unsigned char act[S], mrg[CC], ins[CC];
   int n_merged;
@@ -49,7 +54,8 @@ struct Smem {
   alignas(16) uint32_t keys[2][128];   // ranking scratch of the two thread groups (read as uint4)
   unsigned char dirty[S];   // slots whose key or mean position changed this step
   int dlist[S], n_dirty;
-  uint32_t tbase;           // tensor memory holding RoPE(ak, pm) between steps
+  uint64_t bar[2];          // MMA completion: results in D1 (bar[0]); in D2 or M (bar[1])
+  uint32_t tbase;
 };
 static_assert(offsetof(Smem<128>, keys) % 16 == 0 && offsetof(Smem<64>, keys) % 16 == 0,
               "group_rank reads the ranking keys 16 bytes at a time");
@@ -119,77 +125,6 @@ B3_DEV float half_row_dot(const bf16* x, const bf16* y, int r, int half) {
     }
   }
   return acc;
-}
-
-// ------------------------------------------------------------------------------------------
-// warp-level GEMMs on 16 rows (r0 .. r0+15); fragments follow mma.m16n8k16 layouts
-
-// acc[16 x 128] = A[r0.., K] . B[0..128, K]^T   (A, B swizzled tiles with K = HD columns)
-template <int HD>
-B3_DEV void gemm_nt(float (&acc)[16][4], const bf16* A, int r0, const bf16* B, int lane) {
-#pragma unroll
-  for (int n = 0; n < 16; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
-#pragma unroll
-  for (int kt = 0; kt < HD / 16; ++kt) {
-    uint32_t a[4];
-    ldsm_x4(a, A + swz<HD>(r0 + (lane & 15), kt * 16 + (lane >> 4) * 8));
-#pragma unroll
-    for (int np = 0; np < 8; ++np) {
-      uint32_t b[4];
-      ldsm_x4(b, B + swz<HD>(np * 16 + (lane & 7) + (lane >> 4) * 8, kt * 16 + ((lane >> 3) & 1) * 8));
-      mma16816(acc[2 * np], a, b[0], b[1]);
-      mma16816(acc[2 * np + 1], a, b[2], b[3]);
-    }
-  }
-}
-
-// acc[16 x HD] += P[16 x 128] . B[128 x HD]   (P as A fragments, B swizzled row-major [128][HD])
-template <int HD>
-B3_DEV void gemm_pv(float (&acc)[HD / 8][4], const uint32_t (&pa)[8][4], const bf16* B, int lane) {
-#pragma unroll
-  for (int kt = 0; kt < 8; ++kt) {
-#pragma unroll
-    for (int np = 0; np < HD / 16; ++np) {
-      uint32_t b[4];
-      ldsm_x4_t(b, B + swz<HD>(kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, np * 16 + (lane >> 4) * 8));
-      mma16816(acc[2 * np], pa[kt], b[0], b[1]);
-      mma16816(acc[2 * np + 1], pa[kt], b[2], b[3]);
-    }
-  }
-}
-
-// acc[16 x HD] += A[r0.., 0..HD] . B[HD x HD]   (A swizzled [128][HD], B swizzled [HD][HD])
-template <int HD>
-B3_DEV void gemm_nn(float (&acc)[HD / 8][4], const bf16* A, int r0, const bf16* B, int lane) {
-#pragma unroll
-  for (int kt = 0; kt < HD / 16; ++kt) {
-    uint32_t a[4];
-    ldsm_x4(a, A + swz<HD>(r0 + (lane & 15), kt * 16 + (lane >> 4) * 8));
-#pragma unroll
-    for (int np = 0; np < HD / 16; ++np) {
-      uint32_t b[4];
-      ldsm_x4_t(b, B + swz<HD>(kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, np * 16 + (lane >> 4) * 8));
-      mma16816(acc[2 * np], a, b[0], b[1]);
-      mma16816(acc[2 * np + 1], a, b[2], b[3]);
-    }
-  }
-}
-
-// acc[16 x HD] += A^T[m0.., 0..128] . B[128 x HD]   (A stored [128 tokens][HD], read transposed)
-template <int HD>
-B3_DEV void gemm_tn(float (&acc)[HD / 8][4], const bf16* A, int m0, const bf16* B, int lane) {
-#pragma unroll 2
-  for (int kt = 0; kt < 8; ++kt) {
-    uint32_t a[4];
-    ldsm_x4_t(a, A + swz<HD>(kt * 16 + (lane & 7) + (lane >> 4) * 8, m0 + ((lane >> 3) & 1) * 8));
-#pragma unroll
-    for (int np = 0; np < HD / 16; ++np) {
-      uint32_t b[4];
-      ldsm_x4_t(b, B + swz<HD>(kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, np * 16 + (lane >> 4) * 8));
-      mma16816(acc[2 * np], a, b[0], b[1]);
-      mma16816(acc[2 * np + 1], a, b[2], b[3]);
-    }
-  }
 }
 
 // ------------------------------------------------------------------------------------------
@@ -269,62 +204,119 @@ B3_DEV void copy_row_part(bf16* dst, int sd, const bf16* src, int ss, int lane) 
 
 // ------------------------------------------------------------------------------------------
 
+// tensor-memory columns: M_res, the RoPE(ak, pm) cache, two fp32 result tiles, P (bf16 pairs)
+constexpr uint32_t TM_M = 0, TM_X2 = 128, TM_D1 = 192, TM_D2 = 320, TM_P = 448;
+constexpr uint32_t kWaitIters = 1u << 24;
+
 template <int HD>
 __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_args a) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  Smem<HD>& sm = *reinterpret_cast<Smem<HD>*>(smem_raw);
+  extern __shared__ unsigned char smem_raw[];
+  Smem<HD>& sm = *reinterpret_cast<Smem<HD>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int c = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, t4 = lane & 3;
-  const int r0 = warp * 16;
   const int h = c % a.hkv;
   const float kappa = a.kappa[h];
   const float gam = a.gamma[h];
   constexpr float scale = HD == 128 ? 0.08838834764831845f : 0.125f;  // fp32(HD ** -0.5)
-  const bool m_owner = warp < HD / 16;
+  // row view of tensor memory: this thread owns row (lane) `row` and column half `half`
+  const int row = 32 * (warp & 3) + lane, half = warp >> 2;
+  const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+  constexpr int HH = HD / 2;  // columns of an HD-wide tile per half
 
   bf16* g_ak = reinterpret_cast<bf16*>(a.ak) + (int64_t)c * S * HD;
   bf16* g_av = reinterpret_cast<bf16*>(a.av) + (int64_t)c * S * HD;
   float* g_m = a.m_res + (int64_t)c * HD * HD;
 
-  // ---- load or initialise the bank (bolt3.py:83-92)
+  // ---- tensor memory, barriers
+  if (warp == 0) {
+    tc5::tmem_alloc(&sm.tbase, 512);
+    tc5::tmem_relinquish();
+  }
+  if (tid == 0) {
+    tc5::mbar_init(&sm.bar[0], 1);
+    tc5::mbar_init(&sm.bar[1], 1);
+    tc5::mbar_fence_init();
+  }
+  if constexpr (HD == 64)
+    for (int i = tid; i < 128 * 64 / 8; i += NT) reinterpret_cast<uint4*>(sm.zpad)[i] = make_uint4(0, 0, 0, 0);
+  for (int s2 = tid; s2 < S; s2 += NT) sm.dirty[s2] = 0;
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+  tc5::fence_before_sync();
+  __syncthreads();
+  tc5::fence_after_sync();
+  const uint32_t tb = sm.tbase;
+  uint32_t ph[2] = {0u, 0u};
+  bool timed_out = false;
+  auto wait_mma = [&](int i) {
+    if (!tc5::mbar_wait(&sm.bar[i], ph[i], kWaitIters)) timed_out = true;
+    ph[i] ^= 1u;
+    tc5::fence_after_sync();
+  };
+  // every thread's shared-memory and tensor-memory writes are visible to the MMAs issued next
+  auto handoff = [&]() {
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+    tc5::fence_before_sync();
+    __syncthreads();
+    tc5::fence_after_sync();
+  };
+  // 32-column tensor-memory access of this thread's row
+  auto tld = [&](uint32_t col, uint32_t (&v)[32]) { tc5::ld32(tb + lane_off + col, v); };
+  auto tst = [&](uint32_t col, const uint32_t (&v)[32]) { tc5::st32(tb + lane_off + col, v); };
+
+  // ---- MMA issue (thread 0). Tiles are [128 rows][HD] in 64-column blocks of 16 KB.
+  const uint32_t s_ak = tc5::smem_u32(sm.ak), s_av = tc5::smem_u32(sm.av), s_kr = tc5::smem_u32(sm.kr);
+  const uint32_t s_x1 = tc5::smem_u32(sm.x1), s_x2 = tc5::smem_u32(sm.x2);
+  // D[128 x 128] = A . B^T, both K-major (K = HD)
+  auto mma_abt = [&](uint32_t dcol, uint32_t sa, uint32_t sb) {
+    constexpr uint32_t id = tc5::idesc_bf16(128, 128, false, false);
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
+      tc5::mma_ss(tb + dcol, tc5::sdesc(sa + off, 16, 1024), tc5::sdesc(sb + off, 16, 1024), id, ks > 0);
+    }
+  };
+  // D[128 x HD] (+)= A . B, A K-major [128][HD], B [HD rows = K][HD columns = N] (MN-major)
+  auto mma_ab = [&](uint32_t dcol, uint32_t sa, uint32_t sb, bool acc) {
+    constexpr uint32_t id = tc5::idesc_bf16(128, HD, false, true);
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
+      tc5::mma_ss(tb + dcol, tc5::sdesc(sa + off, 16, 1024), tc5::sdesc(sb + ks * 2048, 16384, 1024), id,
+                  acc || ks > 0);
+    }
+  };
+
+  // ---- load or initialise the bank (bolt3.py:83-92); M_res into tensor memory rows d
   int n_filled;
-  float mr[HD / 8][4];
   if (a.init_blank) {
     n_filled = 0;
     for (int i = tid; i < S * HD / 8; i += NT) {
       *reinterpret_cast<uint4*>(sm.ak + i * 8) = make_uint4(0, 0, 0, 0);
       *reinterpret_cast<uint4*>(sm.av + i * 8) = make_uint4(0, 0, 0, 0);
     }
-    for (int s = tid; s < S; s += NT) {
-      sm.mass[s] = 1.f; sm.util[s] = 0.f; sm.pm[s] = 0.f; sm.act[s] = 0;
+    for (int s2 = tid; s2 < S; s2 += NT) {
+      sm.mass[s2] = 1.f; sm.util[s2] = 0.f; sm.pm[s2] = 0.f; sm.act[s2] = 0;
     }
-#pragma unroll
-    for (int n = 0; n < HD / 8; ++n) mr[n][0] = mr[n][1] = mr[n][2] = mr[n][3] = 0.f;
   } else {
     n_filled = a.n_filled[c];
     g2s_rows<HD>(sm.ak, g_ak, S);
     g2s_rows<HD>(sm.av, g_av, S);
     cp_async_commit();
-    for (int s = tid; s < S; s += NT) {
-      sm.mass[s] = a.mass[(int64_t)c * S + s];
-      sm.util[s] = a.util[(int64_t)c * S + s];
-      sm.pm[s] = a.pm[(int64_t)c * S + s];
-      sm.act[s] = a.act[(int64_t)c * S + s];
-    }
-    if (m_owner) {
-#pragma unroll
-      for (int n = 0; n < HD / 8; ++n) {
-        const float2 u = *reinterpret_cast<const float2*>(g_m + (r0 + g) * HD + n * 8 + 2 * t4);
-        const float2 w = *reinterpret_cast<const float2*>(g_m + (r0 + g + 8) * HD + n * 8 + 2 * t4);
-        mr[n][0] = u.x; mr[n][1] = u.y; mr[n][2] = w.x; mr[n][3] = w.y;
-      }
-    } else {
-#pragma unroll
-      for (int n = 0; n < HD / 8; ++n) mr[n][0] = mr[n][1] = mr[n][2] = mr[n][3] = 0.f;
+    for (int s2 = tid; s2 < S; s2 += NT) {
+      sm.mass[s2] = a.mass[(int64_t)c * S + s2];
+      sm.util[s2] = a.util[(int64_t)c * S + s2];
+      sm.pm[s2] = a.pm[(int64_t)c * S + s2];
+      sm.act[s2] = a.act[(int64_t)c * S + s2];
     }
     cp_async_wait<0>();
   }
+#pragma unroll
+  for (int q = 0; q < HH / 32; ++q) {
+    uint32_t v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      v[j] = (a.init_blank || row >= HD) ? 0u : __float_as_uint(g_m[(int64_t)row * HD + half * HH + q * 32 + j]);
+    tst(TM_M + half * HH + q * 32, v);
+  }
+  tc5::st_wait();
   __syncthreads();
 
   // RoPE(ak, pm) of slots slot_of(0 .. n_slots-1) into x2 (bolt3.py:17-20 in the storage dtype: cos
@@ -332,56 +324,70 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
   // roundings is one conversion
   auto rope_slots = [&](int n_slots, auto slot_of) {
     for (int i = tid; i < n_slots * (HD / 4); i += NT) {
-      const int s = slot_of(i / (HD / 4)), d = (i % (HD / 4)) * 2;
+      const int s2 = slot_of(i / (HD / 4)), d = (i % (HD / 4)) * 2;
       float sn0, cs0, sn1, cs1;
-      sincosf(__fmul_rn(sm.pm[s], a.inv_freq[d]), &sn0, &cs0);
-      sincosf(__fmul_rn(sm.pm[s], a.inv_freq[d + 1]), &sn1, &cs1);
+      sincosf(__fmul_rn(sm.pm[s2], a.inv_freq[d]), &sn0, &cs0);
+      sincosf(__fmul_rn(sm.pm[s2], a.inv_freq[d + 1]), &sn1, &cs1);
       uint32_t t;
       const float2 cs = rbf2(cs0, cs1, t), sn = rbf2(sn0, sn1, t);
-      const float2 x0 = unpack_bf16(*reinterpret_cast<const uint32_t*>(&sm.ak[swz<HD>(s, d)]));
-      const float2 x1 = unpack_bf16(*reinterpret_cast<const uint32_t*>(&sm.ak[swz<HD>(s, d + HD / 2)]));
+      const float2 x0 = unpack_bf16(*reinterpret_cast<const uint32_t*>(&sm.ak[swz<HD>(s2, d)]));
+      const float2 x1 = unpack_bf16(*reinterpret_cast<const uint32_t*>(&sm.ak[swz<HD>(s2, d + HD / 2)]));
       const float2 a0 = rbf2(__fmul_rn(x0.x, cs.x), __fmul_rn(x0.y, cs.y), t);
       const float2 b0 = rbf2(__fmul_rn(-x1.x, sn.x), __fmul_rn(-x1.y, sn.y), t);
       const float2 a1 = rbf2(__fmul_rn(x1.x, cs.x), __fmul_rn(x1.y, cs.y), t);
       const float2 b1 = rbf2(__fmul_rn(x0.x, sn.x), __fmul_rn(x0.y, sn.y), t);
-      *reinterpret_cast<uint32_t*>(&sm.x2[swz<HD>(s, d)]) = pack_bf16(__fadd_rn(a0.x, b0.x), __fadd_rn(a0.y, b0.y));
-      *reinterpret_cast<uint32_t*>(&sm.x2[swz<HD>(s, d + HD / 2)]) =
+      *reinterpret_cast<uint32_t*>(&sm.x2[swz<HD>(s2, d)]) = pack_bf16(__fadd_rn(a0.x, b0.x), __fadd_rn(a0.y, b0.y));
+      *reinterpret_cast<uint32_t*>(&sm.x2[swz<HD>(s2, d + HD / 2)]) =
           pack_bf16(__fadd_rn(a1.x, b1.x), __fadd_rn(a1.y, b1.y));
     }
   };
-  // x2 <-> tensor memory between steps (x2 is scratch inside a step): warp w moves row
-  // 32 * (w % 4) + lane (its TMEM lane), half w / 4 of the columns
-  constexpr int NW2 = HD / 4;  // 32-bit words per half row
-  const int x2_row = 32 * (warp & 3) + lane, x2_half = warp >> 2;
-  auto x2_taddr = [&]() { return sm.tbase + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(x2_half * NW2); };
+  // x2 <-> tensor memory between steps (x2 is scratch inside a step): this thread moves its row,
+  // its half of the columns (HD/4 32-bit words)
+  constexpr int NW2 = HD / 4;
   auto x2_save = [&]() {
     uint32_t w[NW2];
 #pragma unroll
     for (int q = 0; q < NW2 / 4; ++q) {
-      const uint4 u = *reinterpret_cast<const uint4*>(&sm.x2[swz<HD>(x2_row, x2_half * (HD / 2) + q * 8)]);
+      const uint4 u = *reinterpret_cast<const uint4*>(&sm.x2[swz<HD>(row, half * HH + q * 8)]);
       w[4 * q] = u.x; w[4 * q + 1] = u.y; w[4 * q + 2] = u.z; w[4 * q + 3] = u.w;
     }
-    if constexpr (NW2 == 32) tc5::st32(x2_taddr(), w);
-    else tc5::st16(x2_taddr(), w);
+    if constexpr (NW2 == 32) tc5::st32(tb + lane_off + TM_X2 + half * NW2, w);
+    else tc5::st16(tb + lane_off + TM_X2 + half * NW2, w);
     tc5::st_wait();
   };
   auto x2_restore = [&]() {
     uint32_t w[NW2];
-    tc5::ld_cols(x2_taddr(), w);
+    tc5::ld_cols(tb + lane_off + TM_X2 + half * NW2, w);
     tc5::ld_wait();
 #pragma unroll
     for (int q = 0; q < NW2 / 4; ++q)
-      *reinterpret_cast<uint4*>(&sm.x2[swz<HD>(x2_row, x2_half * (HD / 2) + q * 8)]) =
+      *reinterpret_cast<uint4*>(&sm.x2[swz<HD>(row, half * HH + q * 8)]) =
           make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
   };
-  if (warp == 0) {
-    tc5::tmem_alloc(&sm.tbase, 64);
-    tc5::tmem_relinquish();
-  }
-  for (int s = tid; s < S; s += NT) sm.dirty[s] = 0;
-  tc5::fence_before_sync();
-  __syncthreads();
-  tc5::fence_after_sync();
+  // M_res (tensor memory) split into two bf16 terms, written as [d][e] operand images
+  auto m_split = [&](bf16* hi_t, bf16* lo_t) {
+    if (row < HD) {
+#pragma unroll
+      for (int q = 0; q < HH / 32; ++q) {
+        uint32_t v[32];
+        tld(TM_M + half * HH + q * 32, v);
+        tc5::ld_wait();
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t hw[4], lw[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float m0 = __uint_as_float(v[ch * 8 + 2 * u]), m1 = __uint_as_float(v[ch * 8 + 2 * u + 1]);
+            const float2 hh = rbf2(m0, m1, hw[u]);
+            lw[u] = pack_bf16(m0 - hh.x, m1 - hh.y);
+          }
+          const int col = half * HH + q * 32 + ch * 8;
+          *reinterpret_cast<uint4*>(&hi_t[swz<HD>(row, col)]) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          *reinterpret_cast<uint4*>(&lo_t[swz<HD>(row, col)]) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+      }
+    }
+  };
   rope_slots(S, [](int i) { return i; });
   __syncthreads();
   x2_save();
@@ -415,19 +421,19 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
       sm.mrg[j] = 0;
       sm.ins[j] = 0;
     }
-    for (int s = tid; s < S; s += NT) sm.util[s] = __fmul_rn(sm.util[s], GAMMA_U);  // :94
+    for (int s2 = tid; s2 < S; s2 += NT) sm.util[s2] = __fmul_rn(sm.util[s2], GAMMA_U);  // :94
     cp_async_wait<0>();
-    __syncthreads();
+    handoff();
     {
       // row norms of the chunk keys / values and of the slot keys: two threads per row
-      const int r = tid >> 1, half = tid & 1;
-      float kk = half_row_dot<HD>(sm.kr, sm.kr, r, half);
-      float vv2 = half_row_dot<HD>(sm.vv, sm.vv, r, half);
-      float aa = half_row_dot<HD>(sm.ak, sm.ak, r, half);
+      const int r = tid >> 1, hf = tid & 1;
+      float kk = half_row_dot<HD>(sm.kr, sm.kr, r, hf);
+      float vv2 = half_row_dot<HD>(sm.vv, sm.vv, r, hf);
+      float aa = half_row_dot<HD>(sm.ak, sm.ak, r, hf);
       kk += __shfl_xor_sync(0xffffffffu, kk, 1);
       vv2 += __shfl_xor_sync(0xffffffffu, vv2, 1);
       aa += __shfl_xor_sync(0xffffffffu, aa, 1);
-      if (half == 0) {
+      if (hf == 0) {
         sm.nk[r] = sqrtf(kk);
         sm.nv[r] = sqrtf(vv2);
         sm.na[r] = sqrtf(aa);
@@ -436,9 +442,20 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
         sm.rna[r] = 1.0f / fmaxf(sm.na[r], 1e-12f);
       }
     }
+    const bool full = n_filled >= S;
+    if (n_filled > 0) {
+      // attractor prediction: sc = kp . RoPE(ak)^T into D1
+      if (tid == 0) {
+        mma_abt(TM_D1, s_x1, s_x2);
+        tc5::commit(&sm.bar[0]);
+      }
+      for (int s2 = tid; s2 < S; s2 += NT) {
+        const float lm = logf(fmaxf(sm.mass[s2], 1.0f));
+        sm.bias[s2] = full ? __fmul_rn(kappa, lm) : lm;
+      }
+    }
     __syncthreads();
 
-    const bool full = n_filled >= S;
     if (n_filled == 0) {
       // ---- first fill: score = unbiased var(normalize(v)) (bolt3.py:180). The normalised values
       // are fp32 as in the reference; mean and variance accumulate in fp64 (the CPU reference's
@@ -466,106 +483,113 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
       }
       __syncthreads();
     } else {
-      // ---- attractor prediction of each token's value (:97-103 / :169-174)
-      for (int s = tid; s < S; s += NT) {
-        const float lm = logf(fmaxf(sm.mass[s], 1.0f));
-        sm.bias[s] = full ? __fmul_rn(kappa, lm) : lm;
-      }
-      __syncthreads();
-      uint32_t pa[8][4];
+      // ---- attractor prediction of each token's value (:97-103 / :169-174): softmax over the
+      // slots, P = bf16(p) into tensor memory
+      wait_mma(0);
       {
-        float acc[16][4];
-        gemm_nt<HD>(acc, sm.x1, r0, sm.x2, lane);
-        float mx0 = neg_inf(), mx1 = neg_inf();
-#pragma unroll
-        for (int n = 0; n < 16; ++n) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int col = n * 8 + 2 * t4 + (q & 1);
-            float sc = __fadd_rn(__fmul_rn(acc[n][q], scale), sm.bias[col]);
-            if (!full && !sm.act[col]) sc = -1e9f;
-            acc[n][q] = sc;
-          }
-          mx0 = fmaxf(mx0, fmaxf(acc[n][0], acc[n][1]));
-          mx1 = fmaxf(mx1, fmaxf(acc[n][2], acc[n][3]));
-        }
-        mx0 = quad_max(mx0);
-        mx1 = quad_max(mx1);
-        float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-        for (int n = 0; n < 16; ++n) {
-          acc[n][0] = expf(acc[n][0] - mx0); acc[n][1] = expf(acc[n][1] - mx0);
-          acc[n][2] = expf(acc[n][2] - mx1); acc[n][3] = expf(acc[n][3] - mx1);
-          s0 += acc[n][0] + acc[n][1];
-          s1 += acc[n][2] + acc[n][3];
-        }
-        const float i0 = 1.0f / quad_sum(s0), i1 = 1.0f / quad_sum(s1);
-#pragma unroll
-        for (int kt = 0; kt < 8; ++kt) {
-          pa[kt][0] = pack_bf16(__fmul_rn(acc[2 * kt][0], i0), __fmul_rn(acc[2 * kt][1], i0));
-          pa[kt][1] = pack_bf16(__fmul_rn(acc[2 * kt][2], i1), __fmul_rn(acc[2 * kt][3], i1));
-          pa[kt][2] = pack_bf16(__fmul_rn(acc[2 * kt + 1][0], i0), __fmul_rn(acc[2 * kt + 1][1], i0));
-          pa[kt][3] = pack_bf16(__fmul_rn(acc[2 * kt + 1][2], i1), __fmul_rn(acc[2 * kt + 1][3], i1));
-        }
-      }
-      {
-        float acc2[HD / 8][4];
-#pragma unroll
-        for (int n = 0; n < HD / 8; ++n) acc2[n][0] = acc2[n][1] = acc2[n][2] = acc2[n][3] = 0.f;
-        gemm_pv<HD>(acc2, pa, sm.av, lane);
-        float e0 = 0.f, e1 = 0.f;
-#pragma unroll
-        for (int n = 0; n < HD / 8; ++n) {
-          const int col = n * 8 + 2 * t4;
-          const float2 va = unpack_bf16(*reinterpret_cast<const uint32_t*>(&sm.vv[swz<HD>(r0 + g, col)]));
-          const float2 vb = unpack_bf16(*reinterpret_cast<const uint32_t*>(&sm.vv[swz<HD>(r0 + g + 8, col)]));
-          const float v00 = va.x, v01 = va.y, v10 = vb.x, v11 = vb.y;
-          float d;
-          d = v00 - acc2[n][0]; e0 = fmaf(d, d, e0);
-          d = v01 - acc2[n][1]; e0 = fmaf(d, d, e0);
-          d = v10 - acc2[n][2]; e1 = fmaf(d, d, e1);
-          d = v11 - acc2[n][3]; e1 = fmaf(d, d, e1);
-        }
-        e0 = quad_sum(e0);
-        e1 = quad_sum(e1);
-        if (t4 == 0) {
-          sm.rel[r0 + g] = __fdiv_rn(sqrtf(e0), __fadd_rn(sm.nv[r0 + g], 1e-6f));
-          sm.rel[r0 + g + 8] = __fdiv_rn(sqrtf(e1), __fadd_rn(sm.nv[r0 + g + 8], 1e-6f));
-        }
-      }
-      // ---- cosine match against the slots (:104-106, :175-177)
-      {
-        float acc[16][4];
-        gemm_nt<HD>(acc, sm.kr, r0, sm.ak, lane);
-        const float rk0 = sm.rnk[r0 + g], rk1 = sm.rnk[r0 + g + 8];
-        float b0 = neg_inf(), b1 = neg_inf();
-        int i0 = 0x7fffffff, i1 = 0x7fffffff;
-#pragma unroll
-        for (int n = 0; n < 16; ++n) {
+        float x[64];
+        {
+          uint32_t v[32];
 #pragma unroll
           for (int q = 0; q < 2; ++q) {
-            const int col = n * 8 + 2 * t4 + q;
-            const float ra = sm.rna[col];
-            float c0 = __fmul_rn(acc[n][q], __fmul_rn(rk0, ra));
-            float c1 = __fmul_rn(acc[n][2 + q], __fmul_rn(rk1, ra));
-            if (!full && !sm.act[col]) { c0 = 0.f; c1 = 0.f; }
-            if (c0 > b0) { b0 = c0; i0 = col; }
-            if (c1 > b1) { b1 = c1; i1 = col; }
+            tld(TM_D1 + half * 64 + q * 32, v);
+            tc5::ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int col = half * 64 + q * 32 + j;
+              float sc = __fadd_rn(__fmul_rn(__uint_as_float(v[j]), scale), sm.bias[col]);
+              if (!full && !sm.act[col]) sc = -1e9f;
+              x[q * 32 + j] = sc;
+            }
           }
         }
+        float mx = x[0];
 #pragma unroll
-        for (int o = 1; o <= 2; o <<= 1) {
-          const float ob0 = __shfl_xor_sync(0xffffffffu, b0, o);
-          const int oi0 = __shfl_xor_sync(0xffffffffu, i0, o);
-          const float ob1 = __shfl_xor_sync(0xffffffffu, b1, o);
-          const int oi1 = __shfl_xor_sync(0xffffffffu, i1, o);
-          if (ob0 > b0 || (ob0 == b0 && oi0 < i0)) { b0 = ob0; i0 = oi0; }
-          if (ob1 > b1 || (ob1 == b1 && oi1 < i1)) { b1 = ob1; i1 = oi1; }
+        for (int j = 1; j < 64; ++j) mx = fmaxf(mx, x[j]);
+        sm.red[half][row] = mx;
+        __syncthreads();
+        mx = fmaxf(sm.red[0][row], sm.red[1][row]);
+        float sum = 0.f;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+          x[j] = expf(x[j] - mx);
+          sum += x[j];
         }
-        if (t4 == 0) {
-          sm.bsk[r0 + g] = b0; sm.best[r0 + g] = i0;
-          sm.bsk[r0 + g + 8] = b1; sm.best[r0 + g + 8] = i1;
+        sm.red2[half][row] = sum;
+        __syncthreads();
+        const float inv = 1.0f / (sm.red2[0][row] + sm.red2[1][row]);
+        uint32_t pk[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) pk[j] = pack_bf16(__fmul_rn(x[2 * j], inv), __fmul_rn(x[2 * j + 1], inv));
+        tst(TM_P + half * 32, pk);
+        tc5::st_wait();
+      }
+      handoff();
+      if (tid == 0) {
+        // v^ = P . av into D2; cos = kr . ak^T into D1
+        constexpr uint32_t id = tc5::idesc_bf16(128, HD, false, true);
+        for (int ks = 0; ks < S / 16; ++ks)
+          tc5::mma_ts(tb + TM_D2, tb + TM_P + ks * 8, tc5::sdesc(s_av + ks * 2048, 16384, 1024), id, ks > 0);
+        tc5::commit(&sm.bar[1]);
+        mma_abt(TM_D1, s_kr, s_ak);
+        tc5::commit(&sm.bar[0]);
+      }
+      // rel_err = |v - v^| / (|v| + 1e-6)
+      wait_mma(1);
+      {
+        float e = 0.f;
+#pragma unroll
+        for (int q = 0; q < HH / 32; ++q) {
+          uint32_t v[32];
+          tld(TM_D2 + half * HH + q * 32, v);
+          tc5::ld_wait();
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) {
+            const uint4 u = *reinterpret_cast<const uint4*>(&sm.vv[swz<HD>(row, half * HH + q * 32 + ch * 8)]);
+            const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int w2 = 0; w2 < 4; ++w2) {
+              const float2 vf = unpack_bf16(uw[w2]);
+              float d = vf.x - __uint_as_float(v[ch * 8 + 2 * w2]);
+              e = fmaf(d, d, e);
+              d = vf.y - __uint_as_float(v[ch * 8 + 2 * w2 + 1]);
+              e = fmaf(d, d, e);
+            }
+          }
         }
+        sm.red[half][row] = e;
+      }
+      // cosine match against the slots (:104-106, :175-177): best slot, first index on ties
+      wait_mma(0);
+      {
+        const float rk = sm.rnk[row];
+        float b = neg_inf();
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          uint32_t v[32];
+          tld(TM_D1 + half * 64 + q * 32, v);
+          tc5::ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int col = half * 64 + q * 32 + j;
+            float cv = __fmul_rn(__uint_as_float(v[j]), __fmul_rn(rk, sm.rna[col]));
+            if (!full && !sm.act[col]) cv = 0.f;
+            if (cv > b) { b = cv; bi = col; }
+          }
+        }
+        sm.red2[half][row] = b;
+        sm.redi[half][row] = bi;
+      }
+      tc5::fence_before_sync();
+      __syncthreads();
+      tc5::fence_after_sync();
+      if (half == 0) {
+        sm.rel[row] = __fdiv_rn(sqrtf(sm.red[0][row] + sm.red[1][row]), __fadd_rn(sm.nv[row], 1e-6f));
+        const float b0 = sm.red2[0][row], b1 = sm.red2[1][row];
+        const bool second = b1 > b0;
+        sm.bsk[row] = second ? b1 : b0;
+        sm.best[row] = second ? sm.redi[1][row] : sm.redi[0][row];
       }
       __syncthreads();
       if (!full) {
@@ -584,15 +608,15 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
       }
       __syncthreads();
       for (int i = warp; i < m; i += 8) {
-        const int j = sm.tops[i], s = n_filled + i;
-        copy_row_part<HD>(sm.ak, s, sm.kr, j, lane);
-        copy_row_part<HD>(sm.av, s, sm.vv, j, lane);
+        const int j = sm.tops[i], s2 = n_filled + i;
+        copy_row_part<HD>(sm.ak, s2, sm.kr, j, lane);
+        copy_row_part<HD>(sm.av, s2, sm.vv, j, lane);
         if (lane == 0) {
-          sm.pm[s] = sm.pos[j];
-          sm.mass[s] = 1.f;
-          sm.util[s] = sm.rel[j];
-          sm.act[s] = 1;
-          sm.dirty[s] = 1;
+          sm.pm[s2] = sm.pos[j];
+          sm.mass[s2] = 1.f;
+          sm.util[s2] = sm.rel[j];
+          sm.act[s2] = 1;
+          sm.dirty[s2] = 1;
         }
       }
       n_filled += m;
@@ -600,15 +624,15 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
     } else {
       // ---- sim_v, score, merge mask (:107-110): two threads per row
       {
-        const int r = tid >> 1, half = tid & 1;
+        const int r = tid >> 1, hf = tid & 1;
         const int sb = sm.best[r];
         float dot = 0.f, aa = 0.f;
         if (r < l_tok) {
           constexpr int CPR = HD / 8;
 #pragma unroll
-          for (int h = 0; h < CPR / 2; ++h) {
-            // logical chunk ch of row r sits at physical chunk ch ^ (row & 7) of that row
-            const int ch = half * CPR / 2 + h;
+          for (int hh = 0; hh < CPR / 2; ++hh) {
+            // logical chunk ch of row r sits at physical chunk ch ^ (row & 7)
+            const int ch = hf * CPR / 2 + hh;
             const uint4 a4 = *reinterpret_cast<const uint4*>(&sm.vv[swz<HD>(r, ch * 8)]);
             const uint4 b4 = *reinterpret_cast<const uint4*>(&sm.av[swz<HD>(sb, ch * 8)]);
             const uint32_t aw[4] = {a4.x, a4.y, a4.z, a4.w}, bw[4] = {b4.x, b4.y, b4.z, b4.w};
@@ -622,7 +646,7 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
         }
         dot += __shfl_xor_sync(0xffffffffu, dot, 1);
         aa += __shfl_xor_sync(0xffffffffu, aa, 1);
-        if (half == 0 && r < l_tok) {
+        if (hf == 0 && r < l_tok) {
           const float sv = __fdiv_rn(dot, __fmul_rn(fmaxf(sm.nv[r], 1e-8f), fmaxf(sqrtf(aa), 1e-8f)));
           const float bs = sm.bsk[r];
           sm.score[r] = __fmul_rn(sm.rel[r], 1.0f - fminf(fmaxf(bs, 0.f), 1.f));
@@ -645,9 +669,9 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
       __syncthreads();
       const int n_m = sm.n_merged;
       if (n_m > 0) {
-        for (int s = warp; s < S; s += 8) {
+        for (int s2 = warp; s2 < S; s2 += 8) {
           int cnt = 0;
-          for (int q = 0; q < n_m; ++q) cnt += sm.best[sm.mlist[q]] == s;
+          for (int q = 0; q < n_m; ++q) cnt += sm.best[sm.mlist[q]] == s2;
           if (cnt == 0) continue;
           constexpr int EPL = HD / 32;
           float ks[EPL], vs[EPL];
@@ -656,7 +680,7 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
           for (int e = 0; e < EPL; ++e) ks[e] = vs[e] = 0.f;
           for (int q = 0; q < n_m; ++q) {
             const int j = sm.mlist[q];
-            if (sm.best[j] != s) continue;
+            if (sm.best[j] != s2) continue;
 #pragma unroll
             for (int e = 0; e < EPL; ++e) {
               ks[e] = __fadd_rn(ks[e], bf2f(sm.kr[swz<HD>(j, lane * EPL + e)]));
@@ -664,55 +688,60 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
             }
             ps = __fadd_rn(ps, sm.pos[j]);
           }
-          const float ms = sm.mass[s];
+          const float ms = sm.mass[s2];
           const float nm = __fadd_rn(ms, (float)cnt);
 #pragma unroll
           for (int e = 0; e < EPL; ++e) {
             const int d = lane * EPL + e;
-            const float ka = __fadd_rn(__fmul_rn(ms, bf2f(sm.ak[swz<HD>(s, d)])), ks[e]);
-            const float va = __fadd_rn(__fmul_rn(ms, bf2f(sm.av[swz<HD>(s, d)])), vs[e]);
-            sm.ak[swz<HD>(s, d)] = __float2bfloat16_rn(__fdiv_rn(ka, nm));
-            sm.av[swz<HD>(s, d)] = __float2bfloat16_rn(__fdiv_rn(va, nm));
+            const float ka = __fadd_rn(__fmul_rn(ms, bf2f(sm.ak[swz<HD>(s2, d)])), ks[e]);
+            const float va = __fadd_rn(__fmul_rn(ms, bf2f(sm.av[swz<HD>(s2, d)])), vs[e]);
+            sm.ak[swz<HD>(s2, d)] = __float2bfloat16_rn(__fdiv_rn(ka, nm));
+            sm.av[swz<HD>(s2, d)] = __float2bfloat16_rn(__fdiv_rn(va, nm));
           }
           __syncwarp();
-          const float aa = row_sumsq<HD>(sm.ak, s, lane);
+          const float aa = row_sumsq<HD>(sm.ak, s2, lane);
           if (lane == 0) {
-            sm.pm[s] = __fdiv_rn(__fadd_rn(__fmul_rn(ms, sm.pm[s]), ps), nm);
-            sm.mass[s] = nm;
-            sm.dirty[s] = 1;
-            sm.na[s] = sqrtf(aa);
-            sm.rna[s] = 1.0f / fmaxf(sm.na[s], 1e-12f);
+            sm.pm[s2] = __fdiv_rn(__fadd_rn(__fmul_rn(ms, sm.pm[s2]), ps), nm);
+            sm.mass[s2] = nm;
+            sm.dirty[s2] = 1;
+            sm.na[s2] = sqrtf(aa);
+            sm.rna[s2] = 1.0f / fmaxf(sm.na[s2], 1e-12f);
           }
         }
-        __syncthreads();
       }
-      // ---- diversity eviction (:125-152)
+      // ---- diversity eviction (:125-152): pair = ak . ak^T into D1, and already the Gershgorin
+      // gram = kr . kr^T (:156) into D2
+      handoff();
+      if (tid == 0) {
+        mma_abt(TM_D1, s_ak, s_ak);
+        tc5::commit(&sm.bar[0]);
+        mma_abt(TM_D2, s_kr, s_kr);
+        tc5::commit(&sm.bar[1]);
+      }
+      wait_mma(0);
       {
-        float acc[16][4];
-        gemm_nt<HD>(acc, sm.ak, r0, sm.ak, lane);
-        const float ra0 = sm.rna[r0 + g], ra1 = sm.rna[r0 + g + 8];
-        float m0 = neg_inf(), m1 = neg_inf();
+        const float ra = sm.rna[row];
+        float m = neg_inf();
 #pragma unroll
-        for (int n = 0; n < 16; ++n) {
+        for (int q = 0; q < 2; ++q) {
+          uint32_t v[32];
+          tld(TM_D1 + half * 64 + q * 32, v);
+          tc5::ld_wait();
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const int col = n * 8 + 2 * t4 + q;
+          for (int j = 0; j < 32; ++j) {
+            const int col = half * 64 + q * 32 + j;
             // (ra_s * ra_s') is symmetric, so equal cosines of a mutual pair stay bit-identical
-            const float rb = sm.rna[col];
-            float p0 = __fmul_rn(acc[n][q], __fmul_rn(ra0, rb));
-            float p1 = __fmul_rn(acc[n][2 + q], __fmul_rn(ra1, rb));
-            if (col == r0 + g) p0 = -1.0f;
-            if (col == r0 + g + 8) p1 = -1.0f;
-            m0 = fmaxf(m0, p0);
-            m1 = fmaxf(m1, p1);
+            float p = __fmul_rn(__uint_as_float(v[j]), __fmul_rn(ra, sm.rna[col]));
+            if (col == row) p = -1.0f;
+            m = fmaxf(m, p);
           }
         }
-        m0 = quad_max(m0);
-        m1 = quad_max(m1);
-        if (t4 == 0) {
-          sm.keep[r0 + g] = __fmul_rn(sm.util[r0 + g], 1.0f - fminf(fmaxf(m0, 0.f), 0.98f));
-          sm.keep[r0 + g + 8] = __fmul_rn(sm.util[r0 + g + 8], 1.0f - fminf(fmaxf(m1, 0.f), 0.98f));
-        }
+        sm.red[half][row] = m;
+      }
+      __syncthreads();
+      if (half == 0) {
+        const float m = fmaxf(sm.red[0][row], sm.red[1][row]);
+        sm.keep[row] = __fmul_rn(sm.util[row], 1.0f - fminf(fmaxf(m, 0.f), 0.98f));
       }
       for (int j = tid; j < CC; j += NT) sm.wgt[j] = sm.mrg[j] ? -1e9f : sm.score[j];
       __syncthreads();
@@ -734,15 +763,15 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
       for (int i = warp; i < k_cand; i += 8) {
         const float tv = sm.topv[i];
         if (!((tv > sm.botv[i]) && (tv > -1e8f))) continue;  // :135
-        const int j = sm.tops[i], s = sm.bots[i];
-        copy_row_part<HD>(sm.ak, s, sm.kr, j, lane);
-        copy_row_part<HD>(sm.av, s, sm.vv, j, lane);
+        const int j = sm.tops[i], s2 = sm.bots[i];
+        copy_row_part<HD>(sm.ak, s2, sm.kr, j, lane);
+        copy_row_part<HD>(sm.av, s2, sm.vv, j, lane);
         if (lane == 0) {
-          sm.pm[s] = sm.pos[j];
-          sm.mass[s] = 1.f;
-          sm.util[s] = sm.rel[j];
+          sm.pm[s2] = sm.pos[j];
+          sm.mass[s2] = 1.f;
+          sm.util[s2] = sm.rel[j];
           sm.ins[j] = 1;
-          sm.dirty[s] = 1;
+          sm.dirty[s2] = 1;
         }
       }
       __syncthreads();
@@ -750,92 +779,94 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
       for (int j = tid; j < CC; j += NT)
         sm.wgt[j] = (j < l_tok && !sm.mrg[j] && !sm.ins[j]) ? sm.beta[j] : 0.f;
       __syncthreads();
-      float bsafe0, bsafe1;
+      wait_mma(1);
       {
-        float acc[16][4];
-        gemm_nt<HD>(acc, sm.kr, r0, sm.kr, lane);
-        const float rk0 = sm.rnk[r0 + g], rk1 = sm.rnk[r0 + g + 8];
-        float s0 = 0.f, s1 = 0.f;
+        const float rk0 = sm.rnk[row];
+        float s0 = 0.f;
 #pragma unroll
-        for (int n = 0; n < 16; ++n) {
+        for (int q = 0; q < 2; ++q) {
+          uint32_t v[32];
+          tld(TM_D2 + half * 64 + q * 32, v);
+          tc5::ld_wait();
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const int col = n * 8 + 2 * t4 + q;
-            const float rb = sm.rnk[col];
-            const float w = sm.wgt[col];
-            s0 = fmaf(fabsf(__fmul_rn(acc[n][q], __fmul_rn(rk0, rb))), w, s0);
-            s1 = fmaf(fabsf(__fmul_rn(acc[n][2 + q], __fmul_rn(rk1, rb))), w, s1);
+          for (int j = 0; j < 32; ++j) {
+            const int col = half * 64 + q * 32 + j;
+            s0 = fmaf(fabsf(__fmul_rn(__uint_as_float(v[j]), __fmul_rn(rk0, sm.rnk[col]))), sm.wgt[col], s0);
           }
         }
-        s0 = fmaxf(quad_sum(s0), 1.0f);
-        s1 = fmaxf(quad_sum(s1), 1.0f);
-        bsafe0 = __fdiv_rn(sm.wgt[r0 + g], s0);
-        bsafe1 = __fdiv_rn(sm.wgt[r0 + g + 8], s1);
+        sm.red[half][row] = s0;
       }
-      // M split into two bf16 terms, stored [d_in][d_out] in x1 (hi) and x2 (lo)
-      if (m_owner) {
-#pragma unroll
-        for (int n = 0; n < HD / 8; ++n) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int row = r0 + g + (q >> 1) * 8, col = n * 8 + 2 * t4 + (q & 1);
-            const bf16 hi = __float2bfloat16_rn(mr[n][q]);
-            sm.x1[swz<HD>(row, col)] = hi;
-            sm.x2[swz<HD>(row, col)] = __float2bfloat16_rn(mr[n][q] - bf2f(hi));
-          }
-        }
+      // M split into x1 (hi) and x2 (lo) for k^ M
+      m_split(sm.x1, sm.x2);
+      handoff();
+      if (half == 0) sm.bsafe[row] = __fdiv_rn(sm.wgt[row], fmaxf(sm.red[0][row] + sm.red[1][row], 1.0f));
+      if (tid == 0) {
+        mma_ab(TM_D1, s_kr, s_x1, false);
+        mma_ab(TM_D1, s_kr, s_x2, true);
+        tc5::commit(&sm.bar[0]);
       }
       __syncthreads();
-      float err[HD / 8][4];
+      wait_mma(0);
       {
+        // E = ((v - (kr . M) / |kr|) * beta_safe) / |kr|, so that kr^T E = k^T err; split into x1/x2
+        const float rk = sm.rnk[row], bs = sm.bsafe[row];
 #pragma unroll
-        for (int n = 0; n < HD / 8; ++n) err[n][0] = err[n][1] = err[n][2] = err[n][3] = 0.f;
-        gemm_nn<HD>(err, sm.kr, r0, sm.x1, lane);
-        gemm_nn<HD>(err, sm.kr, r0, sm.x2, lane);
-        const float rk0 = sm.rnk[r0 + g], rk1 = sm.rnk[r0 + g + 8];
+        for (int q = 0; q < HH / 32; ++q) {
+          uint32_t v[32];
+          tld(TM_D1 + half * HH + q * 32, v);
+          tc5::ld_wait();
 #pragma unroll
-        for (int n = 0; n < HD / 8; ++n) {
+          for (int ch = 0; ch < 4; ++ch) {
+            const int col = half * HH + q * 32 + ch * 8;
+            const uint4 u = *reinterpret_cast<const uint4*>(&sm.vv[swz<HD>(row, col)]);
+            const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+            uint32_t hw[4], lw[4];
 #pragma unroll
-          for (int hr = 0; hr < 2; ++hr) {
-            const int row = r0 + g + hr * 8, col = n * 8 + 2 * t4;
-            const float rk = hr ? rk1 : rk0;
-            const float bs = hr ? bsafe1 : bsafe0;
-            const float2 vv = unpack_bf16(*reinterpret_cast<const uint32_t*>(&sm.vv[swz<HD>(row, col)]));
-            const float e0 = __fmul_rn(vv.x - __fmul_rn(err[n][2 * hr], rk), bs);
-            const float e1 = __fmul_rn(vv.y - __fmul_rn(err[n][2 * hr + 1], rk), bs);
-            err[n][2 * hr] = __fmul_rn(e0, rk);  // E = err / |k| so that kr^T E = k^T err
-            err[n][2 * hr + 1] = __fmul_rn(e1, rk);
+            for (int w2 = 0; w2 < 4; ++w2) {
+              const float2 vf = unpack_bf16(uw[w2]);
+              const float e0 = __fmul_rn(__fmul_rn(vf.x - __fmul_rn(__uint_as_float(v[ch * 8 + 2 * w2]), rk), bs), rk);
+              const float e1 = __fmul_rn(__fmul_rn(vf.y - __fmul_rn(__uint_as_float(v[ch * 8 + 2 * w2 + 1]), rk), bs), rk);
+              const float2 hh = rbf2(e0, e1, hw[w2]);
+              lw[w2] = pack_bf16(e0 - hh.x, e1 - hh.y);
+            }
+            *reinterpret_cast<uint4*>(&sm.x1[swz<HD>(row, col)]) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *reinterpret_cast<uint4*>(&sm.x2[swz<HD>(row, col)]) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
           }
         }
-      }
-      __syncthreads();  // every warp is done reading the M split
+        // M <- gamma M (rows d; the padding rows of HD = 64 stay zero)
 #pragma unroll
-      for (int n = 0; n < HD / 8; ++n) {
+        for (int q = 0; q < HH / 32; ++q) {
+          uint32_t v[32];
+          tld(TM_M + half * HH + q * 32, v);
+          tc5::ld_wait();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int row = r0 + g + (q >> 1) * 8, col = n * 8 + 2 * t4 + (q & 1);
-          const bf16 hi = __float2bfloat16_rn(err[n][q]);
-          sm.x1[swz<HD>(row, col)] = hi;
-          sm.x2[swz<HD>(row, col)] = __float2bfloat16_rn(err[n][q] - bf2f(hi));
+          for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__fmul_rn(__uint_as_float(v[j]), gam));
+          tst(TM_M + half * HH + q * 32, v);
         }
+        tc5::st_wait();
       }
-      __syncthreads();
-      if (m_owner) {
-#pragma unroll
-        for (int n = 0; n < HD / 8; ++n) {
-          mr[n][0] = __fmul_rn(mr[n][0], gam); mr[n][1] = __fmul_rn(mr[n][1], gam);
-          mr[n][2] = __fmul_rn(mr[n][2], gam); mr[n][3] = __fmul_rn(mr[n][3], gam);
+      handoff();
+      if (tid == 0) {
+        // M += kr^T . E_hi + kr^T . E_lo: A = kr read transposed (rows d = the MN-major M side; at
+        // HD = 64 the second block of 64 rows is the zero tile), B = E [tokens][e]
+        constexpr uint32_t id = tc5::idesc_bf16(128, HD, true, true);
+        const uint32_t lbo_a = HD == 128 ? 16384u : tc5::smem_u32(sm.zpad) - s_kr;
+        for (int hl = 0; hl < 2; ++hl) {
+          const uint32_t sb = hl ? s_x2 : s_x1;
+          for (int ks = 0; ks < CC / 16; ++ks)
+            tc5::mma_ss(tb + TM_M, tc5::sdesc(s_kr + ks * 2048, lbo_a, 1024), tc5::sdesc(sb + ks * 2048, 16384, 1024),
+                        id, 1u);
         }
-        gemm_tn<HD>(mr, sm.kr, r0, sm.x1, lane);
-        gemm_tn<HD>(mr, sm.kr, r0, sm.x2, lane);
+        tc5::commit(&sm.bar[1]);
       }
-      __syncthreads();
+      wait_mma(1);
     }
 
     // ---- state the attention of a later chunk reads: RoPE(ak, pm), av, mass, act, M_res. The
     // shared-memory tiles already have the operand layout the attention's tensor cores read, so
-    // the snapshot is a handful of bulk copies: k_read (x2), av, M_hi (rebuilt in x1), M_lo (kr).
+    // the snapshot is a handful of bulk copies: k_read (x2), av, M_hi (x1), M_lo (kr).
     // k_read: last step's, from tensor memory, with the slots this step changed recomputed.
+    __syncthreads();
     x2_restore();
     if (warp == 0) {
       int base = 0;
@@ -850,19 +881,7 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
     }
     __syncthreads();
     rope_slots(sm.n_dirty, [&](int i) { return sm.dlist[i]; });
-    if (a.snap_ak_rope && m_owner) {
-#pragma unroll
-      for (int n = 0; n < HD / 8; ++n) {
-#pragma unroll
-        for (int hrow = 0; hrow < 2; ++hrow) {
-          const int d = r0 + g + hrow * 8, e = n * 8 + 2 * t4;
-          const float m0 = mr[n][2 * hrow], m1 = mr[n][2 * hrow + 1];
-          const bf16 h0 = __float2bfloat16_rn(m0), h1 = __float2bfloat16_rn(m1);
-          *reinterpret_cast<uint32_t*>(&sm.x1[swz<HD>(d, e)]) = pack_bf16(bf2f(h0), bf2f(h1));
-          *reinterpret_cast<uint32_t*>(&sm.kr[swz<HD>(d, e)]) = pack_bf16(m0 - bf2f(h0), m1 - bf2f(h1));
-        }
-      }
-    }
+    if (a.snap_ak_rope) m_split(sm.x1, sm.kr);
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
     __syncthreads();
     x2_save();
@@ -877,9 +896,9 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
         bulk_s2g(gm + (int64_t)HD * HD * 2, sm.kr, (uint32_t)HD * HD * 2);
         asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
       }
-      for (int s = tid; s < S; s += NT) {
-        a.snap_mass[sn * S + s] = sm.mass[s];
-        a.snap_act[sn * S + s] = sm.act[s];
+      for (int s2 = tid; s2 < S; s2 += NT) {
+        a.snap_mass[sn * S + s2] = sm.mass[s2];
+        a.snap_act[sn * S + s2] = sm.act[s2];
       }
       // the next step overwrites these tiles: wait until the copies have read them
       if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
@@ -891,32 +910,39 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
   s2g_rows<HD>(g_ak, sm.ak);
   s2g_rows<HD>(g_av, sm.av);
   if (a.ak_rope) s2g_rows<HD>(reinterpret_cast<bf16*>(a.ak_rope) + (int64_t)c * S * HD, sm.x2);
-  for (int s = tid; s < S; s += NT) {
-    a.mass[(int64_t)c * S + s] = sm.mass[s];
-    a.util[(int64_t)c * S + s] = sm.util[s];
-    a.pm[(int64_t)c * S + s] = sm.pm[s];
-    a.act[(int64_t)c * S + s] = sm.act[s];
+  for (int s2 = tid; s2 < S; s2 += NT) {
+    a.mass[(int64_t)c * S + s2] = sm.mass[s2];
+    a.util[(int64_t)c * S + s2] = sm.util[s2];
+    a.pm[(int64_t)c * S + s2] = sm.pm[s2];
+    a.act[(int64_t)c * S + s2] = sm.act[s2];
   }
-  if (m_owner) {
+  if (row < HD) {
 #pragma unroll
-    for (int n = 0; n < HD / 8; ++n) {
-      *reinterpret_cast<float2*>(g_m + (r0 + g) * HD + n * 8 + 2 * t4) = make_float2(mr[n][0], mr[n][1]);
-      *reinterpret_cast<float2*>(g_m + (r0 + g + 8) * HD + n * 8 + 2 * t4) = make_float2(mr[n][2], mr[n][3]);
+    for (int q = 0; q < HH / 32; ++q) {
+      uint32_t v[32];
+      tld(TM_M + half * HH + q * 32, v);
+      tc5::ld_wait();
+      float4* dst = reinterpret_cast<float4*>(g_m + (int64_t)row * HD + half * HH + q * 32);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        dst[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]), __uint_as_float(v[4 * j + 2]),
+                             __uint_as_float(v[4 * j + 3]));
     }
   }
   if (tid == 0) {
     a.n_filled[c] = n_filled;
     asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");  // snapshot copies have landed
+    if (timed_out && a.status) atomicOr(a.status, 4);
   }
   tc5::fence_before_sync();
   __syncthreads();
   tc5::fence_after_sync();
-  if (warp == 0) tc5::tmem_dealloc(sm.tbase, 64);
+  if (warp == 0) tc5::tmem_dealloc(tb, 512);
 }
 
 template <int HD>
 int launch(const bolt3_consolidate_args& a, cudaStream_t s) {
-  const size_t smem = sizeof(Smem<HD>);
+  const size_t smem = sizeof(Smem<HD>) + 1024;  // + alignment of the tiles to 1024 bytes
   // the attribute is per function and per device; setting it again is harmless
   if (cudaFuncSetAttribute(consolidate_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem) != cudaSuccess)
