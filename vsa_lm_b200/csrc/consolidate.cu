@@ -47,9 +47,9 @@ struct __align__(1024) Smem {
   float rel[CC], score[CC], bsk[CC], beta[CC], nk[CC], rnk[CC], nv[CC], pos[CC], wgt[CC], topv[CC], bsafe[CC];
   float red[2][128], red2[2][128];  // per-row partial results of the two column halves
   int redi[2][128];
-  int best[CC], tops[CC], bots[S], mlist[CC];
-  unsigned char act[S], mrg[CC], ins[CC];
-  int n_merged;
+  int best[CC], tops[CC], bots[S], mlist[CC], mbest[CC], hlist[S];
+  unsigned char act[S], mrg[CC], ins[CC], hit[S];
+  int n_merged, n_hit;
   b3sel::KV selA[128], selB[128];
   alignas(16) uint32_t keys[2][128];   // ranking scratch of the two thread groups (read as uint4)
   unsigned char dirty[S];   // slots whose key or mean position changed this step
@@ -654,7 +654,9 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
         }
       }
       __syncthreads();
-      // ---- merge: running means of the matched slots (:112-123)
+      // ---- merge: running means of the matched slots (:112-123). The merged tokens are listed in
+      // token order, each with its slot; each slot that receives tokens is one warp's, which sums
+      // them in token order.
       if (warp == 0) {
         int base = 0;
         for (int j0 = 0; j0 < CC; j0 += 32) {
@@ -666,21 +668,39 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
         }
         if (lane == 0) sm.n_merged = base;
       }
+      for (int s2 = tid; s2 < S; s2 += NT) sm.hit[s2] = 0;
       __syncthreads();
       const int n_m = sm.n_merged;
       if (n_m > 0) {
-        for (int s2 = warp; s2 < S; s2 += 8) {
-          int cnt = 0;
-          for (int q = 0; q < n_m; ++q) cnt += sm.best[sm.mlist[q]] == s2;
-          if (cnt == 0) continue;
+        for (int q = tid; q < n_m; q += NT) {
+          const int sb = sm.best[sm.mlist[q]];
+          sm.mbest[q] = sb;
+          sm.hit[sb] = 1;
+        }
+        __syncthreads();
+        if (warp == 0) {
+          int base = 0;
+          for (int s0 = 0; s0 < S; s0 += 32) {
+            const bool hh = sm.hit[s0 + lane] != 0;
+            const unsigned bal = __ballot_sync(0xffffffffu, hh);
+            if (hh) sm.hlist[base + __popc(bal & ((1u << lane) - 1))] = s0 + lane;
+            base += __popc(bal);
+          }
+          if (lane == 0) sm.n_hit = base;
+        }
+        __syncthreads();
+        for (int hi = warp; hi < sm.n_hit; hi += 8) {
+          const int s2 = sm.hlist[hi];
           constexpr int EPL = HD / 32;
           float ks[EPL], vs[EPL];
           float ps = 0.f;
+          int cnt = 0;
 #pragma unroll
           for (int e = 0; e < EPL; ++e) ks[e] = vs[e] = 0.f;
           for (int q = 0; q < n_m; ++q) {
+            if (sm.mbest[q] != s2) continue;
             const int j = sm.mlist[q];
-            if (sm.best[j] != s2) continue;
+            ++cnt;
 #pragma unroll
             for (int e = 0; e < EPL; ++e) {
               ks[e] = __fadd_rn(ks[e], bf2f(sm.kr[swz<HD>(j, lane * EPL + e)]));

@@ -42,6 +42,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
 
   // head rows per token: [0, H) q when parts & 1, then HKV k and HKV v rows when parts & 2
   const bool do_q = a.parts & 1, do_kv = (a.parts & 2) != 0;
+  const bool want_l2 = do_q && a.q_l2 != nullptr;
   const int n_rows = (do_q ? a.H : 0) + (do_kv ? 2 * a.HKV : 0);
   const int n_items = ntb * n_rows;    // (token, row) pairs; consecutive rows of a token are adjacent
   auto row_col = [&](int r, int& kind, int& head) -> int64_t {
@@ -105,13 +106,19 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
       }
     }
     float l2 = 0.f;  // |q_raw| of the stored (bf16) row, for the M_res read-out
+    if (want_l2) {   // uniform over the grid: every lane takes part in the shuffles
 #pragma unroll
-    for (int e = 0; e < 8; ++e) l2 = fmaf(x[e], x[e], l2);
-    l2 = row_sum(l2);
-    // RoPE partner values (element i <-> i + HD/2)
+      for (int e = 0; e < 8; ++e) l2 = fmaf(x[e], x[e], l2);
+      l2 = row_sum(l2);
+    }
+    // RoPE partner values (element i <-> i + HD/2), exchanged as the stored bf16 pairs
     float y[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) y[e] = __shfl_xor_sync(0xffffffffu, x[e], HALF);
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = unpack_bf16(__shfl_xor_sync(0xffffffffu, raw[q], HALF));
+      y[2 * q] = f.x;
+      y[2 * q + 1] = f.y;
+    }
     if (!live) return;
     if (kind == 2) {
       *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(a.v) + off) = make_uint4(raw[0], raw[1], raw[2], raw[3]);
