@@ -449,6 +449,116 @@ class Bolt3Decoder:
                 kv_caches[li] = StaticKV(batch_size, s.HKV, max_kv_len, s.HD, device, dt=torch.bfloat16)
         return states, kv_caches
 
+    # ---- decode state in the reference's format (bolt3.py:302-319 creates it, :343-425 fills it):
+    # per Bolt-3 layer a dict with the bank (ak/av [b*HKV, S, HD], mass/util/pm fp32 [b*HKV, S], act
+    # bool, n_filled), the sinks [b, HKV, 4, HD], and the previous / current chunk windows
+    # {prev,cur}_{kr,kp,v} [b, HKV, len, HD], _pos [1, 1, len] fp32, _b [b, HKV, len]; states[li] is
+    # M_res [b, HKV, HD, HD] fp32 in both formats.
+    _REF_KEYS = ("ak", "av", "mass", "util", "pm", "act", "sink_k", "sink_v", "prev_kr", "prev_kp", "prev_v",
+                 "prev_pos", "prev_b", "cur_kr", "cur_kp", "cur_v", "cur_pos", "cur_b")
+
+    @staticmethod
+    def state_to_reference(model, states, kv_caches):
+        """(states, kv_caches) with every Bolt3LayerState replaced by the reference's dict (copies)."""
+        out = []
+        for li, blk in enumerate(model.blocks):
+            st = kv_caches[li]
+            out.append(Bolt3Decoder._layer_to_dict(st) if hasattr(blk, "vsa") else st)
+        return states, out
+
+    @staticmethod
+    def state_from_reference(model, states, kv_caches, device):
+        """Native (states, kv_caches) from the reference's format; states[li] tensors are moved to
+        `device` as fp32 and then updated in place by the native steps."""
+        out_states, out_caches = list(states), []
+        for li, blk in enumerate(model.blocks):
+            d = kv_caches[li]
+            if hasattr(blk, "vsa"):
+                out_states[li] = states[li].to(device=device, dtype=torch.float32).contiguous()
+                out_caches.append(Bolt3Decoder._layer_from_dict(blk.vsa, d, out_states[li].shape[0], device))
+            else:
+                out_caches.append(d)
+        return out_states, out_caches
+
+    @staticmethod
+    def _layer_to_dict(st: "Bolt3LayerState") -> dict:
+        B, HKV, HD, C = st.B, st.HKV, st.HD, st.C
+        d = {k: None for k in Bolt3Decoder._REF_KEYS}
+        if st.has_bank:
+            bank = st.bank
+            for k in ("ak", "av", "mass", "util", "pm"):
+                d[k] = bank[k].clone()
+            d["act"] = bank["act"].bool()
+            d["n_filled"] = int(st.n_filled)
+        if st.sinks_set:
+            d["sink_k"] = st.sink_k.view(B, HKV, N_SINKS, HD).clone()
+            d["sink_v"] = st.sink_v.view(B, HKV, N_SINKS, HD).clone()
+
+        def window(tag, slot, n):
+            s0 = slot * C
+            d[tag + "_kr"] = st.ring_kr[:, s0:s0 + n].reshape(B, HKV, n, HD).clone()
+            d[tag + "_kp"] = st.ring_kp[:, s0:s0 + n].reshape(B, HKV, n, HD).clone()
+            d[tag + "_v"] = st.ring_v[:, s0:s0 + n].reshape(B, HKV, n, HD).clone()
+            d[tag + "_b"] = st.ring_b[:, s0:s0 + n].reshape(B, HKV, n).to(torch.bfloat16)
+            p0 = st.slot_pos[slot]
+            d[tag + "_pos"] = torch.arange(p0, p0 + n, dtype=torch.float32, device=st.ring_kr.device).view(1, 1, n)
+
+        if st.prev_slot >= 0:
+            window("prev", st.prev_slot, C)
+        if st.cur_len > 0:
+            window("cur", st.cur_slot, st.cur_len)
+        return d
+
+    @staticmethod
+    def _layer_from_dict(ly: Bolt3Attn, d: dict, B: int, device) -> "Bolt3LayerState":
+        st = Bolt3LayerState(ly, B, device)
+        HKV, HD, C, S = ly.HKV, ly.HD, ly.C, ly.S
+        n = B * HKV
+        dev = dict(device=device)
+        if d.get("ak") is not None:
+            bank = st.bank
+            bank["ak"].copy_(d["ak"].reshape(n, S, HD))
+            bank["av"].copy_(d["av"].reshape(n, S, HD))
+            for k in ("mass", "util", "pm"):
+                bank[k].copy_(d[k].reshape(n, S))
+            bank["act"].copy_(d["act"].reshape(n, S).to(torch.uint8))
+            # RoPE of the attractor keys at their mean positions in the storage dtype (bolt3.py:15-18):
+            # x * bf16(cos) + rotate_half(x) * bf16(sin), each product and the sum rounded to bf16
+            ak = bank["ak"]
+            ang = bank["pm"].unsqueeze(-1) * ly.fused(device).consts["inv_freq"].view(1, 1, -1)
+            ang = torch.cat((ang, ang), dim=-1)
+            h = HD // 2
+            rot = torch.cat((-ak[..., h:], ak[..., :h]), dim=-1)
+            bank["ak_rope"].copy_(ak * ang.cos().to(torch.bfloat16) + rot * ang.sin().to(torch.bfloat16))
+            st.n_filled = int(d.get("n_filled", 0))
+            bank["n_filled"].fill_(st.n_filled)
+        if d.get("sink_k") is not None:
+            if d["sink_k"].shape[2] != N_SINKS:
+                raise NotImplementedError("native decoder state holds exactly 4 sinks")
+            st.sink_k.copy_(d["sink_k"].reshape(n, N_SINKS, HD))
+            st.sink_v.copy_(d["sink_v"].reshape(n, N_SINKS, HD))
+            st.sinks_set = True
+
+        def fill(tag, slot):
+            L = d[tag + "_kp"].shape[2]
+            s0 = slot * C
+            st.ring_kr[:, s0:s0 + L].copy_(d[tag + "_kr"].reshape(n, L, HD))
+            st.ring_kp[:, s0:s0 + L].copy_(d[tag + "_kp"].reshape(n, L, HD))
+            st.ring_v[:, s0:s0 + L].copy_(d[tag + "_v"].reshape(n, L, HD))
+            st.ring_b[:, s0:s0 + L].copy_(d[tag + "_b"].reshape(n, L).float())
+            st.slot_pos[slot] = int(d[tag + "_pos"].reshape(-1)[0].item())
+            return L
+
+        if d.get("prev_kp") is not None:
+            if fill("prev", 0) != C:
+                raise NotImplementedError("native decoder state holds a previous chunk of exactly C tokens")
+            st.prev_slot, st.cur_slot = 0, 1
+        if d.get("cur_kp") is not None:
+            st.cur_len = fill("cur", st.cur_slot)
+            if st.cur_len >= C:
+                raise NotImplementedError("a pending chunk of C tokens is consolidated by the step that fills it")
+        return st
+
     @staticmethod
     def _sample(logits, temperature: float, top_k: int = 40, top_p: float = 0.95):
         if temperature <= 1e-5:
