@@ -616,17 +616,24 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// [slices][tokens][hd] bf16, box {64, 128, 1}, 128-byte swizzle; rows past `tokens` read as zero.
-static bool encode_rows(CUtensorMap* m, const void* base, int hd, int64_t tokens, int64_t slices) {
+// bf16 rows [slices][rows][hd], slices `slice_stride` rows apart: box {64, box_rows, 1}, 128-byte
+// swizzle; rows at or past `rows` read as zero. Also used by the decode kernels (attend_decode.cu).
+bool b3_encode_bf16_rows(CUtensorMap* m, const void* base, int hd, int64_t rows, int64_t slice_stride,
+                         int64_t slices, int box_rows) {
   auto fn = encode_fn();
   if (!fn) return false;
-  const cuuint64_t dims[3] = {(cuuint64_t)hd, (cuuint64_t)tokens, (cuuint64_t)slices};
-  const cuuint64_t strides[2] = {(cuuint64_t)hd * 2, (cuuint64_t)tokens * hd * 2};
-  const cuuint32_t box[3] = {64, 128, 1};
+  const cuuint64_t dims[3] = {(cuuint64_t)hd, (cuuint64_t)rows, (cuuint64_t)slices};
+  const cuuint64_t strides[2] = {(cuuint64_t)hd * 2, (cuuint64_t)slice_stride * hd * 2};
+  const cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// [slices][tokens][hd] bf16, box {64, 128, 1}
+static bool encode_rows(CUtensorMap* m, const void* base, int hd, int64_t tokens, int64_t slices) {
+  return b3_encode_bf16_rows(m, base, hd, tokens, tokens, slices, 128);
 }
 
 // decode steps with few query rows per chain (attend_decode.cu)

@@ -18,8 +18,18 @@
 // j <= len_before + i].
 #include "../../include/bolt3.h"
 #include "common.cuh"
+#include "tc5.cuh"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
 #include <type_traits>
+
+// 3-D tensor map of bf16 rows (attend.cu)
+bool b3_encode_bf16_rows(CUtensorMap* m, const void* base, int hd, int64_t rows, int64_t slice_stride,
+                         int64_t slices, int box_rows);
 
 namespace b3dec {
 
@@ -320,12 +330,539 @@ int launch(const bolt3_attend_args* a, cudaStream_t s) {
   return cudaGetLastError() == cudaSuccess ? BOLT3_OK : BOLT3_ERR_CUDA;
 }
 
+
+// ---------------------------------------------------------------------------------------------
+// Tensor-core streaming kernel for HD = 128 and at most four query rows per chain (the one-token step
+// with G <= 4).
+//
+// The step reads every chain's state once, so it is bound by how much of it is in flight. A
+// persistent CTA (one per SM) walks a strided list of chains with three roles: a producer warp whose
+// lane 0 copies the operands with the TMA engine into a ring of NST 32 KB stages, an MMA warp whose
+// lane 0 issues every tensor-core product, and eight consumer warps for the softmax, the M_res
+// read-out and the output. The roles meet only at mbarriers, so no role waits on another's data
+// unless it needs that data. The MMA warp is the ring's one in-order reader; it hands the pieces the
+// consumers read (R) to them through a per-chain mbarrier, so that every wait on a stage is for its
+// current phase. The ring pieces:
+//   R  piece   the chain's small operands: q_rope rows as a 16-row K-major tile (rows past the
+//              chain's own read as zero), the 4 sink keys and values as 16-row tiles, q_raw, and the
+//              bank's mass and act;
+//   K  pieces  one per segment (attractors, previous chunk, current chunk): 128 rows by 3-D tensor
+//              maps into 128-byte swizzled tiles; rows past the segment read as zero;
+//   V  pieces  the value rows of each segment, the same way.
+// The ring carries the chains software-pipelined, R and K of chain i+1 ahead of V of chain i: chain
+// i+1's scores are computed while chain i's softmax runs, and chain i's values are multiplied as soon
+// as they land after it. The fp32 M_res (64 KB) does not travel in the ring: the consumers request
+// the next chain's with cp.async into a buffer of its own as soon as they are done with this one.
+// Scores are one tcgen05.mma per segment and 16-key step, S^T[key][row] = K . Q^T into tensor
+// memory (double-buffered across chains; columns 16 s .. 16 s + 15 of a buffer, a lane per key). The
+// softmax reads them back (exact: a sweep for the max, one for the sum) and writes the bf16
+// probabilities as the K-major B tile of O^T[e][row] = V^T . P^T, issued per value segment with V as
+// the MN-major A operand. The M_res read-out stays on the CUDA cores in fp32 (paired FMAs). Stages
+// are released by a tcgen05.commit once the tensor cores (and, for R, the consumers) are done.
+namespace stream {
+
+constexpr int HD = 128;
+constexpr int NST = 3;             // ring stages
+constexpr int kStage = 32768;      // bytes per stage: 128 rows x 256 bytes
+constexpr int NRM = 4;             // query rows per chain, padded
+constexpr int NCW = 8;             // consumer warps (warps 0-7); warp 8 produces, warp 9 issues the MMAs
+constexpr int NCT = NCW * 32;      // consumer threads
+constexpr int kThreads = NCT + 64;
+constexpr uint32_t kIters = 1u << 24;
+// byte offsets inside the R piece: 16-row tiles (two 64-column halves each) of q_rope, sink keys,
+// sink values; then q_raw, mass, act
+constexpr int kRQ = 0, kRSK = 4096, kRSV = 8192, kRQRaw = 12288, kRMass = 13312, kRAct = 13824;
+constexpr uint32_t kColO = 128;    // TMEM: scores buffer b in columns [64 b, 64 b + 64); O^T at 128
+constexpr uint32_t kTmemCols = 256;
+
+struct __align__(64) Maps {
+  CUtensorMap q;                   // q_rope rows: {HD, NR, chains}, box {64, 16, 1}
+  CUtensorMap k[4], v[4];          // sinks (box {64, 16, 1}); attractors, previous, current chunk (box {64, 128, 1})
+};
+
+struct __align__(1024) Smem {
+  unsigned char ring[NST][kStage];
+  float mres[HD * HD];             // the current chain's fp32 M_res (cp.async)
+  unsigned char svt[2][4096];      // per chain buffer: the sink values' 16-row tile (MN-major A of P@V)
+  unsigned char qbuf[2][4096];     // per chain buffer: the Q tile (K-major B of the score MMAs)
+  unsigned char ptile[4][2][2048]; // probabilities of each segment: 16 rows x (2 x 64 keys), K-major SW128
+  float2 qd[2][HD][NRM];           // per chain buffer: q_raw[row][d], duplicated into both halves of a pair
+  float ypart[4][NRM][HD];         // M_res read-out partial sums of each quarter of d
+  float bias[2][S];
+  float red[NCW][NRM], red2[NCW][NRM];
+  float qn[2][NRM];
+  uint64_t full[NST], empty[NST];
+  uint64_t bar_s[2], bar_o;        // MMA warp -> consumers: scores of a chain buffer; O^T of a chain
+  uint64_t r_done[2], p_ready;     // consumers -> MMA warp: R piece read out (per chain buffer, so that
+                                   // the next chain's arrival cannot overtake this wait); probabilities written
+  uint64_t r_ready[2];             // MMA warp -> consumers: the R piece of a chain has landed
+  uint32_t tbase;
+  int err;
+};
+
+B3_DEV void cons_sync() { asm volatile("bar.sync 1, %0;\n" ::"n"(NCT) : "memory"); }
+// OR of `v` over the consumer threads (also a barrier among them)
+B3_DEV bool cons_any(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n.reg .pred p, q;\nsetp.ne.u32 p, %1, 0;\nbar.red.or.pred q, 1, %2, p;\nselp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(NCT)
+      : "memory");
+  return r != 0;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) attend_stream_kernel(const bolt3_attend_args a,
+                                                                    const __grid_constant__ Maps tm) {
+  extern __shared__ unsigned char smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = a.G, T = (int)a.Tq, NR = G * T, H = a.hkv * G;
+  const bool has_bank = a.has_bank != 0, has_sinks = a.has_sinks != 0;
+  const int len[4] = {has_sinks ? 4 : 0, has_bank ? S : 0, a.seg0_len, a.seg1_len};
+  // the segments that travel as ring pieces (the sinks travel in the R piece)
+  int n_kv = 0, kv_list[3];
+#pragma unroll
+  for (int s = 1; s < 4; ++s)
+    if (len[s] > 0) kv_list[n_kv++] = s;
+  // chains of this CTA: blockIdx.x + li * gridDim.x, li < n_local
+  const int n_local = a.n_chains > (int)blockIdx.x ? (a.n_chains - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+
+  if (tid == 0) {
+    for (int s = 0; s < NST; ++s) {
+      tc5::mbar_init(&sm.full[s], 1);
+      tc5::mbar_init(&sm.empty[s], 1);
+    }
+    tc5::mbar_init(&sm.bar_s[0], 1);
+    tc5::mbar_init(&sm.bar_s[1], 1);
+    tc5::mbar_init(&sm.bar_o, 1);
+    tc5::mbar_init(&sm.r_done[0], 1);
+    tc5::mbar_init(&sm.r_done[1], 1);
+    tc5::mbar_init(&sm.r_ready[0], 1);
+    tc5::mbar_init(&sm.r_ready[1], 1);
+    tc5::mbar_init(&sm.p_ready, 1);
+    tc5::mbar_fence_init();
+    sm.err = 0;
+  }
+  if (warp == 0) {
+    tc5::tmem_alloc(&sm.tbase, kTmemCols);
+    tc5::tmem_relinquish();
+  }
+  tc5::fence_before_sync();
+  __syncthreads();
+  tc5::fence_after_sync();
+  const uint32_t tb = sm.tbase;
+
+  if (warp == NCW) {
+    // ---- producer: per step li = -1 .. n_local - 1, R and K of chain li + 1, then V of chain li
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool stop = false;
+      // one ring piece; false once an error was recorded
+      auto put = [&](auto&& issue) -> bool {
+        const int s = (int)(it % NST);
+        if (it >= (uint32_t)NST && !tc5::mbar_wait(&sm.empty[s], ((it / NST) & 1u) ^ 1u, kIters)) sm.err = 1;
+        if (*reinterpret_cast<volatile int*>(&sm.err)) return false;
+        issue(sm.ring[s], &sm.full[s]);
+        ++it;
+        return true;
+      };
+      for (int li = -1; li < n_local && !stop; ++li) {
+        if (li + 1 < n_local) {
+          const int c = (int)blockIdx.x + (li + 1) * (int)gridDim.x;
+          const int64_t bofs = (int64_t)c * a.bank_cap;
+          stop = !put([&](unsigned char* buf, uint64_t* bar) {
+            const uint32_t qb = (uint32_t)NR * HD * 2;
+            tc5::mbar_expect_tx(bar, 2 * 2048 + (has_sinks ? 4 * 2048 : 0) + qb + (has_bank ? S * 4 + S : 0));
+            for (int h = 0; h < 2; ++h) tc5::tma_load_3d(buf + kRQ + h * 2048, &tm.q, h * 64, 0, c, bar);
+            if (has_sinks)
+              for (int h = 0; h < 2; ++h) {
+                tc5::tma_load_3d(buf + kRSK + h * 2048, &tm.k[0], h * 64, 0, c, bar);
+                tc5::tma_load_3d(buf + kRSV + h * 2048, &tm.v[0], h * 64, 0, c, bar);
+              }
+            tc5::bulk_load(buf + kRQRaw, reinterpret_cast<const bf16*>(a.q_raw) + (int64_t)c * NR * HD, qb, bar);
+            if (has_bank) {
+              tc5::bulk_load(buf + kRMass, a.bank_mass + bofs * S, S * 4, bar);
+              tc5::bulk_load(buf + kRAct, a.bank_act + bofs * S, S, bar);
+            }
+          });
+          for (int i = 0; i < n_kv && !stop; ++i) {
+            const int sg = kv_list[i];
+            stop = !put([&](unsigned char* buf, uint64_t* bar) {
+              tc5::mbar_expect_tx(bar, 2 * 16384);
+              for (int h = 0; h < 2; ++h)
+                tc5::tma_load_3d(buf + h * 16384, &tm.k[sg], h * 64, 0, sg == 1 ? (int)bofs : c, bar);
+            });
+          }
+        }
+        if (li >= 0 && !stop) {
+          const int c = (int)blockIdx.x + li * (int)gridDim.x;
+          const int64_t bofs = (int64_t)c * a.bank_cap;
+          for (int i = 0; i < n_kv && !stop; ++i) {
+            const int sg = kv_list[i];
+            stop = !put([&](unsigned char* buf, uint64_t* bar) {
+              tc5::mbar_expect_tx(bar, 2 * 16384);
+              for (int h = 0; h < 2; ++h)
+                tc5::tma_load_3d(buf + h * 16384, &tm.v[sg], h * 64, 0, sg == 1 ? (int)bofs : c, bar);
+            });
+          }
+        }
+      }
+      // after an early stop, copies may still be in flight: wait (bounded) for the last phase armed
+      // on every stage before the CTA's shared memory is released
+      for (uint32_t j = it > (uint32_t)NST ? it - NST : 0; j < it; ++j)
+        tc5::mbar_wait(&sm.full[j % NST], (j / NST) & 1u, kIters);
+    }
+  } else if (warp == NCW + 1) {
+    // ---- MMA warp: per step, the score MMAs of chain li + 1, then the P@V MMAs of chain li
+    if (lane == 0) {
+      constexpr uint32_t kIdS = tc5::idesc_bf16(128, 16, false, false);
+      constexpr uint32_t kIdO = tc5::idesc_bf16(128, 16, true, false);
+      uint32_t it = 0;
+      auto stage_wait = [&]() -> int {
+        const int s = (int)(it % NST);
+        if (!tc5::mbar_wait(&sm.full[s], (it / NST) & 1u, kIters)) sm.err = 1;
+        tc5::fence_after_sync();
+        return s;
+      };
+      for (int li = -1; li < n_local; ++li) {
+        if (li + 1 < n_local) {
+          // S^T = K . Q^T per segment; the sinks' keys and Q come with the R piece
+          const int bn = (li + 1) & 1;
+          const int sr = stage_wait();
+          ++it;
+          tc5::mbar_arrive(&sm.r_ready[bn]);
+          // the consumers copy Q (and the sink values) out of the R piece; after that, the sink keys
+          // are its last reader and the stage turns over
+          if (!tc5::mbar_wait(&sm.r_done[bn], (uint32_t)((li + 1) >> 1) & 1u, kIters)) sm.err = 1;
+          tc5::fence_after_sync();
+          const uint32_t ra = tc5::smem_u32(sm.ring[sr]);
+          const uint32_t qa = tc5::smem_u32(sm.qbuf[bn]);
+          if (has_sinks) {
+#pragma unroll
+            for (int ks = 0; ks < HD / 16; ++ks)
+              tc5::mma_ss(tb + 64 * bn, tc5::sdesc(ra + kRSK + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024),
+                          tc5::sdesc(qa + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024), kIdS, ks > 0);
+          }
+          tc5::commit(&sm.empty[sr]);
+          // S^T = K . Q^T of the ring segments
+          for (int i = 0; i < n_kv; ++i) {
+            const int s = stage_wait();
+            ++it;
+            const uint32_t ka = tc5::smem_u32(sm.ring[s]);
+            const uint32_t dcol = tb + 64 * bn + 16 * kv_list[i];
+#pragma unroll
+            for (int ks = 0; ks < HD / 16; ++ks)
+              tc5::mma_ss(dcol, tc5::sdesc(ka + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024),
+                          tc5::sdesc(qa + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024), kIdS, ks > 0);
+            tc5::commit(&sm.empty[s]);
+          }
+          tc5::commit(&sm.bar_s[bn]);
+        }
+        if (li >= 0) {
+          // O^T = V^T . P^T once the consumers have written chain li's probabilities
+          const int bi = li & 1;
+          if (!tc5::mbar_wait(&sm.p_ready, (uint32_t)li & 1u, kIters)) sm.err = 1;
+          tc5::fence_after_sync();
+          bool first = true;
+          if (has_sinks) {  // one 16-key step: sink rows 4..15 of the tile are zero, their P columns too
+            tc5::mma_ss(tb + kColO, tc5::sdesc(tc5::smem_u32(sm.svt[bi]), 2048, 1024),
+                        tc5::sdesc(tc5::smem_u32(sm.ptile[0][0]), 16, 1024), kIdO, false);
+            first = false;
+          }
+          for (int i = 0; i < n_kv; ++i) {
+            const int s = stage_wait();
+            ++it;
+            const uint32_t va = tc5::smem_u32(sm.ring[s]);
+            const int sg = kv_list[i];
+            const uint32_t pa = tc5::smem_u32(sm.ptile[sg][0]);
+            const int nks = (len[sg] + 15) / 16;
+            for (int ks = 0; ks < nks; ++ks) {
+              tc5::mma_ss(tb + kColO, tc5::sdesc(va + ks * 2048, 16384, 1024),
+                          tc5::sdesc(pa + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024), kIdO, !first);
+              first = false;
+            }
+            tc5::commit(&sm.empty[s]);
+          }
+          tc5::commit(&sm.bar_o);
+        }
+      }
+    }
+  } else {
+    // ---- consumers (threads 0..255)
+    const int t = tid;
+    constexpr float scale = 0.08838834764831845f;  // fp32(128 ** -0.5)
+    const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+    const int rg = warp >> 2;               // query rows 2 rg, 2 rg + 1 in the softmax and the epilogue
+    const int kq = 32 * (warp & 3) + lane;  // this thread's TMEM lane: a key of a segment, or a column e
+    // ring position: the consumers count every piece but wait only for the ones the MMA warp hands
+    // over (and then for the stage's own barrier, whose phase is by then the current one)
+    uint32_t it = 0;
+    auto handed = [&](uint64_t* ready, uint32_t parity) -> int {
+      const int s = (int)(it % NST);
+      if (!tc5::mbar_wait(ready, parity, kIters)) sm.err = 1;
+      if (!tc5::mbar_wait(&sm.full[s], (it / NST) & 1u, kIters)) sm.err = 1;
+      return s;
+    };
+    // R piece of local chain li (its buffers li & 1); the K pieces after it go to the MMA warp
+    auto front = [&](int li) {
+      const int c = (int)blockIdx.x + li * (int)gridDim.x;
+      const int bi = li & 1;
+      const int kvh = c % a.hkv;
+      const int sr = handed(&sm.r_ready[bi], (uint32_t)(li >> 1) & 1u);
+      const unsigned char* buf = sm.ring[sr];
+      const uint32_t* rs = reinterpret_cast<const uint32_t*>(buf + kRQRaw);
+      for (int idx = t; idx < NRM * HD / 2; idx += NCT) {
+        const int r = idx / (HD / 2), d2 = idx % (HD / 2);
+        const float2 g = r < NR ? unpack_bf16(rs[r * (HD / 2) + d2]) : make_float2(0.f, 0.f);
+        sm.qd[bi][2 * d2][r] = make_float2(g.x, g.x);
+        sm.qd[bi][2 * d2 + 1][r] = make_float2(g.y, g.y);
+      }
+      if (has_bank) {
+        const float kappa = __ldg(a.kappa + kvh);
+        const float* mass = reinterpret_cast<const float*>(buf + kRMass);
+        for (int j = t; j < S; j += NCT)
+          sm.bias[bi][j] = buf[kRAct + j] ? __fmul_rn(kappa, logf(fmaxf(mass[j], 1.0f))) : neg_inf();
+      }
+      // the Q tile and the sink values' tile outlive the stage: one 16-byte chunk of each per thread
+      reinterpret_cast<uint4*>(sm.qbuf[bi])[t] = reinterpret_cast<const uint4*>(buf + kRQ)[t];
+      if (has_sinks) reinterpret_cast<uint4*>(sm.svt[bi])[t] = reinterpret_cast<const uint4*>(buf + kRSV)[t];
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      cons_sync();
+      if (t == 0) tc5::mbar_arrive(&sm.r_done[bi]);
+      ++it;
+      if (has_bank && a.q_l2 == nullptr && warp < NR) {
+        float s2 = 0.f;
+        for (int d = lane; d < HD; d += 32) s2 = fmaf(sm.qd[bi][d][warp].x, sm.qd[bi][d][warp].x, s2);
+        s2 = warp_sum(s2);
+        if (lane == 0) sm.qn[bi][warp] = sqrtf(s2);
+      }
+    };
+
+    // the fp32 M_res of local chain li into sm.mres: 16 chunks of 16 bytes per thread
+    auto load_m = [&](int li) {
+      const int c = (int)blockIdx.x + li * (int)gridDim.x;
+      const float* src = reinterpret_cast<const float*>(a.bank_m) + (int64_t)c * a.bank_cap * HD * HD;
+#pragma unroll
+      for (int j = 0; j < HD * HD / 4 / NCT; ++j) cp_async16(sm.mres + (j * NCT + t) * 4, src + (j * NCT + t) * 4, true);
+      cp_async_commit();
+    };
+    if (n_local > 0) {
+      if (has_bank) load_m(0);
+      front(0);
+      it += n_kv;  // chain 0's keys: the MMA warp's
+    }
+    for (int li = 0; li < n_local; ++li) {
+      const int c = (int)blockIdx.x + li * (int)gridDim.x;
+      const int kvh = c % a.hkv, b = c / a.hkv;
+      const int bi = li & 1;
+      // the epilogue's per-row scalars, requested now and used at the end
+      float eta_r[2], ql2_r[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int r = 2 * rg + j;
+        eta_r[j] = has_bank && r < NR ? __ldg(a.eta + (int64_t)c * NR + r) : 0.f;
+        ql2_r[j] = has_bank && r < NR && a.q_l2 != nullptr ? __ldg(a.q_l2 + (int64_t)c * NR + r) : 0.f;
+      }
+      const float coef = has_bank ? __ldg(a.coef + kvh) : 0.f;
+      const float res_w = has_bank ? __ldg(a.res_w + kq) : 0.f;
+
+      // -- R of the next chain first: the MMA warp can then score its keys during this softmax
+      if (li + 1 < n_local) front(li + 1);
+
+      // -- softmax of chain li: thread (key kq of each segment, rows 2 rg, 2 rg + 1)
+      if (!tc5::mbar_wait(&sm.bar_s[bi], (uint32_t)(li >> 1) & 1u, kIters)) sm.err = 1;
+      tc5::fence_after_sync();
+      uint32_t v[4][4];
+#pragma unroll
+      for (int sg = 0; sg < 4; ++sg)
+        if (len[sg] > 0) tc5::ld4(tb + lane_off + 64 * bi + 16 * sg, v[sg]);
+      tc5::ld_wait();
+      float sv[4][2];
+      float mx[2] = {neg_inf(), neg_inf()};
+#pragma unroll
+      for (int sg = 0; sg < 4; ++sg) {
+        sv[sg][0] = sv[sg][1] = neg_inf();
+        if (kq >= len[sg]) continue;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int r = 2 * rg + u;
+          if (r >= NR) continue;
+          float s2 = __fmul_rn(__uint_as_float(v[sg][r]), scale);
+          if (sg == 1) s2 = __fadd_rn(s2, sm.bias[bi][kq]);
+          if (sg == 3 && kq > a.len_before + r % T) s2 = neg_inf();
+          sv[sg][u] = s2;
+          mx[u] = fmaxf(mx[u], s2);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const float m = warp_max(mx[u]);
+        if (lane == 0) sm.red[warp][2 * rg + u] = m;
+      }
+      cons_sync();
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int r = 2 * rg + u;
+        mx[u] = fmaxf(fmaxf(sm.red[4 * rg][r], sm.red[4 * rg + 1][r]), fmaxf(sm.red[4 * rg + 2][r], sm.red[4 * rg + 3][r]));
+        float sum = 0.f;
+#pragma unroll
+        for (int sg = 0; sg < 4; ++sg)
+          if (kq < len[sg] && r < NR) sum += expf(sv[sg][u] - mx[u]);
+        const float w = warp_sum(sum);
+        if (lane == 0) sm.red2[warp][r] = w;
+      }
+      cons_sync();
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int r = 2 * rg + u;
+        const float tot = sm.red2[4 * rg][r] + sm.red2[4 * rg + 1][r] + sm.red2[4 * rg + 2][r] + sm.red2[4 * rg + 3][r];
+        const float inv = 1.0f / tot;
+#pragma unroll
+        for (int sg = 0; sg < 4; ++sg) {
+          if (len[sg] == 0) continue;
+          const float pv = r < NR && kq < len[sg] ? rbf(__fmul_rn(expf(sv[sg][u] - mx[u]), inv)) : 0.f;
+          *reinterpret_cast<bf16*>(sm.ptile[sg][kq >> 6] + tc5::sw128_off(r, kq & 63)) = __float2bfloat16_rn(pv);
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      tc5::fence_before_sync();
+      cons_sync();
+      if (t == 0) tc5::mbar_arrive(&sm.p_ready);
+      if (li + 1 < n_local) it += n_kv;  // the next chain's keys: the MMA warp's
+      it += n_kv;                        // this chain's values: the MMA warp's
+
+      // -- M_res read-out: R[r][e] = sum_d q_raw[r][d] * M[d][e] in fp32; thread (column pair, quarter
+      // of the rows d), all four rows, two columns per paired FMA
+      float2 ym2[NRM];
+#pragma unroll
+      for (int r = 0; r < NRM; ++r) ym2[r] = make_float2(0.f, 0.f);
+      const int cpm = t & 63, dq = t >> 6;
+      if (has_bank) {
+        cp_async_wait<0>();
+        cons_sync();
+        const int d0 = dq * (HD / 4);
+#pragma unroll 4
+        for (int dd = 0; dd < HD / 4; ++dd) {
+          const float2 m2 = *reinterpret_cast<const float2*>(sm.mres + (d0 + dd) * HD + 2 * cpm);
+          const float4 q01 = *reinterpret_cast<const float4*>(&sm.qd[bi][d0 + dd][0]);
+          const float4 q23 = *reinterpret_cast<const float4*>(&sm.qd[bi][d0 + dd][2]);
+          ym2[0] = __ffma2_rn(make_float2(q01.x, q01.y), m2, ym2[0]);
+          ym2[1] = __ffma2_rn(make_float2(q01.z, q01.w), m2, ym2[1]);
+          ym2[2] = __ffma2_rn(make_float2(q23.x, q23.y), m2, ym2[2]);
+          ym2[3] = __ffma2_rn(make_float2(q23.z, q23.w), m2, ym2[3]);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < NRM; ++r) *reinterpret_cast<float2*>(&sm.ypart[dq][r][2 * cpm]) = ym2[r];
+      cons_sync();
+      // M_res is read: request the next chain's
+      if (has_bank && li + 1 < n_local) load_m(li + 1);
+
+      // -- epilogue: thread (column e = its TMEM lane, rows 2 rg, 2 rg + 1)
+      const int e = kq;
+      if (!tc5::mbar_wait(&sm.bar_o, (uint32_t)li & 1u, kIters)) sm.err = 1;
+      tc5::fence_after_sync();
+      uint32_t ov[4];
+      tc5::ld4(tb + lane_off + kColO, ov);
+      tc5::ld_wait();
+      float ym[2], rs_r[2] = {0.f, 0.f};
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int r = 2 * rg + u;
+        ym[u] = ((sm.ypart[0][r][e] + sm.ypart[1][r][e]) + sm.ypart[2][r][e]) + sm.ypart[3][r][e];
+      }
+      if (has_bank) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int r = 2 * rg + u;
+          const float qn = a.q_l2 != nullptr ? ql2_r[u] : (r < NR ? sm.qn[bi][r] : 1.f);
+          const float iq = 1.0f / fmaxf(qn, 1e-12f);
+          ym[u] = __fmul_rn(__fmul_rn(ym[u], iq), coef);
+          const float ss = warp_sum(__fmul_rn(ym[u], ym[u]));
+          if (lane == 0) sm.red[warp][r] = ss;
+        }
+        cons_sync();
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int r = 2 * rg + u;
+          const float ss = ((sm.red[4 * rg][r] + sm.red[4 * rg + 1][r]) + sm.red[4 * rg + 2][r]) + sm.red[4 * rg + 3][r];
+          rs_r[u] = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)HD), a.eps));
+        }
+      }
+      bf16* y = reinterpret_cast<bf16*>(a.y);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int r = 2 * rg + u;
+        if (r >= NR) break;
+        float yv = rbf(__uint_as_float(ov[r]));
+        if (has_bank) yv = __fadd_rn(yv, rbf(__fmul_rn(eta_r[u], __fmul_rn(__fmul_rn(ym[u], rs_r[u]), res_w))));
+        const int g = r / T, i = r % T;
+        y[(((int64_t)b * a.y_tokens + i) * H + kvh * G + g) * HD + e] = __float2bfloat16_rn(yv);
+      }
+      // the next chain overwrites the probability tile, the partial sums and the exchange rows
+      tc5::fence_before_sync();
+      if (cons_any(*reinterpret_cast<volatile int*>(&sm.err) != 0)) break;
+      tc5::fence_after_sync();
+    }
+    if (t == 0 && sm.err && a.status) atomicOr(a.status, 2);
+  }
+  tc5::fence_before_sync();
+  __syncthreads();
+  tc5::fence_after_sync();
+  if (warp == 0) tc5::tmem_dealloc(tb, kTmemCols);
+}
+
+// encodes the maps and launches one CTA per SM (at most one per chain); < 0: a map could not be
+// encoded (the caller then uses the warp-per-chain kernel)
+int launch(const bolt3_attend_args* a, cudaStream_t s) {
+  Maps m;
+  memset(&m, 0, sizeof(m));
+  const int64_t nc = a->n_chains, NR = (int64_t)a->G * a->Tq;
+  if (!b3_encode_bf16_rows(&m.q, a->q_rope, HD, NR, NR, nc, 16)) return -1;
+  const void* kb[4] = {a->sink_k, a->bank_ak_rope, a->seg0_k, a->seg1_k};
+  const void* vb[4] = {a->sink_v, a->bank_av, a->seg0_v, a->seg1_v};
+  const int64_t rows[4] = {4, S, a->seg0_len, a->seg1_len};
+  const int64_t stride[4] = {a->sink_chain_tokens, S, a->seg0_chain_tokens, a->seg1_chain_tokens};
+  const int64_t slices[4] = {nc, nc * a->bank_cap, nc, nc};
+  const bool on[4] = {a->has_sinks != 0, a->has_bank != 0, a->seg0_len > 0, a->seg1_len > 0};
+  for (int i = 0; i < 4; ++i) {
+    const int box = i == 0 ? 16 : 128;
+    if (on[i] && (!b3_encode_bf16_rows(&m.k[i], kb[i], HD, rows[i], stride[i], slices[i], box) ||
+                  !b3_encode_bf16_rows(&m.v[i], vb[i], HD, rows[i], stride[i], slices[i], box)))
+      return -1;
+  }
+  const size_t smem = sizeof(Smem) + 1024;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(attend_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return BOLT3_ERR_CUDA;
+    attr_set = true;
+  }
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return BOLT3_ERR_CUDA;
+  const int grid = (int)std::min<int64_t>(nc, sms);
+  attend_stream_kernel<<<grid, kThreads, smem, s>>>(*a, m);
+  return cudaGetLastError() == cudaSuccess ? BOLT3_OK : BOLT3_ERR_CUDA;
+}
+
+}  // namespace stream
+
 }  // namespace b3dec
 
 // Launch for bolt3_attend (prefill = 0, G * Tq <= 16); returns a bolt3 status.
 int b3_attend_decode_launch(const bolt3_attend_args* a, cudaStream_t s) {
   const int NR = a->G * (int)a->Tq;
   if (NR > 16 || a->seg0_len + a->seg1_len > 256) return BOLT3_ERR_SHAPE;
+  // HD = 128 with up to four query rows: the tensor-core streaming kernel, when its bulk copies'
+  // alignment holds (the tensor maps are checked as they are encoded; a map that cannot be encoded
+  // selects the warp-per-chain kernel below)
+  const uintptr_t al = (uintptr_t)a->bank_mass | (uintptr_t)a->bank_act;
+  if (NR <= 4 && (al & 15) == 0 && a->HD == 128) {
+    const int rc = b3dec::stream::launch(a, s);
+    if (rc >= 0) return rc;
+  }
   if (a->HD == 128) return NR <= 4 ? b3dec::launch<128, 4>(a, s) : (NR <= 8 ? b3dec::launch<128, 8>(a, s) : b3dec::launch<128, 16>(a, s));
   if (a->HD == 64) return NR <= 4 ? b3dec::launch<64, 4>(a, s) : (NR <= 8 ? b3dec::launch<64, 8>(a, s) : b3dec::launch<64, 16>(a, s));
   return BOLT3_ERR_SHAPE;
