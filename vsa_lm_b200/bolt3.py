@@ -14,6 +14,8 @@ from __future__ import annotations
 
 import math
 
+import types
+
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
@@ -167,6 +169,9 @@ class Bolt3Attn(nn.Module):
     def fused(self, device):
         """(W_in [N, D] bf16, b_in [N] bf16 or None, W_out bf16, consts) for `device`, where the
         fused input projection has columns [q | k | v | beta | eta] (the bolt3_prep layout)."""
+        device = torch.device(device)
+        if device.type == "cuda" and device.index is None:   # "cuda" and "cuda:<current>" share one entry
+            device = torch.device("cuda", torch.cuda.current_device())
         key = self._params_key(device)
         f = self._fused
         if f.key == key:
@@ -406,6 +411,7 @@ class Bolt3LayerState:
         self.prev_slot = -1
         self.sinks_set = False
         self.n_filled = 0
+        self._plans = {}   # per step size: buffers and prebuilt launch arguments (Bolt3Decoder)
 
     @property
     def has_bank(self) -> bool:
@@ -575,6 +581,44 @@ class Bolt3Decoder:
 
     # ---- one Bolt-3 layer (bolt3.py:343-425)
     @staticmethod
+    def _step_plan(ly: Bolt3Attn, st: Bolt3LayerState, b: int, t: int, f, dev):
+        """Buffers and prebuilt bolt3_prep / bolt3_attend arguments of a t-token step."""
+        H, HKV, HD, C, G = ly.H, ly.HKV, ly.HD, ly.C, ly.G
+        c = f.consts
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        # the plan keeps its own references to the tensors its launch arguments point at: fused()
+        # replaces them when the weights change, and the plan is then rebuilt at the next chunk start
+        plan = types.SimpleNamespace(f=f, key=f.key, w_in=f.w_in, b_in=f.b_in, w_out=f.w_out, consts=c, cols=f.cols)
+        plan.q_raw = torch.empty(b * H, t, HD, **bf)
+        plan.q_rope = torch.empty_like(plan.q_raw)
+        plan.eta = torch.empty(b * H, t, dtype=torch.float32, device=dev)
+        plan.q_l2 = torch.empty(b * H, t, dtype=torch.float32, device=dev)
+        plan.y = torch.empty(b, t, H, HD, **bf)
+        plan.ring_kp, plan.ring_v = st.ring_kp.data_ptr(), st.ring_v.data_ptr()
+        plan.ring_row = HD * st.ring_kp.element_size()
+        cols = f.cols
+        ptr = lambda x: None if x is None else x.data_ptr()
+        prep = dict(
+            proj=None, ld=f.w_in.shape[0], B=b, T=t, H=H, HKV=HKV, HD=HD,
+            q_norm_w=ptr(c["qn"]), k_norm_w=ptr(c["kn"]), eps=ly.eps, inv_freq=c["inv_freq"].data_ptr(), pos0=0,
+            q_raw=plan.q_raw.data_ptr(), q_rope=plan.q_rope.data_ptr(), q_head_stride=t, q_t_off=0,
+            eta=plan.eta.data_ptr(), eta_head_stride=t, eta_t_off=0, k_raw=st.ring_kr.data_ptr(),
+            k_rope=st.ring_kp.data_ptr(), v=st.ring_v.data_ptr(), k_head_stride=2 * C, k_t_off=0,
+            beta=st.ring_b.data_ptr(), beta_head_stride=2 * C, beta_t_off=0, q_l2=plan.q_l2.data_ptr(), parts=3,
+            q_col=cols["q_col"], k_col=cols["k_col"], v_col=cols["v_col"], beta_col=cols["beta_col"],
+            eta_col=cols["eta_col"])
+        bk = st.bank
+        attend = dict(
+            n_chains=b * HKV, hkv=HKV, G=G, HD=HD, q_rope=plan.q_rope.data_ptr(), q_raw=plan.q_raw.data_ptr(),
+            eta=plan.eta.data_ptr(), Tq=t, prefill=0, seg0_chain_tokens=2 * C, seg1_chain_tokens=2 * C,
+            sink_k=st.sink_k.data_ptr(), sink_v=st.sink_v.data_ptr(), sink_chain_tokens=N_SINKS,
+            bank_ak_rope=bk["ak_rope"].data_ptr(), bank_av=bk["av"].data_ptr(), bank_mass=bk["mass"].data_ptr(),
+            bank_act=bk["act"].data_ptr(), bank_cap=1, kappa=c["kappa"].data_ptr(), coef=c["coef"].data_ptr(),
+            res_w=c["res_w"].data_ptr(), eps=ly.eps, y=plan.y.data_ptr(), y_tokens=t, q_l2=plan.q_l2.data_ptr())
+        plan.args = K.DecodeStepArgs(prep, attend)
+        return plan
+
+    @staticmethod
     def layer_step(ly: Bolt3Attn, st: Bolt3LayerState, h: torch.Tensor, pos_start: int,
                    m_res: torch.Tensor) -> torch.Tensor:
         """Attention branch of one Bolt-3 layer for t new tokens: returns o_proj(y) [b, t, D] bf16."""
@@ -588,37 +632,30 @@ class Bolt3Decoder:
             st.slot_pos[st.cur_slot] = pos_start
         elif pos_start != st.slot_pos[st.cur_slot] + st.cur_len:
             raise NotImplementedError("native decoder needs contiguous positions within a chunk")
+        if not (m_res.is_cuda and m_res.dtype == torch.float32 and m_res.is_contiguous()):
+            raise ValueError("m_res must be a contiguous fp32 CUDA tensor [B, HKV, HD, HD]")
         dev = h.device
-        f = ly.fused(dev)
-        c = f.consts
-        proj = ly.project(h.reshape(b * t, D).to(torch.bfloat16), f)
-        bf = dict(dtype=torch.bfloat16, device=dev)
-        q_raw = torch.empty(b * H, t, HD, **bf)
-        q_rope = torch.empty_like(q_raw)
-        eta = torch.empty(b * H, t, dtype=torch.float32, device=dev)
-        q_l2 = torch.empty(b * H, t, dtype=torch.float32, device=dev)
-        k_off = st.cur_slot * C + st.cur_len
-        K.prep(proj, B=b, T=t, H=H, HKV=HKV, HD=HD, inv_freq=c["inv_freq"], eps=ly.eps, q_norm_w=c["qn"],
-               k_norm_w=c["kn"], pos0=pos_start, cols=f.cols, parts=3, q_raw=q_raw, q_rope=q_rope, eta=eta,
-               k_raw=st.ring_kr, k_rope=st.ring_kp, v=st.ring_v, beta=st.ring_b, q_head_stride=t, q_t_off=0,
-               k_head_stride=2 * C, k_t_off=k_off, q_l2=q_l2)
+        # the step's buffers and launch arguments, rebuilt when the layer's weights change (checked
+        # whenever a chunk starts) or the step size does
+        plan = st._plans.get(t)
+        if plan is None or st.cur_len == 0:
+            f = ly.fused(dev)
+            if plan is None or plan.key != f.key:
+                plan = Bolt3Decoder._step_plan(ly, st, b, t, f, dev)
+                st._plans[t] = plan
+        proj = F.linear(h.reshape(b * t, D).to(torch.bfloat16), plan.w_in, plan.b_in)
+        plan.args.launch_prep(proj, pos_start, st.cur_slot * C + st.cur_len)
         has_prev = st.prev_slot >= 0
         p0 = st.prev_slot * C if has_prev else 0
         c0 = st.cur_slot * C
-        y = torch.empty(b, t, H, HD, **bf)
-        bank = None
-        if st.has_bank:
-            bank = dict(st.bank)
-            bank["m_res"] = m_res
-        K.attend_decode(
-            n_chains=b * HKV, hkv=HKV, G=G, HD=HD, q_rope=q_rope, q_raw=q_raw, eta=eta, Tq=t,
-            seg0_k=st.ring_kp[:, p0:] if has_prev else st.ring_kp, seg0_v=st.ring_v[:, p0:] if has_prev else st.ring_v,
-            seg0_chain_tokens=2 * C, seg0_len=C if has_prev else 0,
-            seg1_k=st.ring_kp[:, c0:], seg1_v=st.ring_v[:, c0:], seg1_chain_tokens=2 * C,
-            seg1_len=st.cur_len + t, len_before=st.cur_len,
-            sinks=(st.sink_k, st.sink_v) if st.sinks_set else None, bank=bank, kappa=c["kappa"],
-            coef=c["coef"], res_w=c["res_w"], eps=ly.eps, y=y, q_l2=q_l2)
-        out = F.linear(y.view(b, t, H * HD), f.w_out)
+        rk, rv, row = plan.ring_kp, plan.ring_v, plan.ring_row
+        plan.args.launch_attend(
+            seg0_k=rk + p0 * row, seg0_v=rv + p0 * row, seg0_len=C if has_prev else 0,
+            seg1_k=rk + c0 * row, seg1_v=rv + c0 * row, seg1_len=st.cur_len + t, len_before=st.cur_len,
+            has_sinks=st.sinks_set, has_bank=st.has_bank, bank_m=m_res.data_ptr())
+        y = plan.y
+        out = F.linear(y.view(b, t, H * HD), plan.w_out)
+        c = plan.consts
         st.cur_len += t
         if st.cur_len >= C:                                                   # bolt3.py:406-425
             if has_prev:

@@ -374,6 +374,14 @@ constexpr uint32_t kIters = 1u << 24;
 constexpr int kRQ = 0, kRSK = 4096, kRSV = 8192, kRQRaw = 12288, kRMass = 13312, kRAct = 13824;
 constexpr uint32_t kColO = 128;    // TMEM: scores buffer b in columns [64 b, 64 b + 64); O^T at 128
 constexpr uint32_t kTmemCols = 256;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// 2^x on the special-function unit (relative error ~2^-22; results below 2^-126 flush to zero)
+B3_DEV float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
 
 struct __align__(64) Maps {
   CUtensorMap q;                   // q_rope rows: {HD, NR, chains}, box {64, 16, 1}
@@ -707,8 +715,11 @@ __global__ void __launch_bounds__(kThreads, 1) attend_stream_kernel(const bolt3_
         mx[u] = fmaxf(fmaxf(sm.red[4 * rg][r], sm.red[4 * rg + 1][r]), fmaxf(sm.red[4 * rg + 2][r], sm.red[4 * rg + 3][r]));
         float sum = 0.f;
 #pragma unroll
-        for (int sg = 0; sg < 4; ++sg)
-          if (kq < len[sg] && r < NR) sum += expf(sv[sg][u] - mx[u]);
+        for (int sg = 0; sg < 4; ++sg) {
+          // exp(s - max), kept for the probabilities
+          sv[sg][u] = kq < len[sg] && r < NR ? ex2(__fmul_rn(sv[sg][u] - mx[u], kLog2e)) : 0.f;
+          sum += sv[sg][u];
+        }
         const float w = warp_sum(sum);
         if (lane == 0) sm.red2[warp][r] = w;
       }
@@ -721,7 +732,7 @@ __global__ void __launch_bounds__(kThreads, 1) attend_stream_kernel(const bolt3_
 #pragma unroll
         for (int sg = 0; sg < 4; ++sg) {
           if (len[sg] == 0) continue;
-          const float pv = r < NR && kq < len[sg] ? rbf(__fmul_rn(expf(sv[sg][u] - mx[u]), inv)) : 0.f;
+          const float pv = r < NR ? rbf(__fmul_rn(sv[sg][u], inv)) : 0.f;
           *reinterpret_cast<bf16*>(sm.ptile[sg][kq >> 6] + tc5::sw128_off(r, kq & 63)) = __float2bfloat16_rn(pv);
         }
       }

@@ -137,6 +137,36 @@ def attend_decode(*, n_chains: int, hkv: int, G: int, HD: int, q_rope: torch.Ten
     _count(1)
 
 
+class DecodeStepArgs:
+    """The decoder's per-step bolt3_prep and bolt3_attend argument blocks, built once for a (layer,
+    state, step size) and launched every step with only the fields that move rewritten: the
+    projection output, RoPE position and ring write offset (prep), the ring slots, window lengths and
+    whether sinks and a bank exist yet (attend). The buffers the blocks point at are the caller's
+    and must stay alive."""
+
+    def __init__(self, prep_fields: dict, attend_fields: dict):
+        self.lib = _lib.load()
+        self.prep = _lib.PrepArgs(**prep_fields)
+        self.attend = _lib.AttendArgs(**attend_fields)
+
+    def launch_prep(self, proj: torch.Tensor, pos0: int, k_t_off: int) -> None:
+        a = self.prep
+        if proj.stride(0) != a.ld or not proj.is_contiguous():
+            raise ValueError("proj must be a contiguous [tokens, ld] projection output")
+        a.proj, a.pos0, a.k_t_off, a.beta_t_off = proj.data_ptr(), pos0, k_t_off, k_t_off
+        _lib.check(self.lib.bolt3_prep(ctypes.byref(a), _stream()), "bolt3_prep")
+        _count(1)
+
+    def launch_attend(self, *, seg0_k: int, seg0_v: int, seg0_len: int, seg1_k: int, seg1_v: int,
+                      seg1_len: int, len_before: int, has_sinks: bool, has_bank: bool, bank_m: int) -> None:
+        a = self.attend
+        a.seg0_k, a.seg0_v, a.seg0_len = seg0_k, seg0_v, seg0_len
+        a.seg1_k, a.seg1_v, a.seg1_len, a.len_before = seg1_k, seg1_v, seg1_len, len_before
+        a.has_sinks, a.has_bank, a.bank_m = int(has_sinks), int(has_bank), bank_m
+        _lib.check(self.lib.bolt3_attend(ctypes.byref(a), _stream()), "bolt3_attend")
+        _count(1)
+
+
 def prefill_workspace_bytes(n_chains: int, T: int, HD: int) -> int:
     return int(_lib.load().bolt3_prefill_workspace_size(n_chains, T, HD))
 
