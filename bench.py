@@ -350,7 +350,7 @@ def run_decode(args, rank, world, dev, m, cfg, hbm):
     for s in range(0, DEC_PROMPT, 128):
         h = torch.randn(n_seq, 128, D, generator=g, device=dev).to(torch.bfloat16)
         Bolt3Decoder.layer_step(m, st, h, s, m_res)
-    steps = DEC_STEPS
+    steps = args.decode_steps
     toks = torch.randn(steps + args.warmup, n_seq, 1, D, generator=g, device=dev).to(torch.bfloat16)
     pos = [DEC_PROMPT]
     i = [0]
@@ -434,6 +434,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--batch", type=int, default=PREFILL_B, help="prefill sequences per GPU (profiling cases)")
     ap.add_argument("--seq", type=int, default=PREFILL_T, help="prefill tokens per sequence (profiling cases)")
+    ap.add_argument("--decode-only", action="store_true", help="only the configs[2] decode measurement (profiling)")
+    ap.add_argument("--decode-steps", type=int, default=DEC_STEPS, help="timed decode steps")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -451,7 +453,13 @@ def main():
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     try:
-        res = run_native(args, rank, world, local)
+        if args.decode_only:
+            dev = torch.device("cuda", local)
+            torch.cuda.set_device(dev)
+            cfg, m = build_layer(dev)
+            res = {"decode": run_decode(args, rank, world, dev, m, cfg, peaks()[0])}
+        else:
+            res = run_native(args, rank, world, local)
         if rank == 0 and res is not None:
             print(json.dumps(res), flush=True)
     finally:
