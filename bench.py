@@ -383,6 +383,7 @@ def run_decode(args, rank, world, dev, m, cfg, hbm):
             "workload": "configs[2]: one Bolt-3 layer step (projections, attention, o_proj, consolidation "
                         "every 128 steps), 256 sequences after a 4096-token prefill",
             "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                         "attend_traffic": profile_traffic().get("attend_decode"),
                          "bytes_per_step": nb["total"], "state_only_frac": ach_core / hbm}}
 
 
