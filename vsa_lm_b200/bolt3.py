@@ -238,7 +238,9 @@ class Bolt3Attn(nn.Module):
         return self._native_forward(x)
 
     @torch.no_grad()
-    def _native_forward(self, x: torch.Tensor) -> torch.Tensor:
+    def _native_forward(self, x: torch.Tensor, partial_fp32: bool = False) -> torch.Tensor:
+        """The forward on CUDA. partial_fp32: return o_proj's output in fp32, unrounded (a tensor-
+        parallel shard's partial sum, rounded once after the all-reduce)."""
         if not x.is_cuda:
             raise RuntimeError("Bolt3Attn (B200 native) runs on CUDA tensors only; no CPU path exists")
         b, T, D = x.shape
@@ -271,6 +273,8 @@ class Bolt3Attn(nn.Module):
 
         self._scan_and_attend(b, T, q_rope=q_rope, q_raw=q_raw, eta=eta, k_raw=k_raw, k_rope=k_rope, v=v,
                               beta=beta, q_l2=q_l2, ws=ws, bank=bank, y=y, consts=c, before_attend=prep_q)
+        if partial_fp32:
+            return torch.mm(y.view(b * T, H * HD), f.w_out.t(), out_dtype=torch.float32).view(b, T, -1)
         out = F.linear(y.view(b, T, H * HD), f.w_out)
         return out.to(x.dtype)
 
@@ -620,8 +624,9 @@ class Bolt3Decoder:
 
     @staticmethod
     def layer_step(ly: Bolt3Attn, st: Bolt3LayerState, h: torch.Tensor, pos_start: int,
-                   m_res: torch.Tensor) -> torch.Tensor:
-        """Attention branch of one Bolt-3 layer for t new tokens: returns o_proj(y) [b, t, D] bf16."""
+                   m_res: torch.Tensor, partial_fp32: bool = False) -> torch.Tensor:
+        """Attention branch of one Bolt-3 layer for t new tokens: returns o_proj(y) [b, t, D] bf16
+        (fp32 and unrounded with partial_fp32: a tensor-parallel shard's partial sum)."""
         b, t, D = h.shape
         H, HKV, HD, C, G = ly.H, ly.HKV, ly.HD, ly.C, ly.G
         if st.cur_len + t > C:
@@ -654,7 +659,10 @@ class Bolt3Decoder:
             seg1_k=rk + c0 * row, seg1_v=rv + c0 * row, seg1_len=st.cur_len + t, len_before=st.cur_len,
             has_sinks=st.sinks_set, has_bank=st.has_bank, bank_m=m_res.data_ptr())
         y = plan.y
-        out = F.linear(y.view(b, t, H * HD), plan.w_out)
+        if partial_fp32:
+            out = torch.mm(y.view(b * t, H * HD), plan.w_out.t(), out_dtype=torch.float32).view(b, t, -1)
+        else:
+            out = F.linear(y.view(b, t, H * HD), plan.w_out)
         c = plan.consts
         st.cur_len += t
         if st.cur_len >= C:                                                   # bolt3.py:406-425
