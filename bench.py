@@ -33,6 +33,7 @@ METRIC = "Bolt3 prefill tok/s + decode tok/s, Qwen3-4B shape, 1-8 B200, % roofli
 SHAPE = "qwen3_4b"
 PREFILL_B, PREFILL_T, DUP = 8, 8192, 0.3
 DEC_SEQ, DEC_PROMPT, DEC_STEPS = 256, 4096, 512
+LONG_T = 131072
 
 
 def peaks():
@@ -387,6 +388,29 @@ def run_decode(args, rank, world, dev, m, cfg, hbm):
                          "bytes_per_step": nb["total"], "state_only_frac": ach_core / hbm}}
 
 
+def run_long(args, rank, world, dev, tf_peak):
+    """Llama-3-8B-shape Bolt3Attn prefill of 1 x 131072 tokens. On N GPUs every rank
+    holds HKV/N KV heads (Bolt3AttnTP: one NCCL all-reduce of the o_proj partials per forward)."""
+    from vsa_lm_b200 import Bolt3Attn
+    from vsa_lm_b200.tp import Bolt3AttnTP
+
+    cfg = layer_cfg("llama3_8b")
+    full = Bolt3Attn(cfg)
+    full.load_state_dict(make_params(cfg, 0))
+    full = full.to(device=dev, dtype=torch.bfloat16).eval()
+    layer = Bolt3AttnTP(full) if world > 1 else full
+    T = LONG_T
+    x = make_input(1, T, cfg["dim"], dup=0.2, seed=7, device=dev, dtype=torch.bfloat16)
+    t = timed(lambda: layer(x), args.steps, args.warmup, world)
+    flops = prefill_flops(1, T, cfg["dim"], full.H, full.HKV, full.HD)
+    return {"value": T * args.steps / t, "unit": "tok/s", "ms_per_step": t / args.steps * 1e3,
+            "workload": "configs[4]: Bolt3Attn prefill, Llama-3-8B shape (D4096 H32/8 HD128 theta5e5), "
+                        "1 x 131072 tokens, 20% near-duplicates, seeded random weights",
+            "parallelism": f"tp{world} by KV head" if world > 1 else "one GPU, all 8 KV heads",
+            "roofline": {"bound": "tensor", "achieved": flops * args.steps / t / 1e12, "peak": tf_peak,
+                         "unit": "TFLOP/s", "frac": flops * args.steps / t / 1e12 / tf_peak}}
+
+
 def cpu_baseline(args):
     """The reference algorithm on the host cores (oracle port, fp32), bounded sample of configs[1]."""
     from oracle import Store, forward, oracle_cfg
@@ -437,6 +461,7 @@ def main():
     ap.add_argument("--seq", type=int, default=PREFILL_T, help="prefill tokens per sequence (profiling cases)")
     ap.add_argument("--decode-only", action="store_true", help="only the configs[2] decode measurement (profiling)")
     ap.add_argument("--decode-steps", type=int, default=DEC_STEPS, help="timed decode steps")
+    ap.add_argument("--long", action="store_true", help="only the configs[4] long-context prefill")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -454,7 +479,11 @@ def main():
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     try:
-        if args.decode_only:
+        if args.long:
+            dev = torch.device("cuda", local)
+            torch.cuda.set_device(dev)
+            res = {"long_context": run_long(args, rank, world, dev, peaks()[1])}
+        elif args.decode_only:
             dev = torch.device("cuda", local)
             torch.cuda.set_device(dev)
             cfg, m = build_layer(dev)
