@@ -2,10 +2,10 @@
 
 Runs the reference `vsa_lm.config.bolt3` (Bolt3Attn.forward, Bolt3Decoder.step) on the CPU in fp32
 on seeded inputs and writes the outputs, the per-consolidation bank states and the merge/evict
-decisions to `tests/golden/*.pt`. The reference source tree is needed only here (default path
-/root/reference, override with VSA_LM_REF); the fixtures travel with the repository.
+decisions to `tests/golden/*.pt`. The reference source tree (the vsa_lm checkout, given by the
+VSA_LM_REF environment variable) is needed only here; the fixtures travel with the repository.
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py
+    VSA_LM_REF=<vsa_lm checkout> PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py
 """
 from __future__ import annotations
 
@@ -17,7 +17,9 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 sys.dont_write_bytecode = True
-REF = os.environ.get("VSA_LM_REF", "/root/reference")
+REF = os.environ.get("VSA_LM_REF")
+if not REF:
+    sys.exit("set VSA_LM_REF to the reference vsa_lm source tree")
 sys.path.insert(0, REF)
 
 from vsa_lm.config.bolt3 import Bolt3Attn, Bolt3Decoder  # noqa: E402  (reference)
