@@ -402,7 +402,7 @@ def run_long(args, rank, world, dev, tf_peak):
     T = LONG_T
     x = make_input(1, T, cfg["dim"], dup=0.2, seed=7, device=dev, dtype=torch.bfloat16)
     t = timed(lambda: layer(x), args.steps, args.warmup, world)
-    flops = prefill_flops(1, T, cfg["dim"], full.H, full.HKV, full.HD)
+    flops = prefill_flops(1, T, cfg["dim"], full.H, full.HKV, full.HD)["total"]
     return {"value": T * args.steps / t, "unit": "tok/s", "ms_per_step": t / args.steps * 1e3,
             "workload": "configs[4]: Bolt3Attn prefill, Llama-3-8B shape (D4096 H32/8 HD128 theta5e5), "
                         "1 x 131072 tokens, 20% near-duplicates, seeded random weights",

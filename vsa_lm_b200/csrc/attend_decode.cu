@@ -24,6 +24,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <type_traits>
 
@@ -844,15 +845,18 @@ int launch(const bolt3_attend_args* a, cudaStream_t s) {
       return -1;
   }
   const size_t smem = sizeof(Smem) + 1024;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(attend_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return BOLT3_ERR_CUDA;
-    attr_set = true;
-  }
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return BOLT3_ERR_CUDA;
+  // the shared-memory opt-in is per device: set it the first time each device launches
+  constexpr int kMaxDev = 64;
+  static std::atomic<bool> attr_set[kMaxDev];
+  if (dev >= kMaxDev) return BOLT3_ERR_CUDA;
+  if (!attr_set[dev].load(std::memory_order_acquire)) {
+    if (cudaFuncSetAttribute(attend_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return BOLT3_ERR_CUDA;
+    attr_set[dev].store(true, std::memory_order_release);
+  }
   const int grid = (int)std::min<int64_t>(nc, sms);
   attend_stream_kernel<<<grid, kThreads, smem, s>>>(*a, m);
   return cudaGetLastError() == cudaSuccess ? BOLT3_OK : BOLT3_ERR_CUDA;
