@@ -126,6 +126,7 @@ def test_consolidation_teacher_forced(shape, B, T, dup):
     ("config0", 1, 1024, "chunks"),
     ("qwen3_4b", 2, 1024, 0.3),
     ("llama3_8b", 1, 896, 0.2),     # configs[4]'s shape: no qk-norm, RoPE theta 5e5, D 4096
+    ("tiny", 1, 8960, 0.2),         # 68 consolidations: scan segments past the front-loaded table
     ("tiny", 2, 700, 0.3),
     ("tiny", 1, 100, 0.0), ("tiny", 1, 128, 0.0), ("tiny", 1, 132, 0.0), ("tiny", 1, 256, 0.0),
     ("tiny", 1, 257, 0.0), ("tiny", 3, 300, 0.0), ("tiny", 1, 1, 0.0),

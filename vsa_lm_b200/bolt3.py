@@ -282,12 +282,18 @@ class Bolt3Attn(nn.Module):
     # Scan segment lengths, front-loaded: the attention of bank-reading chunks cannot start before the
     # q projection is done anyway, while every relaunch costs a bank reload and the slowest chain.
     SCAN_SEGMENTS = (32, 12, 8, 6, 4)
+    # Past the table (long sequences) the segments double up to this length: each relaunch costs a
+    # bank reload and a launch gap, while a long segment only delays the attention of its own chunks.
+    SCAN_SEGMENT_MAX = 64
 
     def _scan_segments(self, n_cons: int):
-        """(first step, steps) of each scan launch; the last length repeats past the table."""
+        """(first step, steps) of each scan launch: the table, then doubling lengths up to
+        SCAN_SEGMENT_MAX."""
         out, s0, i = [], 0, 0
+        nt = len(self.SCAN_SEGMENTS)
         while s0 < n_cons:
-            n = min(self.SCAN_SEGMENTS[min(i, len(self.SCAN_SEGMENTS) - 1)], n_cons - s0)
+            n = self.SCAN_SEGMENTS[i] if i < nt else min(self.SCAN_SEGMENT_MAX, self.SCAN_SEGMENTS[-1] << (i - nt + 1))
+            n = min(n, n_cons - s0)
             out.append((s0, n))
             s0 += n
             i += 1
