@@ -111,42 +111,3 @@ def test_tp_decode_shards_sum_to_layer():
         got = got.to(torch.bfloat16)
         output_close(got.cpu(), ref.float().cpu(), f"decode step at {p}")
 
-
-def _nccl_worker(rank: int, world: int, port: int, out):
-    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
-    from datetime import timedelta
-
-    from vsa_lm_b200.tp import Bolt3AttnTP
-    torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
-                            device_id=torch.device("cuda", rank))
-    try:
-        cfg = layer_cfg("qwen3_4b")
-        m = bf16_module(cfg, 0, device=f"cuda:{rank}")
-        tp = Bolt3AttnTP(m)
-        x = make_input(2, 700, cfg["dim"], dup=0.3, seed=4).to(torch.bfloat16).cuda()
-        y = tp(x)
-        torch.cuda.synchronize()
-        if rank == 0:
-            out.put((y.float().cpu(), m(x).float().cpu()))
-        dist.barrier()
-    finally:
-        dist.destroy_process_group()
-
-
-@pytest.mark.gpu
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp_nccl_two_gpus_matches_layer():
-    """Bolt3AttnTP over two GPUs (one NCCL all-reduce of the o_proj partials) against the
-    unsharded native layer on GPU 0."""
-    ctx = mp.get_context("spawn")
-    out = ctx.Queue()
-    port = 29600 + os.getpid() % 1000
-    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, out)) for r in range(2)]
-    for p in procs:
-        p.start()
-    y, ref = out.get(timeout=600)
-    for p in procs:
-        p.join(timeout=120)
-        assert p.exitcode == 0
-    output_close(y, ref, "two-GPU tensor-parallel layer")
