@@ -16,6 +16,20 @@ namespace {
 
 using namespace b3;
 
+// Packed bf16 pair arithmetic, each result rounded to nearest even on its own (no contraction of a
+// multiply into a following add).
+B3_DEV uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+B3_DEV uint32_t add_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+B3_DEV uint32_t neg_bf16x2(uint32_t a) { return a ^ 0x80008000u; }
+
 template <int HD, int TB>
 __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
   constexpr int LPR = HD / 8;          // lanes per head row
@@ -29,15 +43,17 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
   const int sub = lane / LPR, l = lane % LPR;   // row slot within the warp, lane within the row
   const bool first = l < HALF;         // holds elements of the first half
 
-  // cos/sin of the HD/2 frequencies for each of the block's tokens, shared by all their heads
-  __shared__ float s_cos[TB][HD / 2], s_sin[TB][HD / 2];
-  for (int i = threadIdx.x; i < ntb * (HD / 2); i += blockDim.x) {
-    const int tl = i / (HD / 2), fi = i % (HD / 2);
+  // bf16 cos/sin of the HD/2 frequencies for each of the block's tokens, shared by all their
+  // heads, stored as pairs of adjacent frequencies (the operands of the packed RoPE below)
+  __shared__ uint32_t s_cos[TB][HD / 4], s_sin[TB][HD / 4];
+  for (int i = threadIdx.x; i < ntb * (HD / 4); i += blockDim.x) {
+    const int tl = i / (HD / 4), fp = i % (HD / 4);
     const float pos = (float)(a.pos0 + (tok0 + tl) % a.T);
-    float sv, cv;
-    sincosf(__fmul_rn(pos, a.inv_freq[fi]), &sv, &cv);
-    s_cos[tl][fi] = rbf(cv);
-    s_sin[tl][fi] = rbf(sv);
+    float s0, c0, s1, c1;
+    sincosf(__fmul_rn(pos, a.inv_freq[2 * fp]), &s0, &c0);
+    sincosf(__fmul_rn(pos, a.inv_freq[2 * fp + 1]), &s1, &c1);
+    s_cos[tl][fp] = pack_bf16(c0, c1);
+    s_sin[tl][fp] = pack_bf16(s0, s1);
   }
 
   // head rows per token: [0, H) q when parts & 1, then HKV k and HKV v rows when parts & 2
@@ -112,13 +128,9 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
       l2 = row_sum(l2);
     }
     // RoPE partner values (element i <-> i + HD/2), exchanged as the stored bf16 pairs
-    float y[8];
+    uint32_t yp[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float2 f = unpack_bf16(__shfl_xor_sync(0xffffffffu, raw[q], HALF));
-      y[2 * q] = f.x;
-      y[2 * q + 1] = f.y;
-    }
+    for (int q = 0; q < 4; ++q) yp[q] = __shfl_xor_sync(0xffffffffu, raw[q], HALF);
     if (!live) return;
     if (kind == 2) {
       *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(a.v) + off) = make_uint4(raw[0], raw[1], raw[2], raw[3]);
@@ -126,19 +138,18 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
     }
     if (kind == 0 && a.q_l2 != nullptr && l == 0)
       a.q_l2[((int64_t)b * a.H + head) * a.eta_head_stride + a.eta_t_off + t] = sqrtf(l2);
-    const float* cs = &s_cos[tl][(l % HALF) * 8];  // frequency index: element index mod HD/2
-    const float* sn = &s_sin[tl][(l % HALF) * 8];
-    // rope = bf16(bf16(x cos) + bf16(partner sin)), the roundings done two at a time;
-    // rotate_half: the first half pairs with -x[i + HD/2], the second half with x[i - HD/2]
+    const uint32_t* cs = &s_cos[tl][(l % HALF) * 4];  // frequency index: element index mod HD/2
+    const uint32_t* sn = &s_sin[tl][(l % HALF) * 4];
+    // rope = bf16(bf16(x cos) + bf16(partner sin)), two elements per packed bf16 operation: the
+    // product of two bf16 values is exact in fp32, so one rounding of it is the reference's
+    // fp32-product-then-bf16 value, and the sum of two bf16 values rounds the same way directly
+    // or through fp32 (exact in fp32 unless one term is below the other's rounding unit, when both
+    // give the larger). rotate_half: the first half pairs with -x[i + HD/2], the second with x[i - HD/2].
     uint32_t rot[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const int e0 = 2 * q, e1 = 2 * q + 1;
-      const float p0 = first ? -y[e0] : y[e0], p1 = first ? -y[e1] : y[e1];
-      uint32_t tmp;
-      const float2 xc = rbf2(__fmul_rn(x[e0], cs[e0]), __fmul_rn(x[e1], cs[e1]), tmp);
-      const float2 ps = rbf2(__fmul_rn(p0, sn[e0]), __fmul_rn(p1, sn[e1]), tmp);
-      rot[q] = pack_bf16(__fadd_rn(xc.x, ps.x), __fadd_rn(xc.y, ps.y));
+      const uint32_t ps = mul_bf16x2(yp[q], sn[q]);
+      rot[q] = add_bf16x2(mul_bf16x2(raw[q], cs[q]), first ? neg_bf16x2(ps) : ps);
     }
     *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(kind == 0 ? a.q_raw : a.k_raw) + off) =
         make_uint4(raw[0], raw[1], raw[2], raw[3]);
