@@ -434,17 +434,37 @@ def cpu_baseline(args):
 
 
 def run_reference(args, rank, world):
+    """The reference arm: the reference algorithm (CPU oracle port, fp32) on the host cores, with
+    all host threads, on configs[1]'s shape. Each of the --warmup untimed and --steps timed steps is
+    one bounded sample: a forward of 1 x --cpu-tokens tokens. Rank 0 only."""
     if rank != 0:
         return None
-    cpu = cpu_baseline(args)
-    return {"metric": METRIC, "impl": "reference", "value": cpu["value"], "unit": "tok/s", "n_gpus": world,
-            "steps": 1, "warmup": 0, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "configs[1] shape prefill on the host cores (reference algorithm, CPU "
-                                   "PyTorch port)", "global_batch": 1, "seq_len": args.cpu_tokens,
-                       "parallelism": "host threads"},
-            "cpu_baseline": cpu,
-            "e2e": {"value": cpu["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    from oracle import Store, forward, oracle_cfg
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = layer_cfg(SHAPE)
+    P = make_params(cfg, 0)
+    oc = oracle_cfg(cfg)
+    T = args.cpu_tokens
+    x = make_input(1, T, cfg["dim"], dup=DUP, seed=1)
+    for _ in range(args.warmup):
+        forward(P, oc, x, Store("fp32"))
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        forward(P, oc, x, Store("fp32"))
+    dt = time.perf_counter() - t0
+    value = args.steps * T / dt
+    sample = f"configs[1] shape, 1 x {T} tokens per step, fp32, {args.steps} timed step(s) in {dt:.1f} s"
+    return {"metric": METRIC, "impl": "reference", "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "configs[1]: Bolt3Attn prefill, Qwen3-4B shape (D2560 H32/8 HD128 theta1e6 "
+                                   "qk_norm), 30% near-duplicates, seeded random weights; reference algorithm on "
+                                   "the host cores, a bounded sample per step",
+                       "global_batch": 1, "seq_len": T, "parallelism": "host threads"},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def main():
