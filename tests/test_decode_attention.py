@@ -19,6 +19,8 @@ C, S = 128, 128
     (128, 4, 40, 0, 4, 1, False, False),       # first chunk: no previous chunk, no bank
     (128, 4, 40, 128, 0, 1, False, True),      # second chunk's first token, bank not yet formed
     (128, 2, 40, 128, 70, 2, True, False),     # two tokens of two query heads (4 rows)
+    (128, 1, 40, 128, 10, 1, True, False),     # one query head per KV head: 1 row, 3 padded
+    (128, 3, 40, 128, 50, 1, True, True),      # three query heads per KV head: 3 rows
     (64, 3, 40, 128, 100, 1, True, False),     # HD = 64: the warp-per-chain kernel
 ])
 def test_decode_attention_matches_oracle(HD, G, B, L0, len_before, Tq, bank, q_l2):
