@@ -590,6 +590,8 @@ class Bolt3Decoder:
         return ti.gather(-1, torch.multinomial(F.softmax(tv, -1), 1))
 
     # ---- one Bolt-3 layer (bolt3.py:343-425)
+    PLAN_MAX_TOKENS = 16   # steps of up to this many tokens keep their buffers and arguments
+
     @staticmethod
     def _step_plan(ly: Bolt3Attn, st: Bolt3LayerState, b: int, t: int, f, dev):
         """Buffers and prebuilt bolt3_prep / bolt3_attend arguments of a t-token step."""
@@ -653,7 +655,10 @@ class Bolt3Decoder:
             f = ly.fused(dev)
             if plan is None or plan.key != f.key:
                 plan = Bolt3Decoder._step_plan(ly, st, b, t, f, dev)
-                st._plans[t] = plan
+                # only decode-sized steps keep their plan: a prompt chunk's buffers are large and
+                # the per-call set-up is small next to its work
+                if t <= Bolt3Decoder.PLAN_MAX_TOKENS:
+                    st._plans[t] = plan
         proj = F.linear(h.reshape(b * t, D).to(torch.bfloat16), plan.w_in, plan.b_in)
         plan.args.launch_prep(proj, pos_start, st.cur_slot * C + st.cur_len)
         has_prev = st.prev_slot >= 0
