@@ -11,3 +11,4 @@ tree, which exists only in the build container) on seeded inputs and commits the
 test `tests/test_oracle_golden.py` checks this oracle against those fixtures.
 """
 from .bolt3_oracle import *  # noqa: F401,F403
+from .model_oracle import ModelDecoderOracle  # noqa: F401

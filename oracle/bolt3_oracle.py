@@ -202,9 +202,12 @@ def consolidate(bank: dict | None, kr: torch.Tensor, kp: torch.Tensor, v: torch.
         gersh = torch.bmm(gram, w_ev.unsqueeze(-1)).squeeze(-1).clamp_min(1.0)
         err = (v32 - torch.bmm(kr_n, m_res)) * (w_ev / gersh).unsqueeze(-1)
         m_res = gam.float().repeat(b).view(bh, 1, 1) * m_res + torch.bmm(kr_n.transpose(1, 2), err)
-        rec.update(kind="full", rel_err=rel_err, best_sim_k=best_sim_k, best_slot=best_slot, sim_v=sim_v,
-                   merge=merge, score=score_j, keep=keep, top_vals=top_vals, top_toks=top_toks,
-                   bot_vals=bot_vals, bot_slots=bot_slots, win=win, ins=ins)
+        # runner-up cosine of each token: a near-tie with best_sim_k makes the merge target ambiguous
+        second_sim_k = cos_k.topk(2, dim=-1).values[..., 1] if S > 1 else best_sim_k
+        rec.update(kind="full", rel_err=rel_err, best_sim_k=best_sim_k, second_sim_k=second_sim_k,
+                   best_slot=best_slot, sim_v=sim_v, merge=merge, score=score_j, keep=keep,
+                   top_vals=top_vals, top_toks=top_toks, bot_vals=bot_vals, bot_slots=bot_slots, win=win,
+                   ins=ins)
         if record is not None:
             record.append(rec)
         return dict(ak=ak, av=av, mass=mass, util=util, pm=pm, act=act, m_res=m_res, n_filled=n_filled)
@@ -286,17 +289,21 @@ def n_consolidations(T: int, C: int) -> int:
 
 
 def forward(params: dict, cfg: dict, x: torch.Tensor, store: Store, *, S: int = 128, C: int = 128,
-            record: list | None = None, snapshots: list | None = None, return_y_heads: bool = False):
+            record: list | None = None, snapshots: list | None = None, return_y_heads: bool = False,
+            proj: tuple | None = None):
     """Bolt3Attn.forward (bolt3.py:194-276): chunked three-field attention + o_proj.
 
     x: [b, T, D]. Returns [b, T, D] (stored values). `record` collects the per-consolidation
-    decisions; `snapshots` collects the bank after each consolidation.
+    decisions; `snapshots` collects the bank after each consolidation. `proj` (optional) replaces
+    the projections with given stored values (q_raw, k_raw, v, beta, eta) in project()'s layouts,
+    so that the rest of the algorithm can be checked on exactly the inputs another implementation
+    computed.
     """
     b, T, _ = x.shape
     H, HKV, HD = cfg["H"], cfg["HKV"], cfg["HD"]
     G = H // HKV
     inv_freq = cfg["inv_freq"]
-    q_r, k_r, v, beta, eta = project(params, cfg, x, store)
+    q_r, k_r, v, beta, eta = project(params, cfg, x, store) if proj is None else [t.float() for t in proj]
     pos = torch.arange(T, dtype=torch.float32)
     q_p = rope_at(q_r, pos, inv_freq, store)
     k_p = rope_at(k_r, pos, inv_freq, store)
@@ -361,13 +368,14 @@ class LayerDecoderOracle:
                     pm=self.sc["pm"], act=self.sc["act"],
                     m_res=self.m_res.view(-1, self.cfg["HD"], self.cfg["HD"]), n_filled=self.n_filled)
 
-    def step(self, h: torch.Tensor, pos_start: int) -> torch.Tensor:
+    def step(self, h: torch.Tensor, pos_start: int, proj: tuple | None = None) -> torch.Tensor:
+        """`proj` (optional): the step's projections as stored values, as in forward()."""
         p, cfg, st, sc = self.p, self.cfg, self.store, self.sc
         b, t, _ = h.shape
         H, HKV, HD = cfg["H"], cfg["HKV"], cfg["HD"]
         G = H // HKV
         inv_freq = cfg["inv_freq"]
-        q_r, k_r, v, beta, eta = project(p, cfg, h, st)
+        q_r, k_r, v, beta, eta = project(p, cfg, h, st) if proj is None else [t_.float() for t_ in proj]
         pos = torch.arange(pos_start, pos_start + t, dtype=torch.float32)
         q_p, k_p = rope_at(q_r, pos, inv_freq, st), rope_at(k_r, pos, inv_freq, st)
         gam = gamma_delta(p["log_gamma"])

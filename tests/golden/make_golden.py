@@ -24,7 +24,8 @@ sys.path.insert(0, REF)
 
 from vsa_lm.config.bolt3 import Bolt3Attn, Bolt3Decoder  # noqa: E402  (reference)
 
-from vsa_lm_b200.workloads import layer_cfg, make_input, make_params  # noqa: E402
+from vsa_lm_b200.workloads import (MODEL_SHAPES, layer_cfg, make_input, make_model_params,  # noqa: E402
+                                   make_params)
 
 torch.set_num_threads(max(1, os.cpu_count() or 1))
 
@@ -152,6 +153,53 @@ def decoder_case(name, shape, B, prompt_T, n_decode, seed=0, xseed=3):
     print(name, "steps", len(steps), "consolidations", len(calls))
 
 
+def model_case(name, shape="tiny_lm", seed=0, prompt_T=300, n_steps=24, doc_a=768, doc_b=256, question=50,
+               n_new=12):
+    """A whole hybrid model (reference UniversalVSALM with is_bolt3=True) under the reference
+    Bolt3Decoder: prefill + teacher-forced one-token steps (final hidden states and logits), then
+    the memory-bank flow: memorize document A from a blank state, memorize B after it, forget B,
+    continue_generate a question greedily (bolt3.py:449-557). Document A is long enough for full-bank
+    consolidations to write M_res before B starts, so that forgetting B leaves a nonzero state."""
+    from vsa_lm.config.standard import UniversalVSALM
+
+    mcfg = dict(MODEL_SHAPES[shape])
+    model = UniversalVSALM(**mcfg, max_T=2048, chunk_size=128, is_bolt3=True, bolt3_S=128, bolt3_C=128)
+    params = make_model_params(mcfg, seed)
+    missing, unexpected = model.load_state_dict(params, strict=False)
+    assert not unexpected and all(".rope." in k for k in missing), (missing, unexpected)
+    model.eval()
+    dec = Bolt3Decoder(model)
+    V = mcfg["vocab_size"]
+    g = torch.Generator().manual_seed(seed + 77)
+    ids = torch.randint(0, V, (1, prompt_T + n_steps), generator=g)
+    out = {"kind": "model", "shape": shape, "mcfg": mcfg, "seed": seed, "ids": ids,
+           "layer_types": model.config["layer_types"]}
+    clones = lambda xs: [x.clone() if x is not None else None for x in xs]
+    with torch.no_grad():
+        h, states, kv = dec.prefill(ids[:, :prompt_T])
+        hs, logits = [h[:, -1].clone()], [model.lm_head(h[:, -1]).clone()]
+        for i in range(n_steps):
+            p0 = prompt_T + i
+            h, states, kv = dec.step(ids[:, p0:p0 + 1], p0, states, kv)
+            hs.append(h[:, -1].clone())
+            logits.append(model.lm_head(h[:, -1]).clone())
+        out.update(h_last=torch.stack(hs, 1), logits=torch.stack(logits, 1))
+        doc = torch.randint(0, V, (1, doc_a + doc_b), generator=g)
+        q_ids = torch.randint(0, V, (1, question), generator=g)
+        states, kv = Bolt3Decoder.blank_state(model, 1, "cpu", max_kv_len=2048)
+        states, kv, pos_a, _ = dec.memorize(doc[:, :doc_a], states, kv, 0)
+        states, kv, pos_b, traces = dec.memorize(doc[:, doc_a:], states, kv, pos_a)
+        after_b = clones(states)
+        states = dec.forget(traces, states, next_pos=pos_b)
+        toks, states, kv, pos = dec.continue_generate(q_ids, states, kv, pos_b, n_new, temperature=0.0)
+        out.update(doc=doc, q_ids=q_ids, pos_a=pos_a, pos_b=pos_b, states_after_b=clones(after_b),
+                   traces=[None if t is None else (t[0], t[1].clone()) for t in traces],
+                   states_after_forget=clones(dec.forget(traces, clones(after_b), pos_b)),
+                   gen=toks.clone(), gen_pos=pos, states_final=clones(states))
+    torch.save(out, os.path.join(HERE, f"{name}.pt"))
+    print(name, "layers", out["layer_types"], "generated", toks.tolist())
+
+
 if __name__ == "__main__":
     forward_case("config0_fp32", "config0", 1, 1024, "chunks", keep=(0, 2, 5))
     forward_case("tiny_ragged_bias_fp32", "tiny", 2, 700, 0.3, seed=2, xseed=5, qkv_bias=True,
@@ -161,3 +209,4 @@ if __name__ == "__main__":
         forward_case(f"tiny_T{T}_fp32", "tiny", 1, T, 0.0, seed=4, xseed=T, keep=(0,),
                      full_y=T <= 132)
     decoder_case("decoder_tiny_fp32", "tiny", 2, 300, 150)
+    model_case("model_tiny_lm_fp32")

@@ -6,11 +6,11 @@ import pytest
 import torch
 
 from oracle import Store, forward, LayerDecoderOracle, oracle_cfg
-from vsa_lm_b200.workloads import make_input, make_params
+from vsa_lm_b200.workloads import make_input, make_model_params, make_params
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 GOLD = os.path.join(HERE, "golden")
-FORWARD = sorted(p for p in glob.glob(os.path.join(GOLD, "*.pt")) if "decoder" not in p)
+FORWARD = sorted(p for p in glob.glob(os.path.join(GOLD, "*.pt")) if "decoder" not in p and "model" not in p)
 
 
 def row_digest(y):
@@ -67,3 +67,58 @@ def test_decoder_matches_reference():
     for k in ("ak", "av", "mass", "util", "pm"):
         torch.testing.assert_close(dec.sc[k], g["final"][k], rtol=1e-4, atol=2e-5)
     assert torch.equal(dec.sc["act"], g["final"]["act"])
+
+
+def _model_oracle(g, store):
+    from oracle import ModelDecoderOracle
+
+    mcfg = g["mcfg"]
+    params = make_model_params(mcfg, g["seed"])
+    lcfg = oracle_cfg(dict(dim=mcfg["dim"], num_heads=mcfg["num_heads"], num_kv_heads=mcfg["num_kv_heads"],
+                           head_dim=mcfg["head_dim"], eps=mcfg["eps"], rope_theta=mcfg["rope_theta"],
+                           qk_norm=mcfg["qk_norm"]))
+    return lambda: ModelDecoderOracle(params, lcfg, g["layer_types"], 1, store, mcfg["eps"])
+
+
+def test_model_decoder_matches_reference():
+    """The model-level decode oracle (embedding, norms, Bolt-3 layers, softmax anchor, MLP) against
+    the reference UniversalVSALM under Bolt3Decoder: prefill, one-token steps, and the memory-bank
+    flow (memorize twice, forget, greedy continue_generate)."""
+    g = load(os.path.join(GOLD, "model_tiny_lm_fp32.pt"))
+    new = _model_oracle(g, Store("fp32"))
+    ids = g["ids"]
+    T = ids.shape[1] - g["logits"].shape[1] + 1
+    o = new()
+    h, pos = o.feed(ids[:, :T], 0)
+    hs, lg = [h[:, -1]], [o.logits(h[:, -1])]
+    for i in range(g["logits"].shape[1] - 1):
+        h = o.step(ids[:, T + i:T + i + 1], T + i)
+        hs.append(h[:, -1])
+        lg.append(o.logits(h[:, -1]))
+    torch.testing.assert_close(torch.stack(hs, 1), g["h_last"], rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(torch.stack(lg, 1), g["logits"], rtol=1e-4, atol=1e-4)
+
+    o = new()
+    doc, na = g["doc"], g["pos_a"]
+    pos_a, _ = o.memorize(doc[:, :na], 0)
+    pos_b, traces = o.memorize(doc[:, na:], pos_a)
+    assert (pos_a, pos_b) == (g["pos_a"], g["pos_b"])
+    vsa = [i for i, t in enumerate(g["layer_types"]) if t == "vsa"]
+    for i in vsa:
+        torch.testing.assert_close(o.m_res(i), g["states_after_b"][i], rtol=1e-4, atol=1e-5)
+        assert traces[i][0] == g["traces"][i][0]
+        torch.testing.assert_close(traces[i][1], g["traces"][i][1], rtol=1e-4, atol=1e-5)
+    o.forget(traces, pos_b)
+    for i in vsa:
+        torch.testing.assert_close(o.m_res(i), g["states_after_forget"][i], rtol=1e-4, atol=1e-5)
+    h, pos = o.feed(g["q_ids"], pos_b)
+    toks = []
+    for _ in range(g["gen"].shape[1]):
+        nxt = o.logits(h[:, -1]).argmax(-1, keepdim=True)
+        toks.append(nxt)
+        h = o.step(nxt, pos)
+        pos += 1
+    assert torch.equal(torch.cat(toks, 1), g["gen"])
+    assert pos == g["gen_pos"]
+    for i in vsa:
+        torch.testing.assert_close(o.m_res(i), g["states_final"][i], rtol=1e-4, atol=1e-5)

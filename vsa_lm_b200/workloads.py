@@ -103,3 +103,60 @@ def make_input(B: int, T: int, D: int, dup=0.0, seed: int = 1, C: int = 128,
             # read sources from the clean copy so that chains of copies stay near their origin
             x[bi, tt] = x[bi, src[bi, pick[bi]]] + noise[bi, pick[bi]]
     return x.to(dtype)
+
+
+# Hybrid model shapes for the decoder-level tests (Bolt3LM keyword arguments). "tiny_lm" has two
+# Bolt-3 layers and one softmax anchor (hybrid_every = 3).
+MODEL_SHAPES = {
+    "tiny_lm": dict(vocab_size=512, dim=256, num_layers=3, num_heads=4, num_kv_heads=2, head_dim=64,
+                    intermediate=512, hybrid_every=3, rope_theta=1e4, eps=1e-5, qk_norm=False,
+                    tie_word_embeddings=False),
+}
+
+
+def model_layer_types(mcfg: dict) -> list[str]:
+    """Bolt-3 ("vsa") or softmax anchor per layer: every hybrid_every-th layer is an anchor
+    (vsa_lm/config/inspector.py:55-58)."""
+    he = int(mcfg["hybrid_every"])
+    return ["softmax" if he > 0 and (li + 1) % he == 0 else "vsa" for li in range(int(mcfg["num_layers"]))]
+
+
+def make_model_params(mcfg: dict, seed: int = 0) -> dict:
+    """Seeded parameters of a whole hybrid model with the reference's state_dict keys
+    (vsa_lm/config/standard.py:366-399): every Bolt-3 layer from make_params, anchors and MLPs
+    uniform in +-1/sqrt(fan_in), norms near 1, embedding N(0, 1)."""
+    g = torch.Generator().manual_seed(seed)
+    D, V, I = int(mcfg["dim"]), int(mcfg["vocab_size"]), int(mcfg["intermediate"])
+    H, HKV = int(mcfg["num_heads"]), int(mcfg["num_kv_heads"])
+    HD = int(mcfg.get("head_dim") or D // H)
+
+    def lin(n_out, n_in):
+        return (torch.rand(n_out, n_in, generator=g) * 2 - 1) / math.sqrt(n_in)
+
+    def norm(n):
+        return 1.0 + 0.05 * torch.randn(n, generator=g)
+
+    lcfg = dict(dim=D, num_heads=H, num_kv_heads=HKV, head_dim=HD, rope_theta=mcfg["rope_theta"],
+                eps=mcfg["eps"], qk_norm=mcfg.get("qk_norm", False))
+    p = {"embed_tokens.weight": torch.randn(V, D, generator=g)}
+    for li, t in enumerate(model_layer_types(mcfg)):
+        pre = f"blocks.{li}."
+        p[pre + "norm1.weight"] = norm(D)
+        if t == "vsa":
+            for k, v in make_params(lcfg, seed * 1000 + li).items():
+                p[pre + "vsa." + k] = v
+        else:
+            p[pre + "attn.q_proj.weight"] = lin(H * HD, D)
+            p[pre + "attn.k_proj.weight"] = lin(HKV * HD, D)
+            p[pre + "attn.v_proj.weight"] = lin(HKV * HD, D)
+            p[pre + "attn.o_proj.weight"] = lin(D, H * HD)
+            if mcfg.get("qk_norm", False):
+                p[pre + "attn.q_norm.weight"] = norm(HD)
+                p[pre + "attn.k_norm.weight"] = norm(HD)
+        p[pre + "norm2.weight"] = norm(D)
+        p[pre + "mlp.gate_proj.weight"] = lin(I, D)
+        p[pre + "mlp.up_proj.weight"] = lin(I, D)
+        p[pre + "mlp.down_proj.weight"] = lin(D, I)
+    p["norm.weight"] = norm(D)
+    p["lm_head.weight"] = p["embed_tokens.weight"] if mcfg.get("tie_word_embeddings", True) else lin(V, D)
+    return p
