@@ -50,20 +50,28 @@ def profile_traffic():
     return json.load(open(p)) if os.path.exists(p) else {}
 
 
+def pci_bus_id(dev) -> str:
+    """The PCI bus id of a CUDA device as nvidia-smi names it. nvidia-smi ignores
+    CUDA_VISIBLE_DEVICES, so on a leased GPU its index would select another device."""
+    p = torch.cuda.get_device_properties(dev)
+    return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+
+
 class Clocks:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Samples nvidia-smi clocks and throttle reasons of one GPU (by PCI bus id) while the timed
+    region runs."""
 
     Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index, self.proc, self.out = index, None, None
+    def __init__(self, dev):
+        self.bus_id, self.proc, self.out = pci_bus_id(dev), None, None
 
     def __enter__(self):
         try:
             self.out = open(os.path.join("/tmp", f"bolt3_clocks_{os.getpid()}.csv"), "w+")
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.bus_id, f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=self.out, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
@@ -78,7 +86,8 @@ class Clocks:
 
     def summary(self):
         if self.proc is None or self.out is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"],
+                    "gpu_pci_bus_id": self.bus_id}
         self.out.seek(0)
         rows = [r.split(",") for r in self.out.read().strip().splitlines() if r.strip()]
         sm, mx, reasons = [], None, set()
@@ -93,7 +102,7 @@ class Clocks:
             except (ValueError, IndexError):
                 continue
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "samples": len(sm),
-                "reasons": sorted(reasons)}
+                "reasons": sorted(reasons), "gpu_pci_bus_id": self.bus_id}
 
 
 def timed(fn, steps: int, warmup: int, world: int, stream=None):
@@ -275,7 +284,7 @@ def run_native(args, rank, world, local):
     c0 = K.launch_count()
     step()
     launches_per_step = K.launch_count() - c0  # this library's kernels in one step (cuBLAS GEMMs excluded)
-    with Clocks(local) as clk:
+    with Clocks(dev) as clk:
         t_prefill = timed(step, args.steps, args.warmup, world)
     clocks = clk.summary()
     tok = B * T

@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define BOLT3_ABI_VERSION 5
+#define BOLT3_ABI_VERSION 6
 
 enum bolt3_status {
   BOLT3_OK = 0,
@@ -81,7 +81,10 @@ int bolt3_prep(const bolt3_prep_args* a, void* stream);
  *   (ak, av, ak_rope, m_res) is written in the plain row-major layouts listed at the top.
  * `ak_rope` (optional) receives RoPE(ak, pm) of the final bank. `status` (optional, device int)
  * is OR-ed with 1 when a kernel-side bounds check of the tie-order emulation fires, and with 4 when
- * a bounded wait for a tensor-core product expired. */
+ * a bounded wait for a tensor-core product expired.
+ * `wait_probe` is a failure-path test hook and 0 in normal use. When nonzero, every CTA's first
+ * thread polls a barrier that nothing arrives at `wait_probe` times; the wait runs out, status
+ * bit 4 is set, and the kernel returns without touching the bank or starting any copy or MMA. */
 typedef struct bolt3_consolidate_args {
   int n_chains, hkv, HD;
   void* ak; void* av; void* ak_rope;
@@ -94,6 +97,7 @@ typedef struct bolt3_consolidate_args {
   void* snap_ak_rope; void* snap_av; float* snap_mass; uint8_t* snap_act; void* snap_m;
   int64_t snap_cap; int64_t snap0;
   int32_t* status;
+  uint32_t wait_probe;                /* test hook, 0 in normal use (see above) */
 } bolt3_consolidate_args;
 int bolt3_consolidate(const bolt3_consolidate_args* a, void* stream);
 
@@ -112,7 +116,11 @@ int bolt3_consolidate(const bolt3_consolidate_args* a, void* stream);
  *     bank (slot 0 of [chains][bank_cap] arrays) are given explicitly.
  * bank_m: prefill = 1 reads the split bf16 image bolt3_consolidate writes to snap_m; prefill = 0
  * reads M_res itself, fp32 [chains][HD][HD]. q_l2 (optional, [B*H][Tq] fp32) holds |q_raw| per row
- * as bolt3_prep writes it; without it the kernel computes the norms. */
+ * as bolt3_prep writes it; without it the kernel computes the norms.
+ * `wait_probe` is a failure-path test hook and 0 in normal use. When nonzero, the kernels that
+ * have bounded waits (the tensor-core prefill tile and the streaming one-token decode kernel) poll
+ * a barrier that nothing arrives at `wait_probe` times, set status bit 2 and return without
+ * writing y. The warp-per-chain decode kernel has no waits and ignores it. */
 typedef struct bolt3_attend_args {
   int n_chains, hkv, G, HD;
   const void* q_rope; const void* q_raw; const float* eta; int64_t Tq;
@@ -133,6 +141,7 @@ typedef struct bolt3_attend_args {
   const float* q_l2;                   /* optional |q_raw| per row, [B*H][Tq] */
   int64_t blk_begin, blk_count;        /* prefill: query blocks [blk_begin, blk_begin + blk_count)
                                           (blk_count = 0: every block) */
+  uint32_t wait_probe;                 /* test hook, 0 in normal use (see above) */
 } bolt3_attend_args;
 int bolt3_attend(const bolt3_attend_args* a, void* stream);
 
@@ -164,13 +173,16 @@ int bolt3_prefill_fwd(const bolt3_prefill_args* a, void* stream);
  * For hosts that cannot allocate device memory on their hot path (an engine that pools all of HBM
  * itself, a C-ABI host without a device allocator, a loop that cannot afford cudaMalloc's implicit
  * device synchronisation). The snapshot workspace is a fixed BOLT3_NOALLOC_SCRATCH_BYTES array
- * inside the library, reserved on every GPU that loads it until the process exits; `workspace` and
+ * inside the library: CUDA reserves it in a context when the library's device code is first used
+ * there (lazy module loading) and holds it until the process exits. `workspace` and
  * `workspace_bytes` of the arguments are ignored. Work needing more than that returns
  * BOLT3_ERR_CAPACITY (32 MiB covers 254 chain-consolidations at HD = 128: e.g. one Qwen3-4B-shape
- * sequence of up to 4224 tokens, or configs[0] whole). The first call on a device looks up the
- * array's device address with that device current; make it before any stream capture. Calls share
- * the array: two calls that overlap on the GPU (different streams, or different host threads)
- * race and must be ordered by the caller. Allocates nothing (no cudaMalloc / cudaFree). */
+ * sequence of up to 4224 tokens, or configs[0] whole). The first call in a context (each device's
+ * primary context, or a context the host created) looks up the array's device address with that
+ * context current and caches it under the context's unique id; make that first call before any
+ * stream capture. Calls share the array: two calls that overlap on the GPU (different streams, or
+ * different host threads) race and must be ordered by the caller. Allocates nothing (no
+ * cudaMalloc / cudaFree). */
 #define BOLT3_NOALLOC_SCRATCH_BYTES (32u << 20)
 int bolt3_prefill_fwd_noalloc(const bolt3_prefill_args* a, void* stream);
 

@@ -35,10 +35,11 @@ def _prepared(m, x):
     return t
 
 
-def test_noalloc_prefill_matches_workspace_prefill_twice():
+@pytest.mark.parametrize("shape,B,T", [("qwen3_4b", 1, 2048), ("tiny", 2, 1300)])   # HD = 128 and HD = 64
+def test_noalloc_prefill_matches_workspace_prefill_twice(shape, B, T):
     """Two calls in a row, on different inputs, each against the allocating entry point."""
-    cfg, _, x1 = inputs("qwen3_4b", 1, 2048, 0.3, seed=11)
-    _, _, x2 = inputs("qwen3_4b", 1, 2048, 0.3, seed=12)
+    cfg, _, x1 = inputs(shape, B, T, 0.3, seed=11)
+    _, _, x2 = inputs(shape, B, T, 0.3, seed=12)
     m = bf16_module(cfg, 0)
     for x in (x1, x2):
         t = _prepared(m, x)

@@ -18,6 +18,11 @@ _SZ = ctypes.c_size_t
 STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported shape", 3: "misaligned pointer",
           4: "buffer too small", 5: "CUDA error"}
 
+# Bits of the device status word the kernels OR into (include/bolt3.h)
+DEVICE_STATUS_BITS = {1: "a bounds check of the consolidation's tie-order emulation fired",
+                      2: "a bounded wait in an attention kernel expired",
+                      4: "a bounded wait in the consolidation scan expired"}
+
 
 class PrepArgs(ctypes.Structure):
     _fields_ = [
@@ -49,6 +54,7 @@ class ConsolidateArgs(ctypes.Structure):
         ("snap_ak_rope", _P), ("snap_av", _P), ("snap_mass", _P), ("snap_act", _P), ("snap_m", _P),
         ("snap_cap", _I64), ("snap0", _I64),
         ("status", _P),
+        ("wait_probe", ctypes.c_uint32),
     ]
 
 
@@ -68,6 +74,7 @@ class AttendArgs(ctypes.Structure):
         ("status", _P),
         ("q_l2", _P),
         ("blk_begin", _I64), ("blk_count", _I64),
+        ("wait_probe", ctypes.c_uint32),
     ]
 
 
@@ -100,6 +107,8 @@ SIGNATURES = {
     "bolt3_topk_order_host": ([_P, _I, _I, _I, _P], _I),
 }
 
+ABI_VERSION = 6   # BOLT3_ABI_VERSION in include/bolt3.h
+
 # Fixed scratch of bolt3_prefill_fwd_noalloc (BOLT3_NOALLOC_SCRATCH_BYTES in include/bolt3.h)
 NOALLOC_SCRATCH_BYTES = 32 << 20
 
@@ -124,7 +133,7 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = argt
             fn.restype = rest
-        if lib.bolt3_abi_version() != 5:
+        if lib.bolt3_abi_version() != ABI_VERSION:
             raise RuntimeError("libbolt3.so ABI version mismatch; rebuild with `python -m vsa_lm_b200.build`")
         _lib = lib
         return lib

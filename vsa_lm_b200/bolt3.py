@@ -29,7 +29,8 @@ N_SINKS = 4
 # helper modules with the reference's parameter layout (vsa_lm/surgery.py:43-93)
 
 class LlamaRMSNorm(nn.Module):
-    """RMSNorm with an fp32 interior (surgery.py:43-53)."""
+    """RMSNorm computed in fp32 and cast back to the input dtype; parameter `weight` as in the
+    reference (surgery.py:43-53), so checkpoints load."""
 
     def __init__(self, dim: int, eps: float = 1e-5):
         super().__init__()
@@ -37,14 +38,13 @@ class LlamaRMSNorm(nn.Module):
         self.eps = eps
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        dt = x.dtype
-        xf = x.float()
-        xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
-        return (xf * self.weight.float()).to(dt)
+        out = F.rms_norm(x.float(), (x.shape[-1],), self.weight.float(), self.eps)
+        return out.to(x.dtype)
 
 
 def llama_inv_freq(head_dim: int, theta: float, rope_scaling: dict | None, device=None) -> torch.Tensor:
-    """RoPE inverse frequencies with optional llama3 scaling (surgery.py:56-72)."""
+    """RoPE inverse frequencies with optional llama3 scaling. The values must equal the reference's
+    bit for bit (surgery.py:56-72), so the arithmetic follows it step by step."""
     inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64, device=device).float() / head_dim))
     if rope_scaling and rope_scaling.get("rope_type") == "llama3":
         old_ctx = float(rope_scaling["original_max_position_embeddings"])
@@ -60,7 +60,9 @@ def llama_inv_freq(head_dim: int, theta: float, rope_scaling: dict | None, devic
 
 
 class LlamaRoPE(nn.Module):
-    """Rotate-half RoPE with a non-persistent inv_freq buffer (surgery.py:80-93)."""
+    """Rotate-half RoPE at integer positions pos_start + t, with cos/sin rounded to the input dtype
+    and the products and sums in that dtype (the reference's arithmetic, surgery.py:80-93). The
+    `inv_freq` buffer is non-persistent, as in the reference."""
 
     def __init__(self, head_dim: int, theta: float, rope_scaling: dict | None):
         super().__init__()
@@ -68,13 +70,11 @@ class LlamaRoPE(nn.Module):
                              persistent=False)
 
     def forward(self, x: torch.Tensor, pos_start: int = 0) -> torch.Tensor:
-        T = x.shape[2]
-        t = torch.arange(pos_start, pos_start + T, device=x.device, dtype=torch.float32)
-        freqs = t[:, None] * self.inv_freq.to(x.device)
-        emb = torch.cat((freqs, freqs), dim=-1)
-        cos, sin = emb.cos().to(x.dtype)[None, None], emb.sin().to(x.dtype)[None, None]
-        h = x.shape[-1] // 2
-        return x * cos + torch.cat((-x[..., h:], x[..., :h]), dim=-1) * sin
+        pos = torch.arange(x.shape[2], device=x.device, dtype=torch.float32) + float(pos_start)
+        ang = torch.outer(pos, self.inv_freq.to(device=x.device, dtype=torch.float32))
+        c, s = ang.cos().to(x.dtype), ang.sin().to(x.dtype)
+        x1, x2 = x.chunk(2, dim=-1)
+        return torch.cat((x1 * c - x2 * s, x2 * c + x1 * s), dim=-1)
 
 
 # --------------------------------------------------------------------------------------------
@@ -237,10 +237,26 @@ class Bolt3Attn(nn.Module):
             return _NativeForward.apply(x, self, *[p for p in self.parameters() if p.requires_grad])
         return self._native_forward(x)
 
+    # ---- device status word (include/bolt3.h): one per device this module runs on
+    def device_status(self, device) -> K.DeviceStatus:
+        cache = self.__dict__.setdefault("_status_words", {})
+        key = str(torch.device(device))
+        if key not in cache:
+            cache[key] = K.DeviceStatus(device)
+        return cache[key]
+
+    def check_status(self, block: bool = True) -> None:
+        """Raise RuntimeError if a kernel of an earlier forward reported an error (an expired
+        bounded wait or a failed bounds check). Every forward already checks the previous one's
+        status without waiting; `block` waits for the last forward's kernels to finish."""
+        for st in self.__dict__.get("_status_words", {}).values():
+            st.check(block)
+
     @torch.no_grad()
-    def _native_forward(self, x: torch.Tensor, partial_fp32: bool = False) -> torch.Tensor:
-        """The forward on CUDA. partial_fp32: return o_proj's output in fp32, unrounded (a tensor-
-        parallel shard's partial sum, rounded once after the all-reduce)."""
+    def _prepare(self, x: torch.Tensor):
+        """Projections + RMSNorm/RoPE/gates of the whole input (phase A, bolt3.py:196-199), as the
+        head-major buffers the scan and the attention read. Returns a namespace of the buffers and a
+        callable that runs the q/eta half (so the caller can start the scan on k/v/beta first)."""
         if not x.is_cuda:
             raise RuntimeError("Bolt3Attn (B200 native) runs on CUDA tensors only; no CPU path exists")
         b, T, D = x.shape
@@ -250,32 +266,55 @@ class Bolt3Attn(nn.Module):
         c = f.consts
         x2 = x.reshape(b * T, D).to(torch.bfloat16)
         bf = dict(dtype=torch.bfloat16, device=dev)
-        q_raw = torch.empty(b * H, T, HD, **bf)
-        q_rope = torch.empty_like(q_raw)
-        k_raw = torch.empty(b * HKV, T, HD, **bf)
-        k_rope = torch.empty_like(k_raw)
-        v = torch.empty_like(k_raw)
-        beta = torch.empty(b * HKV, T, dtype=torch.float32, device=dev)
-        eta = torch.empty(b * H, T, dtype=torch.float32, device=dev)
-        q_l2 = torch.empty(b * H, T, dtype=torch.float32, device=dev)
+        p = types.SimpleNamespace(b=b, T=T, f=f, consts=c)
+        p.q_raw = torch.empty(b * H, T, HD, **bf)
+        p.q_rope = torch.empty_like(p.q_raw)
+        p.k_raw = torch.empty(b * HKV, T, HD, **bf)
+        p.k_rope = torch.empty_like(p.k_raw)
+        p.v = torch.empty_like(p.k_raw)
+        p.beta = torch.empty(b * HKV, T, dtype=torch.float32, device=dev)
+        p.eta = torch.empty(b * H, T, dtype=torch.float32, device=dev)
+        p.q_l2 = torch.empty(b * H, T, dtype=torch.float32, device=dev)
         common = dict(B=b, T=T, H=H, HKV=HKV, HD=HD, inv_freq=c["inv_freq"], eps=self.eps, q_norm_w=c["qn"],
                       k_norm_w=c["kn"], pos0=0)
         # k/v/beta first: the consolidation scan waits only on them
-        K.prep(self.project(x2, f, "kv"), cols=f.cols_kv, parts=2, k_raw=k_raw, k_rope=k_rope, v=v, beta=beta,
-               k_head_stride=T, k_t_off=0, **common)
-        ws = torch.empty(max(1, K.prefill_workspace_bytes(b * HKV, T, HD)), dtype=torch.uint8, device=dev)
-        bank = K.new_bank(b * HKV, HD, dev)
-        y = torch.empty(b, T, H, HD, **bf)
+        K.prep(self.project(x2, f, "kv"), cols=f.cols_kv, parts=2, k_raw=p.k_raw, k_rope=p.k_rope, v=p.v,
+               beta=p.beta, k_head_stride=T, k_t_off=0, **common)
 
         def prep_q():
-            K.prep(self.project(x2, f, "q"), cols=f.cols_q, parts=1, q_raw=q_raw, q_rope=q_rope, eta=eta,
-                   q_head_stride=T, q_t_off=0, q_l2=q_l2, **common)
+            K.prep(self.project(x2, f, "q"), cols=f.cols_q, parts=1, q_raw=p.q_raw, q_rope=p.q_rope, eta=p.eta,
+                   q_head_stride=T, q_t_off=0, q_l2=p.q_l2, **common)
+        return p, prep_q
 
-        self._scan_and_attend(b, T, q_rope=q_rope, q_raw=q_raw, eta=eta, k_raw=k_raw, k_rope=k_rope, v=v,
-                              beta=beta, q_l2=q_l2, ws=ws, bank=bank, y=y, consts=c, before_attend=prep_q)
+    @torch.no_grad()
+    def _attention_heads(self, x: torch.Tensor) -> torch.Tensor:
+        """The attention output of every head before o_proj, y [b, T, H, HD] bf16 (phases A-C of
+        bolt3.py:194-274). Checks the previous call's device status without waiting, and arms this
+        call's."""
+        status = self.device_status(x.device)
+        status.check(block=False)
+        p, prep_q = self._prepare(x)
+        b, T = p.b, p.T
+        dev = x.device
+        ws = torch.empty(max(1, K.prefill_workspace_bytes(b * self.HKV, T, self.HD)), dtype=torch.uint8, device=dev)
+        bank = K.new_bank(b * self.HKV, self.HD, dev)
+        y = torch.empty(b, T, self.H, self.HD, dtype=torch.bfloat16, device=dev)
+        self._scan_and_attend(b, T, q_rope=p.q_rope, q_raw=p.q_raw, eta=p.eta, k_raw=p.k_raw, k_rope=p.k_rope,
+                              v=p.v, beta=p.beta, q_l2=p.q_l2, ws=ws, bank=bank, y=y, consts=p.consts,
+                              before_attend=prep_q, status=status)
+        status.arm(f"Bolt3Attn forward of {b} x {T} tokens")
+        return y
+
+    @torch.no_grad()
+    def _native_forward(self, x: torch.Tensor, partial_fp32: bool = False) -> torch.Tensor:
+        """The forward on CUDA. partial_fp32: return o_proj's output in fp32, unrounded (a tensor-
+        parallel shard's partial sum, rounded once after the all-reduce)."""
+        y = self._attention_heads(x)
+        b, T = x.shape[:2]
+        f = self.fused(x.device)
         if partial_fp32:
-            return torch.mm(y.view(b * T, H * HD), f.w_out.t(), out_dtype=torch.float32).view(b, T, -1)
-        out = F.linear(y.view(b, T, H * HD), f.w_out)
+            return torch.mm(y.view(b * T, self.H * self.HD), f.w_out.t(), out_dtype=torch.float32).view(b, T, -1)
+        out = F.linear(y.view(b, T, self.H * self.HD), f.w_out)
         return out.to(x.dtype)
 
     # scan steps per segment when the consolidation scan overlaps the attention
@@ -309,7 +348,7 @@ class Bolt3Attn(nn.Module):
         return cache[key]
 
     def _scan_and_attend(self, b, T, *, q_rope, q_raw, eta, k_raw, k_rope, v, beta, q_l2, ws, bank, y, consts,
-                         before_attend=None):
+                         before_attend=None, status=None):
         """Phases B and C of the forward (bolt3.py:210-273), overlapped on two streams.
 
         The consolidation scan is sequential per chain and fills only b*HKV SMs, so it runs on a
@@ -321,7 +360,7 @@ class Bolt3Attn(nn.Module):
         n_cons = K.n_consolidations(T)
         att = dict(n_chains=b * HKV, hkv=HKV, G=G, HD=HD, T=T, q_rope=q_rope, q_raw=q_raw, eta=eta,
                    k_rope=k_rope, v=v, n_cons=n_cons, kappa=c["kappa"], coef=c["coef"], res_w=c["res_w"],
-                   eps=self.eps, y=y, q_l2=q_l2)
+                   eps=self.eps, y=y, q_l2=q_l2, status=status)
         if n_cons == 0:
             if before_attend is not None:
                 before_attend()
@@ -339,7 +378,8 @@ class Bolt3Attn(nn.Module):
                 K.consolidate(n_chains=b * HKV, hkv=HKV, HD=HD, bank=bank, init_blank=s0 == 0, kr=k_raw, kp=k_rope,
                               v=v, beta=beta, chain_tokens=T, token0=s0 * self.C, step_tokens=self.C,
                               skip0=N_SINKS if s0 == 0 else 0, chunk_len=self.C, pos0=0, n_steps=n,
-                              kappa=c["kappa"], gamma=c["gamma"], inv_freq=c["inv_freq"], snaps=snaps, snap0=s0)
+                              kappa=c["kappa"], gamma=c["gamma"], inv_freq=c["inv_freq"], snaps=snaps, snap0=s0,
+                              status=status)
                 ev = torch.cuda.Event()
                 ev.record(aux)
                 done.append((s0 + n, ev))
@@ -387,7 +427,10 @@ class Bolt3Attn(nn.Module):
         K.consolidate(n_chains=bh, hkv=hkv, HD=hd, bank=bank, init_blank=blank, kr=kr, kp=kp, v=vv, beta=bb,
                       chain_tokens=l_tok, token0=0, step_tokens=l_tok, skip0=0, chunk_len=l_tok, pos0=pos0,
                       n_steps=1, kappa=f.consts["kappa"], gamma=gam.float().contiguous(),
-                      inv_freq=f.consts["inv_freq"])
+                      inv_freq=f.consts["inv_freq"], status=self.device_status(dev))
+        st = self.device_status(dev)
+        st.arm(f"_consolidate_functional of {bh} chains")
+        st.check(block=True)
         nf = 0 if blank else int(n_filled)
         nf = nf if nf >= self.S else nf + min(self.S - nf, l_tok)
         return (bank["ak"].to(dt), bank["av"].to(dt), bank["mass"], bank["util"], bank["pm"],
@@ -422,10 +465,23 @@ class Bolt3LayerState:
         self.sinks_set = False
         self.n_filled = 0
         self._plans = {}   # per step size: buffers and prebuilt launch arguments (Bolt3Decoder)
+        # device status word of this state's kernels, checked at every chunk boundary
+        self.status = K.DeviceStatus(device)
 
     @property
     def has_bank(self) -> bool:
         return self.n_filled > 0
+
+    @staticmethod
+    def bytes_per_sequence(ly: Bolt3Attn) -> int:
+        """Device bytes one sequence's state of layer `ly` occupies: the buffers __init__ allocates
+        (window ring kr/kp/v/beta, sinks, bank ak/av/ak_rope/mass/util/pm/act/n_filled) plus the
+        caller's M_res."""
+        HKV, HD, C, S = ly.HKV, ly.HD, ly.C, ly.S
+        ring = 3 * 2 * C * HD * 2 + 2 * C * 4
+        sinks = 2 * N_SINKS * HD * 2
+        bank = 3 * S * HD * 2 + 3 * S * 4 + S + 4
+        return HKV * (ring + sinks + bank + HD * HD * 4)
 
 
 class Bolt3Decoder:
@@ -442,28 +498,37 @@ class Bolt3Decoder:
 
     @staticmethod
     def state_bytes(model):
-        flat, per_tok = 0, 0
-        for blk in model.blocks:
-            if hasattr(blk, "vsa"):
-                ly = blk.vsa
-                flat += ly.HKV * ly.HD * ly.HD * 4 + 2 * ly.S * ly.HKV * ly.HD * 2 + 4 * ly.C * ly.HKV * ly.HD * 2
-            else:
-                s = blk.attn
-                per_tok += 2 * s.HKV * s.HD * 2
-        return flat, per_tok
+        """(bytes of fixed-size state per sequence, bytes per token of the anchor layers' KV caches),
+        the same pair the reference reports (bolt3.py:290-300), counted from the buffers this
+        decoder actually keeps (Bolt3LayerState.bytes_per_sequence, AnchorKV's bf16 k and v)."""
+        fixed = sum(Bolt3LayerState.bytes_per_sequence(b.vsa) for b in model.blocks if hasattr(b, "vsa"))
+        per_token = sum(2 * b.attn.HKV * b.attn.HD * 2 for b in model.blocks if not hasattr(b, "vsa"))
+        return fixed, per_token
 
     @staticmethod
     def blank_state(model, batch_size: int, device, max_kv_len: int = 4096, state_dtype=torch.float32, **kwargs):
-        states, kv_caches = [None] * len(model.blocks), [None] * len(model.blocks)
-        for li, blk in enumerate(model.blocks):
+        """(states, kv_caches) for `batch_size` sequences (bolt3.py:302-319): per Bolt-3 layer an fp32
+        M_res [B, HKV, HD, HD] in states and a Bolt3LayerState in kv_caches; per softmax anchor an
+        AnchorKV with room for max_kv_len tokens. M_res is always fp32 (the kernels update it in place)."""
+        states, kv_caches = [], []
+        for blk in model.blocks:
             if hasattr(blk, "vsa"):
                 ly = blk.vsa
-                states[li] = torch.zeros(batch_size, ly.HKV, ly.HD, ly.HD, device=device, dtype=torch.float32)
-                kv_caches[li] = Bolt3LayerState(ly, batch_size, device)
+                states.append(torch.zeros(batch_size, ly.HKV, ly.HD, ly.HD, device=device, dtype=torch.float32))
+                kv_caches.append(Bolt3LayerState(ly, batch_size, device))
             else:
-                s = blk.attn
-                kv_caches[li] = StaticKV(batch_size, s.HKV, max_kv_len, s.HD, device, dt=torch.bfloat16)
+                a = blk.attn
+                states.append(None)
+                kv_caches.append(AnchorKV(batch_size, a.HKV, max_kv_len, a.HD, device, dt=torch.bfloat16))
         return states, kv_caches
+
+    @staticmethod
+    def check_status(kv_caches, block: bool = True) -> None:
+        """Raise RuntimeError if a kernel of an earlier step reported an error (an expired bounded
+        wait or a failed bounds check). Steps already check at every chunk boundary."""
+        for st in kv_caches:
+            if isinstance(st, Bolt3LayerState):
+                st.status.check(block)
 
     # ---- decode state in the reference's format (bolt3.py:302-319 creates it, :343-425 fills it):
     # per Bolt-3 layer a dict with the bank (ak/av [b*HKV, S, HD], mass/util/pm fp32 [b*HKV, S], act
@@ -577,17 +642,24 @@ class Bolt3Decoder:
 
     @staticmethod
     def _sample(logits, temperature: float, top_k: int = 40, top_p: float = 0.95):
+        """Next token of every row, [B, 1] (the reference's sampling rule, bolt3.py:321-333): greedy
+        for temperature ~ 0; otherwise a draw from softmax(logits / temperature) restricted to the
+        nucleus (the tokens, by descending probability, whose preceding mass is <= top_p) when
+        top_p < 1, else to the top_k logits. The draw is a Gumbel-max on the device, so nothing
+        waits on the host."""
         if temperature <= 1e-5:
-            return logits.argmax(-1, keepdim=True)
-        probs = F.softmax(logits.float() / temperature, dim=-1)
+            return logits.argmax(dim=-1, keepdim=True)
+        z = logits.float() / temperature
         if top_p < 1.0:
-            sp, si = torch.sort(probs, descending=True, dim=-1)
-            cp = torch.cumsum(sp, dim=-1)
-            sp[cp - sp > top_p] = 0.0
-            sp.div_(sp.sum(dim=-1, keepdim=True).clamp_min(1e-12))
-            return si.gather(-1, torch.multinomial(sp, 1))
-        tv, ti = torch.topk(logits.float() / temperature, min(top_k, logits.size(-1)), dim=-1)
-        return ti.gather(-1, torch.multinomial(F.softmax(tv, -1), 1))
+            probs, order = torch.sort(torch.softmax(z, dim=-1), dim=-1, descending=True)
+            ahead = torch.cumsum(probs, dim=-1) - probs
+            cand = torch.where(ahead > top_p, torch.full_like(probs, float("-inf")), probs.log())
+        else:
+            vals, order = torch.topk(z, min(top_k, z.shape[-1]), dim=-1)
+            cand = torch.log_softmax(vals, dim=-1)
+        u = torch.rand_like(cand).clamp_(1e-20, 1.0)
+        pick = torch.argmax(cand - torch.log(-torch.log(u)), dim=-1, keepdim=True)
+        return order.gather(-1, pick)
 
     # ---- one Bolt-3 layer (bolt3.py:343-425)
     PLAN_MAX_TOKENS = 16   # steps of up to this many tokens keep their buffers and arguments
@@ -626,7 +698,8 @@ class Bolt3Decoder:
             sink_k=st.sink_k.data_ptr(), sink_v=st.sink_v.data_ptr(), sink_chain_tokens=N_SINKS,
             bank_ak_rope=bk["ak_rope"].data_ptr(), bank_av=bk["av"].data_ptr(), bank_mass=bk["mass"].data_ptr(),
             bank_act=bk["act"].data_ptr(), bank_cap=1, kappa=c["kappa"].data_ptr(), coef=c["coef"].data_ptr(),
-            res_w=c["res_w"].data_ptr(), eps=ly.eps, y=plan.y.data_ptr(), y_tokens=t, q_l2=plan.q_l2.data_ptr())
+            res_w=c["res_w"].data_ptr(), eps=ly.eps, y=plan.y.data_ptr(), y_tokens=t, q_l2=plan.q_l2.data_ptr(),
+            status=st.status.word.data_ptr())
         plan.args = K.DecodeStepArgs(prep, attend)
         return plan
 
@@ -638,15 +711,23 @@ class Bolt3Decoder:
         b, t, D = h.shape
         H, HKV, HD, C, G = ly.H, ly.HKV, ly.HD, ly.C, ly.G
         if st.cur_len + t > C:
+            # The reference then lets the pending chunk grow past C and later consolidates a chunk of
+            # up to 2C-1 tokens (bolt3.py:355-363, 406-425); the native kernels hold chunks of at
+            # most C tokens and windows of two such chunks.
             raise NotImplementedError(
-                f"a step of {t} tokens on top of {st.cur_len} pending ones exceeds one chunk ({C}); "
-                "the native decoder keeps at most one chunk pending")
+                f"a step of {t} tokens on top of {st.cur_len} pending ones exceeds one chunk ({C}); the native "
+                f"decoder consolidates chunks of exactly {C} tokens: split the step at the chunk boundary")
+        if b != st.B or h.device != m_res.device or not h.is_cuda:
+            raise ValueError(f"hidden states [{b}, {t}, {D}] on {h.device} do not match a state of {st.B} sequences "
+                             f"with M_res on {m_res.device}")
+        if h.device.index != torch.cuda.current_device():
+            raise RuntimeError(f"the step's tensors are on {h.device}; make that device current")
+        if not (m_res.dtype == torch.float32 and m_res.is_contiguous() and tuple(m_res.shape) == (b, HKV, HD, HD)):
+            raise ValueError(f"m_res must be a contiguous fp32 CUDA tensor [{b}, {HKV}, {HD}, {HD}]")
         if st.cur_len == 0:
             st.slot_pos[st.cur_slot] = pos_start
         elif pos_start != st.slot_pos[st.cur_slot] + st.cur_len:
             raise NotImplementedError("native decoder needs contiguous positions within a chunk")
-        if not (m_res.is_cuda and m_res.dtype == torch.float32 and m_res.is_contiguous()):
-            raise ValueError("m_res must be a contiguous fp32 CUDA tensor [B, HKV, HD, HD]")
         dev = h.device
         # the step's buffers and launch arguments, rebuilt when the layer's weights change (checked
         # whenever a chunk starts) or the step size does
@@ -677,6 +758,8 @@ class Bolt3Decoder:
         c = plan.consts
         st.cur_len += t
         if st.cur_len >= C:                                                   # bolt3.py:406-425
+            # errors of the previous chunk's kernels (their status copy finished long ago)
+            st.status.check(block=True)
             if has_prev:
                 skip = 0
                 if not st.sinks_set:
@@ -690,94 +773,212 @@ class Bolt3Decoder:
                               kr=st.ring_kr, kp=st.ring_kp, v=st.ring_v, beta=st.ring_b, chain_tokens=2 * C,
                               token0=p0, step_tokens=C, skip0=skip, chunk_len=C,
                               pos0=st.slot_pos[st.prev_slot] - p0, n_steps=1, kappa=c["kappa"],
-                              gamma=c["gamma"], inv_freq=c["inv_freq"])
+                              gamma=c["gamma"], inv_freq=c["inv_freq"], status=st.status)
                 nf = st.n_filled
                 st.n_filled = nf if nf >= ly.S else nf + min(ly.S - nf, C - skip)
             st.prev_slot, st.cur_slot, st.cur_len = st.cur_slot, 1 - st.cur_slot, 0
+            st.status.arm(f"Bolt-3 decode chunk ending at position {pos_start + t}")
         return out
+
+    @staticmethod
+    def _anchor_attention(ly, cache: "AnchorKV", h: torch.Tensor, pos_start: int) -> torch.Tensor:
+        """A softmax anchor layer's attention branch for t new tokens (bolt3.py:426-445): RoPE at
+        pos_start, the new k/v appended to the layer's cache, causal within the new block."""
+        b, t, _ = h.shape
+        q, k, v = ly.head_qkv(h)
+        q, k = ly.rope(q, pos_start=pos_start), ly.rope(k, pos_start=pos_start)
+        n_before = cache.n
+        keys, vals = cache.append(k, v)
+        mask = None
+        if t > 1:   # query i sees every cached key and the new keys up to itself
+            mask = torch.ones(t, n_before + t, dtype=torch.bool, device=h.device).tril(diagonal=n_before)
+        y = F.scaled_dot_product_attention(q, keys.to(q.dtype), vals.to(q.dtype), attn_mask=mask,
+                                           enable_gqa=ly.G > 1)
+        return ly.o_proj(y.transpose(1, 2).reshape(b, t, ly.H * ly.HD))
 
     @torch.no_grad()
     def step(self, tokens: torch.Tensor, pos_start: int, states, kv_caches, record=None):
+        """Run t new tokens [b, t] at positions pos_start.. through every block; returns the final
+        normed hidden states [b, t, D] and the (updated in place) state lists (bolt3.py:335-447)."""
         m = self.model
-        b, t_s = tokens.shape
         with torch.autocast("cuda", torch.bfloat16, enabled=tokens.is_cuda):
             x = m.embed_tokens(tokens)
             for li, blk in enumerate(m.blocks):
                 h = blk.norm1(x)
                 if hasattr(blk, "vsa"):
-                    x = x + self.layer_step(blk.vsa, kv_caches[li], h, pos_start, states[li]).to(x.dtype)
+                    attn = self.layer_step(blk.vsa, kv_caches[li], h, pos_start, states[li])
                 else:
-                    ly = blk.attn
-                    q, k, v = ly.head_qkv(h)
-                    q, k = ly.rope(q, pos_start=pos_start), ly.rope(k, pos_start=pos_start)
-                    n_prev = kv_caches[li].n
-                    pk, pv = kv_caches[li].append(k, v)
-                    mask = None
-                    if t_s > 1:
-                        qi = torch.arange(t_s, device=tokens.device)[:, None]
-                        kj = torch.arange(n_prev + t_s, device=tokens.device)[None, :]
-                        mask = (kj <= (n_prev + qi)).view(1, 1, t_s, n_prev + t_s)
-                    y = F.scaled_dot_product_attention(q, pk.to(q.dtype), pv.to(q.dtype), attn_mask=mask,
-                                                       enable_gqa=(ly.G > 1))
-                    x = x + ly.o_proj(y.transpose(1, 2).reshape(b, t_s, ly.H * ly.HD))
+                    attn = self._anchor_attention(blk.attn, kv_caches[li], h, pos_start)
+                x = x + attn.to(x.dtype)
                 x = x + blk.mlp(blk.norm2(x))
             return m.norm(x), states, kv_caches
 
+    def _feed(self, ids: torch.Tensor, pos: int, states, kv_caches):
+        """Run a prompt through step() in C-token slices from position `pos`; returns the last
+        slice's hidden states and the position after the prompt."""
+        h = None
+        for s0 in range(0, ids.shape[1], self.C):
+            piece = ids[:, s0:s0 + self.C]
+            h, states, kv_caches = self.step(piece, pos, states, kv_caches)
+            pos += piece.shape[1]
+        return h, pos
+
     @torch.no_grad()
     def prefill(self, ids: torch.Tensor, max_kv_len: int = 4096):
-        b, t = ids.shape
-        states, kv = self.blank_state(self.model, b, ids.device, max_kv_len=max(max_kv_len, t + 1024))
-        h = None
-        for s in range(0, t, self.C):
-            e = min(t, s + self.C)
-            h, states, kv = self.step(ids[:, s:e], s, states, kv)
+        """Fresh state for ids [b, t] and the prompt run through it (bolt3.py:449-457)."""
+        states, kv = self.blank_state(self.model, ids.shape[0], ids.device, max_kv_len=max(max_kv_len, ids.shape[1] + 1024))
+        h, _ = self._feed(ids, 0, states, kv)
         return h, states, kv
 
     @torch.no_grad()
     def generate_batch(self, ids: torch.Tensor, max_new_tokens: int, temperature: float = 0.6, top_k: int = 40,
                        top_p: float = 0.95, eos_ids: set[int] | None = None,
                        close_think_ids: list[int] | None = None):
+        """Decode max_new_tokens for every row of ids [B, T] after prefilling it (bolt3.py:459-500).
+        Returns (tokens [B, n], lengths [B]): a row's length is the step at which it produced an
+        end-of-sequence id (inclusive), else max_new_tokens; decoding stops early once every row has
+        finished (checked every 16 tokens). With close_think_ids, rows that have not closed their
+        thinking block by step max(64, max_new_tokens - 64) are forced to emit that token sequence."""
         B, T = ids.shape
+        dev = ids.device
         h, states, kv = self.prefill(ids, max_kv_len=T + max_new_tokens + 64)
         logits = self.model.lm_head(h[:, -1, :])
-        eos = torch.tensor(sorted(eos_ids or ()), device=ids.device, dtype=torch.long)
-        done = torch.zeros(B, dtype=torch.bool, device=ids.device)
-        lengths = torch.full((B,), max_new_tokens, dtype=torch.long, device=ids.device)
-        out, pos = [], T
+        eos = torch.tensor(sorted(eos_ids or ()), dtype=torch.long, device=dev)
+        finished = torch.zeros(B, dtype=torch.bool, device=dev)
+        lengths = torch.full((B,), max_new_tokens, dtype=torch.long, device=dev)
+        forced = None
+        if close_think_ids:
+            forced = torch.tensor(list(close_think_ids), dtype=torch.long, device=dev)
+            closer = int(close_think_ids[1]) if len(close_think_ids) > 1 else None
+            cursor = torch.full((B,), -1, dtype=torch.long, device=dev)   # next forced token, -1 = none
+            closed = torch.zeros(B, dtype=torch.bool, device=dev)
+            trigger = max(64, max_new_tokens - 64)
+        toks = []
         for i in range(max_new_tokens):
             nxt = self._sample(logits, temperature, top_k=top_k, top_p=top_p)
-            out.append(nxt)
+            if forced is not None:
+                if i == trigger:
+                    cursor = torch.where(~closed & ~finished & (cursor < 0), torch.zeros_like(cursor), cursor)
+                active = cursor >= 0
+                nxt = torch.where(active[:, None], forced[cursor.clamp(min=0)][:, None], nxt)
+                cursor = torch.where(active, cursor + 1, cursor)
+                done_forcing = active & (cursor >= forced.numel())
+                closed = closed | done_forcing
+                cursor = torch.where(done_forcing, torch.full_like(cursor, -1), cursor)
+                if closer is not None:
+                    closed = closed | (nxt[:, 0] == closer)
+            toks.append(nxt)
             if eos.numel():
-                hit = torch.isin(nxt[:, 0], eos) & ~done
-                lengths[hit] = i + 1
-                done |= hit
-                if i % 16 == 15 and bool(done.all()):
+                newly = torch.isin(nxt[:, 0], eos) & ~finished
+                lengths = torch.where(newly, torch.full_like(lengths, i + 1), lengths)
+                finished = finished | newly
+                if i % 16 == 15 and bool(finished.all()):
                     break
-            h, states, kv = self.step(nxt, pos, states, kv)
+            h, states, kv = self.step(nxt, T + i, states, kv)
+            logits = self.model.lm_head(h[:, -1, :])
+        return torch.cat(toks, dim=1), lengths
+
+    @torch.no_grad()
+    def generate(self, prompt: torch.Tensor, max_new_tokens: int, temperature: float = 0.0, top_k: int = 40,
+                 top_p: float = 0.95, eos_ids: set[int] | None = None, close_think_ids: list[int] | None = None):
+        """The prompt followed by the first row's generated tokens up to its length (bolt3.py:502-506)."""
+        toks, n = self.generate_batch(prompt, max_new_tokens, temperature, top_k, top_p, eos_ids, close_think_ids)
+        return torch.cat([prompt, toks[:, :int(n[0])]], dim=1)
+
+    @torch.no_grad()
+    def continue_generate(self, ids: torch.Tensor, states, kv_caches, start_pos: int, max_new_tokens: int,
+                          temperature: float = 0.0, top_k: int = 40, top_p: float = 0.95,
+                          eos_ids: set[int] | None = None):
+        """Feed ids from start_pos onto existing state, then decode up to max_new_tokens, stopping
+        before the step of an end-of-sequence id of row 0 (bolt3.py:508-526). Returns (tokens,
+        states, kv_caches, next position)."""
+        h, pos = self._feed(ids, start_pos, states, kv_caches)
+        logits = self.model.lm_head(h[:, -1, :])
+        toks = []
+        for _ in range(max_new_tokens):
+            nxt = self._sample(logits, temperature, top_k=top_k, top_p=top_p)
+            toks.append(nxt)
+            if eos_ids and int(nxt[0, 0]) in eos_ids:
+                break
+            h, states, kv_caches = self.step(nxt, pos, states, kv_caches)
             logits = self.model.lm_head(h[:, -1, :])
             pos += 1
-        return torch.cat(out, dim=1), lengths
+        out = torch.cat(toks, dim=1) if toks else torch.empty(ids.shape[0], 0, dtype=torch.long, device=ids.device)
+        return out, states, kv_caches, pos
+
+    @torch.no_grad()
+    def memorize(self, ids: torch.Tensor, states, kv_caches, start_pos: int):
+        """Feed a document from start_pos and record, per Bolt-3 layer, the change it made to M_res
+        net of the decay the earlier state went through: trace = (end position, M_after -
+        gamma^(n_tokens // C) * M_before) (bolt3.py:528-545). Other layers get None."""
+        before = {li: states[li].clone() for li, blk in enumerate(self.model.blocks) if hasattr(blk, "vsa")}
+        _, pos = self._feed(ids, start_pos, states, kv_caches)
+        n_tok = ids.shape[1]
+        traces = []
+        for li, blk in enumerate(self.model.blocks):
+            if li not in before:
+                traces.append(None)
+                continue
+            decay = blk.vsa.gamma_delta().to(states[li].device).view(1, -1, 1, 1) ** (n_tok // blk.vsa.C)
+            traces.append((pos, states[li] - decay * before[li]))
+        return states, kv_caches, pos, traces
+
+    @torch.no_grad()
+    def forget(self, traces, states, next_pos: int, kv_caches=None, pre_kv_lens=None):
+        """Subtract memorized traces from M_res, each decayed by the chunks consolidated since its
+        end position: M -= gamma^max(0, (next_pos - end) // C) * delta (bolt3.py:547-557). The new
+        states[li] are fresh fp32 tensors; later steps update them in place."""
+        for li, tr in enumerate(traces):
+            if tr is None or states[li] is None:
+                continue
+            end, delta = tr
+            ly = self.model.blocks[li].vsa
+            k = max(0, (next_pos - end) // ly.C)
+            decay = ly.gamma_delta().to(delta.device).view(1, -1, 1, 1) ** k
+            states[li] = (states[li] - decay * delta).contiguous()
+        return states
 
 
-class StaticKV:
-    """Growing KV cache of a softmax anchor layer (reference: vsa_lm/decode.py:88-106)."""
+class AnchorKV:
+    """KV cache of one softmax anchor layer: a single buffer [2, B, HKV, capacity, HD] written in
+    place. `k`, `v` (views of the buffer) and `n` (tokens held) carry the names of the reference's
+    cache (vsa_lm/decode.py:88-106), so code that reads a cache, such as a cartridge writer, works
+    unchanged. The capacity is max_kv_len rounded up to a multiple of 256 tokens; an append that
+    does not fit doubles it (one copy of the held tokens)."""
 
     def __init__(self, B: int, HKV: int, Tmax: int, HD: int, dev, dt=torch.bfloat16):
-        self.k = torch.empty(B, HKV, Tmax, HD, device=dev, dtype=dt)
-        self.v = torch.empty_like(self.k)
+        cap = max(256, -(-int(Tmax) // 256) * 256)
+        self.buf = torch.empty(2, B, HKV, cap, HD, device=dev, dtype=dt)
         self.n = 0
 
+    @property
+    def k(self) -> torch.Tensor:
+        return self.buf[0]
+
+    @property
+    def v(self) -> torch.Tensor:
+        return self.buf[1]
+
+    @property
+    def capacity(self) -> int:
+        return self.buf.shape[3]
+
     def append(self, k_new: torch.Tensor, v_new: torch.Tensor):
+        """Write L new keys/values [B, HKV, L, HD] after the held ones; returns views of all n."""
         L = k_new.shape[2]
-        if self.n + L > self.k.shape[2]:
-            new_max = max(self.n + L + 1024, self.k.shape[2] * 2)
-            nk = torch.empty(self.k.shape[0], self.k.shape[1], new_max, self.k.shape[3], device=self.k.device,
-                             dtype=self.k.dtype)
-            nv = torch.empty_like(nk)
-            nk[:, :, :self.n] = self.k[:, :, :self.n]
-            nv[:, :, :self.n] = self.v[:, :, :self.n]
-            self.k, self.v = nk, nv
-        self.k[:, :, self.n:self.n + L] = k_new
-        self.v[:, :, self.n:self.n + L] = v_new
+        if self.n + L > self.capacity:
+            cap = self.capacity
+            while cap < self.n + L:
+                cap *= 2
+            grown = torch.empty(*self.buf.shape[:3], cap, self.buf.shape[4], device=self.buf.device,
+                                dtype=self.buf.dtype)
+            grown[:, :, :, :self.n].copy_(self.buf[:, :, :, :self.n])
+            self.buf = grown
+        self.buf[0, :, :, self.n:self.n + L].copy_(k_new)
+        self.buf[1, :, :, self.n:self.n + L].copy_(v_new)
         self.n += L
-        return self.k[:, :, :self.n], self.v[:, :, :self.n]
+        return self.buf[0, :, :, :self.n], self.buf[1, :, :, :self.n]
+
+
+# the reference's name for the anchor-layer cache class (vsa_lm/decode.py:88)
+StaticKV = AnchorKV

@@ -98,6 +98,10 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
   extern __shared__ unsigned char smem_raw[];
   Smem<HD>& sm = *reinterpret_cast<Smem<HD>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5;
+  if (a.wait_probe) {  // failure-path test hook: an expired bounded wait, reported as bit 2
+    if (tid == 0 && !tc5::probe_wait(&sm.bar_s, a.wait_probe) && a.status) atomicOr(a.status, 2);
+    return;
+  }
   const int G = a.G;
   const int g_fast = blockIdx.x;  // head group within the KV head: the G CTAs of one chain-chunk run
   const int blk = (int)a.blk_begin + blockIdx.y;  // together and share K/V through L2

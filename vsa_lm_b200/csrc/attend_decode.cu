@@ -426,6 +426,10 @@ __global__ void __launch_bounds__(kThreads, 1) attend_stream_kernel(const bolt3_
   extern __shared__ unsigned char smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (a.wait_probe) {  // failure-path test hook: an expired bounded wait, reported as bit 2
+    if (tid == 0 && !tc5::probe_wait(&sm.bar_o, a.wait_probe) && a.status) atomicOr(a.status, 2);
+    return;
+  }
   const int G = a.G, T = (int)a.Tq, NR = G * T, H = a.hkv * G;
   const bool has_bank = a.has_bank != 0, has_sinks = a.has_sinks != 0;
   const int len[4] = {has_sinks ? 4 : 0, has_bank ? S : 0, a.seg0_len, a.seg1_len};

@@ -214,6 +214,10 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
   Smem<HD>& sm = *reinterpret_cast<Smem<HD>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int c = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (a.wait_probe) {  // failure-path test hook: an expired bounded wait, reported as bit 4
+    if (tid == 0 && !tc5::probe_wait(&sm.bar[0], a.wait_probe) && a.status) atomicOr(a.status, 4);
+    return;
+  }
   const int h = c % a.hkv;
   const float kappa = a.kappa[h];
   const float gam = a.gamma[h];

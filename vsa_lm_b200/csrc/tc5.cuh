@@ -179,4 +179,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   return false;
 }
 
+// Failure-path test hook (the `wait_probe` argument of bolt3_consolidate / bolt3_attend): one
+// thread initialises `bar` for a single arrival that nothing ever makes and polls it `iters` times.
+// The wait always runs out and returns false; the kernel then reports the expired wait in its status
+// word and returns before it allocates tensor memory or starts any copy or MMA.
+__device__ __forceinline__ bool probe_wait(uint64_t* bar, uint32_t iters) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_u32(bar)) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  return mbar_wait(bar, 0, iters);
+}
+
 }  // namespace tc5

@@ -1,6 +1,11 @@
-"""Torch-facing wrappers of the Bolt-3 C-ABI: check devices, dtypes and contiguity, pass raw pointers
-and the current CUDA stream. PyTorch only provides device memory and streams here; every kernel is
-in libbolt3.so. Nothing here falls back to a CPU or PyTorch implementation.
+"""Torch-facing wrappers of the Bolt-3 C-ABI: check devices, dtypes, layouts and sizes, pass raw
+pointers and the current CUDA stream. PyTorch only provides device memory and streams here; every
+kernel is in libbolt3.so. Nothing here falls back to a CPU or PyTorch implementation.
+
+The C side cannot tell a host pointer from a device pointer, nor a tensor of the current device
+from one on another GPU, so every tensor argument is checked here before its address is passed:
+a CPU tensor, a tensor on a device other than the current one, the wrong dtype, a non-contiguous
+view or too few elements raise before anything is launched.
 """
 from __future__ import annotations
 
@@ -33,13 +38,52 @@ def _count(n: int) -> None:
     _launches += n
 
 
-def _need(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
+def _need(t: torch.Tensor, dtype: torch.dtype, name: str, numel: int | None = None) -> None:
+    """`t` is a contiguous `dtype` tensor on the current CUDA device holding at least `numel`
+    elements (when given)."""
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor, got {type(t).__name__}")
     if not t.is_cuda:
         raise RuntimeError(f"{name} must be a CUDA tensor (the Bolt-3 path has no CPU implementation)")
+    cur = torch.cuda.current_device()
+    if t.device.index != cur:
+        raise RuntimeError(f"{name} is on {t.device}, but the current device is cuda:{cur}; the kernels are "
+                           f"launched on the current device")
     if t.dtype != dtype:
         raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
     if not t.is_contiguous():
         raise ValueError(f"{name} must be contiguous")
+    if numel is not None and t.numel() < numel:
+        raise ValueError(f"{name} holds {t.numel()} elements; the described work needs {numel}")
+
+
+def _need_rows(t: torch.Tensor, name: str, n_chains: int, chain_tokens: int, length: int, HD: int) -> None:
+    """`t` holds bf16 rows of HD values, chain_tokens rows per chain, and the kernel reads rows
+    [0, length) of each of n_chains chains from t's first element. `t` may be a view into a larger
+    buffer (a window ring slot): its rows must be dense, consecutive chains chain_tokens rows apart,
+    and every row read must lie inside t's storage."""
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor (the Bolt-3 path has no CPU implementation)")
+    cur = torch.cuda.current_device()
+    if t.device.index != cur:
+        raise RuntimeError(f"{name} is on {t.device}, but the current device is cuda:{cur}")
+    if t.dtype != torch.bfloat16:
+        raise TypeError(f"{name} must be torch.bfloat16, got {t.dtype}")
+    if length < 0 or length > chain_tokens:
+        raise ValueError(f"{name}: {length} rows in a segment of {chain_tokens} rows per chain")
+    if t.dim() < 2 or t.shape[-1] != HD or t.stride(-1) != 1 or (t.shape[-2] > 1 and t.stride(-2) != HD):
+        raise ValueError(f"{name} must hold dense rows of {HD} values")
+    if t.dim() == 3 and t.shape[0] > 1 and t.stride(0) != chain_tokens * HD:
+        raise ValueError(f"{name}: chains must be {chain_tokens} rows apart")
+    if length > 0:
+        end = t.storage_offset() + ((n_chains - 1) * chain_tokens + length) * HD
+        if end * t.element_size() > t.untyped_storage().nbytes():
+            raise ValueError(f"{name}: the rows read run past the tensor's storage")
+
+
+def _opt(t: torch.Tensor | None, dtype: torch.dtype, name: str, numel: int | None = None) -> None:
+    if t is not None:
+        _need(t, dtype, name, numel)
 
 
 def _stream() -> int:
@@ -50,6 +94,43 @@ def n_consolidations(T: int, C: int = CHUNK) -> int:
     """Consolidations Bolt3Attn.forward runs for T tokens (vsa_lm/config/bolt3.py:262)."""
     full = T // C
     return max(0, full - 2) if T % C == 0 else max(0, full - 1)
+
+
+class DeviceStatus:
+    """The device status word the kernels OR error bits into (include/bolt3.h), and its host side.
+
+    `word` is one int32 on the device, passed as `status` to every kernel call. `arm()` enqueues an
+    asynchronous copy of it into pinned host memory on the current stream, behind the kernels just
+    launched, and records an event. `check(block)` reads that copy once the event has completed
+    (waiting for it when `block`) and raises RuntimeError if any bit is set, clearing the word so
+    that later calls start clean. Nothing here synchronises unless `block` is true."""
+
+    def __init__(self, device):
+        self.word = torch.zeros(1, dtype=torch.int32, device=device)
+        self.host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.event = None
+        self.what = ""
+
+    def arm(self, what: str) -> None:
+        self.host.copy_(self.word, non_blocking=True)
+        self.event = torch.cuda.Event()
+        self.event.record()
+        self.what = what
+
+    def check(self, block: bool = False) -> None:
+        ev = self.event
+        if ev is None:
+            return
+        if block:
+            ev.synchronize()
+        elif not ev.query():
+            return
+        self.event = None
+        bits = int(self.host[0])
+        if bits:
+            self.word.zero_()
+            why = "; ".join(msg for b, msg in _lib.DEVICE_STATUS_BITS.items() if bits & b) or "unknown bits"
+            raise RuntimeError(f"{self.what}: device status {bits:#x} ({why}); the outputs of that call are invalid")
 
 
 def prep(proj: torch.Tensor, *, B: int, T: int, H: int, HKV: int, HD: int, inv_freq: torch.Tensor,
@@ -63,15 +144,23 @@ def prep(proj: torch.Tensor, *, B: int, T: int, H: int, HKV: int, HD: int, inv_f
     |q_raw| per row."""
     lib = _lib.load()
     _need(proj, torch.bfloat16, "proj")
+    if proj.dim() != 2 or proj.shape[0] < B * T:
+        raise ValueError(f"proj must be [tokens >= {B * T}, ld], got {tuple(proj.shape)}")
     outs = []
+    q_rows = B * H * (q_head_stride if q_head_stride else T)
+    k_rows = B * HKV * (k_head_stride if k_head_stride else T)
     if parts & 1:
-        outs += [("q_raw", q_raw, torch.bfloat16), ("q_rope", q_rope, torch.bfloat16), ("eta", eta, torch.float32)]
+        outs += [("q_raw", q_raw, torch.bfloat16, q_rows * HD), ("q_rope", q_rope, torch.bfloat16, q_rows * HD),
+                 ("eta", eta, torch.float32, q_rows)]
     if parts & 2:
-        outs += [("k_raw", k_raw, torch.bfloat16), ("k_rope", k_rope, torch.bfloat16), ("v", v, torch.bfloat16),
-                 ("beta", beta, torch.float32)]
-    for name, t, dt in outs:
-        _need(t, dt, name)
-    _need(inv_freq, torch.float32, "inv_freq")
+        outs += [("k_raw", k_raw, torch.bfloat16, k_rows * HD), ("k_rope", k_rope, torch.bfloat16, k_rows * HD),
+                 ("v", v, torch.bfloat16, k_rows * HD), ("beta", beta, torch.float32, k_rows)]
+    for name, t, dt, n in outs:
+        _need(t, dt, name, n)
+    _need(inv_freq, torch.float32, "inv_freq", HD // 2)
+    _opt(q_norm_w, torch.float32, "q_norm_w", HD)
+    _opt(k_norm_w, torch.float32, "k_norm_w", HD)
+    _opt(q_l2, torch.float32, "q_l2", q_rows)
     a = _lib.PrepArgs(
         proj=proj.data_ptr(), ld=proj.stride(0), B=B, T=T, H=H, HKV=HKV, HD=HD,
         q_norm_w=_ptr(q_norm_w), k_norm_w=_ptr(k_norm_w), eps=eps, inv_freq=inv_freq.data_ptr(),
@@ -85,17 +174,61 @@ def prep(proj: torch.Tensor, *, B: int, T: int, H: int, HKV: int, HD: int, inv_f
     _count(1)
 
 
+def check_bank(bank: dict, n_chains: int, HD: int, S: int = S_SLOTS) -> None:
+    """The state tensors of n_chains chains (new_bank's layout)."""
+    bf, f32 = torch.bfloat16, torch.float32
+    _need(bank["ak"], bf, "bank ak", n_chains * S * HD)
+    _need(bank["av"], bf, "bank av", n_chains * S * HD)
+    if bank.get("ak_rope") is not None:
+        _need(bank["ak_rope"], bf, "bank ak_rope", n_chains * S * HD)
+    for k in ("mass", "util", "pm"):
+        _need(bank[k], f32, "bank " + k, n_chains * S)
+    _need(bank["act"], torch.uint8, "bank act", n_chains * S)
+    _need(bank["m_res"], f32, "bank m_res", n_chains * HD * HD)
+    _need(bank["n_filled"], torch.int32, "bank n_filled", n_chains)
+
+
+def _status(status) -> int | None:
+    if status is None:
+        return None
+    if isinstance(status, DeviceStatus):
+        status = status.word
+    _need(status, torch.int32, "status", 1)
+    return status.data_ptr()
+
+
+def _check_snaps(sn: dict, n_chains: int, n_cons: int, HD: int) -> None:
+    ns = n_chains * n_cons
+    _need(sn["ak_rope"], torch.bfloat16, "snapshot ak_rope", ns * S_SLOTS * HD)
+    _need(sn["av"], torch.bfloat16, "snapshot av", ns * S_SLOTS * HD)
+    _need(sn["mass"], torch.float32, "snapshot mass", ns * S_SLOTS)
+    _need(sn["act"], torch.uint8, "snapshot act", ns * S_SLOTS)
+    _need(sn["m"], torch.float32, "snapshot M_res", ns * HD * HD)
+
+
 def consolidate(*, n_chains: int, hkv: int, HD: int, bank: dict, init_blank: bool,
                 kr: torch.Tensor, kp: torch.Tensor, v: torch.Tensor, beta: torch.Tensor,
                 chain_tokens: int, token0: int, step_tokens: int, skip0: int, chunk_len: int,
                 pos0: int, n_steps: int, kappa: torch.Tensor, gamma: torch.Tensor,
                 inv_freq: torch.Tensor, snaps: dict | None = None, snap0: int = 0,
-                status: torch.Tensor | None = None) -> None:
+                status=None, wait_probe: int = 0) -> None:
     """Run n_steps consolidations on every chain (bolt3_consolidate). `bank` holds the state
     tensors ak, av, ak_rope (bf16 [chains,S,HD]), mass, util, pm (fp32 [chains,S]), act (uint8),
-    m_res (fp32 [chains,HD,HD]) and n_filled (int32 [chains]); they are updated in place."""
+    m_res (fp32 [chains,HD,HD]) and n_filled (int32 [chains]); they are updated in place.
+    `status`: a DeviceStatus or a device int32 tensor the kernel ORs error bits into."""
     lib = _lib.load()
     snaps = snaps or {}
+    check_bank(bank, n_chains, HD)
+    for name, t in (("kr", kr), ("kp", kp), ("v", v)):
+        _need(t, torch.bfloat16, name, n_chains * chain_tokens * HD)
+    _need(beta, torch.float32, "beta", n_chains * chain_tokens)
+    _need(kappa, torch.float32, "kappa", hkv)
+    _need(gamma, torch.float32, "gamma", hkv)
+    _need(inv_freq, torch.float32, "inv_freq", HD // 2)
+    snap_cap = 0
+    if snaps:
+        snap_cap = int(snaps["ak_rope"].shape[1])
+        _check_snaps(snaps, n_chains, snap_cap, HD)
     a = _lib.ConsolidateArgs(
         n_chains=n_chains, hkv=hkv, HD=HD,
         ak=bank["ak"].data_ptr(), av=bank["av"].data_ptr(), ak_rope=_ptr(bank.get("ak_rope")),
@@ -107,7 +240,7 @@ def consolidate(*, n_chains: int, hkv: int, HD: int, bank: dict, init_blank: boo
         inv_freq=inv_freq.data_ptr(),
         snap_ak_rope=_ptr(snaps.get("ak_rope")), snap_av=_ptr(snaps.get("av")),
         snap_mass=_ptr(snaps.get("mass")), snap_act=_ptr(snaps.get("act")), snap_m=_ptr(snaps.get("m")),
-        snap_cap=int(snaps["ak_rope"].shape[1]) if snaps else 0, snap0=snap0, status=_ptr(status))
+        snap_cap=snap_cap, snap0=snap0, status=_status(status), wait_probe=wait_probe)
     _lib.check(lib.bolt3_consolidate(ctypes.byref(a), _stream()), "bolt3_consolidate")
     _count(1 if a.n_steps > 0 else 0)
 
@@ -117,9 +250,33 @@ def attend_decode(*, n_chains: int, hkv: int, G: int, HD: int, q_rope: torch.Ten
                   seg0_chain_tokens: int, seg0_len: int, seg1_k: torch.Tensor, seg1_v: torch.Tensor,
                   seg1_chain_tokens: int, seg1_len: int, len_before: int,
                   sinks: tuple | None, bank: dict | None, kappa: torch.Tensor, coef: torch.Tensor,
-                  res_w: torch.Tensor, eps: float, y: torch.Tensor, q_l2: torch.Tensor | None = None) -> None:
+                  res_w: torch.Tensor, eps: float, y: torch.Tensor, q_l2: torch.Tensor | None = None,
+                  status=None, wait_probe: int = 0) -> None:
     """Attention of Tq new tokens over sinks, the current bank and the two-chunk window."""
     lib = _lib.load()
+    nq = n_chains * G * Tq
+    _need(q_rope, torch.bfloat16, "q_rope", nq * HD)
+    _need(q_raw, torch.bfloat16, "q_raw", nq * HD)
+    _need(eta, torch.float32, "eta", nq)
+    _opt(q_l2, torch.float32, "q_l2", nq)
+    _need(y, torch.bfloat16, "y", nq * HD)
+    for name, t, ct, ln in (("seg0_k", seg0_k, seg0_chain_tokens, seg0_len),
+                            ("seg0_v", seg0_v, seg0_chain_tokens, seg0_len),
+                            ("seg1_k", seg1_k, seg1_chain_tokens, seg1_len),
+                            ("seg1_v", seg1_v, seg1_chain_tokens, seg1_len)):
+        _need_rows(t, name, n_chains, ct, ln, HD)
+    if sinks:
+        _need(sinks[0], torch.bfloat16, "sink_k", n_chains * N_SINKS * HD)
+        _need(sinks[1], torch.bfloat16, "sink_v", n_chains * N_SINKS * HD)
+    if bank:
+        _need(bank["ak_rope"], torch.bfloat16, "bank ak_rope", n_chains * S_SLOTS * HD)
+        _need(bank["av"], torch.bfloat16, "bank av", n_chains * S_SLOTS * HD)
+        _need(bank["mass"], torch.float32, "bank mass", n_chains * S_SLOTS)
+        _need(bank["act"], torch.uint8, "bank act", n_chains * S_SLOTS)
+        _need(bank["m_res"], torch.float32, "bank m_res", n_chains * HD * HD)
+    _need(kappa, torch.float32, "kappa", hkv)
+    _need(coef, torch.float32, "coef", hkv)
+    _need(res_w, torch.float32, "res_w", HD)
     a = _lib.AttendArgs(
         n_chains=n_chains, hkv=hkv, G=G, HD=HD, q_rope=q_rope.data_ptr(), q_raw=q_raw.data_ptr(),
         eta=eta.data_ptr(), Tq=Tq, prefill=0,
@@ -132,7 +289,7 @@ def attend_decode(*, n_chains: int, hkv: int, G: int, HD: int, q_rope: torch.Ten
         bank_mass=_ptr(bank["mass"]) if bank else None, bank_act=_ptr(bank["act"]) if bank else None,
         bank_m=_ptr(bank["m_res"]) if bank else None, bank_cap=1, has_bank=int(bank is not None),
         kappa=kappa.data_ptr(), coef=coef.data_ptr(), res_w=res_w.data_ptr(), eps=eps,
-        y=y.data_ptr(), y_tokens=Tq, q_l2=_ptr(q_l2))
+        y=y.data_ptr(), y_tokens=Tq, q_l2=_ptr(q_l2), status=_status(status), wait_probe=wait_probe)
     _lib.check(lib.bolt3_attend(ctypes.byref(a), _stream()), "bolt3_attend")
     _count(1)
 
@@ -142,7 +299,7 @@ class DecodeStepArgs:
     state, step size) and launched every step with only the fields that move rewritten: the
     projection output, RoPE position and ring write offset (prep), the ring slots, window lengths and
     whether sinks and a bank exist yet (attend). The buffers the blocks point at are the caller's
-    and must stay alive."""
+    and must stay alive; they belong to the plan and state that built the blocks."""
 
     def __init__(self, prep_fields: dict, attend_fields: dict):
         self.lib = _lib.load()
@@ -151,7 +308,8 @@ class DecodeStepArgs:
 
     def launch_prep(self, proj: torch.Tensor, pos0: int, k_t_off: int) -> None:
         a = self.prep
-        if proj.stride(0) != a.ld or not proj.is_contiguous():
+        _need(proj, torch.bfloat16, "proj", a.B * a.T * a.ld)
+        if proj.stride(0) != a.ld:
             raise ValueError("proj must be a contiguous [tokens, ld] projection output")
         a.proj, a.pos0, a.k_t_off, a.beta_t_off = proj.data_ptr(), pos0, k_t_off, k_t_off
         _lib.check(self.lib.bolt3_prep(ctypes.byref(a), _stream()), "bolt3_prep")
@@ -188,13 +346,36 @@ def snapshot_views(ws: torch.Tensor, n_chains: int, n_cons: int, HD: int, S: int
     return views
 
 
+def _check_prepared(B: int, T: int, H: int, HKV: int, HD: int, q_rope, q_raw, eta, k_rope, v, kappa, coef,
+                    res_w, y, q_l2) -> None:
+    nq, nk = B * H * T, B * HKV * T
+    _need(q_rope, torch.bfloat16, "q_rope", nq * HD)
+    _need(q_raw, torch.bfloat16, "q_raw", nq * HD)
+    _need(eta, torch.float32, "eta", nq)
+    _opt(q_l2, torch.float32, "q_l2", nq)
+    _need(k_rope, torch.bfloat16, "k_rope", nk * HD)
+    _need(v, torch.bfloat16, "v", nk * HD)
+    _need(kappa, torch.float32, "kappa", HKV)
+    _need(coef, torch.float32, "coef", HKV)
+    _need(res_w, torch.float32, "res_w", HD)
+    _need(y, torch.bfloat16, "y", nq * HD)
+
+
 def attend_prefill(*, n_chains: int, hkv: int, G: int, HD: int, T: int, q_rope, q_raw, eta, k_rope, v,
                    snaps: dict | None, n_cons: int, kappa, coef, res_w, eps: float, y: torch.Tensor,
-                   blk_begin: int = 0, blk_count: int = 0, q_l2=None, status=None) -> None:
+                   blk_begin: int = 0, blk_count: int = 0, q_l2=None, status=None, wait_probe: int = 0) -> None:
     """Attention of prefill query blocks [blk_begin, blk_begin + blk_count) (bolt3_attend, prefill
     mode): chunk r reads snapshot r - 2 of the consolidation scan."""
     lib = _lib.load()
+    if n_chains % hkv:
+        raise ValueError(f"{n_chains} chains are not a whole number of sequences of {hkv} KV heads")
+    _check_prepared(n_chains // hkv, T, hkv * G, hkv, HD, q_rope, q_raw, eta, k_rope, v, kappa, coef, res_w, y,
+                    q_l2)
     sn = snaps or {}
+    if n_cons > 0 and T > 2 * CHUNK:
+        if not sn:
+            raise ValueError("a prefill of more than two chunks reads consolidation snapshots")
+        _check_snaps(sn, n_chains, n_cons, HD)
     a = _lib.AttendArgs(
         n_chains=n_chains, hkv=hkv, G=G, HD=HD, q_rope=q_rope.data_ptr(), q_raw=q_raw.data_ptr(),
         eta=eta.data_ptr(), Tq=T, prefill=1, seg0_k=k_rope.data_ptr(), seg0_v=v.data_ptr(),
@@ -202,51 +383,68 @@ def attend_prefill(*, n_chains: int, hkv: int, G: int, HD: int, T: int, q_rope, 
         bank_ak_rope=_ptr(sn.get("ak_rope")), bank_av=_ptr(sn.get("av")), bank_mass=_ptr(sn.get("mass")),
         bank_act=_ptr(sn.get("act")), bank_m=_ptr(sn.get("m")), bank_cap=n_cons,
         kappa=kappa.data_ptr(), coef=coef.data_ptr(), res_w=res_w.data_ptr(), eps=eps,
-        y=y.data_ptr(), y_tokens=T, status=_ptr(status), q_l2=_ptr(q_l2), blk_begin=blk_begin,
-        blk_count=blk_count)
+        y=y.data_ptr(), y_tokens=T, status=_status(status), q_l2=_ptr(q_l2), blk_begin=blk_begin,
+        blk_count=blk_count, wait_probe=wait_probe)
     _lib.check(lib.bolt3_attend(ctypes.byref(a), _stream()), "bolt3_attend")
     _count(1)
 
 
-def prefill(*, B: int, T: int, H: int, HKV: int, HD: int, q_rope, q_raw, eta, k_raw, k_rope, v, beta,
-            kappa, gamma, coef, inv_freq, res_w, eps: float, workspace: torch.Tensor, bank: dict,
-            y: torch.Tensor, status: torch.Tensor | None = None, q_l2: torch.Tensor | None = None) -> None:
-    """Phases B + C of Bolt3Attn.forward on prepared q/k/v (bolt3_prefill_fwd)."""
-    lib = _lib.load()
-    a = _lib.PrefillArgs(
+def _prefill_args(B, T, H, HKV, HD, q_rope, q_raw, eta, k_raw, k_rope, v, beta, kappa, gamma, coef, inv_freq,
+                  res_w, eps, bank, y, status, q_l2, workspace=None) -> "_lib.PrefillArgs":
+    if B <= 0 or T <= 0 or HKV <= 0 or H % HKV:
+        raise ValueError(f"unsupported prefill shape B={B} T={T} H={H} HKV={HKV}")
+    _check_prepared(B, T, H, HKV, HD, q_rope, q_raw, eta, k_rope, v, kappa, coef, res_w, y, q_l2)
+    _need(k_raw, torch.bfloat16, "k_raw", B * HKV * T * HD)
+    _need(beta, torch.float32, "beta", B * HKV * T)
+    _need(gamma, torch.float32, "gamma", HKV)
+    _need(inv_freq, torch.float32, "inv_freq", HD // 2)
+    check_bank(bank, B * HKV, HD)
+    ws_bytes = 0
+    if workspace is not None:
+        _need(workspace, torch.uint8, "workspace", prefill_workspace_bytes(B * HKV, T, HD))
+        ws_bytes = workspace.numel()
+    return _lib.PrefillArgs(
         B=B, T=T, H=H, HKV=HKV, HD=HD, q_rope=q_rope.data_ptr(), q_raw=q_raw.data_ptr(),
         eta=eta.data_ptr(), k_raw=k_raw.data_ptr(), k_rope=k_rope.data_ptr(), v=v.data_ptr(),
         beta=beta.data_ptr(), kappa=kappa.data_ptr(), gamma=gamma.data_ptr(), coef=coef.data_ptr(),
         inv_freq=inv_freq.data_ptr(), res_w=res_w.data_ptr(), eps=eps,
-        workspace=workspace.data_ptr(), workspace_bytes=workspace.numel() * workspace.element_size(),
+        workspace=_ptr(workspace), workspace_bytes=ws_bytes,
         ak=bank["ak"].data_ptr(), av=bank["av"].data_ptr(), ak_rope=_ptr(bank.get("ak_rope")),
         mass=bank["mass"].data_ptr(), util=bank["util"].data_ptr(), pm=bank["pm"].data_ptr(),
         act=bank["act"].data_ptr(), m_res=bank["m_res"].data_ptr(), n_filled=bank["n_filled"].data_ptr(),
-        y=y.data_ptr(), status=_ptr(status), q_l2=_ptr(q_l2))
+        y=y.data_ptr(), status=_status(status), q_l2=_ptr(q_l2))
+
+
+def prefill(*, B: int, T: int, H: int, HKV: int, HD: int, q_rope, q_raw, eta, k_raw, k_rope, v, beta,
+            kappa, gamma, coef, inv_freq, res_w, eps: float, workspace: torch.Tensor, bank: dict,
+            y: torch.Tensor, status=None, q_l2: torch.Tensor | None = None) -> None:
+    """Phases B + C of Bolt3Attn.forward on prepared q/k/v (bolt3_prefill_fwd)."""
+    lib = _lib.load()
+    a = _prefill_args(B, T, H, HKV, HD, q_rope, q_raw, eta, k_raw, k_rope, v, beta, kappa, gamma, coef, inv_freq,
+                      res_w, eps, bank, y, status, q_l2, workspace=workspace)
     _lib.check(lib.bolt3_prefill_fwd(ctypes.byref(a), _stream()), "bolt3_prefill_fwd")
     _count(2)  # the scan, then the attention
 
 
+def noalloc_fits(B: int, T: int, HKV: int, HD: int) -> bool:
+    """Whether a prefill of B x T tokens fits the fixed scratch of bolt3_prefill_fwd_noalloc."""
+    return prefill_workspace_bytes(B * HKV, T, HD) <= _lib.NOALLOC_SCRATCH_BYTES
+
+
 def prefill_noalloc(*, B: int, T: int, H: int, HKV: int, HD: int, q_rope, q_raw, eta, k_raw, k_rope, v, beta,
                     kappa, gamma, coef, inv_freq, res_w, eps: float, bank: dict, y: torch.Tensor,
-                    status: torch.Tensor | None = None, q_l2: torch.Tensor | None = None) -> None:
+                    status=None, q_l2: torch.Tensor | None = None) -> None:
     """Phases B + C like `prefill`, with the snapshot workspace taken from the library's fixed
     per-GPU array instead of the caller (bolt3_prefill_fwd_noalloc). For hosts that cannot allocate
-    device memory on their hot path; the work must fit in `_lib.NOALLOC_SCRATCH_BYTES`."""
+    device memory on their hot path; the work must fit in `_lib.NOALLOC_SCRATCH_BYTES` (checked
+    here, before anything else, and again by the library)."""
     lib = _lib.load()
     need = prefill_workspace_bytes(B * HKV, T, HD)
     if need > _lib.NOALLOC_SCRATCH_BYTES:
         raise ValueError(f"prefill of {B} x {T} tokens needs {need} bytes of scratch; the no-alloc entry point "
                          f"has a fixed {_lib.NOALLOC_SCRATCH_BYTES} bytes (use `prefill` with a workspace)")
-    a = _lib.PrefillArgs(
-        B=B, T=T, H=H, HKV=HKV, HD=HD, q_rope=q_rope.data_ptr(), q_raw=q_raw.data_ptr(),
-        eta=eta.data_ptr(), k_raw=k_raw.data_ptr(), k_rope=k_rope.data_ptr(), v=v.data_ptr(),
-        beta=beta.data_ptr(), kappa=kappa.data_ptr(), gamma=gamma.data_ptr(), coef=coef.data_ptr(),
-        inv_freq=inv_freq.data_ptr(), res_w=res_w.data_ptr(), eps=eps, workspace=None, workspace_bytes=0,
-        ak=bank["ak"].data_ptr(), av=bank["av"].data_ptr(), ak_rope=_ptr(bank.get("ak_rope")),
-        mass=bank["mass"].data_ptr(), util=bank["util"].data_ptr(), pm=bank["pm"].data_ptr(),
-        act=bank["act"].data_ptr(), m_res=bank["m_res"].data_ptr(), n_filled=bank["n_filled"].data_ptr(),
-        y=y.data_ptr(), status=_ptr(status), q_l2=_ptr(q_l2))
+    a = _prefill_args(B, T, H, HKV, HD, q_rope, q_raw, eta, k_raw, k_rope, v, beta, kappa, gamma, coef, inv_freq,
+                      res_w, eps, bank, y, status, q_l2)
     _lib.check(lib.bolt3_prefill_fwd_noalloc(ctypes.byref(a), _stream()), "bolt3_prefill_fwd_noalloc")
     _count(2)
 
