@@ -324,7 +324,10 @@ def run_native(args, rank, world, local):
     e2e_value = world * tok * e2e_steps / t_e2e
 
     decode = None if args.no_decode else run_decode(args, rank, world, dev, m, cfg, hbm)
-    cpu = cpu_baseline(args) if (rank == 0 and world == 1 and not args.no_cpu) else None
+    legs = cpu_baseline(args, m, cfg, dev) if (rank == 0 and world == 1 and not args.no_cpu) else {}
+    cpu = legs.get("prefill")
+    if decode is not None and legs:
+        decode["cpu_baseline"] = legs["decode"]
     res = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": t_prefill / args.steps * 1e3, "higher_is_better": True,
@@ -345,6 +348,8 @@ def run_native(args, rank, world, local):
         "decode": decode,
         "cpu_baseline": cpu,
     }
+    if "parity" in legs:
+        res["parity"] = legs["parity"]
     return res
 
 
@@ -420,26 +425,175 @@ def run_long(args, rank, world, dev, tf_peak):
                          "unit": "TFLOP/s", "frac": flops * args.steps / t / 1e12 / tf_peak}}
 
 
-def cpu_baseline(args):
-    """The reference algorithm on the host cores (oracle port, fp32), bounded sample of configs[1]."""
+def _oracle_setup(m, cfg):
+    from oracle import oracle_cfg
+
+    P = {k: v.detach().cpu() for k, v in m.state_dict().items()}
+    oc = oracle_cfg(cfg)
+    oc["inv_freq"] = m.rope.inv_freq.detach().float().cpu()
+    return P, oc
+
+
+def _flag_counts(rec: list) -> tuple:
+    """Per consolidation, the chains whose outcome rounding may change; totals split by reason."""
+    from oracle.parity import decision_ties, near_threshold
+
+    flags = [decision_ties(r) for r in rec]
+    thr = sum(int(near_threshold(r).sum()) for r in rec)
+    return flags, thr, sum(int(f.sum()) for f in flags) - thr
+
+
+def parity_prefill(m, cfg, dev, n_seq: int = 2):
+    """configs[1] check: n_seq sequences of PREFILL_T tokens through Bolt3Attn's native forward,
+    against the oracle run on the GPU's own projections. A chain may deviate from the oracle only
+    after a consolidation whose decision rounding can change (oracle.parity.decision_ties); such
+    chains are counted as flips."""
+    from oracle import Store, forward
+
+    T = PREFILL_T
+    x = make_input(n_seq, T, cfg["dim"], dup=DUP, seed=1, device=dev, dtype=torch.bfloat16)
+    P, oc = _oracle_setup(m, cfg)
+    p, prep_q = m._prepare(x)
+    prep_q()
+    H, HKV, HD, G = m.H, m.HKV, m.HD, m.G
+    cpu = lambda t, *shape: t.float().cpu().view(*shape)
+    proj = (cpu(p.q_raw, n_seq, H, T, HD), cpu(p.k_raw, n_seq, HKV, T, HD), cpu(p.v, n_seq, HKV, T, HD),
+            cpu(p.beta, n_seq, HKV, T), cpu(p.eta, n_seq, H, T))
+    rec = []
+    _, yh_ref = forward(P, oc, x, Store("bf16"), record=rec, return_y_heads=True, proj=proj)
+    got = m._attention_heads(x).float().cpu().permute(0, 2, 1, 3)
+    m.check_status()
+    flags, thr, tie = _flag_counts(rec)
+    rms = yh_ref.pow(2).mean().sqrt().item()
+    n_chunks = T // 128
+    gone, unflagged, worst, compared = {}, 0, 0.0, 0
+    for r in range(n_chunks):
+        for c in range(n_seq * HKV):
+            if c in gone:
+                continue
+            bi, h = divmod(c, HKV)
+            g_ = got[bi, h * G:(h + 1) * G, r * 128:(r + 1) * 128]
+            f_ = yh_ref[bi, h * G:(h + 1) * G, r * 128:(r + 1) * 128]
+            err = (g_ - f_).abs()
+            if (err > 2e-2 * f_.abs() + 2e-2 * rms).any():
+                gone[c] = r
+                unflagged += not any(bool(flags[j][c]) for j in range(0, r - 1))
+                continue
+            worst = max(worst, err.max().item() / rms)
+            compared += 1
+    steps = len(rec) * n_seq * HKV
+    return {"sample": f"{n_seq} sequences x {T} tokens (configs[1] shape), oracle on the GPU's projections",
+            "chain_steps": steps, "flagged_near_threshold": thr, "flagged_near_tie": tie, "flips": len(gone),
+            "unflagged_deviations": unflagged, "flip_rate": len(gone) / max(steps, 1),
+            "compared_chain_chunks": compared, "total_chain_chunks": n_chunks * n_seq * HKV,
+            "max_err_rel_rms": worst, "tolerance": "rtol 2e-2, atol 2e-2 x RMS"}
+
+
+def parity_decode(m, cfg, dev, n_seq: int = 4, prompt: int = DEC_PROMPT, steps: int = DEC_STEPS):
+    """configs[2] check: n_seq sequences, a prompt of `prompt` tokens in C-token slices then
+    `steps` one-token steps through Bolt3Decoder.layer_step, against the oracle's decoder run on the
+    GPU's projections of every step. A sequence may deviate only after a consolidation of one of its
+    chains whose decision rounding can change; it is then counted as a flip and left out."""
+    from oracle import LayerDecoderOracle, Store
+    from vsa_lm_b200 import Bolt3Decoder, Bolt3LayerState
+
+    P, oc = _oracle_setup(m, cfg)
+    g = torch.Generator(device=dev).manual_seed(200)
+    hs = torch.randn(n_seq, prompt + steps, cfg["dim"], generator=g, device=dev).to(torch.bfloat16)
+    st = Bolt3LayerState(m, n_seq, dev)
+    m_res = torch.zeros(n_seq, m.HKV, m.HD, m.HD, device=dev)
+    dec = LayerDecoderOracle(P, oc, n_seq, Store("bf16"))
+    plan = [(s, 128) for s in range(0, prompt, 128)] + [(prompt + i, 1) for i in range(steps)]
+    gone, unflagged, worst, compared = {}, 0, 0.0, 0
+    for pos, n in plan:
+        h = hs[:, pos:pos + n]
+        proj = tuple(t.float().cpu() for t in m.step_projections(h, pos))
+        out = Bolt3Decoder.layer_step(m, st, h, pos, m_res).float().cpu()
+        ref = dec.step(h, pos, proj=proj)
+        rms = ref.pow(2).mean().sqrt().item()
+        for bi in range(n_seq):
+            if bi in gone:
+                continue
+            err = (out[bi] - ref[bi]).abs()
+            if (err > 2e-2 * ref[bi].abs() + 2e-2 * rms).any():
+                gone[bi] = pos
+                flags, _, _ = _flag_counts(dec.record)
+                mine = range(bi * m.HKV, (bi + 1) * m.HKV)
+                unflagged += not any(bool(f[c]) for f in flags for c in mine)
+                continue
+            worst = max(worst, err.max().item() / rms)
+            compared += 1
+    Bolt3Decoder.check_status([st])
+    _, thr, tie = _flag_counts(dec.record)
+    chain_steps = len(dec.record) * n_seq * m.HKV
+    return {"sample": f"{n_seq} sequences, {prompt}-token prompt + {steps} one-token steps (configs[2] shape), "
+                      f"oracle on the GPU's projections",
+            "chain_steps": chain_steps, "flagged_near_threshold": thr, "flagged_near_tie": tie,
+            "flips": len(gone), "unflagged_deviations": unflagged, "flip_rate": len(gone) * m.HKV / max(chain_steps, 1),
+            "compared_sequence_steps": compared, "total_sequence_steps": len(plan) * n_seq,
+            "max_err_rel_rms": worst, "tolerance": "rtol 2e-2, atol 2e-2 x RMS"}
+
+
+def cpu_prefill_rate(seconds: float, T: int) -> dict:
+    """The reference algorithm's prefill (the oracle port, fp32) on the host cores: forwards of
+    1 x T tokens of the configs[1] shape for about `seconds`."""
     from oracle import Store, forward, oracle_cfg
 
     torch.set_num_threads(os.cpu_count() or 1)
     cfg = layer_cfg(SHAPE)
     P = make_params(cfg, 0)
     oc = oracle_cfg(cfg)
-    T = args.cpu_tokens
     x = make_input(1, T, cfg["dim"], dup=DUP, seed=1)
     t0 = time.perf_counter()
     n = 0
     while True:
         forward(P, oc, x, Store("fp32"))
         n += 1
-        if time.perf_counter() - t0 > args.cpu_seconds:
+        if time.perf_counter() - t0 > seconds:
             break
     dt = time.perf_counter() - t0
     return {"value": n * T / dt, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
             "sample": f"configs[1] shape, 1 x {T} tokens, fp32, {n} forward(s) in {dt:.1f} s"}
+
+
+def cpu_decode_rate(seconds: float, B: int = 8, prompt: int = 512) -> dict:
+    """The reference algorithm's decode step (the oracle port of Bolt3Decoder.step for one Bolt-3
+    layer, fp32) on the host cores: B sequences after a `prompt`-token prefill (untimed), then
+    one-token steps for about `seconds`."""
+    from oracle import LayerDecoderOracle, Store, oracle_cfg
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = layer_cfg(SHAPE)
+    P = make_params(cfg, 0)
+    oc = oracle_cfg(cfg)
+    g = torch.Generator().manual_seed(300)
+    dec = LayerDecoderOracle(P, oc, B, Store("fp32"))
+    for s in range(0, prompt, 128):
+        dec.step(torch.randn(B, 128, cfg["dim"], generator=g), s)
+    pos, n = prompt, 0
+    t0 = time.perf_counter()
+    while True:
+        dec.step(torch.randn(B, 1, cfg["dim"], generator=g), pos)
+        pos, n = pos + 1, n + 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": B * n / dt, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"configs[2] shape, {B} sequences after a {prompt}-token prefill, {n} one-token steps "
+                      f"of one Bolt-3 layer, fp32, in {dt:.1f} s"}
+
+
+def cpu_baseline(args, m=None, cfg=None, dev=None):
+    """The CPU leg (rank 0, one GPU, outside every timed region): the reference algorithm on the host
+    cores (the oracle port, fp32), timed on bounded samples of the prefill and the decode step; and
+    the same oracle as the checker of the GPU path's results on configs[1]- and configs[2]-shaped
+    samples (parity and the merge/evict flip rate)."""
+    out = {"prefill": cpu_prefill_rate(args.cpu_seconds, args.cpu_tokens),
+           "decode": cpu_decode_rate(args.cpu_seconds / 2)}
+    if m is not None and not args.no_parity:
+        out["parity"] = {"configs[1]": parity_prefill(m, cfg, dev),
+                         "configs[2]": parity_decode(m, cfg, dev, steps=args.parity_decode_steps)}
+    return out
 
 
 def run_reference(args, rank, world):
@@ -464,6 +618,7 @@ def run_reference(args, rank, world):
     dt = time.perf_counter() - t0
     value = args.steps * T / dt
     sample = f"configs[1] shape, 1 x {T} tokens per step, fp32, {args.steps} timed step(s) in {dt:.1f} s"
+    decode = cpu_decode_rate(args.cpu_seconds / 2)
     return {"metric": METRIC, "impl": "reference", "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -473,7 +628,8 @@ def run_reference(args, rank, world):
                        "global_batch": 1, "seq_len": T, "parallelism": "host threads"},
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
                              "sample": sample},
-            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "decode": {"value": decode["value"], "unit": "tok/s", "cpu_baseline": decode}}
 
 
 def main():
@@ -491,6 +647,9 @@ def main():
     ap.add_argument("--decode-only", action="store_true", help="only the configs[2] decode measurement (profiling)")
     ap.add_argument("--decode-steps", type=int, default=DEC_STEPS, help="timed decode steps")
     ap.add_argument("--long", action="store_true", help="only the configs[4] long-context prefill")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the GPU results")
+    ap.add_argument("--parity-decode-steps", type=int, default=DEC_STEPS,
+                    help="one-token steps of the configs[2] parity sample")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))

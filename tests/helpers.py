@@ -6,6 +6,7 @@ from __future__ import annotations
 import torch
 
 from oracle import Store, oracle_cfg
+from oracle.parity import NEAR, TIE_REL, decision_ties, near_threshold  # noqa: F401
 from vsa_lm_b200 import Bolt3Attn
 from vsa_lm_b200.workloads import layer_cfg, make_input, make_params
 
@@ -15,16 +16,12 @@ RTOL = 2e-2
 ATOL_RMS = 2e-2
 # fp32 state tolerance (M_res, mass, pm, util)
 STATE_RTOL = 1e-4
-NEAR = 1e-3   # merge decisions within this distance of 0.88 / 0.80 may flip
 # A slot's utility is the token's prediction error rel_err = |v - P.av| / |v| at insertion, with the
 # softmax probabilities P rounded to bf16 before the product (the reference's CUDA arithmetic). Both
 # sides round the same fp32 probabilities, but a value within one fp32 ulp of a bf16 rounding
 # boundary may round either way; for a token whose duplicate already sits in the bank P is
 # concentrated (p ~ 1), and one such rounding moves rel_err by up to p * 2^-9 ~ 2e-3.
 UTIL_ATOL = 2e-3
-# Two distinct ranking keys closer than this (relative) are ordered by rounding noise: the CUDA path
-# and the fp32 CPU oracle accumulate in different orders, so either may rank them either way.
-TIE_REL = 1e-5
 
 
 def bf16_module(cfg: dict, seed: int, device="cuda") -> Bolt3Attn:
@@ -57,66 +54,6 @@ def output_close(got: torch.Tensor, ref: torch.Tensor, what: str = "output") -> 
                 max_rel_rms=(err.max().item() / max(rms, 1e-30)))
     assert not bad.any(), f"{what}: {int(bad.sum())} elements outside rtol {RTOL} / atol {ATOL_RMS}*rms: {info}"
     return info
-
-
-def near_threshold(rec: dict) -> torch.Tensor:
-    """Chains whose merge decision has a cosine within NEAR of a threshold (flip allowed)."""
-    if rec.get("kind") != "full":
-        return torch.zeros(rec["score"].shape[0], dtype=torch.bool)
-    nk = (rec["best_sim_k"] - 0.88).abs() < NEAR
-    nv = (rec["sim_v"] - 0.80).abs() < NEAR
-    return (nk | nv).any(dim=-1)
-
-
-def _near(a: torch.Tensor, b: torch.Tensor, rel: float) -> torch.Tensor:
-    d = (a - b).abs()
-    return (d > 0) & (d <= rel * torch.maximum(a.abs(), b.abs()))
-
-
-def decision_ties(rec: dict, rel: float = TIE_REL) -> torch.Tensor:
-    """Chains of one consolidation whose OUTCOME (the bank as a set of slots, M_res) a near-tie or a
-    near-threshold cosine can change. Near-ties that only reorder slots are not flagged: the tests
-    compare banks up to a permutation of slots.
-
-    fill (bolt3.py:165-192): the m selected tokens are a set; only the pair of sorted scores straddling
-    position m-1 / m decides which tokens are kept, and only when m < l_tok.
-    full (bolt3.py:96-152):
-      - a cosine within NEAR of 0.88 / 0.80 (the merge decision itself, north-star rule);
-      - for a token that may merge (best cosine >= 0.88 - NEAR), its two best slot cosines nearly
-        tied: the merge target is ambiguous;
-      - eviction: win = top > bot is a prefix of length w of the sorted pairs. Swaps among winners
-        only move inserted tokens between evicted slots (a permutation); the outcome changes only
-        through a near-tie at the boundary: top[i] ~ bot[i] for i in {w-1, w}, or top[w-1] ~ top[w]
-        (which token is inserted), or bot[w-1] ~ bot[w] (which slot is evicted), or the k_cand
-        boundary of the slot ranking when k_cand < S.
-    Exact ties (equal keys) are not flagged: the kernels reproduce CPU torch.topk's order of equal
-    keys."""
-    if rec.get("kind") != "full":
-        m, l_tok = rec["m"], rec["l_tok"]
-        n = rec["score"].shape[0]
-        if m >= l_tok or m <= 0:
-            return torch.zeros(n, dtype=torch.bool)
-        sc = torch.sort(rec["score"], dim=-1, descending=True).values
-        return _near(sc[:, m - 1], sc[:, m], rel)
-    flag = near_threshold(rec)
-    s1, s2 = rec["best_sim_k"], rec["second_sim_k"]
-    flag |= ((s1 >= 0.88 - NEAR) & _near(s1, s2, rel)).any(dim=-1)
-    top, bot, win = rec["top_vals"], rec["bot_vals"], rec["win"]
-    k = top.shape[1]
-    w = win.long().sum(dim=-1)
-    rows = torch.arange(top.shape[0])
-    for off in (-1, 0):
-        i = (w + off).clamp(0, k - 1)
-        ok = (w + off >= 0) & (w + off < k)
-        flag |= ok & _near(top[rows, i], bot[rows, i], rel)
-    j0, j1 = (w - 1).clamp(0, k - 1), w.clamp(0, k - 1)
-    inside = (w >= 1) & (w < k)
-    flag |= inside & (_near(top[rows, j0], top[rows, j1], rel) | _near(bot[rows, j0], bot[rows, j1], rel))
-    keep = rec["keep"]
-    if k < keep.shape[1]:
-        ks = torch.sort(keep, dim=-1).values
-        flag |= _near(ks[:, k - 1], ks[:, k], rel)
-    return flag
 
 
 BANK_KEYS = ("ak", "av", "mass", "util", "pm", "act")
@@ -253,26 +190,9 @@ def inputs(shape: str, B: int, T: int, dup, seed: int = 1, device="cuda"):
 
 
 def decoder_projections(m, h, pos):
-    """The projections Bolt3Decoder.layer_step computes for h [b, t, D] (one fused GEMM + prep), in
-    the oracle's layouts."""
-    from vsa_lm_b200 import kernels as K
-
-    b, t, D = h.shape
-    H, HKV, HD = m.H, m.HKV, m.HD
-    f = m.fused(h.device)
-    c = f.consts
-    bf = dict(dtype=torch.bfloat16, device=h.device)
-    q_raw, q_rope = torch.empty(b * H, t, HD, **bf), torch.empty(b * H, t, HD, **bf)
-    k_raw, k_rope, v = (torch.empty(b * HKV, t, HD, **bf) for _ in range(3))
-    beta = torch.empty(b * HKV, t, dtype=torch.float32, device=h.device)
-    eta = torch.empty(b * H, t, dtype=torch.float32, device=h.device)
-    proj = torch.nn.functional.linear(h.reshape(b * t, D).to(torch.bfloat16), f.w_in, f.b_in)
-    K.prep(proj, B=b, T=t, H=H, HKV=HKV, HD=HD, inv_freq=c["inv_freq"], eps=m.eps, q_norm_w=c["qn"],
-           k_norm_w=c["kn"], pos0=pos, cols=f.cols, q_raw=q_raw, q_rope=q_rope, eta=eta, k_raw=k_raw,
-           k_rope=k_rope, v=v, beta=beta, q_head_stride=t, q_t_off=0, k_head_stride=t, k_t_off=0)
-    g = lambda x_, *shape: x_.float().cpu().view(*shape)
-    return (g(q_raw, b, H, t, HD), g(k_raw, b, HKV, t, HD), g(v, b, HKV, t, HD), g(beta, b, HKV, t),
-            g(eta, b, H, t))
+    """The projections Bolt3Decoder.layer_step computes for h [b, t, D], in the oracle's layouts
+    (fp32 on the CPU)."""
+    return tuple(t.float().cpu() for t in m.step_projections(h, pos))
 
 
 class LockstepTap:

@@ -226,6 +226,7 @@ def _gpu_projections(m, x):
     ("tiny", 2, 700, 0.3),
     ("tiny", 1, 100, 0.0), ("tiny", 1, 128, 0.0), ("tiny", 1, 132, 0.0), ("tiny", 1, 256, 0.0),
     ("tiny", 1, 257, 0.0), ("tiny", 3, 300, 0.0), ("tiny", 1, 1, 0.0),
+    ("llama3_8b", 1, 131072, 0.2),  # configs[4] itself: 1022 consolidations, mean positions up to 1.3e5
 ])
 def test_forward_matches_oracle(shape, B, T, dup):
     """Bolt3Attn.forward itself (projections, segmented scan overlapped with the attention,

@@ -395,6 +395,29 @@ class Bolt3Attn(nn.Module):
                 K.attend_prefill(snaps=snaps, blk_begin=blk, blk_count=last - blk, **att)
                 blk = last
 
+    @torch.no_grad()
+    def step_projections(self, h: torch.Tensor, pos_start: int):
+        """The projections a decode step of h [b, t, D] at positions pos_start.. computes (the fused
+        input GEMM and bolt3_prep, as Bolt3Decoder.layer_step runs them), returned in the
+        reference's head-major layouts: q_raw [b, H, t, HD], k_raw and v [b, HKV, t, HD] bf16,
+        beta [b, HKV, t] and eta [b, H, t] fp32. For inspecting a step, e.g. to check its other
+        phases on exactly these inputs."""
+        b, t, D = h.shape
+        H, HKV, HD = self.H, self.HKV, self.HD
+        f = self.fused(h.device)
+        c = f.consts
+        bf = dict(dtype=torch.bfloat16, device=h.device)
+        q_raw, q_rope = torch.empty(b * H, t, HD, **bf), torch.empty(b * H, t, HD, **bf)
+        k_raw, k_rope, v = (torch.empty(b * HKV, t, HD, **bf) for _ in range(3))
+        beta = torch.empty(b * HKV, t, dtype=torch.float32, device=h.device)
+        eta = torch.empty(b * H, t, dtype=torch.float32, device=h.device)
+        proj = F.linear(h.reshape(b * t, D).to(torch.bfloat16), f.w_in, f.b_in)
+        K.prep(proj, B=b, T=t, H=H, HKV=HKV, HD=HD, inv_freq=c["inv_freq"], eps=self.eps, q_norm_w=c["qn"],
+               k_norm_w=c["kn"], pos0=pos_start, cols=f.cols, q_raw=q_raw, q_rope=q_rope, eta=eta, k_raw=k_raw,
+               k_rope=k_rope, v=v, beta=beta, q_head_stride=t, q_t_off=0, k_head_stride=t, k_t_off=0)
+        return (q_raw.view(b, H, t, HD), k_raw.view(b, HKV, t, HD), v.view(b, HKV, t, HD), beta.view(b, HKV, t),
+                eta.view(b, H, t))
+
     # ---- one consolidation on reference-format tensors (bolt3.py:68-192), natively
     @torch.no_grad()
     def _consolidate_functional(self, ak, av, mass, util, pm, act, m_res, k_raw, k_rope, v_old, pos_old,
