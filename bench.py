@@ -324,6 +324,9 @@ def run_native(args, rank, world, local):
     e2e_value = world * tok * e2e_steps / t_e2e
 
     decode = None if args.no_decode else run_decode(args, rank, world, dev, m, cfg, hbm)
+    decode_tp = run_decode_tp(args, rank, world, dev, m, cfg) if (world > 1 and not args.no_decode) else None
+    long_ctx = None if args.no_long else run_long(args, rank, world, dev, tf_burst, steps=3, warmup=3)
+    torch.cuda.empty_cache()
     legs = cpu_baseline(args, m, cfg, dev) if (rank == 0 and world == 1 and not args.no_cpu) else {}
     cpu = legs.get("prefill")
     if decode is not None and legs:
@@ -346,6 +349,8 @@ def run_native(args, rank, world, local):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
         "decode": decode,
+        "decode_tp": decode_tp,
+        "long_context": long_ctx,
         "cpu_baseline": cpu,
     }
     if "parity" in legs:
@@ -402,9 +407,38 @@ def run_decode(args, rank, world, dev, m, cfg, hbm):
                          "bytes_per_step": nb["total"], "state_only_frac": ach_core / hbm}}
 
 
-def run_long(args, rank, world, dev, tf_peak):
+def run_decode_tp(args, rank, world, dev, m, cfg):
+    """configs[2] decode with the layer split by KV head over the N ranks (Bolt3AttnTP): every rank
+    steps all 256 sequences on its KV heads and the o_proj partials meet in one NCCL all-reduce per
+    step. Total work is fixed, so this is the strong-scaling alternative to sharding sequences."""
+    from vsa_lm_b200.tp import Bolt3AttnTP
+
+    tp = Bolt3AttnTP(m)
+    n_seq, D = DEC_SEQ, cfg["dim"]
+    st, m_res = tp.new_decode_state(n_seq, dev)
+    g = torch.Generator(device=dev).manual_seed(100)
+    for s in range(0, DEC_PROMPT, 128):
+        tp.decode_step(st, torch.randn(n_seq, 128, D, generator=g, device=dev).to(torch.bfloat16), s, m_res)
+    steps = min(args.decode_steps, 128)
+    toks = torch.randn(steps + args.warmup, n_seq, 1, D, generator=g, device=dev).to(torch.bfloat16)
+    pos, i = [DEC_PROMPT], [0]
+
+    def one():
+        tp.decode_step(st, toks[i[0]], pos[0], m_res)
+        pos[0] += 1
+        i[0] += 1
+
+    t = timed(one, steps, args.warmup, world)
+    return {"value": n_seq * steps / t, "unit": "tok/s", "ms_per_step": t / steps * 1e3, "steps": steps,
+            "sequences": n_seq, "parallelism": f"tp{world} by KV head",
+            "collective": "NCCL all-reduce of the fp32 o_proj partials, one per step"}
+
+
+def run_long(args, rank, world, dev, tf_peak, steps=None, warmup=None):
     """Llama-3-8B-shape Bolt3Attn prefill of 1 x 131072 tokens. On N GPUs every rank
     holds HKV/N KV heads (Bolt3AttnTP: one NCCL all-reduce of the o_proj partials per forward)."""
+    steps = args.steps if steps is None else steps
+    warmup = args.warmup if warmup is None else warmup
     from vsa_lm_b200 import Bolt3Attn
     from vsa_lm_b200.tp import Bolt3AttnTP
 
@@ -415,9 +449,10 @@ def run_long(args, rank, world, dev, tf_peak):
     layer = Bolt3AttnTP(full) if world > 1 else full
     T = LONG_T
     x = make_input(1, T, cfg["dim"], dup=0.2, seed=7, device=dev, dtype=torch.bfloat16)
-    t = timed(lambda: layer(x), args.steps, args.warmup, world)
+    t = timed(lambda: layer(x), steps, warmup, world)
     flops = prefill_flops(1, T, cfg["dim"], full.H, full.HKV, full.HD)["total"]
-    return {"value": T * args.steps / t, "unit": "tok/s", "ms_per_step": t / args.steps * 1e3,
+    return {"value": T * steps / t, "unit": "tok/s", "ms_per_step": t / steps * 1e3, "steps": steps,
+            "warmup": warmup, "collective": "NCCL all-reduce of the fp32 o_proj partials" if world > 1 else None,
             "workload": "configs[4]: Bolt3Attn prefill, Llama-3-8B shape (D4096 H32/8 HD128 theta5e5), "
                         "1 x 131072 tokens, 20% near-duplicates, seeded random weights",
             "parallelism": f"tp{world} by KV head" if world > 1 else "one GPU, all 8 KV heads",
@@ -648,6 +683,7 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=DEC_STEPS, help="timed decode steps")
     ap.add_argument("--long", action="store_true", help="only the configs[4] long-context prefill")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the GPU results")
+    ap.add_argument("--no-long", action="store_true", help="skip the configs[4] leg of the default line")
     ap.add_argument("--parity-decode-steps", type=int, default=DEC_STEPS,
                     help="one-token steps of the configs[2] parity sample")
     args = ap.parse_args()

@@ -38,6 +38,24 @@ def _gloo_worker(rank: int, world: int, port: int, out):
         dist.destroy_process_group()
 
 
+def _get_while_alive(q, procs, deadline_s: float):
+    """The first item of `q`, polling in short waits; fails as soon as a rank has exited with an
+    error or the deadline passes, instead of blocking on a rank that died."""
+    import queue
+    import time
+
+    t0 = time.monotonic()
+    while time.monotonic() - t0 < deadline_s:
+        try:
+            return q.get(timeout=2)
+        except queue.Empty:
+            dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+            assert not dead, f"a rank exited with {dead}"
+    for p in procs:
+        p.kill()
+    raise AssertionError(f"no result within {deadline_s} s")
+
+
 def test_kv_head_range_splits_evenly():
     assert [kv_head_range(8, r, 4) for r in range(4)] == [(0, 2), (2, 4), (4, 6), (6, 8)]
     with pytest.raises(ValueError):
@@ -65,7 +83,7 @@ def test_tp_oracle_allreduce_matches_full_layer_gloo():
     procs = [ctx.Process(target=_gloo_worker, args=(r, 2, port, out)) for r in range(2)]
     for p in procs:
         p.start()
-    y = out.get(timeout=300)
+    y = _get_while_alive(out, procs, deadline_s=240)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -111,3 +129,28 @@ def test_tp_decode_shards_sum_to_layer():
         got = got.to(torch.bfloat16)
         output_close(got.cpu(), ref.float().cpu(), f"decode step at {p}")
 
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp_nccl_two_gpus_matches_layer(tmp_path):
+    """Bolt3AttnTP over two GPUs (one NCCL all-reduce of the o_proj partials per call), forward and
+    decode steps, against the unsharded native layer on GPU 0. The ranks run under
+    torch.distributed.run as child processes with a hard time limit, so a rank that dies or hangs
+    fails the test instead of stalling it; NVLS is off."""
+    import subprocess
+    import sys
+
+    out = tmp_path / "tp.pt"
+    here = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    port = 29600 + os.getpid() % 1000
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", f"--master-port={port}", os.path.join(here, "tp_nccl_worker.py"),
+           "--out", str(out)]
+    r = subprocess.run(cmd, env=env, timeout=240, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    res = torch.load(out, weights_only=False)
+    assert res["world"] == 2
+    output_close(res["y"], res["ref"], "two-GPU tensor-parallel forward")
+    output_close(res["dec"], res["ref_dec"], "two-GPU tensor-parallel decode steps")
