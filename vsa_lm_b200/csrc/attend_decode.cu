@@ -363,20 +363,18 @@ int launch(const bolt3_attend_args* a, cudaStream_t s) {
 namespace stream {
 
 constexpr int HD = 128;
-constexpr int NST = 3;             // ring stages
+constexpr int NST = 2;             // ring stages (two CTAs share an SM: four stages per SM)
 constexpr int kStage = 32768;      // bytes per stage: 128 rows x 256 bytes
 constexpr int NRM = 4;             // query rows per chain, padded
-constexpr int NGRP = 2;            // consumer groups: group g takes the CTA's chains g, g + 2, ...
-constexpr int GW = 8;              // warps per consumer group
-constexpr int GT = GW * 32;        // threads per consumer group
-constexpr int NCW = NGRP * GW;     // consumer warps (0 .. 15); warp 16 produces, warp 17 issues the MMAs
-constexpr int kThreads = NCW * 32 + 64;
-constexpr int NSET = 4;            // per-chain buffer sets: chain j uses set j % 4
+constexpr int NCW = 8;             // consumer warps (warps 0-7); warp 8 produces, warp 9 issues the MMAs
+constexpr int NCT = NCW * 32;      // consumer threads
+constexpr int kThreads = NCT + 64;
+constexpr int kCtasPerSm = 2;      // two independent CTAs per SM interleave their chains' dependent phases
 constexpr uint32_t kIters = 1u << 24;
 // byte offsets inside the R piece: 16-row tiles (two 64-column halves each) of q_rope, sink keys,
 // sink values; then q_raw, mass, act
 constexpr int kRQ = 0, kRSK = 4096, kRSV = 8192, kRQRaw = 12288, kRMass = 13312, kRAct = 13824;
-constexpr uint32_t kColO = 128;    // TMEM: scores buffer b in columns [64 b, 64 b + 64); O^T buffer b at 128 + 32 b
+constexpr uint32_t kColO = 128;    // TMEM: scores buffer b in columns [64 b, 64 b + 64); O^T at 128
 constexpr uint32_t kTmemCols = 256;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -394,42 +392,42 @@ struct __align__(64) Maps {
 
 struct __align__(1024) Smem {
   unsigned char ring[NST][kStage];
-  unsigned char svt[NSET][4096];       // per chain set: the sink values' 16-row tile (MN-major A of P@V)
-  unsigned char qbuf[NSET][4096];      // per chain set: the Q tile (K-major B of the score MMAs)
-  unsigned char ptile[NGRP][4][2][2048];  // per group: probabilities of each segment, 16 rows x (2 x 64 keys)
-  float2 qd[NSET][HD][NRM];            // per chain set: q_raw[row][d], duplicated into both halves of a pair
-  float ypart[NGRP][4][NRM][HD];       // per group: M_res read-out partial sums of each quarter of d
-  float bias[NSET][S];
-  float red[NGRP][GW][NRM], red2[NGRP][GW][NRM];
-  float qn[NSET][NRM];
+  unsigned char svt[2][4096];      // per chain buffer: the sink values' 16-row tile (MN-major A of P@V)
+  unsigned char qbuf[2][4096];     // per chain buffer: the Q tile (K-major B of the score MMAs)
+  unsigned char ptile[4][2][2048]; // probabilities of each segment: 16 rows x (2 x 64 keys), K-major SW128
+  float qd[2][HD][NRM];            // per chain buffer: q_raw[row][d]
+  float ypart[4][NRM][HD];         // M_res read-out partial sums of each quarter of d
+  float bias[2][S];
+  float red[NCW][NRM], red2[NCW][NRM];
+  float qn[2][NRM];
   uint64_t full[NST], empty[NST];
-  uint64_t bar_s[2], bar_o[2];         // MMA warp -> consumers: scores / O^T of a chain buffer (chain parity)
-  uint64_t r_ready[NSET], r_done[NSET];  // R piece of a chain: landed (MMA warp -> group) / read out (group -> MMA warp)
-  uint64_t p_ready[NGRP];              // group -> MMA warp: the probabilities of its chain are written
+  uint64_t bar_s[2], bar_o;        // MMA warp -> consumers: scores of a chain buffer; O^T of a chain
+  uint64_t r_done[2], p_ready;     // consumers -> MMA warp: R piece read out (per chain buffer, so that
+                                   // the next chain's arrival cannot overtake this wait); probabilities written
+  uint64_t r_ready[2];             // MMA warp -> consumers: the R piece of a chain has landed
   uint32_t tbase;
   int err;
 };
 
-// barrier of consumer group g (named barrier 1 + g)
-B3_DEV void grp_sync(int g) { asm volatile("bar.sync %0, %1;\n" ::"r"(1 + g), "n"(GT) : "memory"); }
-// OR of `v` over the threads of group g (also a barrier among them)
-B3_DEV bool grp_any(int g, bool v) {
+B3_DEV void cons_sync() { asm volatile("bar.sync 1, %0;\n" ::"n"(NCT) : "memory"); }
+// OR of `v` over the consumer threads (also a barrier among them)
+B3_DEV bool cons_any(bool v) {
   uint32_t r;
   asm volatile(
-      "{\n.reg .pred p, q;\nsetp.ne.u32 p, %1, 0;\nbar.red.or.pred q, %2, %3, p;\nselp.u32 %0, 1, 0, q;\n}\n"
+      "{\n.reg .pred p, q;\nsetp.ne.u32 p, %1, 0;\nbar.red.or.pred q, 1, %2, p;\nselp.u32 %0, 1, 0, q;\n}\n"
       : "=r"(r)
-      : "r"((uint32_t)v), "r"(1 + g), "n"(GT)
+      : "r"((uint32_t)v), "n"(NCT)
       : "memory");
   return r != 0;
 }
 
-__global__ void __launch_bounds__(kThreads, 1) attend_stream_kernel(const bolt3_attend_args a,
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(const bolt3_attend_args a,
                                                                     const __grid_constant__ Maps tm) {
   extern __shared__ unsigned char smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (a.wait_probe) {  // failure-path test hook: an expired bounded wait, reported as bit 2
-    if (tid == 0 && !tc5::probe_wait(&sm.bar_o[0], a.wait_probe) && a.status) atomicOr(a.status, 2);
+    if (tid == 0 && !tc5::probe_wait(&sm.bar_o, a.wait_probe) && a.status) atomicOr(a.status, 2);
     return;
   }
   const int G = a.G, T = (int)a.Tq, NR = G * T, H = a.hkv * G;
@@ -442,24 +440,20 @@ __global__ void __launch_bounds__(kThreads, 1) attend_stream_kernel(const bolt3_
     if (len[s] > 0) kv_list[n_kv++] = s;
   // chains of this CTA: blockIdx.x + li * gridDim.x, li < n_local
   const int n_local = a.n_chains > (int)blockIdx.x ? (a.n_chains - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  // ring position of local chain j's R piece: the producer emits R(0) K(0)..., then per step li >= 0
-  // R(li + 1) K(li + 1)... V(li)...
-  auto r_index = [&](int j) -> uint32_t { return j == 0 ? 0u : (uint32_t)(j * (1 + 2 * n_kv) - n_kv); };
 
   if (tid == 0) {
     for (int s = 0; s < NST; ++s) {
       tc5::mbar_init(&sm.full[s], 1);
       tc5::mbar_init(&sm.empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      tc5::mbar_init(&sm.bar_s[b], 1);
-      tc5::mbar_init(&sm.bar_o[b], 1);
-    }
-    for (int s = 0; s < NSET; ++s) {
-      tc5::mbar_init(&sm.r_ready[s], 1);
-      tc5::mbar_init(&sm.r_done[s], 1);
-    }
-    for (int g = 0; g < NGRP; ++g) tc5::mbar_init(&sm.p_ready[g], 1);
+    tc5::mbar_init(&sm.bar_s[0], 1);
+    tc5::mbar_init(&sm.bar_s[1], 1);
+    tc5::mbar_init(&sm.bar_o, 1);
+    tc5::mbar_init(&sm.r_done[0], 1);
+    tc5::mbar_init(&sm.r_done[1], 1);
+    tc5::mbar_init(&sm.r_ready[0], 1);
+    tc5::mbar_init(&sm.r_ready[1], 1);
+    tc5::mbar_init(&sm.p_ready, 1);
     tc5::mbar_fence_init();
     sm.err = 0;
   }
@@ -551,16 +545,17 @@ __global__ void __launch_bounds__(kThreads, 1) attend_stream_kernel(const bolt3_
       };
       for (int li = -1; li < n_local; ++li) {
         if (li + 1 < n_local) {
-          // S^T = K . Q^T per segment into scores buffer (li + 1) & 1; the sinks' keys and Q come with
-          // the R piece, which the chain's consumer group reads first
-          const int j = li + 1, bn = j & 1, set = j & (NSET - 1);
+          // S^T = K . Q^T per segment; the sinks' keys and Q come with the R piece
+          const int bn = (li + 1) & 1;
           const int sr = stage_wait();
           ++it;
-          tc5::mbar_arrive(&sm.r_ready[set]);
-          if (!tc5::mbar_wait(&sm.r_done[set], (uint32_t)(j / NSET) & 1u, kIters)) sm.err = 1;
+          tc5::mbar_arrive(&sm.r_ready[bn]);
+          // the consumers copy Q (and the sink values) out of the R piece; after that, the sink keys
+          // are its last reader and the stage turns over
+          if (!tc5::mbar_wait(&sm.r_done[bn], (uint32_t)((li + 1) >> 1) & 1u, kIters)) sm.err = 1;
           tc5::fence_after_sync();
           const uint32_t ra = tc5::smem_u32(sm.ring[sr]);
-          const uint32_t qa = tc5::smem_u32(sm.qbuf[set]);
+          const uint32_t qa = tc5::smem_u32(sm.qbuf[bn]);
           if (has_sinks) {
 #pragma unroll
             for (int ks = 0; ks < HD / 16; ++ks)
@@ -568,6 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1) attend_stream_kernel(const bolt3_
                           tc5::sdesc(qa + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024), kIdS, ks > 0);
           }
           tc5::commit(&sm.empty[sr]);
+          // S^T = K . Q^T of the ring segments
           for (int i = 0; i < n_kv; ++i) {
             const int s = stage_wait();
             ++it;
@@ -582,15 +578,14 @@ __global__ void __launch_bounds__(kThreads, 1) attend_stream_kernel(const bolt3_
           tc5::commit(&sm.bar_s[bn]);
         }
         if (li >= 0) {
-          // O^T = V^T . P^T into O buffer li & 1 once chain li's group has written its probabilities
-          const int bi = li & 1, set = li & (NSET - 1);
-          if (!tc5::mbar_wait(&sm.p_ready[bi], (uint32_t)(li >> 1) & 1u, kIters)) sm.err = 1;
+          // O^T = V^T . P^T once the consumers have written chain li's probabilities
+          const int bi = li & 1;
+          if (!tc5::mbar_wait(&sm.p_ready, (uint32_t)li & 1u, kIters)) sm.err = 1;
           tc5::fence_after_sync();
-          const uint32_t dcol = tb + kColO + 32 * bi;
           bool first = true;
           if (has_sinks) {  // one 16-key step: sink rows 4..15 of the tile are zero, their P columns too
-            tc5::mma_ss(dcol, tc5::sdesc(tc5::smem_u32(sm.svt[set]), 2048, 1024),
-                        tc5::sdesc(tc5::smem_u32(sm.ptile[bi][0][0]), 16, 1024), kIdO, false);
+            tc5::mma_ss(tb + kColO, tc5::sdesc(tc5::smem_u32(sm.svt[bi]), 2048, 1024),
+                        tc5::sdesc(tc5::smem_u32(sm.ptile[0][0]), 16, 1024), kIdO, false);
             first = false;
           }
           for (int i = 0; i < n_kv; ++i) {
@@ -598,82 +593,94 @@ __global__ void __launch_bounds__(kThreads, 1) attend_stream_kernel(const bolt3_
             ++it;
             const uint32_t va = tc5::smem_u32(sm.ring[s]);
             const int sg = kv_list[i];
-            const uint32_t pa = tc5::smem_u32(sm.ptile[bi][sg][0]);
+            const uint32_t pa = tc5::smem_u32(sm.ptile[sg][0]);
             const int nks = (len[sg] + 15) / 16;
             for (int ks = 0; ks < nks; ++ks) {
-              tc5::mma_ss(dcol, tc5::sdesc(va + ks * 2048, 16384, 1024),
+              tc5::mma_ss(tb + kColO, tc5::sdesc(va + ks * 2048, 16384, 1024),
                           tc5::sdesc(pa + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024), kIdO, !first);
               first = false;
             }
             tc5::commit(&sm.empty[s]);
           }
-          tc5::commit(&sm.bar_o[bi]);
+          tc5::commit(&sm.bar_o);
         }
       }
     }
   } else {
-    // ---- consumer group g (threads gt = 0 .. 255 of warps 8 g .. 8 g + 7): chains g, g + 2, ...
-    const int g = warp / GW, gw = warp % GW, gt = tid - g * GT;
+    // ---- consumers (threads 0..255)
+    const int t = tid;
     constexpr float scale = 0.08838834764831845f;  // fp32(128 ** -0.5)
-    const uint32_t lane_off = (uint32_t)(32 * (gw & 3)) << 16;
-    const int rg = gw >> 2;                 // query rows 2 rg, 2 rg + 1 in the softmax and the epilogue
-    const int kq = 32 * (gw & 3) + lane;    // this thread's TMEM lane: a key of a segment, or a column e
-    // R piece of local chain j into its buffer set j % 4; the K pieces after it go to the MMA warp
-    auto front = [&](int j) {
-      const int c = (int)blockIdx.x + j * (int)gridDim.x;
-      const int set = j & (NSET - 1);
+    const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+    const int rg = warp >> 2;               // query rows 2 rg, 2 rg + 1 in the softmax and the epilogue
+    const int kq = 32 * (warp & 3) + lane;  // this thread's TMEM lane: a key of a segment, or a column e
+    // ring position: the consumers count every piece but wait only for the ones the MMA warp hands
+    // over (and then for the stage's own barrier, whose phase is by then the current one)
+    uint32_t it = 0;
+    auto handed = [&](uint64_t* ready, uint32_t parity) -> int {
+      const int s = (int)(it % NST);
+      if (!tc5::mbar_wait(ready, parity, kIters)) sm.err = 1;
+      if (!tc5::mbar_wait(&sm.full[s], (it / NST) & 1u, kIters)) sm.err = 1;
+      return s;
+    };
+    // R piece of local chain li (its buffers li & 1); the K pieces after it go to the MMA warp
+    auto front = [&](int li) {
+      const int c = (int)blockIdx.x + li * (int)gridDim.x;
+      const int bi = li & 1;
       const int kvh = c % a.hkv;
-      const uint32_t idx = r_index(j);
-      const int sr = (int)(idx % NST);
-      if (!tc5::mbar_wait(&sm.r_ready[set], (uint32_t)(j / NSET) & 1u, kIters)) sm.err = 1;
-      if (!tc5::mbar_wait(&sm.full[sr], (idx / NST) & 1u, kIters)) sm.err = 1;
+      const int sr = handed(&sm.r_ready[bi], (uint32_t)(li >> 1) & 1u);
       const unsigned char* buf = sm.ring[sr];
       const uint32_t* rs = reinterpret_cast<const uint32_t*>(buf + kRQRaw);
-      for (int i = gt; i < NRM * HD / 2; i += GT) {
-        const int r = i / (HD / 2), d2 = i % (HD / 2);
-        const float2 q2 = r < NR ? unpack_bf16(rs[r * (HD / 2) + d2]) : make_float2(0.f, 0.f);
-        sm.qd[set][2 * d2][r] = make_float2(q2.x, q2.x);
-        sm.qd[set][2 * d2 + 1][r] = make_float2(q2.y, q2.y);
+      for (int idx = t; idx < NRM * HD / 2; idx += NCT) {
+        const int r = idx / (HD / 2), d2 = idx % (HD / 2);
+        const float2 g = r < NR ? unpack_bf16(rs[r * (HD / 2) + d2]) : make_float2(0.f, 0.f);
+        sm.qd[bi][2 * d2][r] = g.x;
+        sm.qd[bi][2 * d2 + 1][r] = g.y;
       }
       if (has_bank) {
         const float kappa = __ldg(a.kappa + kvh);
         const float* mass = reinterpret_cast<const float*>(buf + kRMass);
-        for (int i = gt; i < S; i += GT)
-          sm.bias[set][i] = buf[kRAct + i] ? __fmul_rn(kappa, logf(fmaxf(mass[i], 1.0f))) : neg_inf();
+        for (int j = t; j < S; j += NCT)
+          sm.bias[bi][j] = buf[kRAct + j] ? __fmul_rn(kappa, logf(fmaxf(mass[j], 1.0f))) : neg_inf();
       }
       // the Q tile and the sink values' tile outlive the stage: one 16-byte chunk of each per thread
-      reinterpret_cast<uint4*>(sm.qbuf[set])[gt] = reinterpret_cast<const uint4*>(buf + kRQ)[gt];
-      if (has_sinks) reinterpret_cast<uint4*>(sm.svt[set])[gt] = reinterpret_cast<const uint4*>(buf + kRSV)[gt];
+      reinterpret_cast<uint4*>(sm.qbuf[bi])[t] = reinterpret_cast<const uint4*>(buf + kRQ)[t];
+      if (has_sinks) reinterpret_cast<uint4*>(sm.svt[bi])[t] = reinterpret_cast<const uint4*>(buf + kRSV)[t];
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-      grp_sync(g);
-      if (gt == 0) tc5::mbar_arrive(&sm.r_done[set]);
-      if (has_bank && a.q_l2 == nullptr && gw < NR) {
+      cons_sync();
+      if (t == 0) tc5::mbar_arrive(&sm.r_done[bi]);
+      ++it;
+      if (has_bank && a.q_l2 == nullptr && warp < NR) {
         float s2 = 0.f;
-        for (int d = lane; d < HD; d += 32) s2 = fmaf(sm.qd[set][d][gw].x, sm.qd[set][d][gw].x, s2);
+        for (int d = lane; d < HD; d += 32) s2 = fmaf(sm.qd[bi][d][warp], sm.qd[bi][d][warp], s2);
         s2 = warp_sum(s2);
-        if (lane == 0) sm.qn[set][gw] = sqrtf(s2);
+        if (lane == 0) sm.qn[bi][warp] = sqrtf(s2);
       }
     };
 
-    if (g < n_local) front(g);
-    for (int j = g; j < n_local; j += NGRP) {
-      const int c = (int)blockIdx.x + j * (int)gridDim.x;
+    if (n_local > 0) {
+      front(0);
+      it += n_kv;  // chain 0's keys: the MMA warp's
+    }
+    for (int li = 0; li < n_local; ++li) {
+      const int c = (int)blockIdx.x + li * (int)gridDim.x;
       const int kvh = c % a.hkv, b = c / a.hkv;
-      const int bi = j & 1, set = j & (NSET - 1);
-      const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+      const int bi = li & 1;
       // the epilogue's per-row scalars, requested now and used at the end
       float eta_r[2], ql2_r[2];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int r = 2 * rg + u;
-        eta_r[u] = has_bank && r < NR ? __ldg(a.eta + (int64_t)c * NR + r) : 0.f;
-        ql2_r[u] = has_bank && r < NR && a.q_l2 != nullptr ? __ldg(a.q_l2 + (int64_t)c * NR + r) : 0.f;
+      for (int j = 0; j < 2; ++j) {
+        const int r = 2 * rg + j;
+        eta_r[j] = has_bank && r < NR ? __ldg(a.eta + (int64_t)c * NR + r) : 0.f;
+        ql2_r[j] = has_bank && r < NR && a.q_l2 != nullptr ? __ldg(a.q_l2 + (int64_t)c * NR + r) : 0.f;
       }
       const float coef = has_bank ? __ldg(a.coef + kvh) : 0.f;
       const float res_w = has_bank ? __ldg(a.res_w + kq) : 0.f;
 
-      // -- softmax of chain j: thread (key kq of each segment, rows 2 rg, 2 rg + 1)
-      if (!tc5::mbar_wait(&sm.bar_s[bi], ph, kIters)) sm.err = 1;
+      // -- R of the next chain first: the MMA warp can then score its keys during this softmax
+      if (li + 1 < n_local) front(li + 1);
+
+      // -- softmax of chain li: thread (key kq of each segment, rows 2 rg, 2 rg + 1)
+      if (!tc5::mbar_wait(&sm.bar_s[bi], (uint32_t)(li >> 1) & 1u, kIters)) sm.err = 1;
       tc5::fence_after_sync();
       uint32_t v[4][4];
 #pragma unroll
@@ -691,7 +698,7 @@ __global__ void __launch_bounds__(kThreads, 1) attend_stream_kernel(const bolt3_
           const int r = 2 * rg + u;
           if (r >= NR) continue;
           float s2 = __fmul_rn(__uint_as_float(v[sg][r]), scale);
-          if (sg == 1) s2 = __fadd_rn(s2, sm.bias[set][kq]);
+          if (sg == 1) s2 = __fadd_rn(s2, sm.bias[bi][kq]);
           if (sg == 3 && kq > a.len_before + r % T) s2 = neg_inf();
           sv[sg][u] = s2;
           mx[u] = fmaxf(mx[u], s2);
@@ -700,14 +707,13 @@ __global__ void __launch_bounds__(kThreads, 1) attend_stream_kernel(const bolt3_
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const float m = warp_max(mx[u]);
-        if (lane == 0) sm.red[g][gw][2 * rg + u] = m;
+        if (lane == 0) sm.red[warp][2 * rg + u] = m;
       }
-      grp_sync(g);
+      cons_sync();
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const int r = 2 * rg + u;
-        mx[u] = fmaxf(fmaxf(sm.red[g][4 * rg][r], sm.red[g][4 * rg + 1][r]),
-                      fmaxf(sm.red[g][4 * rg + 2][r], sm.red[g][4 * rg + 3][r]));
+        mx[u] = fmaxf(fmaxf(sm.red[4 * rg][r], sm.red[4 * rg + 1][r]), fmaxf(sm.red[4 * rg + 2][r], sm.red[4 * rg + 3][r]));
         float sum = 0.f;
 #pragma unroll
         for (int sg = 0; sg < 4; ++sg) {
@@ -716,35 +722,36 @@ __global__ void __launch_bounds__(kThreads, 1) attend_stream_kernel(const bolt3_
           sum += sv[sg][u];
         }
         const float w = warp_sum(sum);
-        if (lane == 0) sm.red2[g][gw][r] = w;
+        if (lane == 0) sm.red2[warp][r] = w;
       }
-      grp_sync(g);
+      cons_sync();
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const int r = 2 * rg + u;
-        const float tot = sm.red2[g][4 * rg][r] + sm.red2[g][4 * rg + 1][r] + sm.red2[g][4 * rg + 2][r] +
-                          sm.red2[g][4 * rg + 3][r];
+        const float tot = sm.red2[4 * rg][r] + sm.red2[4 * rg + 1][r] + sm.red2[4 * rg + 2][r] + sm.red2[4 * rg + 3][r];
         const float inv = 1.0f / tot;
 #pragma unroll
         for (int sg = 0; sg < 4; ++sg) {
           if (len[sg] == 0) continue;
           const float pv = r < NR ? rbf(__fmul_rn(sv[sg][u], inv)) : 0.f;
-          *reinterpret_cast<bf16*>(sm.ptile[g][sg][kq >> 6] + tc5::sw128_off(r, kq & 63)) = __float2bfloat16_rn(pv);
+          *reinterpret_cast<bf16*>(sm.ptile[sg][kq >> 6] + tc5::sw128_off(r, kq & 63)) = __float2bfloat16_rn(pv);
         }
       }
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
       tc5::fence_before_sync();
-      grp_sync(g);
-      if (gt == 0) tc5::mbar_arrive(&sm.p_ready[g]);
+      cons_sync();
+      if (t == 0) tc5::mbar_arrive(&sm.p_ready);
+      if (li + 1 < n_local) it += n_kv;  // the next chain's keys: the MMA warp's
+      it += n_kv;                        // this chain's values: the MMA warp's
 
-      // -- M_res read-out: R[r][e] = sum_d q_raw[r][d] * M[d][e] in fp32, M read from L2 (the
-      // producer prefetched it); thread (column pair, quarter of the rows d), all four rows, two
-      // columns per paired FMA, eight rows of M in flight
+      // -- M_res read-out: R[r][e] = sum_d q_raw[r][d] * M[d][e] in fp32; thread (column pair, quarter
+      // of the rows d), all four rows, two columns per paired FMA
       float2 ym2[NRM];
 #pragma unroll
       for (int r = 0; r < NRM; ++r) ym2[r] = make_float2(0.f, 0.f);
-      const int cpm = gt & 63, dq = gt >> 6;
+      const int cpm = t & 63, dq = t >> 6;
       if (has_bank) {
+        // M read from L2 (the producer prefetched it), eight rows of M in flight
         const int d0 = dq * (HD / 4);
         const float2* mg = reinterpret_cast<const float2*>(reinterpret_cast<const float*>(a.bank_m) +
                                                            (int64_t)c * a.bank_cap * HD * HD + (int64_t)d0 * HD) + cpm;
@@ -760,53 +767,47 @@ __global__ void __launch_bounds__(kThreads, 1) attend_stream_kernel(const bolt3_
           }
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
-            const int dd = blk * 8 + u;
             const float2 m2 = mb[cur][u];
-            const float4 q01 = *reinterpret_cast<const float4*>(&sm.qd[set][d0 + dd][0]);
-            const float4 q23 = *reinterpret_cast<const float4*>(&sm.qd[set][d0 + dd][2]);
-            ym2[0] = __ffma2_rn(make_float2(q01.x, q01.y), m2, ym2[0]);
-            ym2[1] = __ffma2_rn(make_float2(q01.z, q01.w), m2, ym2[1]);
-            ym2[2] = __ffma2_rn(make_float2(q23.x, q23.y), m2, ym2[2]);
-            ym2[3] = __ffma2_rn(make_float2(q23.z, q23.w), m2, ym2[3]);
+            const float4 q = *reinterpret_cast<const float4*>(&sm.qd[bi][d0 + blk * 8 + u][0]);
+            ym2[0] = __ffma2_rn(make_float2(q.x, q.x), m2, ym2[0]);
+            ym2[1] = __ffma2_rn(make_float2(q.y, q.y), m2, ym2[1]);
+            ym2[2] = __ffma2_rn(make_float2(q.z, q.z), m2, ym2[2]);
+            ym2[3] = __ffma2_rn(make_float2(q.w, q.w), m2, ym2[3]);
           }
         }
       }
 #pragma unroll
-      for (int r = 0; r < NRM; ++r) *reinterpret_cast<float2*>(&sm.ypart[g][dq][r][2 * cpm]) = ym2[r];
-      grp_sync(g);
-
-      // -- the R piece of this group's next chain (its scores are computed while this one finishes)
-      if (j + NGRP < n_local) front(j + NGRP);
+      for (int r = 0; r < NRM; ++r) *reinterpret_cast<float2*>(&sm.ypart[dq][r][2 * cpm]) = ym2[r];
+      cons_sync();
 
       // -- epilogue: thread (column e = its TMEM lane, rows 2 rg, 2 rg + 1)
       const int e = kq;
-      if (!tc5::mbar_wait(&sm.bar_o[bi], ph, kIters)) sm.err = 1;
+      if (!tc5::mbar_wait(&sm.bar_o, (uint32_t)li & 1u, kIters)) sm.err = 1;
       tc5::fence_after_sync();
       uint32_t ov[4];
-      tc5::ld4(tb + lane_off + kColO + 32 * bi, ov);
+      tc5::ld4(tb + lane_off + kColO, ov);
       tc5::ld_wait();
       float ym[2], rs_r[2] = {0.f, 0.f};
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const int r = 2 * rg + u;
-        ym[u] = ((sm.ypart[g][0][r][e] + sm.ypart[g][1][r][e]) + sm.ypart[g][2][r][e]) + sm.ypart[g][3][r][e];
+        ym[u] = ((sm.ypart[0][r][e] + sm.ypart[1][r][e]) + sm.ypart[2][r][e]) + sm.ypart[3][r][e];
       }
       if (has_bank) {
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int r = 2 * rg + u;
-          const float qn = a.q_l2 != nullptr ? ql2_r[u] : (r < NR ? sm.qn[set][r] : 1.f);
+          const float qn = a.q_l2 != nullptr ? ql2_r[u] : (r < NR ? sm.qn[bi][r] : 1.f);
           const float iq = 1.0f / fmaxf(qn, 1e-12f);
           ym[u] = __fmul_rn(__fmul_rn(ym[u], iq), coef);
           const float ss = warp_sum(__fmul_rn(ym[u], ym[u]));
-          if (lane == 0) sm.red[g][gw][r] = ss;
+          if (lane == 0) sm.red[warp][r] = ss;
         }
-        grp_sync(g);
+        cons_sync();
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int r = 2 * rg + u;
-          const float ss = ((sm.red[g][4 * rg][r] + sm.red[g][4 * rg + 1][r]) + sm.red[g][4 * rg + 2][r]) +
-                           sm.red[g][4 * rg + 3][r];
+          const float ss = ((sm.red[4 * rg][r] + sm.red[4 * rg + 1][r]) + sm.red[4 * rg + 2][r]) + sm.red[4 * rg + 3][r];
           rs_r[u] = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)HD), a.eps));
         }
       }
@@ -817,15 +818,15 @@ __global__ void __launch_bounds__(kThreads, 1) attend_stream_kernel(const bolt3_
         if (r >= NR) break;
         float yv = rbf(__uint_as_float(ov[r]));
         if (has_bank) yv = __fadd_rn(yv, rbf(__fmul_rn(eta_r[u], __fmul_rn(__fmul_rn(ym[u], rs_r[u]), res_w))));
-        const int gq = r / T, i = r % T;
-        y[(((int64_t)b * a.y_tokens + i) * H + kvh * G + gq) * HD + e] = __float2bfloat16_rn(yv);
+        const int g = r / T, i = r % T;
+        y[(((int64_t)b * a.y_tokens + i) * H + kvh * G + g) * HD + e] = __float2bfloat16_rn(yv);
       }
-      // the group's next chain overwrites its probability tile, partial sums and exchange rows
+      // the next chain overwrites the probability tile, the partial sums and the exchange rows
       tc5::fence_before_sync();
-      if (grp_any(g, *reinterpret_cast<volatile int*>(&sm.err) != 0)) break;
+      if (cons_any(*reinterpret_cast<volatile int*>(&sm.err) != 0)) break;
       tc5::fence_after_sync();
     }
-    if (gt == 0 && sm.err && a.status) atomicOr(a.status, 2);
+    if (t == 0 && sm.err && a.status) atomicOr(a.status, 2);
   }
   tc5::fence_before_sync();
   __syncthreads();
@@ -833,7 +834,7 @@ __global__ void __launch_bounds__(kThreads, 1) attend_stream_kernel(const bolt3_
   if (warp == 0) tc5::tmem_dealloc(tb, kTmemCols);
 }
 
-// encodes the maps and launches one CTA per SM (at most one per chain); < 0: a map could not be
+// encodes the maps and launches kCtasPerSm CTAs per SM (at most one per chain); < 0: a map could not be
 // encoded (the caller then uses the warp-per-chain kernel)
 int launch(const bolt3_attend_args* a, cudaStream_t s) {
   Maps m;
@@ -861,11 +862,12 @@ int launch(const bolt3_attend_args* a, cudaStream_t s) {
   static std::atomic<bool> attr_set[kMaxDev];
   if (dev >= kMaxDev) return BOLT3_ERR_CUDA;
   if (!attr_set[dev].load(std::memory_order_acquire)) {
-    if (cudaFuncSetAttribute(attend_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(attend_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
+        cudaFuncSetAttribute(attend_stream_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
       return BOLT3_ERR_CUDA;
     attr_set[dev].store(true, std::memory_order_release);
   }
-  const int grid = (int)std::min<int64_t>(nc, sms);
+  const int grid = (int)std::min<int64_t>(nc, (int64_t)sms * kCtasPerSm);
   attend_stream_kernel<<<grid, kThreads, smem, s>>>(*a, m);
   return cudaGetLastError() == cudaSuccess ? BOLT3_OK : BOLT3_ERR_CUDA;
 }
