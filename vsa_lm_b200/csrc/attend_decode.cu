@@ -336,8 +336,8 @@ int launch(const bolt3_attend_args* a, cudaStream_t s) {
 // Tensor-core streaming kernel for HD = 128 and at most four query rows per chain (the one-token step
 // with G <= 4).
 //
-// The step reads every chain's state once, so it is bound by how much of it is in flight. A
-// persistent CTA (one per SM) walks a strided list of chains with three roles: a producer warp whose
+// The step reads every chain's state once, so it is bound by how much of it is in flight. Persistent
+// CTAs (two per SM) walk strided lists of chains with three roles: a producer warp whose
 // lane 0 copies the operands with the TMA engine into a ring of NST 32 KB stages, an MMA warp whose
 // lane 0 issues every tensor-core product, and eight consumer warps for the softmax, the M_res
 // read-out and the output. The roles meet only at mbarriers, so no role waits on another's data
@@ -350,10 +350,11 @@ int launch(const bolt3_attend_args* a, cudaStream_t s) {
 //   K  pieces  one per segment (attractors, previous chunk, current chunk): 128 rows by 3-D tensor
 //              maps into 128-byte swizzled tiles; rows past the segment read as zero;
 //   V  pieces  the value rows of each segment, the same way.
-// The ring carries the chains software-pipelined, R and K of chain i+1 ahead of V of chain i: chain
-// i+1's scores are computed while chain i's softmax runs, and chain i's values are multiplied as soon
-// as they land after it. The fp32 M_res (64 KB) does not travel in the ring: the consumers request
-// the next chain's with cp.async into a buffer of its own as soon as they are done with this one.
+// Every ring operand is read once, so its copies carry an evict-first L2 policy. The ring carries the
+// chains software-pipelined, R and K of chain i+1 ahead of V of chain i: chain i+1's scores are
+// computed while chain i's softmax runs, and chain i's values are multiplied as soon as they land
+// after it. The fp32 M_res (64 KB) does not travel in the ring: a bulk prefetch pulls it into L2 when
+// the consumers start the chain, and they read it from there with plain loads after the softmax.
 // Scores are one tcgen05.mma per segment and 16-key step, S^T[key][row] = K . Q^T into tensor
 // memory (double-buffered across chains; columns 16 s .. 16 s + 15 of a buffer, a lane per key). The
 // softmax reads them back (exact: a sweep for the max, one for the sum) and writes the bf16
@@ -471,6 +472,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
     if (lane == 0) {
       uint32_t it = 0;
       bool stop = false;
+      // every ring operand is read once: its L2 lines go first, ahead of the prefetched M_res
+      const uint64_t pol = tc5::policy_evict_first();
       // one ring piece; false once an error was recorded
       auto put = [&](auto&& issue) -> bool {
         const int s = (int)(it % NST);
@@ -484,24 +487,19 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
         if (li + 1 < n_local) {
           const int c = (int)blockIdx.x + (li + 1) * (int)gridDim.x;
           const int64_t bofs = (int64_t)c * a.bank_cap;
-          if (has_bank) {
-            // the chain's fp32 M_res is read by the consumers straight from L2: pull it in now
-            const float* mp = reinterpret_cast<const float*>(a.bank_m) + bofs * HD * HD;
-            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(mp), "r"(HD * HD * 4) : "memory");
-          }
           stop = !put([&](unsigned char* buf, uint64_t* bar) {
             const uint32_t qb = (uint32_t)NR * HD * 2;
             tc5::mbar_expect_tx(bar, 2 * 2048 + (has_sinks ? 4 * 2048 : 0) + qb + (has_bank ? S * 4 + S : 0));
-            for (int h = 0; h < 2; ++h) tc5::tma_load_3d(buf + kRQ + h * 2048, &tm.q, h * 64, 0, c, bar);
+            for (int h = 0; h < 2; ++h) tc5::tma_load_3d(buf + kRQ + h * 2048, &tm.q, h * 64, 0, c, bar, pol);
             if (has_sinks)
               for (int h = 0; h < 2; ++h) {
-                tc5::tma_load_3d(buf + kRSK + h * 2048, &tm.k[0], h * 64, 0, c, bar);
-                tc5::tma_load_3d(buf + kRSV + h * 2048, &tm.v[0], h * 64, 0, c, bar);
+                tc5::tma_load_3d(buf + kRSK + h * 2048, &tm.k[0], h * 64, 0, c, bar, pol);
+                tc5::tma_load_3d(buf + kRSV + h * 2048, &tm.v[0], h * 64, 0, c, bar, pol);
               }
-            tc5::bulk_load(buf + kRQRaw, reinterpret_cast<const bf16*>(a.q_raw) + (int64_t)c * NR * HD, qb, bar);
+            tc5::bulk_load(buf + kRQRaw, reinterpret_cast<const bf16*>(a.q_raw) + (int64_t)c * NR * HD, qb, bar, pol);
             if (has_bank) {
-              tc5::bulk_load(buf + kRMass, a.bank_mass + bofs * S, S * 4, bar);
-              tc5::bulk_load(buf + kRAct, a.bank_act + bofs * S, S, bar);
+              tc5::bulk_load(buf + kRMass, a.bank_mass + bofs * S, S * 4, bar, pol);
+              tc5::bulk_load(buf + kRAct, a.bank_act + bofs * S, S, bar, pol);
             }
           });
           for (int i = 0; i < n_kv && !stop; ++i) {
@@ -509,7 +507,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
             stop = !put([&](unsigned char* buf, uint64_t* bar) {
               tc5::mbar_expect_tx(bar, 2 * 16384);
               for (int h = 0; h < 2; ++h)
-                tc5::tma_load_3d(buf + h * 16384, &tm.k[sg], h * 64, 0, sg == 1 ? (int)bofs : c, bar);
+                tc5::tma_load_3d(buf + h * 16384, &tm.k[sg], h * 64, 0, sg == 1 ? (int)bofs : c, bar, pol);
             });
           }
         }
@@ -521,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
             stop = !put([&](unsigned char* buf, uint64_t* bar) {
               tc5::mbar_expect_tx(bar, 2 * 16384);
               for (int h = 0; h < 2; ++h)
-                tc5::tma_load_3d(buf + h * 16384, &tm.v[sg], h * 64, 0, sg == 1 ? (int)bofs : c, bar);
+                tc5::tma_load_3d(buf + h * 16384, &tm.v[sg], h * 64, 0, sg == 1 ? (int)bofs : c, bar, pol);
             });
           }
         }
@@ -665,6 +663,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
       const int c = (int)blockIdx.x + li * (int)gridDim.x;
       const int kvh = c % a.hkv, b = c / a.hkv;
       const int bi = li & 1;
+      // the chain's fp32 M_res is read straight from L2 after the softmax: pull it in now (earlier,
+      // and the operands streaming through L2 meanwhile evict much of it before it is read)
+      if (has_bank && t == 0)
+        tc5::prefetch_l2(reinterpret_cast<const float*>(a.bank_m) + (int64_t)c * a.bank_cap * HD * HD, HD * HD * 4);
       // the epilogue's per-row scalars, requested now and used at the end
       float eta_r[2], ql2_r[2];
 #pragma unroll
