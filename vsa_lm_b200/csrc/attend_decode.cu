@@ -341,9 +341,10 @@ int launch(const bolt3_attend_args* a, cudaStream_t s) {
 // lane 0 copies the operands with the TMA engine into a ring of NST 32 KB stages, an MMA warp whose
 // lane 0 issues every tensor-core product, and eight consumer warps for the softmax, the M_res
 // read-out and the output. The roles meet only at mbarriers, so no role waits on another's data
-// unless it needs that data. The MMA warp is the ring's one in-order reader; it hands the pieces the
-// consumers read (R) to them through a per-chain mbarrier, so that every wait on a stage is for its
-// current phase. The ring pieces:
+// unless it needs that data. The MMA warp is the ring's one reader: as an R piece lands, the whole
+// warp copies the chain's operands out of it into per-chain buffers (the Q tile and the sink values'
+// tile, the attractor score bias, q_raw transposed, the rows' norms) and hands them to the consumers
+// through a per-chain mbarrier, so the stage turns over without waiting for them. The ring pieces:
 //   R  piece   the chain's small operands: q_rope rows as a 16-row K-major tile (rows past the
 //              chain's own read as zero), the 4 sink keys and values as 16-row tiles, q_raw, and the
 //              bank's mass and act;
@@ -396,16 +397,16 @@ struct __align__(1024) Smem {
   unsigned char svt[2][4096];      // per chain buffer: the sink values' 16-row tile (MN-major A of P@V)
   unsigned char qbuf[2][4096];     // per chain buffer: the Q tile (K-major B of the score MMAs)
   unsigned char ptile[4][2][2048]; // probabilities of each segment: 16 rows x (2 x 64 keys), K-major SW128
-  float qd[2][HD][NRM];            // per chain buffer: q_raw[row][d]
+  bf16 qd[3][HD][NRM];             // per chain buffer (local chain % 3): q_raw[row][d]
   float ypart[4][NRM][HD];         // M_res read-out partial sums of each quarter of d
-  float bias[2][S];
+  float bias[2][S];                // per chain buffer: the attractors' score bias
   float red[NCW][NRM], red2[NCW][NRM];
-  float qn[2][NRM];
+  float qn[3][NRM];                // per chain buffer (local chain % 3): |q_raw| of each row
   uint64_t full[NST], empty[NST];
   uint64_t bar_s[2], bar_o;        // MMA warp -> consumers: scores of a chain buffer; O^T of a chain
-  uint64_t r_done[2], p_ready;     // consumers -> MMA warp: R piece read out (per chain buffer, so that
-                                   // the next chain's arrival cannot overtake this wait); probabilities written
-  uint64_t r_ready[2];             // MMA warp -> consumers: the R piece of a chain has landed
+  uint64_t p_ready;                // consumers -> MMA warp: probabilities written
+  uint64_t r_ready[2];             // MMA warp -> consumers: a chain's bias, q_raw and norms are written
+  uint64_t fin;                    // the MMA warp's last commit
   uint32_t tbase;
   int err;
 };
@@ -441,6 +442,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
     if (len[s] > 0) kv_list[n_kv++] = s;
   // chains of this CTA: blockIdx.x + li * gridDim.x, li < n_local
   const int n_local = a.n_chains > (int)blockIdx.x ? (a.n_chains - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  // a wait that gives up records the error; once one has, the MMA warp skips its later waits (the
+  // work after them is void) so that the CTA ends quickly
+  auto wait_or_flag = [&](uint64_t* bar, uint32_t parity) {
+    if (*reinterpret_cast<volatile int*>(&sm.err) == 0 && !tc5::mbar_wait(bar, parity, kIters)) sm.err = 1;
+  };
 
   if (tid == 0) {
     for (int s = 0; s < NST; ++s) {
@@ -450,11 +456,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
     tc5::mbar_init(&sm.bar_s[0], 1);
     tc5::mbar_init(&sm.bar_s[1], 1);
     tc5::mbar_init(&sm.bar_o, 1);
-    tc5::mbar_init(&sm.r_done[0], 1);
-    tc5::mbar_init(&sm.r_done[1], 1);
     tc5::mbar_init(&sm.r_ready[0], 1);
     tc5::mbar_init(&sm.r_ready[1], 1);
     tc5::mbar_init(&sm.p_ready, 1);
+    tc5::mbar_init(&sm.fin, 1);
     tc5::mbar_fence_init();
     sm.err = 0;
   }
@@ -530,28 +535,70 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
         tc5::mbar_wait(&sm.full[j % NST], (j / NST) & 1u, kIters);
     }
   } else if (warp == NCW + 1) {
-    // ---- MMA warp: per step, the score MMAs of chain li + 1, then the P@V MMAs of chain li
-    if (lane == 0) {
-      constexpr uint32_t kIdS = tc5::idesc_bf16(128, 16, false, false);
-      constexpr uint32_t kIdO = tc5::idesc_bf16(128, 16, true, false);
-      uint32_t it = 0;
-      auto stage_wait = [&]() -> int {
-        const int s = (int)(it % NST);
-        if (!tc5::mbar_wait(&sm.full[s], (it / NST) & 1u, kIters)) sm.err = 1;
+    // ---- MMA warp: per step, the R piece and the score MMAs of chain li + 1, then the P@V MMAs of
+    // chain li. The whole warp copies the R piece's operands out as soon as it lands, so that its
+    // stage turns over without waiting for the consumers; lane 0 issues the MMAs and commits.
+    constexpr uint32_t kIdS = tc5::idesc_bf16(128, 16, false, false);
+    constexpr uint32_t kIdO = tc5::idesc_bf16(128, 16, true, false);
+    uint32_t it = 0;
+    auto stage_wait = [&]() -> int {
+      const int s = (int)(it % NST);
+      wait_or_flag(&sm.full[s], (it / NST) & 1u);
+      tc5::fence_after_sync();
+      return s;
+    };
+    for (int li = -1; li < n_local; ++li) {
+      if (li + 1 < n_local) {
+        const int cn = li + 1, bn = cn & 1, qi = cn % 3;
+        const int c = (int)blockIdx.x + cn * (int)gridDim.x;
+        const int sr = stage_wait();
+        ++it;
+        // buffers of chain cn: qbuf and bias were last read by chain cn - 2's scores and softmax
+        // (complete: this warp has seen chain li - 1's probabilities); svt by its P@V, which may
+        // still run; qd and qn are three-deep (chain cn - 3's read-out and epilogue are done)
+        if (li >= 1 && has_sinks) wait_or_flag(&sm.bar_o, (uint32_t)(li - 1) & 1u);
         tc5::fence_after_sync();
-        return s;
-      };
-      for (int li = -1; li < n_local; ++li) {
-        if (li + 1 < n_local) {
-          // S^T = K . Q^T per segment; the sinks' keys and Q come with the R piece
-          const int bn = (li + 1) & 1;
-          const int sr = stage_wait();
-          ++it;
+        const unsigned char* buf = sm.ring[sr];
+        for (int j = lane; j < 4096 / 16; j += 32) {
+          reinterpret_cast<uint4*>(sm.qbuf[bn])[j] = reinterpret_cast<const uint4*>(buf + kRQ)[j];
+          if (has_sinks) reinterpret_cast<uint4*>(sm.svt[bn])[j] = reinterpret_cast<const uint4*>(buf + kRSV)[j];
+        }
+        if (has_bank) {
+          const float kappa = __ldg(a.kappa + c % a.hkv);
+          const float* mass = reinterpret_cast<const float*>(buf + kRMass);
+          for (int j = lane; j < S; j += 32)
+            sm.bias[bn][j] = buf[kRAct + j] ? __fmul_rn(kappa, logf(fmaxf(mass[j], 1.0f))) : neg_inf();
+          // q_raw transposed to qd[d][row] (rows past NR zero): lane takes d = 4 lane .. 4 lane + 3
+          const uint32_t* qr = reinterpret_cast<const uint32_t*>(buf + kRQRaw);
+          uint2 w[NRM];
+#pragma unroll
+          for (int r = 0; r < NRM; ++r) w[r] = r < NR ? make_uint2(qr[r * (HD / 2) + 2 * lane], qr[r * (HD / 2) + 2 * lane + 1])
+                                                      : make_uint2(0u, 0u);
+          uint2* qo = reinterpret_cast<uint2*>(&sm.qd[qi][4 * lane][0]);
+          qo[0] = make_uint2(__byte_perm(w[0].x, w[1].x, 0x5410), __byte_perm(w[2].x, w[3].x, 0x5410));
+          qo[1] = make_uint2(__byte_perm(w[0].x, w[1].x, 0x7632), __byte_perm(w[2].x, w[3].x, 0x7632));
+          qo[2] = make_uint2(__byte_perm(w[0].y, w[1].y, 0x5410), __byte_perm(w[2].y, w[3].y, 0x5410));
+          qo[3] = make_uint2(__byte_perm(w[0].y, w[1].y, 0x7632), __byte_perm(w[2].y, w[3].y, 0x7632));
+          if (a.q_l2 == nullptr) {
+            // |q_raw| per row: lane sums d = lane, lane + 32, ... in order, then the warp
+            const bf16* qb = reinterpret_cast<const bf16*>(buf + kRQRaw);
+            for (int r = 0; r < NR; ++r) {
+              float s2 = 0.f;
+              for (int d = lane; d < HD; d += 32) {
+                const float q = __bfloat162float(qb[r * HD + d]);
+                s2 = fmaf(q, q, s2);
+              }
+              s2 = warp_sum(s2);
+              if (lane == 0) sm.qn[qi][r] = sqrtf(s2);
+            }
+          }
+        }
+        // the copies are read by the tensor cores (Q, sink values) and by the consumers
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
           tc5::mbar_arrive(&sm.r_ready[bn]);
-          // the consumers copy Q (and the sink values) out of the R piece; after that, the sink keys
-          // are its last reader and the stage turns over
-          if (!tc5::mbar_wait(&sm.r_done[bn], (uint32_t)((li + 1) >> 1) & 1u, kIters)) sm.err = 1;
-          tc5::fence_after_sync();
+          // S^T = K . Q^T per segment; the sinks' keys are read from the R piece itself
           const uint32_t ra = tc5::smem_u32(sm.ring[sr]);
           const uint32_t qa = tc5::smem_u32(sm.qbuf[bn]);
           if (has_sinks) {
@@ -561,10 +608,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
                           tc5::sdesc(qa + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024), kIdS, ks > 0);
           }
           tc5::commit(&sm.empty[sr]);
-          // S^T = K . Q^T of the ring segments
-          for (int i = 0; i < n_kv; ++i) {
-            const int s = stage_wait();
-            ++it;
+        }
+        // S^T = K . Q^T of the ring segments
+        const uint32_t qa = tc5::smem_u32(sm.qbuf[bn]);
+        for (int i = 0; i < n_kv; ++i) {
+          const int s = stage_wait();
+          ++it;
+          if (lane == 0) {
             const uint32_t ka = tc5::smem_u32(sm.ring[s]);
             const uint32_t dcol = tb + 64 * bn + 16 * kv_list[i];
 #pragma unroll
@@ -573,37 +623,46 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
                           tc5::sdesc(qa + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024), kIdS, ks > 0);
             tc5::commit(&sm.empty[s]);
           }
-          tc5::commit(&sm.bar_s[bn]);
         }
-        if (li >= 0) {
-          // O^T = V^T . P^T once the consumers have written chain li's probabilities
-          const int bi = li & 1;
-          if (!tc5::mbar_wait(&sm.p_ready, (uint32_t)li & 1u, kIters)) sm.err = 1;
-          tc5::fence_after_sync();
-          bool first = true;
-          if (has_sinks) {  // one 16-key step: sink rows 4..15 of the tile are zero, their P columns too
-            tc5::mma_ss(tb + kColO, tc5::sdesc(tc5::smem_u32(sm.svt[bi]), 2048, 1024),
-                        tc5::sdesc(tc5::smem_u32(sm.ptile[0][0]), 16, 1024), kIdO, false);
-            first = false;
-          }
-          for (int i = 0; i < n_kv; ++i) {
-            const int s = stage_wait();
-            ++it;
+        if (lane == 0) tc5::commit(&sm.bar_s[bn]);
+        __syncwarp();
+      }
+      if (li >= 0) {
+        // O^T = V^T . P^T once the consumers have written chain li's probabilities
+        const int bi = li & 1;
+        wait_or_flag(&sm.p_ready, (uint32_t)li & 1u);
+        tc5::fence_after_sync();
+        bool first = true;
+        if (has_sinks && lane == 0) {  // one 16-key step: sink rows 4..15 of the tile are zero, their P columns too
+          tc5::mma_ss(tb + kColO, tc5::sdesc(tc5::smem_u32(sm.svt[bi]), 2048, 1024),
+                      tc5::sdesc(tc5::smem_u32(sm.ptile[0][0]), 16, 1024), kIdO, false);
+        }
+        if (has_sinks) first = false;
+        for (int i = 0; i < n_kv; ++i) {
+          const int s = stage_wait();
+          ++it;
+          const int sg = kv_list[i];
+          const int nks = (len[sg] + 15) / 16;
+          if (lane == 0) {
             const uint32_t va = tc5::smem_u32(sm.ring[s]);
-            const int sg = kv_list[i];
             const uint32_t pa = tc5::smem_u32(sm.ptile[sg][0]);
-            const int nks = (len[sg] + 15) / 16;
-            for (int ks = 0; ks < nks; ++ks) {
+            for (int ks = 0; ks < nks; ++ks)
               tc5::mma_ss(tb + kColO, tc5::sdesc(va + ks * 2048, 16384, 1024),
-                          tc5::sdesc(pa + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024), kIdO, !first);
-              first = false;
-            }
+                          tc5::sdesc(pa + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024), kIdO, !first || ks > 0);
             tc5::commit(&sm.empty[s]);
           }
-          tc5::commit(&sm.bar_o);
+          if (nks > 0) first = false;
         }
+        if (lane == 0) tc5::commit(&sm.bar_o);
+        __syncwarp();
       }
     }
+    // every product issued has completed before the tensor memory is released (also after an error)
+    if (lane == 0) {
+      tc5::commit(&sm.fin);
+      tc5::mbar_wait(&sm.fin, 0, kIters);
+    }
+    __syncwarp();
   } else {
     // ---- consumers (threads 0..255)
     const int t = tid;
@@ -611,54 +670,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
     const int rg = warp >> 2;               // query rows 2 rg, 2 rg + 1 in the softmax and the epilogue
     const int kq = 32 * (warp & 3) + lane;  // this thread's TMEM lane: a key of a segment, or a column e
-    // ring position: the consumers count every piece but wait only for the ones the MMA warp hands
-    // over (and then for the stage's own barrier, whose phase is by then the current one)
-    uint32_t it = 0;
-    auto handed = [&](uint64_t* ready, uint32_t parity) -> int {
-      const int s = (int)(it % NST);
-      if (!tc5::mbar_wait(ready, parity, kIters)) sm.err = 1;
-      if (!tc5::mbar_wait(&sm.full[s], (it / NST) & 1u, kIters)) sm.err = 1;
-      return s;
-    };
-    // R piece of local chain li (its buffers li & 1); the K pieces after it go to the MMA warp
-    auto front = [&](int li) {
-      const int c = (int)blockIdx.x + li * (int)gridDim.x;
-      const int bi = li & 1;
-      const int kvh = c % a.hkv;
-      const int sr = handed(&sm.r_ready[bi], (uint32_t)(li >> 1) & 1u);
-      const unsigned char* buf = sm.ring[sr];
-      const uint32_t* rs = reinterpret_cast<const uint32_t*>(buf + kRQRaw);
-      for (int idx = t; idx < NRM * HD / 2; idx += NCT) {
-        const int r = idx / (HD / 2), d2 = idx % (HD / 2);
-        const float2 g = r < NR ? unpack_bf16(rs[r * (HD / 2) + d2]) : make_float2(0.f, 0.f);
-        sm.qd[bi][2 * d2][r] = g.x;
-        sm.qd[bi][2 * d2 + 1][r] = g.y;
-      }
-      if (has_bank) {
-        const float kappa = __ldg(a.kappa + kvh);
-        const float* mass = reinterpret_cast<const float*>(buf + kRMass);
-        for (int j = t; j < S; j += NCT)
-          sm.bias[bi][j] = buf[kRAct + j] ? __fmul_rn(kappa, logf(fmaxf(mass[j], 1.0f))) : neg_inf();
-      }
-      // the Q tile and the sink values' tile outlive the stage: one 16-byte chunk of each per thread
-      reinterpret_cast<uint4*>(sm.qbuf[bi])[t] = reinterpret_cast<const uint4*>(buf + kRQ)[t];
-      if (has_sinks) reinterpret_cast<uint4*>(sm.svt[bi])[t] = reinterpret_cast<const uint4*>(buf + kRSV)[t];
-      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-      cons_sync();
-      if (t == 0) tc5::mbar_arrive(&sm.r_done[bi]);
-      ++it;
-      if (has_bank && a.q_l2 == nullptr && warp < NR) {
-        float s2 = 0.f;
-        for (int d = lane; d < HD; d += 32) s2 = fmaf(sm.qd[bi][d][warp], sm.qd[bi][d][warp], s2);
-        s2 = warp_sum(s2);
-        if (lane == 0) sm.qn[bi][warp] = sqrtf(s2);
-      }
-    };
-
-    if (n_local > 0) {
-      front(0);
-      it += n_kv;  // chain 0's keys: the MMA warp's
-    }
     for (int li = 0; li < n_local; ++li) {
       const int c = (int)blockIdx.x + li * (int)gridDim.x;
       const int kvh = c % a.hkv, b = c / a.hkv;
@@ -678,10 +689,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
       const float coef = has_bank ? __ldg(a.coef + kvh) : 0.f;
       const float res_w = has_bank ? __ldg(a.res_w + kq) : 0.f;
 
-      // -- R of the next chain first: the MMA warp can then score its keys during this softmax
-      if (li + 1 < n_local) front(li + 1);
-
       // -- softmax of chain li: thread (key kq of each segment, rows 2 rg, 2 rg + 1)
+      if (!tc5::mbar_wait(&sm.r_ready[bi], (uint32_t)(li >> 1) & 1u, kIters)) sm.err = 1;
       if (!tc5::mbar_wait(&sm.bar_s[bi], (uint32_t)(li >> 1) & 1u, kIters)) sm.err = 1;
       tc5::fence_after_sync();
       uint32_t v[4][4];
@@ -743,8 +752,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
       tc5::fence_before_sync();
       cons_sync();
       if (t == 0) tc5::mbar_arrive(&sm.p_ready);
-      if (li + 1 < n_local) it += n_kv;  // the next chain's keys: the MMA warp's
-      it += n_kv;                        // this chain's values: the MMA warp's
 
       // -- M_res read-out: R[r][e] = sum_d q_raw[r][d] * M[d][e] in fp32; thread (column pair, quarter
       // of the rows d), all four rows, two columns per paired FMA
@@ -753,7 +760,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
       for (int r = 0; r < NRM; ++r) ym2[r] = make_float2(0.f, 0.f);
       const int cpm = t & 63, dq = t >> 6;
       if (has_bank) {
-        // M read from L2 (the producer prefetched it), eight rows of M in flight
+        // M read from L2 (prefetched at the start of the chain), eight rows of M in flight
         const int d0 = dq * (HD / 4);
         const float2* mg = reinterpret_cast<const float2*>(reinterpret_cast<const float*>(a.bank_m) +
                                                            (int64_t)c * a.bank_cap * HD * HD + (int64_t)d0 * HD) + cpm;
@@ -770,7 +777,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
             const float2 m2 = mb[cur][u];
-            const float4 q = *reinterpret_cast<const float4*>(&sm.qd[bi][d0 + blk * 8 + u][0]);
+            const uint2 qq = *reinterpret_cast<const uint2*>(&sm.qd[li % 3][d0 + blk * 8 + u][0]);
+            const float2 q01 = unpack_bf16(qq.x), q23 = unpack_bf16(qq.y);
+            const float4 q = make_float4(q01.x, q01.y, q23.x, q23.y);
             ym2[0] = __ffma2_rn(make_float2(q.x, q.x), m2, ym2[0]);
             ym2[1] = __ffma2_rn(make_float2(q.y, q.y), m2, ym2[1]);
             ym2[2] = __ffma2_rn(make_float2(q.z, q.z), m2, ym2[2]);
@@ -799,7 +808,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int r = 2 * rg + u;
-          const float qn = a.q_l2 != nullptr ? ql2_r[u] : (r < NR ? sm.qn[bi][r] : 1.f);
+          const float qn = a.q_l2 != nullptr ? ql2_r[u] : (r < NR ? sm.qn[li % 3][r] : 1.f);
           const float iq = 1.0f / fmaxf(qn, 1e-12f);
           ym[u] = __fmul_rn(__fmul_rn(ym[u], iq), coef);
           const float ss = warp_sum(__fmul_rn(ym[u], ym[u]));
