@@ -46,6 +46,12 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
   // bf16 cos/sin of the HD/2 frequencies for each of the block's tokens, shared by all their
   // heads, stored as pairs of adjacent frequencies (the operands of the packed RoPE below)
   __shared__ uint32_t s_cos[TB][HD / 4], s_sin[TB][HD / 4];
+  // each token's sequence and position, once per block (64-bit divisions kept out of the item loop)
+  __shared__ int s_b[TB], s_t[TB];
+  for (int i = threadIdx.x; i < ntb; i += blockDim.x) {
+    s_b[i] = (int)((tok0 + i) / a.T);
+    s_t[i] = (int)((tok0 + i) % a.T);
+  }
   for (int i = threadIdx.x; i < ntb * (HD / 4); i += blockDim.x) {
     const int tl = i / (HD / 4), fp = i % (HD / 4);
     const float pos = (float)(a.pos0 + (tok0 + tl) % a.T);
@@ -61,6 +67,18 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
   const bool want_l2 = do_q && a.q_l2 != nullptr;
   const int n_rows = (do_q ? a.H : 0) + (do_kv ? 2 * a.HKV : 0);
   const int n_items = ntb * n_rows;    // (token, row) pairs; consecutive rows of a token are adjacent
+  // it / n_rows as a multiply and shift: with m = ceil(2^20 / n_rows), floor(it m / 2^20) is exact
+  // for it * (m n_rows - 2^20) < 2^20, which holds for it < n_items (at most 16 tokens x a few
+  // hundred rows; the launcher checks the bound)
+  const uint32_t div_m = ((1u << 20) + (uint32_t)n_rows - 1) / (uint32_t)n_rows;
+  auto token_of = [&](int it) { return (int)(((uint32_t)it * div_m) >> 20); };
+  // this lane's eight RMSNorm weights of q and k rows (constant over the items)
+  float wq[8], wk[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    wq[e] = a.q_norm_w != nullptr ? a.q_norm_w[l * 8 + e] : 0.f;
+    wk[e] = a.k_norm_w != nullptr ? a.k_norm_w[l * 8 + e] : 0.f;
+  }
   auto row_col = [&](int r, int& kind, int& head) -> int64_t {
     if (do_q && r < a.H) { kind = 0; head = r; return a.q_col + (int64_t)head * HD; }
     const int rk = r - (do_q ? a.H : 0);
@@ -69,7 +87,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
     return a.v_col + (int64_t)head * HD;
   };
   auto src = [&](int it) -> const uint4* {
-    const int tl = it / n_rows;
+    const int tl = token_of(it);
     int kd, hd_;
     const int64_t col = row_col(it - tl * n_rows, kd, hd_);
     return reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(a.proj) + (tok0 + tl) * a.ld + col + l * 8);
@@ -78,9 +96,8 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
   auto item = [&](int pass) { return warp * RPW + pass * NW * RPW + sub; };
   auto process = [&](int it, const uint4 u) {
     const bool live = it < n_items;
-    const int tl = live ? it / n_rows : 0;
-    const int64_t tok = tok0 + tl;
-    const int b = (int)(tok / a.T), t = (int)(tok % a.T);
+    const int tl = live ? token_of(it) : 0;
+    const int b = s_b[tl], t = s_t[tl];
     int kind = 2, head = 0;  // 0 = q, 1 = k, 2 = v
     if (live) row_col(it - tl * n_rows, kind, head);
     float x[8];
@@ -103,7 +120,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
       for (int o = LPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
       return v;
     };
-    const float* nw = kind == 0 ? a.q_norm_w : a.k_norm_w;
+    const bool has_norm = (kind == 0 ? a.q_norm_w : a.k_norm_w) != nullptr;
     // all lanes take part in the shuffles below, whatever their row's kind
     float ss = 0.f;
 #pragma unroll
@@ -111,12 +128,12 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
     ss = row_sum(ss);
     // the stored row: the loaded bf16 values as they are, or their RMSNorm rounded to bf16
     uint32_t raw[4] = {u.x, u.y, u.z, u.w};
-    if (kind != 2 && nw != nullptr) {
+    if (kind != 2 && has_norm) {
       const float rr = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)HD), a.eps));
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const float2 r2 = rbf2(__fmul_rn(__fmul_rn(x[2 * q], rr), nw[l * 8 + 2 * q]),
-                               __fmul_rn(__fmul_rn(x[2 * q + 1], rr), nw[l * 8 + 2 * q + 1]), raw[q]);
+        const float w0 = kind == 0 ? wq[2 * q] : wk[2 * q], w1 = kind == 0 ? wq[2 * q + 1] : wk[2 * q + 1];
+        const float2 r2 = rbf2(__fmul_rn(__fmul_rn(x[2 * q], rr), w0), __fmul_rn(__fmul_rn(x[2 * q + 1], rr), w1), raw[q]);
         x[2 * q] = r2.x;
         x[2 * q + 1] = r2.y;
       }
@@ -179,7 +196,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
   for (int i = threadIdx.x; i < ntb * n_gates; i += blockDim.x) {
     const int tl = i / n_gates, gi = i % n_gates;
     const int64_t tok = tok0 + tl;
-    const int b = (int)(tok / a.T), t = (int)(tok % a.T);
+    const int b = s_b[tl], t = s_t[tl];
     const bf16* row = reinterpret_cast<const bf16*>(a.proj) + tok * a.ld;
     if (do_kv && gi < a.HKV) {
       const float z = bf2f(row[a.beta_col + gi]);
@@ -221,11 +238,14 @@ extern "C" int bolt3_prep(const bolt3_prep_args* a, void* stream) {
   if (n_tok > 0x7fffffff) return BOLT3_ERR_SHAPE;
   // 16 tokens per block when there are enough tokens to fill the GPU several times over (prefill);
   // one token per block otherwise (decode steps), so that every SM gets work
-  const bool big = n_tok >= 16 * 1024;
+  // (token, row) pairs per block: the kernel's multiply-shift division by the row count is exact
+  // while pairs x (row count - 1) < 2^20 (16-token blocks hold for up to ~250 rows)
+  const int64_t rows = a->H + 2 * a->HKV;
+  const auto fits = [&](int64_t tb) { return tb * rows * (rows - 1) < ((int64_t)1 << 20); };
+  if (!fits(1)) return BOLT3_ERR_SHAPE;
+  const bool big = n_tok >= 16 * 1024 && fits(16);
   const int tb = big ? 16 : 1;
   const unsigned grid = (unsigned)((n_tok + tb - 1) / tb);
-  // (token, row) pairs per block must fit an int
-  if ((int64_t)tb * (a->H + 2 * a->HKV) > 0x7fffffff) return BOLT3_ERR_SHAPE;
   cudaStream_t s = (cudaStream_t)stream;
   if (a->HD == 128) big ? prep_kernel<128, 16><<<grid, 256, 0, s>>>(*a) : prep_kernel<128, 1><<<grid, 256, 0, s>>>(*a);
   else if (a->HD == 64) big ? prep_kernel<64, 16><<<grid, 256, 0, s>>>(*a) : prep_kernel<64, 1><<<grid, 256, 0, s>>>(*a);
