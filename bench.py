@@ -327,6 +327,14 @@ def run_native(args, rank, world, local):
     decode_tp = run_decode_tp(args, rank, world, dev, m, cfg) if (world > 1 and not args.no_decode) else None
     long_ctx = None if args.no_long else run_long(args, rank, world, dev, tf_burst, steps=3, warmup=3)
     torch.cuda.empty_cache()
+    full = None
+    if not args.no_full:
+        # a secondary leg: an error there is reported in the line instead of failing the run
+        try:
+            full = run_full_model(args, rank, world, dev)
+        except Exception as exc:  # noqa: BLE001
+            full = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+            torch.cuda.empty_cache()
     legs = cpu_baseline(args, m, cfg, dev) if (rank == 0 and world == 1 and not args.no_cpu) else {}
     cpu = legs.get("prefill")
     if decode is not None and legs:
@@ -351,6 +359,7 @@ def run_native(args, rank, world, local):
         "decode": decode,
         "decode_tp": decode_tp,
         "long_context": long_ctx,
+        "full_model": full,
         "cpu_baseline": cpu,
     }
     if "parity" in legs:
@@ -405,6 +414,73 @@ def run_decode(args, rank, world, dev, m, cfg, hbm):
             "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
                          "attend_traffic": profile_traffic().get("attend_decode"),
                          "bytes_per_step": nb["total"], "state_only_frac": ach_core / hbm}}
+
+
+FULL_B, FULL_T, FULL_NEW = 64, 2048, 256
+
+
+def run_full_model(args, rank, world, dev):
+    """the whole hybrid model (Qwen3-4B architecture: 36 layers, 27 Bolt-3 and 9 softmax
+    anchors, SwiGLU 9728, vocab 151936, seeded random weights drawn on the GPU), 64 prompts of 2048
+    random token ids (split by prompt over the ranks), prefilled through Bolt3Decoder, then greedy
+    decoding of 256 tokens with the logits read on the device. The prompt prefill and the decode
+    steps are timed separately with CUDA events (max over ranks), after one warm-up round."""
+    from vsa_lm_b200 import Bolt3Decoder
+    from vsa_lm_b200.model import Bolt3LM
+    from vsa_lm_b200.workloads import MODEL_SHAPES, init_model_on_device
+
+    mcfg = dict(MODEL_SHAPES["qwen3_4b_lm"])
+    with torch.device(dev):
+        model = Bolt3LM(**mcfg)
+    init_model_on_device(model, seed=0)
+    model = model.to(torch.bfloat16).eval()
+    dec = Bolt3Decoder(model)
+    B, T, n_new = max(1, FULL_B // world), FULL_T, args.full_new_tokens
+    ids = torch.randint(0, mcfg["vocab_size"], (B, T), generator=torch.Generator(device=dev).manual_seed(100 + rank),
+                        device=dev)
+
+    @torch.no_grad()
+    def greedy(h, states, kv, n):
+        logits = model.lm_head(h[:, -1, :])
+        for i in range(n):
+            nxt = logits.argmax(-1, keepdim=True)
+            h, states, kv = dec.step(nxt, T + i, states, kv)
+            logits = model.lm_head(h[:, -1, :])
+        return logits
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    # warm-up round: plans, workspaces, library heuristics
+    h, states, kv = dec.prefill(ids, max_kv_len=T + n_new + 64)
+    greedy(h, states, kv, 8)
+    del h, states, kv
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1, e2 = ev(), ev(), ev()
+    e0.record()
+    h, states, kv = dec.prefill(ids, max_kv_len=T + n_new + 64)
+    e1.record()
+    greedy(h, states, kv, n_new)
+    e2.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / 1e3, e1.elapsed_time(e2) / 1e3], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t_pre, t_dec = float(t[0]), float(t[1])
+    n_vsa = sum(1 for lt in model.config["layer_types"] if lt == "vsa")
+    del model, dec, h, states, kv
+    torch.cuda.empty_cache()
+    return {"workload": f"configs[3]: hybrid LM with the Qwen3-4B architecture ({mcfg['num_layers']} layers, {n_vsa} "
+                        f"Bolt-3, hybrid_every {mcfg['hybrid_every']}, SwiGLU {mcfg['intermediate']}, vocab "
+                        f"{mcfg['vocab_size']}), seeded random weights, {B * world} prompts of {T} random token ids, "
+                        f"then {n_new} greedy tokens",
+            "parallelism": f"dp{world} (prompts split over the GPUs; KV-head tensor parallelism of the full model, "
+                           f"with the MLP sharded, is not built)",
+            "prefill": {"value": world * B * T / t_pre, "unit": "tok/s", "ms": t_pre * 1e3},
+            "decode": {"value": world * B * n_new / t_dec, "unit": "tok/s", "ms_per_step": t_dec / n_new * 1e3,
+                       "steps": n_new, "sequences": B * world}}
 
 
 def run_decode_tp(args, rank, world, dev, m, cfg):
@@ -684,6 +760,9 @@ def main():
     ap.add_argument("--long", action="store_true", help="only the configs[4] long-context prefill")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the GPU results")
     ap.add_argument("--no-long", action="store_true", help="skip the configs[4] leg of the default line")
+    ap.add_argument("--full-model", action="store_true", help="only the configs[3] whole-model leg")
+    ap.add_argument("--no-full", action="store_true", help="skip the configs[3] leg of the default line")
+    ap.add_argument("--full-new-tokens", type=int, default=FULL_NEW, help="greedy tokens of the configs[3] leg")
     ap.add_argument("--parity-decode-steps", type=int, default=DEC_STEPS,
                     help="one-token steps of the configs[2] parity sample")
     args = ap.parse_args()
@@ -707,6 +786,10 @@ def main():
             dev = torch.device("cuda", local)
             torch.cuda.set_device(dev)
             res = {"long_context": run_long(args, rank, world, dev, peaks()[1])}
+        elif args.full_model:
+            dev = torch.device("cuda", local)
+            torch.cuda.set_device(dev)
+            res = {"full_model": run_full_model(args, rank, world, dev)}
         elif args.decode_only:
             dev = torch.device("cuda", local)
             torch.cuda.set_device(dev)

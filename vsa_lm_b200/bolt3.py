@@ -12,6 +12,7 @@ M_res are fp32. Results are compared with the fp32 CPU oracle restating the refe
 """
 from __future__ import annotations
 
+import contextlib
 import math
 
 import types
@@ -19,6 +20,7 @@ import types
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
+from torch.nn.attention import SDPBackend, sdpa_kernel
 
 from . import kernels as K
 
@@ -815,8 +817,12 @@ class Bolt3Decoder:
         mask = None
         if t > 1:   # query i sees every cached key and the new keys up to itself
             mask = torch.ones(t, n_before + t, dtype=torch.bool, device=h.device).tril(diagonal=n_before)
-        y = F.scaled_dot_product_attention(q, keys.to(q.dtype), vals.to(q.dtype), attn_mask=mask,
-                                           enable_gqa=ly.G > 1)
+        # one-token steps avoid the cuDNN backend: it builds a new plan for every cache length,
+        # milliseconds of host time per call when the cache grows by a token each step (prompt chunks,
+        # with their mask, keep the default choice)
+        with sdpa_kernel(_ANCHOR_SDPA) if t == 1 else contextlib.nullcontext():
+            y = F.scaled_dot_product_attention(q, keys.to(q.dtype), vals.to(q.dtype), attn_mask=mask,
+                                               enable_gqa=ly.G > 1)
         return ly.o_proj(y.transpose(1, 2).reshape(b, t, ly.H * ly.HD))
 
     @torch.no_grad()
@@ -1002,6 +1008,9 @@ class AnchorKV:
         self.n += L
         return self.buf[0, :, :, :self.n], self.buf[1, :, :, :self.n]
 
+
+# scaled-dot-product-attention backends of the softmax anchors' decode steps
+_ANCHOR_SDPA = [SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]
 
 # the reference's name for the anchor-layer cache class (vsa_lm/decode.py:88)
 StaticKV = AnchorKV

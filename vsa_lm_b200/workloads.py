@@ -111,6 +111,10 @@ MODEL_SHAPES = {
     "tiny_lm": dict(vocab_size=512, dim=256, num_layers=3, num_heads=4, num_kv_heads=2, head_dim=64,
                     intermediate=512, hybrid_every=3, rope_theta=1e4, eps=1e-5, qk_norm=False,
                     tie_word_embeddings=False),
+    # the Qwen3-4B architecture as a hybrid (27 Bolt-3 layers, 9 softmax anchors)
+    "qwen3_4b_lm": dict(vocab_size=151936, dim=2560, num_layers=36, num_heads=32, num_kv_heads=8, head_dim=128,
+                        intermediate=9728, hybrid_every=4, rope_theta=1e6, eps=1e-6, qk_norm=True,
+                        tie_word_embeddings=True, max_T=4096),
 }
 
 
@@ -160,3 +164,37 @@ def make_model_params(mcfg: dict, seed: int = 0) -> dict:
     p["norm.weight"] = norm(D)
     p["lm_head.weight"] = p["embed_tokens.weight"] if mcfg.get("tie_word_embeddings", True) else lin(V, D)
     return p
+
+
+@torch.no_grad()
+def init_model_on_device(model: torch.nn.Module, seed: int = 0) -> None:
+    """Seeded random weights for a whole hybrid model, drawn on the model's device (a model of
+    billions of parameters would take minutes to build through make_model_params on the CPU). The
+    laws are make_model_params's: linear weights uniform in +-1/sqrt(fan_in), the embedding N(0, 1),
+    norms 1 + 0.05 N(0, 1), and the Bolt-3 layers' own parameters as in make_params (kappa, log_gamma,
+    the beta / eta gates, res_norm)."""
+    dev = next(model.parameters()).device
+    g = torch.Generator(device=dev).manual_seed(seed)
+    for name, p in model.named_parameters():
+        leaf = name.rsplit(".", 1)[-1] if "." in name else name
+        mod = name.rsplit(".", 2)[-2] if name.count(".") >= 1 else ""
+        if name == "embed_tokens.weight":
+            p.normal_(0.0, 1.0, generator=g)
+        elif leaf == "kappa":
+            p.normal_(0.0, 0.1, generator=g).add_(1.0)
+        elif leaf == "log_gamma":
+            p.normal_(0.0, 0.5, generator=g).add_(3.5)
+        elif mod in ("beta_proj", "eta_proj"):
+            if leaf == "weight":
+                p.normal_(0.0, 0.02, generator=g)
+            else:
+                p.fill_(-1.0 if mod == "beta_proj" else 0.0)
+        elif mod == "res_norm":
+            p.fill_(0.05)
+        elif p.dim() == 1:   # norm weights
+            p.normal_(0.0, 0.05, generator=g).add_(1.0)
+        elif p.dim() == 2:   # linear weights [out, in]
+            bound = 1.0 / math.sqrt(p.shape[1])
+            p.uniform_(-bound, bound, generator=g)
+        else:
+            raise ValueError(f"no initialisation law for {name} {tuple(p.shape)}")
