@@ -92,7 +92,9 @@ struct __align__(64) AttendMaps {
   CUtensorMap q_rope, q_raw, k0, v0, k1, v1;
 };
 
-template <int HD>
+// PREFILL selects the prefill geometry and the TMA loads at compile time (a.prefill must agree), so
+// that each instantiation carries only its own path's code
+template <int HD, bool PREFILL>
 __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_args a,
                                                           const __grid_constant__ AttendMaps tm) {
   extern __shared__ unsigned char smem_raw[];
@@ -111,14 +113,14 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
 
   // ---- geometry
   const int ntok = (int)min((int64_t)128, a.Tq - (int64_t)blk * 128);
-  const int gn = a.prefill ? 1 : max(1, min(G, 128 / ntok));
+  const int gn = PREFILL ? 1 : max(1, min(G, 128 / ntok));
   const int g0 = g_fast * gn;
   const int n_rows = min(gn, G - g0) * ntok;
   int L0, L1, len_before;
   const bf16 *k0, *v0, *k1, *v1, *sk = nullptr, *sv = nullptr;
   bool has_sinks, has_bank;
   int64_t bank_idx = 0;
-  if (a.prefill) {
+  if constexpr (PREFILL) {
     const int64_t base = (int64_t)c * a.seg0_chain_tokens;
     L0 = blk >= 1 ? CC : 0;
     L1 = ntok;
@@ -165,7 +167,7 @@ __global__ void __launch_bounds__(NT, 1) attend_tc_kernel(const bolt3_attend_arg
   };
 
   // ---- stage 1: Q (q_rope), K tiles, sinks, attractor bias
-  const bool use_tma = a.prefill != 0;
+  constexpr bool use_tma = PREFILL;
   constexpr uint32_t kTileBytes = 128 * HD * 2;
   if (tid == 0) {
     tc5::mbar_init(&sm.bar_s, 1);
@@ -696,14 +698,16 @@ extern "C" int bolt3_attend(const bolt3_attend_args* a, void* stream) {
   constexpr size_t kMinSmem = 120 * 1024;
   if (a->HD == 128) {
     const size_t smem = std::max(sizeof(Smem<128>) + 1024, kMinSmem);
-    if (cudaFuncSetAttribute(attend_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    auto kern = a->prefill ? attend_tc_kernel<128, true> : attend_tc_kernel<128, false>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return BOLT3_ERR_CUDA;
-    attend_tc_kernel<128><<<grid, NT, smem, s>>>(*a, maps);
+    kern<<<grid, NT, smem, s>>>(*a, maps);
   } else if (a->HD == 64) {
     const size_t smem = std::max(sizeof(Smem<64>) + 1024, kMinSmem);
-    if (cudaFuncSetAttribute(attend_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    auto kern = a->prefill ? attend_tc_kernel<64, true> : attend_tc_kernel<64, false>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return BOLT3_ERR_CUDA;
-    attend_tc_kernel<64><<<grid, NT, smem, s>>>(*a, maps);
+    kern<<<grid, NT, smem, s>>>(*a, maps);
   } else {
     return BOLT3_ERR_SHAPE;
   }
