@@ -66,7 +66,12 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
   const bool do_q = a.parts & 1, do_kv = (a.parts & 2) != 0;
   const bool want_l2 = do_q && a.q_l2 != nullptr;
   const int n_rows = (do_q ? a.H : 0) + (do_kv ? 2 * a.HKV : 0);
-  const int n_items = ntb * n_rows;    // (token, row) pairs; consecutive rows of a token are adjacent
+  // one-token blocks (decode steps) split the token's rows over blockIdx.y, one warp pass each, so
+  // that a block's work is one dependent pass; multi-token blocks take every row of their tokens
+  constexpr int kRowGroup = NW * RPW;
+  const int row_base = TB == 1 ? (int)blockIdx.y * kRowGroup : 0;
+  const int n_items = TB == 1 ? min(kRowGroup, n_rows - row_base)
+                              : ntb * n_rows;  // (token, row) pairs; consecutive rows of a token are adjacent
   // it / n_rows as a multiply and shift: with m = ceil(2^20 / n_rows), floor(it m / 2^20) is exact
   // for it * (m n_rows - 2^20) < 2^20, which holds for it < n_items (at most 16 tokens x a few
   // hundred rows; the launcher checks the bound)
@@ -89,7 +94,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
   auto src = [&](int it) -> const uint4* {
     const int tl = token_of(it);
     int kd, hd_;
-    const int64_t col = row_col(it - tl * n_rows, kd, hd_);
+    const int64_t col = row_col(row_base + it - tl * n_rows, kd, hd_);
     return reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(a.proj) + (tok0 + tl) * a.ld + col + l * 8);
   };
   // the row item a lane handles in warp pass `pass`
@@ -99,7 +104,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
     const int tl = live ? token_of(it) : 0;
     const int b = s_b[tl], t = s_t[tl];
     int kind = 2, head = 0;  // 0 = q, 1 = k, 2 = v
-    if (live) row_col(it - tl * n_rows, kind, head);
+    if (live) row_col(row_base + it - tl * n_rows, kind, head);
     float x[8];
     {
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
@@ -192,7 +197,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
   }
 
   // gates: HKV beta logits and H eta logits per token
-  const int n_gates = (do_kv ? a.HKV : 0) + (do_q ? a.H : 0);
+  const int n_gates = blockIdx.y == 0 ? (do_kv ? a.HKV : 0) + (do_q ? a.H : 0) : 0;  // the first row group's
   for (int i = threadIdx.x; i < ntb * n_gates; i += blockDim.x) {
     const int tl = i / n_gates, gi = i % n_gates;
     const int64_t tok = tok0 + tl;
@@ -245,7 +250,9 @@ extern "C" int bolt3_prep(const bolt3_prep_args* a, void* stream) {
   if (!fits(1)) return BOLT3_ERR_SHAPE;
   const bool big = n_tok >= 16 * 1024 && fits(16);
   const int tb = big ? 16 : 1;
-  const unsigned grid = (unsigned)((n_tok + tb - 1) / tb);
+  // one-token blocks: the rows in groups of a warp pass (16 rows at HD = 128, 32 at 64)
+  const int row_group = 8 * (32 / (a->HD / 8));
+  const dim3 grid((unsigned)((n_tok + tb - 1) / tb), big ? 1u : (unsigned)((rows + row_group - 1) / row_group));
   cudaStream_t s = (cudaStream_t)stream;
   if (a->HD == 128) big ? prep_kernel<128, 16><<<grid, 256, 0, s>>>(*a) : prep_kernel<128, 1><<<grid, 256, 0, s>>>(*a);
   else if (a->HD == 64) big ? prep_kernel<64, 16><<<grid, 256, 0, s>>>(*a) : prep_kernel<64, 1><<<grid, 256, 0, s>>>(*a);
