@@ -288,6 +288,12 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
     }
   };
 
+  // fp32 M_res staged in x1..x2 (64 KB at HD = 128, 16 KB at 64: x1 and x2 are consecutive): row r,
+  // 16-byte chunk ch at chunk ch ^ (r & 7), so that a warp's 32 rows read or write one chunk each
+  // without bank conflicts
+  float* const m_stage = reinterpret_cast<float*>(sm.x1);
+  auto m_swz = [](int r, int ch) { return r * HD + ((ch ^ (r & 7)) << 2); };
+
   // ---- load or initialise the bank (bolt3.py:83-92); M_res into tensor memory rows d
   int n_filled;
   if (a.init_blank) {
@@ -303,6 +309,12 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
     n_filled = a.n_filled[c];
     g2s_rows<HD>(sm.ak, g_ak, S);
     g2s_rows<HD>(sm.av, g_av, S);
+    // M_res through shared memory (x1, x2 are free until the chunk arrives): coalesced copies in,
+    // then each thread takes its row (below)
+    for (int i = tid; i < HD * HD / 4; i += NT) {
+      const int r = i / (HD / 4), ch = i % (HD / 4);
+      cp_async16(m_stage + m_swz(r, ch), g_m + (int64_t)r * HD + ch * 4, true);
+    }
     cp_async_commit();
     for (int s2 = tid; s2 < S; s2 += NT) {
       sm.mass[s2] = a.mass[(int64_t)c * S + s2];
@@ -312,12 +324,19 @@ __global__ void __launch_bounds__(NT, 1) consolidate_kernel(bolt3_consolidate_ar
     }
     cp_async_wait<0>();
   }
+  __syncthreads();
 #pragma unroll
   for (int q = 0; q < HH / 32; ++q) {
     uint32_t v[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      v[j] = (a.init_blank || row >= HD) ? 0u : __float_as_uint(g_m[(int64_t)row * HD + half * HH + q * 32 + j]);
+    for (int c4 = 0; c4 < 8; ++c4) {
+      float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (!a.init_blank && row < HD) f = *reinterpret_cast<const float4*>(m_stage + m_swz(row, (half * HH + q * 32) / 4 + c4));
+      v[4 * c4] = __float_as_uint(f.x);
+      v[4 * c4 + 1] = __float_as_uint(f.y);
+      v[4 * c4 + 2] = __float_as_uint(f.z);
+      v[4 * c4 + 3] = __float_as_uint(f.w);
+    }
     tst(TM_M + half * HH + q * 32, v);
   }
   tc5::st_wait();
