@@ -471,6 +471,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
   __syncthreads();
   tc5::fence_after_sync();
   const uint32_t tb = sm.tbase;
+  // launched overlapped with the step's prep kernel: the set-up above touched only this CTA's own
+  // shared and tensor memory; q, q_raw, the gates and the new window rows are read from here on
+  b3::grid_dep_wait();
 
   if (warp == NCW) {
     // ---- producer: per step li = -1 .. n_local - 1, R and K of chain li + 1, then V of chain li
@@ -879,8 +882,10 @@ int launch(const bolt3_attend_args* a, cudaStream_t s) {
     attr_set[dev].store(true, std::memory_order_release);
   }
   const int grid = (int)std::min<int64_t>(nc, (int64_t)sms * kCtasPerSm);
-  attend_stream_kernel<<<grid, kThreads, smem, s>>>(*a, m);
-  return cudaGetLastError() == cudaSuccess ? BOLT3_OK : BOLT3_ERR_CUDA;
+  // overlapped with the kernel before it (the step's prep): the CTAs allocate tensor memory and
+  // initialise their barriers while prep finishes
+  const cudaError_t e = b3::launch_overlapped(attend_stream_kernel, dim3(grid), dim3(kThreads), smem, s, *a, m);
+  return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? BOLT3_OK : BOLT3_ERR_CUDA;
 }
 
 }  // namespace stream

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 typedef __nv_bfloat16 bf16;
 
 #define B3_DEV __device__ __forceinline__
@@ -98,6 +100,33 @@ B3_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N))
 B3_DEV uint32_t fkey(float f) {
   uint32_t u = __float_as_uint(f);
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// ---- programmatic dependent launch. A kernel launched with programmatic stream serialisation
+// may start while the kernel before it on the stream is still running; it must call
+// grid_dep_wait() before it reads anything that kernel writes (or writes anything it reads).
+// grid_dep_wait() returns once every earlier grid of the stream has completed and its writes are
+// visible; in a kernel launched without the attribute it returns at once. grid_dep_launch() lets
+// the next such kernel begin launching once every block of this grid has called it or exited.
+B3_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+B3_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
+// <<<grid, block, smem, s>>> with programmatic stream serialisation: the kernel's blocks may be
+// scheduled before the previous kernel on `s` has finished (it calls grid_dep_wait() first)
+template <typename... P, typename... A>
+inline cudaError_t launch_overlapped(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                     A&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<A>(args)...);
 }
 
 }  // namespace b3

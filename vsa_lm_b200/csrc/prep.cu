@@ -42,6 +42,9 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane / LPR, l = lane % LPR;   // row slot within the warp, lane within the row
   const bool first = l < HALF;         // holds elements of the first half
+  // the attention kernel that follows a decode step's prep may start its set-up now (it waits for
+  // this grid's completion before it reads any of its outputs)
+  grid_dep_launch();
 
   // bf16 cos/sin of the HD/2 frequencies for each of the block's tokens, shared by all their
   // heads, stored as pairs of adjacent frequencies (the operands of the packed RoPE below)
@@ -183,6 +186,9 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
   constexpr int kPre = 4;
   auto fetch = [&](int it) { return it < n_items ? *src(it) : make_uint4(0, 0, 0, 0); };
   uint4 buf[kPre];
+  // launched overlapped with the projection GEMM (decode steps): everything above reads only the
+  // layer's constants; the projection is read from here on
+  grid_dep_wait();
 #pragma unroll
   for (int p = 0; p < kPre; ++p) buf[p] = fetch(item(p));
   __syncthreads();  // trig table
@@ -254,8 +260,17 @@ extern "C" int bolt3_prep(const bolt3_prep_args* a, void* stream) {
   const int row_group = 8 * (32 / (a->HD / 8));
   const dim3 grid((unsigned)((n_tok + tb - 1) / tb), big ? 1u : (unsigned)((rows + row_group - 1) / row_group));
   cudaStream_t s = (cudaStream_t)stream;
-  if (a->HD == 128) big ? prep_kernel<128, 16><<<grid, 256, 0, s>>>(*a) : prep_kernel<128, 1><<<grid, 256, 0, s>>>(*a);
-  else if (a->HD == 64) big ? prep_kernel<64, 16><<<grid, 256, 0, s>>>(*a) : prep_kernel<64, 1><<<grid, 256, 0, s>>>(*a);
-  else return BOLT3_ERR_SHAPE;
-  return cudaGetLastError() == cudaSuccess ? BOLT3_OK : BOLT3_ERR_CUDA;
+  // one-token blocks (decode steps, a few microseconds of work): launched overlapped with the
+  // projection GEMM before them, so that their blocks are scheduled as the GEMM's leave
+  cudaError_t e = cudaSuccess;
+  if (a->HD == 128) {
+    if (big) prep_kernel<128, 16><<<grid, 256, 0, s>>>(*a);
+    else e = launch_overlapped(prep_kernel<128, 1>, grid, dim3(256), 0, s, *a);
+  } else if (a->HD == 64) {
+    if (big) prep_kernel<64, 16><<<grid, 256, 0, s>>>(*a);
+    else e = launch_overlapped(prep_kernel<64, 1>, grid, dim3(256), 0, s, *a);
+  } else {
+    return BOLT3_ERR_SHAPE;
+  }
+  return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? BOLT3_OK : BOLT3_ERR_CUDA;
 }
