@@ -422,21 +422,29 @@ FULL_B, FULL_T, FULL_NEW = 64, 2048, 256
 def run_full_model(args, rank, world, dev):
     """the whole hybrid model (Qwen3-4B architecture: 36 layers, 27 Bolt-3 and 9 softmax
     anchors, SwiGLU 9728, vocab 151936, seeded random weights drawn on the GPU), 64 prompts of 2048
-    random token ids (split by prompt over the ranks), prefilled through Bolt3Decoder, then greedy
-    decoding of 256 tokens with the logits read on the device. The prompt prefill and the decode
-    steps are timed separately with CUDA events (max over ranks), after one warm-up round."""
+    random token ids prefilled through the decoder, then greedy decoding of 256 tokens with the
+    logits read on the device. Under torchrun the model is split over the N ranks (Bolt3LMTP:
+    attention by KV head, the MLP by feature, an NCCL all-reduce of fp32 partials after each) and
+    every rank steps all 64 sequences. The prompt prefill and the decode steps are timed separately
+    with CUDA events (max over ranks), after one warm-up round."""
     from vsa_lm_b200 import Bolt3Decoder
     from vsa_lm_b200.model import Bolt3LM
+    from vsa_lm_b200.tp import Bolt3DecoderTP, Bolt3LMTP
     from vsa_lm_b200.workloads import MODEL_SHAPES, init_model_on_device
 
     mcfg = dict(MODEL_SHAPES["qwen3_4b_lm"])
     with torch.device(dev):
         model = Bolt3LM(**mcfg)
-    init_model_on_device(model, seed=0)
+    init_model_on_device(model, seed=0)     # the same weights on every rank
     model = model.to(torch.bfloat16).eval()
-    dec = Bolt3Decoder(model)
-    B, T, n_new = max(1, FULL_B // world), FULL_T, args.full_new_tokens
-    ids = torch.randint(0, mcfg["vocab_size"], (B, T), generator=torch.Generator(device=dev).manual_seed(100 + rank),
+    if world > 1:
+        model = Bolt3LMTP(model)            # this rank's shards; the unsharded blocks are released
+        torch.cuda.empty_cache()
+        dec = Bolt3DecoderTP(model)
+    else:
+        dec = Bolt3Decoder(model)
+    B, T, n_new = FULL_B, FULL_T, args.full_new_tokens
+    ids = torch.randint(0, mcfg["vocab_size"], (B, T), generator=torch.Generator(device=dev).manual_seed(100),
                         device=dev)
 
     @torch.no_grad()
@@ -474,13 +482,14 @@ def run_full_model(args, rank, world, dev):
     torch.cuda.empty_cache()
     return {"workload": f"configs[3]: hybrid LM with the Qwen3-4B architecture ({mcfg['num_layers']} layers, {n_vsa} "
                         f"Bolt-3, hybrid_every {mcfg['hybrid_every']}, SwiGLU {mcfg['intermediate']}, vocab "
-                        f"{mcfg['vocab_size']}), seeded random weights, {B * world} prompts of {T} random token ids, "
+                        f"{mcfg['vocab_size']}), seeded random weights, {B} prompts of {T} random token ids, "
                         f"then {n_new} greedy tokens",
-            "parallelism": f"dp{world} (prompts split over the GPUs; KV-head tensor parallelism of the full model, "
-                           f"with the MLP sharded, is not built)",
-            "prefill": {"value": world * B * T / t_pre, "unit": "tok/s", "ms": t_pre * 1e3},
-            "decode": {"value": world * B * n_new / t_dec, "unit": "tok/s", "ms_per_step": t_dec / n_new * 1e3,
-                       "steps": n_new, "sequences": B * world}}
+            "parallelism": (f"tp{world}: attention split by KV head, the MLP by intermediate feature, an NCCL "
+                            f"all-reduce of the fp32 partial sums after every attention and every MLP (72 per step)"
+                            if world > 1 else "one GPU"),
+            "prefill": {"value": B * T / t_pre, "unit": "tok/s", "ms": t_pre * 1e3},
+            "decode": {"value": B * n_new / t_dec, "unit": "tok/s", "ms_per_step": t_dec / n_new * 1e3,
+                       "steps": n_new, "sequences": B}}
 
 
 def run_decode_tp(args, rank, world, dev, m, cfg):

@@ -1,6 +1,8 @@
 """KV-head tensor parallelism (vsa_lm_b200/tp.py): the shards' partial outputs sum to the full
-layer's output. CPU: two gloo ranks run the oracle on their shards and all-reduce. GPU: the native
-shards of one layer on one device, for the forward and the decode step."""
+layer's output. CPU: two gloo ranks run the oracle on their shards and all-reduce; two gloo ranks
+split a softmax anchor by KV head and a SwiGLU MLP by feature. GPU: the native shards of one layer
+on one device, for the forward and the decode step; the whole hybrid model split over two ranks
+(gloo, one GPU; NCCL, two GPUs) against the unsharded decoder."""
 import os
 
 import pytest
@@ -11,7 +13,8 @@ import torch.multiprocessing as mp
 from helpers import BF16, bf16_module, oracle_cfg_of, oracle_params, output_close
 from oracle import Store, forward
 from vsa_lm_b200 import Bolt3Attn, Bolt3Decoder, Bolt3LayerState
-from vsa_lm_b200.tp import kv_head_range, shard_by_kv_head
+from vsa_lm_b200.model import LlamaMLP, SoftmaxAttn
+from vsa_lm_b200.tp import anchor_partial, kv_head_range, mlp_partial, shard_by_kv_head, shard_mlp, shard_softmax_attn
 from vsa_lm_b200.workloads import layer_cfg, make_input, make_params
 
 FP32 = Store("fp32")
@@ -38,6 +41,35 @@ def _gloo_worker(rank: int, world: int, port: int, out):
         dist.destroy_process_group()
 
 
+_ANCHOR_CFG = dict(dim=256, num_heads=8, num_kv_heads=4, head_dim=32, eps=1e-6, rope_theta=1e4, qk_norm=True,
+                   intermediate=512)
+
+
+def _anchor_mlp(seed: int = 0):
+    torch.manual_seed(seed)
+    attn, mlp = SoftmaxAttn(_ANCHOR_CFG), LlamaMLP(_ANCHOR_CFG)
+    with torch.no_grad():
+        attn.q_norm.weight.uniform_(0.5, 1.5)
+        attn.k_norm.weight.uniform_(0.5, 1.5)
+    return attn, mlp, torch.randn(2, 50, _ANCHOR_CFG["dim"], generator=torch.Generator().manual_seed(seed + 1))
+
+
+def _gloo_anchor_mlp_worker(rank: int, world: int, port: int, out):
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        attn, mlp, x = _anchor_mlp()
+        with torch.no_grad():
+            ya = anchor_partial(shard_softmax_attn(attn, rank, world), x)
+            ym = mlp_partial(shard_mlp(mlp, rank, world), x)
+        dist.all_reduce(ya, op=dist.ReduceOp.SUM)
+        dist.all_reduce(ym, op=dist.ReduceOp.SUM)
+        if rank == 0:
+            out.put((ya, ym))
+    finally:
+        dist.destroy_process_group()
+
+
 def _get_while_alive(q, procs, deadline_s: float):
     """The first item of `q`, polling in short waits; fails as soon as a rank has exited with an
     error or the deadline passes, instead of blocking on a rank that died."""
@@ -51,6 +83,7 @@ def _get_while_alive(q, procs, deadline_s: float):
         except queue.Empty:
             dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
             assert not dead, f"a rank exited with {dead}"
+            assert any(p.exitcode is None for p in procs), "every rank exited without a result"
     for p in procs:
         p.kill()
     raise AssertionError(f"no result within {deadline_s} s")
@@ -93,6 +126,59 @@ def test_tp_oracle_allreduce_matches_full_layer_gloo():
     x = make_input(1, 300, cfg["dim"], dup=0.3, seed=3)
     ref = forward(oracle_params(full), oracle_cfg_of(full, cfg), x, FP32)
     output_close(y, ref, "all-reduced shard outputs")
+
+
+def test_tp_anchor_and_mlp_allreduce_gloo():
+    """Two gloo ranks: a softmax anchor split by KV head and a SwiGLU MLP split by intermediate
+    feature; their fp32 partials, all-reduced, are the unsharded modules' outputs."""
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = 30500 + os.getpid() % 1000
+    procs = [ctx.Process(target=_gloo_anchor_mlp_worker, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    ya, ym = _get_while_alive(out, procs, deadline_s=240)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    attn, mlp, x = _anchor_mlp()
+    with torch.no_grad():
+        torch.testing.assert_close(ya, attn(x), rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(ym, mlp(x), rtol=1e-5, atol=1e-5)
+
+
+def _run_model_worker(tmp_path, backend: str, nproc: int):
+    import subprocess
+    import sys
+
+    out = tmp_path / f"tp_model_{backend}.pt"
+    here = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    port = 31600 + os.getpid() % 1000 + (7 if backend == "gloo" else 0)
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={nproc}",
+           "--master-addr=127.0.0.1", f"--master-port={port}", os.path.join(here, "tp_model_worker.py"),
+           "--out", str(out), "--backend", backend]
+    r = subprocess.run(cmd, env=env, timeout=240, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    res = torch.load(out, weights_only=False)
+    assert res["world"] == nproc
+    output_close(res["got"], res["ref"], f"{nproc}-rank tensor-parallel model over {backend}")
+
+
+@pytest.mark.gpu
+def test_tp_model_two_ranks_gloo_one_gpu(tmp_path):
+    """The whole hybrid model split over two ranks that share one GPU (gloo all-reduces through the
+    host), prefill and one-token decode steps, against the unsharded decoder. Each rank's kernels
+    are independent launches; only the host-side collective joins them."""
+    _run_model_worker(tmp_path, "gloo", 2)
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp_model_nccl_two_gpus(tmp_path):
+    """The whole hybrid model split over two GPUs (NCCL all-reduces after every attention and every
+    MLP) against the unsharded decoder."""
+    _run_model_worker(tmp_path, "nccl", 2)
 
 
 @pytest.mark.gpu

@@ -806,9 +806,11 @@ class Bolt3Decoder:
         return out
 
     @staticmethod
-    def _anchor_attention(ly, cache: "AnchorKV", h: torch.Tensor, pos_start: int) -> torch.Tensor:
+    def _anchor_attention(ly, cache: "AnchorKV", h: torch.Tensor, pos_start: int,
+                          partial_fp32: bool = False) -> torch.Tensor:
         """A softmax anchor layer's attention branch for t new tokens (bolt3.py:426-445): RoPE at
-        pos_start, the new k/v appended to the layer's cache, causal within the new block."""
+        pos_start, the new k/v appended to the layer's cache, causal within the new block
+        (partial_fp32: o_proj's output in fp32, unrounded, as a tensor-parallel shard's partial sum)."""
         b, t, _ = h.shape
         q, k, v = ly.head_qkv(h)
         q, k = ly.rope(q, pos_start=pos_start), ly.rope(k, pos_start=pos_start)
@@ -823,7 +825,11 @@ class Bolt3Decoder:
         with sdpa_kernel(_ANCHOR_SDPA) if t == 1 else contextlib.nullcontext():
             y = F.scaled_dot_product_attention(q, keys.to(q.dtype), vals.to(q.dtype), attn_mask=mask,
                                                enable_gqa=ly.G > 1)
-        return ly.o_proj(y.transpose(1, 2).reshape(b, t, ly.H * ly.HD))
+        y = y.transpose(1, 2).reshape(b, t, ly.H * ly.HD)
+        if partial_fp32:
+            w = ly.o_proj.weight
+            return torch.mm(y.reshape(b * t, -1).to(w.dtype), w.t(), out_dtype=torch.float32).view(b, t, -1)
+        return ly.o_proj(y)
 
     @torch.no_grad()
     def step(self, tokens: torch.Tensor, pos_start: int, states, kv_caches, record=None):
