@@ -436,7 +436,8 @@ def run_full_model(args, rank, world, dev):
     with torch.device(dev):
         model = Bolt3LM(**mcfg)
     init_model_on_device(model, seed=0)     # the same weights on every rank
-    model = model.to(torch.bfloat16).eval()
+    # the device move also takes the RoPE frequency buffers, which the modules create on the host
+    model = model.to(device=dev, dtype=torch.bfloat16).eval()
     if world > 1:
         model = Bolt3LMTP(model)            # this rank's shards; the unsharded blocks are released
         torch.cuda.empty_cache()
@@ -447,13 +448,23 @@ def run_full_model(args, rank, world, dev):
     ids = torch.randint(0, mcfg["vocab_size"], (B, T), generator=torch.Generator(device=dev).manual_seed(100),
                         device=dev)
 
+    graphs = dec.graphs_supported(dev)
+    captures = [0]
+
     @torch.no_grad()
     def greedy(h, states, kv, n):
+        # one-token steps replayed from CUDA graphs (captured once per chunk of 128 positions, inside
+        # the timed region), as Bolt3Decoder.generate_batch runs them
         logits = model.lm_head(h[:, -1, :])
+        runner = dec.step_graph(states, kv) if graphs else None
         for i in range(n):
             nxt = logits.argmax(-1, keepdim=True)
-            h, states, kv = dec.step(nxt, T + i, states, kv)
+            if runner is not None:
+                h = runner.step(nxt, T + i)
+            else:
+                h, states, kv = dec.step(nxt, T + i, states, kv)
             logits = model.lm_head(h[:, -1, :])
+        captures[0] = runner.captures if runner is not None else 0
         return logits
 
     def ev():
@@ -489,7 +500,7 @@ def run_full_model(args, rank, world, dev):
                             if world > 1 else "one GPU"),
             "prefill": {"value": B * T / t_pre, "unit": "tok/s", "ms": t_pre * 1e3},
             "decode": {"value": B * n_new / t_dec, "unit": "tok/s", "ms_per_step": t_dec / n_new * 1e3,
-                       "steps": n_new, "sequences": B}}
+                       "steps": n_new, "sequences": B, "cuda_graphs": graphs, "graph_captures": captures[0]}}
 
 
 def run_decode_tp(args, rank, world, dev, m, cfg):

@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define BOLT3_ABI_VERSION 6
+#define BOLT3_ABI_VERSION 7
 
 enum bolt3_status {
   BOLT3_OK = 0,
@@ -45,6 +45,14 @@ enum bolt3_status {
  * column blocks must start on multiples of 8.
  * Output element (b, head, t) of a head-major array lives at
  *   ((b * n_heads + head) * head_stride + t_off + t) * HD      (q_*: n_heads = H, k/v: HKV). */
+/* Device step position. A one-token decode step replayed from a CUDA graph cannot take its
+ * position as a launch argument; bolt3_prep and bolt3_attend (prefill = 0) then read it from the
+ * device. With pos_dev non-NULL the kernel reads d = *pos_dev - pos_ref, which must lie in
+ * [0, pos_span): bolt3_prep uses RoPE position pos0 + d and writes k / v / beta at k_t_off + d and
+ * beta_t_off + d (q and eta offsets are unchanged); bolt3_attend uses seg1_len + d keys of segment 1
+ * and len_before + d. The launch checks every size for the largest d, pos_span - 1; segment 1's
+ * rows past seg1_len + d must hold finite values (they are read and masked). A d outside the range
+ * makes both kernels skip the step, and bolt3_attend ORs 8 into its status word. */
 typedef struct bolt3_prep_args {
   const void* proj; int64_t ld;       /* bf16 [B*T][ld] */
   int B, T, H, HKV, HD;
@@ -60,6 +68,8 @@ typedef struct bolt3_prep_args {
   float* q_l2;                        /* optional: |q_raw| per (head, token), laid out like eta */
   int parts;                          /* 1 = q/eta, 2 = k/v/beta, 3 = both */
   int64_t q_col, k_col, v_col, beta_col, eta_col;
+  /* optional step position on the device (see "Device step position" below); NULL otherwise */
+  const int64_t* pos_dev; int64_t pos_ref; int64_t pos_span;
 } bolt3_prep_args;
 int bolt3_prep(const bolt3_prep_args* a, void* stream);
 
@@ -137,13 +147,35 @@ typedef struct bolt3_attend_args {
   const float* coef;                   /* [hkv]: (1 - gamma) / sqrt(HD), fp32 */
   const float* res_w; float eps;       /* res_norm weight [HD] (fp32), eps */
   void* y; int64_t y_tokens;           /* bf16 [B][y_tokens][H][HD]; row of query token t: t */
-  int32_t* status;                     /* optional device int: OR-ed with 2 if a bounded wait expired */
+  int32_t* status;                     /* optional device int: OR-ed with 2 if a bounded wait expired,
+                                          with 8 if a device step position was out of range */
   const float* q_l2;                   /* optional |q_raw| per row, [B*H][Tq] */
   int64_t blk_begin, blk_count;        /* prefill: query blocks [blk_begin, blk_begin + blk_count)
                                           (blk_count = 0: every block) */
   uint32_t wait_probe;                 /* test hook, 0 in normal use (see above) */
+  /* optional step position on the device (prefill = 0 only; see "Device step position") */
+  const int64_t* pos_dev; int64_t pos_ref; int64_t pos_span;
 } bolt3_attend_args;
 int bolt3_attend(const bolt3_attend_args* a, void* stream);
+
+/* ---- Softmax anchor layers of the hybrid model: one-token decode step.
+ * Replaces the anchor branch of Bolt3Decoder.step for one new token (vsa_lm/config/bolt3.py:426-445:
+ * the cache append of vsa_lm/decode.py:88-106, then scaled_dot_product_attention with enable_gqa).
+ * For every (sequence b, KV head): writes k_new / v_new at cache position n, then the exact softmax
+ * attention of its G = H / HKV query heads over cache positions 0..n (scores q.k * scale in fp32),
+ * y rounded to bf16 once. q: bf16 [B][H][HD] (RoPE applied); k_new, v_new: bf16 [B][HKV][HD];
+ * k_cache, v_cache: bf16 [B][HKV][cap][HD]; y: bf16 [B][H][HD]. HD 64 or 128, G <= 8. With pos_dev
+ * (the device step position of bolt3_prep) the position is n + *pos_dev - pos_ref, within
+ * [n, n + pos_span); outside it the step is skipped and status gets 8. */
+typedef struct bolt3_anchor_args {
+  int B, H, HKV, HD;
+  const void* q; const void* k_new; const void* v_new;
+  void* k_cache; void* v_cache; int64_t cap; int64_t n;
+  void* y; float scale;
+  int32_t* status;                     /* optional device int (bit 8: device position out of range) */
+  const int64_t* pos_dev; int64_t pos_ref; int64_t pos_span;
+} bolt3_anchor_args;
+int bolt3_anchor_decode(const bolt3_anchor_args* a, void* stream);
 
 /* Bytes of snapshot workspace bolt3_prefill_fwd needs for n_chains chains of T tokens. */
 size_t bolt3_prefill_workspace_size(int n_chains, int64_t T, int HD);
@@ -189,6 +221,9 @@ int bolt3_prefill_fwd_noalloc(const bolt3_prefill_args* a, void* stream);
 /* ---- utilities */
 int bolt3_abi_version(void);
 const char* bolt3_status_string(int status);
+/* sizeof of an argument struct (0 prep, 1 consolidate, 2 attend, 3 prefill, 4 anchor; 0 for others), so a
+ * binding can check its own layout of the structs against the compiled one */
+size_t bolt3_args_size(int which);
 /* Host-only: reorder indices 0..n-1 of `vals` into the order CPU torch.topk(vals, k, largest)
  * returns (first k written to out_idx). Returns 0, or 1 if a bounds check fired. */
 int bolt3_topk_order_host(const float* vals, int n, int k, int largest, int32_t* out_idx);

@@ -24,15 +24,18 @@ def test_library_exports_every_declared_symbol():
     for n in names:
         assert hasattr(lib, n), f"{n} declared in include/bolt3.h but not exported"
         assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
-    assert lib.bolt3_abi_version() == _lib.ABI_VERSION == 6
+    assert lib.bolt3_abi_version() == _lib.ABI_VERSION == 7
     assert lib.bolt3_status_string(0) == b"ok"
     assert b"shape" in lib.bolt3_status_string(2)
 
 
 def test_struct_sizes_are_c_layout():
-    # every pointer field is 8 bytes and aligned; the structs have no hidden padding surprises
-    for st in (_lib.PrepArgs, _lib.ConsolidateArgs, _lib.AttendArgs, _lib.PrefillArgs):
+    # the ctypes mirrors have the compiled structs' sizes (a field added on one side only shows here)
+    lib = _lib.load()
+    for i, st in enumerate((_lib.PrepArgs, _lib.ConsolidateArgs, _lib.AttendArgs, _lib.PrefillArgs, _lib.AnchorArgs)):
         assert ctypes.sizeof(st) % 8 == 0
+        assert lib.bolt3_args_size(i) == ctypes.sizeof(st), st.__name__
+    assert lib.bolt3_args_size(5) == 0
 
 
 def test_entry_points_reject_bad_arguments_without_a_gpu():
@@ -41,6 +44,16 @@ def test_entry_points_reject_bad_arguments_without_a_gpu():
     assert lib.bolt3_consolidate(None, None) == 1
     assert lib.bolt3_attend(None, None) == 1
     assert lib.bolt3_prefill_fwd(None, None) == 1
+    assert lib.bolt3_anchor_decode(None, None) == 1
+    an = _lib.AnchorArgs(B=2, H=8, HKV=2, HD=128, q=16, k_new=32, v_new=48, k_cache=64, v_cache=80, cap=10, n=10,
+                         y=96, scale=0.1)
+    assert lib.bolt3_anchor_decode(ctypes.byref(an), None) == 4    # no room for the appended token
+    an.n, an.HD = 3, 96
+    assert lib.bolt3_anchor_decode(ctypes.byref(an), None) == 2    # unsupported head dim
+    an.HD, an.q = 128, 8
+    assert lib.bolt3_anchor_decode(ctypes.byref(an), None) == 3    # misaligned query rows
+    an.q, an.pos_dev, an.pos_ref, an.pos_span = 16, 112, 3, 8
+    assert lib.bolt3_anchor_decode(ctypes.byref(an), None) == 4    # 3 + 7 + 1 > 10
     a = _lib.ConsolidateArgs()
     assert lib.bolt3_consolidate(ctypes.byref(a), None) == 1      # null state pointers
     assert lib.bolt3_prefill_workspace_size(4, 1024, 96) == 0      # unsupported head dim

@@ -1,0 +1,154 @@
+"""One-token decode steps replayed from CUDA graphs (Bolt3Decoder.step_graph) and the pieces that
+make them possible: the device step position of the Bolt-3 decode kernels, and the anchor layers'
+one-token attention kernel (bolt3_anchor_decode), checked against a plain PyTorch fp32 reference.
+
+A replayed step runs the same kernels on the same data as an eager step, so its hidden states must
+equal step()'s bit for bit; the chunk-boundary consolidations run eagerly after the replay."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from vsa_lm_b200 import Bolt3Decoder, Bolt3LayerState, kernels as K
+from vsa_lm_b200.model import Bolt3LM
+from vsa_lm_b200.workloads import MODEL_SHAPES, layer_cfg, make_input, make_model_params
+from helpers import bf16_module
+
+pytestmark = pytest.mark.gpu
+
+
+def _anchor_ref(q, kc, vc, n, k_new, v_new, scale):
+    """fp32 softmax attention of q [B, H, HD] over cache rows 0..n-1 plus the new row."""
+    B, H, HD = q.shape
+    HKV = kc.shape[1]
+    keys = torch.cat([kc[:, :, :n].float(), k_new.float()[:, :, None]], 2)
+    vals = torch.cat([vc[:, :, :n].float(), v_new.float()[:, :, None]], 2)
+    keys = keys.repeat_interleave(H // HKV, 1)
+    vals = vals.repeat_interleave(H // HKV, 1)
+    p = torch.softmax((q.float()[:, :, None] @ keys.transpose(-1, -2)) * scale, -1)
+    return (p @ vals)[:, :, 0]
+
+
+@pytest.mark.parametrize("HD,G,n", [(128, 4, 0), (128, 4, 255), (128, 4, 256), (128, 4, 2300), (64, 2, 700),
+                                    (64, 8, 31), (128, 1, 1000)])
+def test_anchor_decode_matches_fp32_reference(HD, G, n):
+    torch.manual_seed(n + HD)
+    B, HKV, cap = 3, 2, 2560
+    H = HKV * G
+    q = torch.randn(B, H, HD, device="cuda").bfloat16()
+    kc = torch.randn(B, HKV, cap, HD, device="cuda").bfloat16()
+    vc = torch.randn(B, HKV, cap, HD, device="cuda").bfloat16()
+    k_new = torch.randn(B, HKV, HD, device="cuda").bfloat16()
+    v_new = torch.randn(B, HKV, HD, device="cuda").bfloat16()
+    ref = _anchor_ref(q, kc, vc, n, k_new, v_new, HD ** -0.5)
+    y = torch.empty(B, H, HD, device="cuda", dtype=torch.bfloat16)
+    K.anchor_decode(q=q, k_new=k_new, v_new=v_new, k_cache=kc, v_cache=vc, n=n, y=y, scale=HD ** -0.5)
+    assert torch.equal(kc[:, :, n], k_new) and torch.equal(vc[:, :, n], v_new)
+    torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2 * ref.pow(2).mean().sqrt().item())
+
+
+def test_anchor_decode_device_position():
+    """The same launch, built for position 40 with a span of 8, replayed at 40 + d from the device."""
+    torch.manual_seed(5)
+    B, HKV, G, HD, cap = 2, 2, 4, 128, 512
+    q = torch.randn(B, HKV * G, HD, device="cuda").bfloat16()
+    kc = torch.randn(B, HKV, cap, HD, device="cuda").bfloat16()
+    vc = torch.randn(B, HKV, cap, HD, device="cuda").bfloat16()
+    k_new = torch.randn(B, HKV, HD, device="cuda").bfloat16()
+    v_new = torch.randn(B, HKV, HD, device="cuda").bfloat16()
+    pos = K.DevicePosition("cuda")
+    pos.ref, pos.span = 40, 8
+    status = K.DeviceStatus("cuda")
+    for d in (0, 3, 7):
+        kc2, vc2 = kc.clone(), vc.clone()
+        y = torch.empty_like(q)
+        y2 = torch.empty_like(q)
+        pos.set(40 + d)
+        K.anchor_decode(q=q, k_new=k_new, v_new=v_new, k_cache=kc2, v_cache=vc2, n=100, y=y, scale=HD ** -0.5,
+                        dev_pos=pos, status=status)
+        K.anchor_decode(q=q, k_new=k_new, v_new=v_new, k_cache=kc.clone(), v_cache=vc.clone(), n=100 + d, y=y2,
+                        scale=HD ** -0.5)
+        assert torch.equal(y, y2) and torch.equal(kc2[:, :, 100 + d], k_new)
+    # a position outside the span: nothing is written and the status word says so
+    pos.set(40 + 8)
+    y = torch.zeros_like(q)
+    K.anchor_decode(q=q, k_new=k_new, v_new=v_new, k_cache=kc, v_cache=vc, n=100, y=y, scale=HD ** -0.5,
+                    dev_pos=pos, status=status)
+    torch.cuda.synchronize()
+    assert int(status.word.item()) & 8 and not y.any()
+    status.word.zero_()
+
+
+@pytest.mark.parametrize("shape", ["qwen3_4b", "tiny"])
+def test_decode_kernels_device_position_equal_eager(shape):
+    """A Bolt-3 layer's one-token launches built once at a chunk's first position and given later
+    positions through the device give the eager steps' outputs bit for bit (the streaming kernel at
+    HD = 128, the warp-per-chain kernel at HD = 64), across two chunk boundaries."""
+    cfg = layer_cfg(shape)
+    m = bf16_module(cfg, 0)
+    B, prompt, n_dec = 2, 256, 200
+    x = make_input(B, prompt + n_dec, cfg["dim"], dup=0.3, seed=6).to(torch.bfloat16).cuda()
+    sts = [Bolt3LayerState(m, B, "cuda") for _ in range(2)]
+    mres = [torch.zeros(B, m.HKV, m.HD, m.HD, device="cuda") for _ in range(2)]
+    for s in range(0, prompt, 128):
+        for st, mr in zip(sts, mres):
+            Bolt3Decoder.layer_step(m, st, x[:, s:s + 128], s, mr)
+    pos = K.DevicePosition("cuda")
+    for p in range(prompt, prompt + n_dec):
+        h = x[:, p:p + 1]
+        ref = Bolt3Decoder.layer_step(m, sts[0], h, p, mres[0])
+        st = sts[1]
+        if st.cur_len == 0 or p == prompt:
+            pos.ref, pos.span = p, m.C - st.cur_len
+            launch_pos = p
+        pos.set(p)
+        # the launch is built as at its reference position, then the device position moves it
+        cur = st.cur_len
+        st.cur_len = cur - (p - launch_pos)
+        got = Bolt3Decoder._layer_launch(m, st, h, launch_pos, mres[1], dev_pos=pos)
+        st.cur_len = cur
+        Bolt3Decoder._layer_advance(m, st, 1, p, mres[1])
+        assert torch.equal(got, ref), f"position {p}"
+    assert torch.equal(mres[0], mres[1])
+
+
+def _model(shape):
+    mcfg = dict(MODEL_SHAPES[shape])
+    model = Bolt3LM(**mcfg)
+    model.load_state_dict(make_model_params(mcfg, 0), strict=True)
+    return mcfg, model.to(device="cuda", dtype=torch.bfloat16).eval()
+
+
+@pytest.mark.parametrize("shape", ["small_lm", "tiny_lm"])
+def test_step_graph_equals_eager_steps(shape):
+    """Greedy decoding through Bolt3Decoder.step_graph (one capture per chunk) against eager step()
+    calls on a copy of the state: the same hidden states bit for bit over 300 steps (three chunk
+    boundaries), and the same final M_res."""
+    mcfg, model = _model(shape)
+    dec = Bolt3Decoder(model)
+    g = torch.Generator().manual_seed(3)
+    B, T = 2, 300
+    ids = torch.randint(0, mcfg["vocab_size"], (B, T), generator=g).cuda()
+    steps = torch.randint(0, mcfg["vocab_size"], (B, 300), generator=g).cuda()
+    h0, st_e, kv_e = dec.prefill(ids, max_kv_len=T + 320)
+    h1, st_g, kv_g = dec.prefill(ids, max_kv_len=T + 320)
+    assert torch.equal(h0, h1)
+    runner = dec.step_graph(st_g, kv_g)
+    for i in range(steps.shape[1]):
+        tok = steps[:, i:i + 1]
+        he, st_e, kv_e = dec.step(tok, T + i, st_e, kv_e)
+        hg = runner.step(tok, T + i)
+        assert torch.equal(hg, he), f"step {i}"
+    assert runner.captures == 3      # the chunk the prompt left open (300..383), then 384.., 512..
+    for a, b in zip(st_e, st_g):
+        if a is not None:
+            assert torch.equal(a, b)
+    Bolt3Decoder.check_status(kv_g)
+
+
+def test_generate_batch_graphs_equal_eager():
+    """generate_batch with graph replay and without it (cuda_graphs=False) gives the same tokens."""
+    mcfg, model = _model("small_lm")
+    ids = torch.randint(0, mcfg["vocab_size"], (3, 200), generator=torch.Generator().manual_seed(9)).cuda()
+    a, la = Bolt3Decoder(model).generate_batch(ids, 150, temperature=0.0)
+    b, lb = Bolt3Decoder(model, cuda_graphs=False).generate_batch(ids, 150, temperature=0.0)
+    assert torch.equal(a, b) and torch.equal(la, lb)

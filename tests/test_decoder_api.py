@@ -78,7 +78,9 @@ def test_generate_batch_greedy_matches_model_oracle():
     mcfg, model, oracle = _models()
     B, T, n = 2, 260, 24
     ids = torch.randint(0, mcfg["vocab_size"], (B, T), generator=torch.Generator().manual_seed(9))
-    dec = Bolt3Decoder(model)
+    # eager steps, so that the tap sees (and checks) every layer step; the runs below replay the
+    # steps from CUDA graphs and must give the same tokens
+    dec = Bolt3Decoder(model, cuda_graphs=False)
     o, ledger = oracle(B), FlipLedger("generate_batch")
     with LockstepTap(model, o, ledger):
         toks, lengths = dec.generate_batch(ids.cuda(), n, temperature=0.0)
@@ -131,7 +133,7 @@ def test_memory_bank_flow_matches_model_oracle():
     V = mcfg["vocab_size"]
     doc = torch.randint(0, V, (1, 768 + 256), generator=g)
     q_ids = torch.randint(0, V, (1, 50), generator=g)
-    dec = Bolt3Decoder(model)
+    dec = Bolt3Decoder(model, cuda_graphs=False)   # eager steps: the tap checks each one
     o, ledger = oracle(1), FlipLedger("memory-bank flow")
     tap = LockstepTap(model, o, ledger)
     vsa = [i for i, t in enumerate(model.config["layer_types"]) if t == "vsa"]

@@ -21,7 +21,8 @@ STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported shape", 3: "misaligned
 # Bits of the device status word the kernels OR into (include/bolt3.h)
 DEVICE_STATUS_BITS = {1: "a bounds check of the consolidation's tie-order emulation fired",
                       2: "a bounded wait in an attention kernel expired",
-                      4: "a bounded wait in the consolidation scan expired"}
+                      4: "a bounded wait in the consolidation scan expired",
+                      8: "a decode step's device position was outside the range its launch was built for"}
 
 
 class PrepArgs(ctypes.Structure):
@@ -37,6 +38,7 @@ class PrepArgs(ctypes.Structure):
         ("q_l2", _P),
         ("parts", _I),
         ("q_col", _I64), ("k_col", _I64), ("v_col", _I64), ("beta_col", _I64), ("eta_col", _I64),
+        ("pos_dev", _P), ("pos_ref", _I64), ("pos_span", _I64),
     ]
 
 
@@ -75,6 +77,18 @@ class AttendArgs(ctypes.Structure):
         ("q_l2", _P),
         ("blk_begin", _I64), ("blk_count", _I64),
         ("wait_probe", ctypes.c_uint32),
+        ("pos_dev", _P), ("pos_ref", _I64), ("pos_span", _I64),
+    ]
+
+
+class AnchorArgs(ctypes.Structure):
+    _fields_ = [
+        ("B", _I), ("H", _I), ("HKV", _I), ("HD", _I),
+        ("q", _P), ("k_new", _P), ("v_new", _P),
+        ("k_cache", _P), ("v_cache", _P), ("cap", _I64), ("n", _I64),
+        ("y", _P), ("scale", _F),
+        ("status", _P),
+        ("pos_dev", _P), ("pos_ref", _I64), ("pos_span", _I64),
     ]
 
 
@@ -99,15 +113,17 @@ SIGNATURES = {
     "bolt3_prep": ([ctypes.POINTER(PrepArgs), _P], _I),
     "bolt3_consolidate": ([ctypes.POINTER(ConsolidateArgs), _P], _I),
     "bolt3_attend": ([ctypes.POINTER(AttendArgs), _P], _I),
+    "bolt3_anchor_decode": ([ctypes.POINTER(AnchorArgs), _P], _I),
     "bolt3_prefill_fwd": ([ctypes.POINTER(PrefillArgs), _P], _I),
     "bolt3_prefill_fwd_noalloc": ([ctypes.POINTER(PrefillArgs), _P], _I),
     "bolt3_prefill_workspace_size": ([_I, _I64, _I], _SZ),
     "bolt3_abi_version": ([], _I),
+    "bolt3_args_size": ([_I], _SZ),
     "bolt3_status_string": ([_I], ctypes.c_char_p),
     "bolt3_topk_order_host": ([_P, _I, _I, _I, _P], _I),
 }
 
-ABI_VERSION = 6   # BOLT3_ABI_VERSION in include/bolt3.h
+ABI_VERSION = 7   # BOLT3_ABI_VERSION in include/bolt3.h
 
 # Fixed scratch of bolt3_prefill_fwd_noalloc (BOLT3_NOALLOC_SCRATCH_BYTES in include/bolt3.h)
 NOALLOC_SCRATCH_BYTES = 32 << 20
@@ -135,6 +151,10 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
             fn.restype = rest
         if lib.bolt3_abi_version() != ABI_VERSION:
             raise RuntimeError("libbolt3.so ABI version mismatch; rebuild with `python -m vsa_lm_b200.build`")
+        for i, st in enumerate((PrepArgs, ConsolidateArgs, AttendArgs, PrefillArgs, AnchorArgs)):
+            if lib.bolt3_args_size(i) != ctypes.sizeof(st):
+                raise RuntimeError(f"{st.__name__} has {ctypes.sizeof(st)} bytes here but "
+                                   f"{lib.bolt3_args_size(i)} in libbolt3.so: the bindings and the header differ")
         _lib = lib
         return lib
 

@@ -12,7 +12,6 @@ M_res are fp32. Results are compared with the fp32 CPU oracle restating the refe
 """
 from __future__ import annotations
 
-import contextlib
 import math
 
 import types
@@ -20,7 +19,6 @@ import types
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
-from torch.nn.attention import SDPBackend, sdpa_kernel
 
 from . import kernels as K
 
@@ -73,6 +71,10 @@ class LlamaRoPE(nn.Module):
 
     def forward(self, x: torch.Tensor, pos_start: int = 0) -> torch.Tensor:
         pos = torch.arange(x.shape[2], device=x.device, dtype=torch.float32) + float(pos_start)
+        return self.forward_at(x, pos)
+
+    def forward_at(self, x: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        """RoPE at the fp32 positions `pos` [T] held on the device (the same arithmetic as forward)."""
         ang = torch.outer(pos, self.inv_freq.to(device=x.device, dtype=torch.float32))
         c, s = ang.cos().to(x.dtype), ang.sin().to(x.dtype)
         x1, x2 = x.chunk(2, dim=-1)
@@ -477,9 +479,11 @@ class Bolt3LayerState:
         self.B, self.HKV, self.HD, self.C = B, ly.HKV, ly.HD, ly.C
         n = B * ly.HKV
         bf = dict(dtype=torch.bfloat16, device=device)
-        self.ring_kr = torch.empty(n, 2 * self.C, self.HD, **bf)
-        self.ring_kp = torch.empty_like(self.ring_kr)
-        self.ring_v = torch.empty_like(self.ring_kr)
+        # zeros, not empty: a step replayed from a CUDA graph reads its window slot past the current
+        # length and masks those keys, and a masked value row must still be finite (0 x NaN is NaN)
+        self.ring_kr = torch.zeros(n, 2 * self.C, self.HD, **bf)
+        self.ring_kp = torch.zeros_like(self.ring_kr)
+        self.ring_v = torch.zeros_like(self.ring_kr)
         self.ring_b = torch.empty(n, 2 * self.C, dtype=torch.float32, device=device)
         self.sink_k = torch.empty(n, N_SINKS, self.HD, **bf)
         self.sink_v = torch.empty_like(self.sink_k)
@@ -490,6 +494,7 @@ class Bolt3LayerState:
         self.sinks_set = False
         self.n_filled = 0
         self._plans = {}   # per step size: buffers and prebuilt launch arguments (Bolt3Decoder)
+        self._consts = None  # the layer constants of the last step's plan (its chunk boundary uses them)
         # device status word of this state's kernels, checked at every chunk boundary
         self.status = K.DeviceStatus(device)
 
@@ -515,11 +520,15 @@ class Bolt3Decoder:
     Softmax anchor layers use a static KV cache and SDPA as in the reference (bolt3.py:426-445).
     """
 
-    def __init__(self, model, wrap_positions: bool = False, max_cache_pos: int = 65536, **kwargs):
+    def __init__(self, model, wrap_positions: bool = False, max_cache_pos: int = 65536, cuda_graphs: bool = True,
+                 **kwargs):
         self.model = model.eval()
         self.max_T = model.config["max_T"]
         self.max_cache_pos = max_cache_pos
         self.C = int(model.config.get("bolt3_C", 128))
+        # generation loops replay their one-token steps from CUDA graphs (the reference runs them
+        # eagerly, bolt3.py:287-288: a step of a 36-layer model is hundreds of launches)
+        self.use_cuda_graphs = cuda_graphs
 
     @staticmethod
     def state_bytes(model):
@@ -733,6 +742,17 @@ class Bolt3Decoder:
                    m_res: torch.Tensor, partial_fp32: bool = False) -> torch.Tensor:
         """Attention branch of one Bolt-3 layer for t new tokens: returns o_proj(y) [b, t, D] bf16
         (fp32 and unrounded with partial_fp32: a tensor-parallel shard's partial sum)."""
+        out = Bolt3Decoder._layer_launch(ly, st, h, pos_start, m_res, partial_fp32)
+        Bolt3Decoder._layer_advance(ly, st, h.shape[1], pos_start, m_res)
+        return out
+
+    @staticmethod
+    def _layer_launch(ly: Bolt3Attn, st: Bolt3LayerState, h: torch.Tensor, pos_start: int, m_res: torch.Tensor,
+                      partial_fp32: bool = False, dev_pos: "K.DevicePosition | None" = None) -> torch.Tensor:
+        """The kernels of a Bolt-3 layer step (projection, prep, attention, o_proj), enqueued on the
+        current stream; the state's host bookkeeping is _layer_advance's. With dev_pos (a step captured
+        into a CUDA graph) the kernels read the step's position from the device: the launch is built
+        for position dev_pos.ref and stays valid for dev_pos.span positions of the current chunk."""
         b, t, D = h.shape
         H, HKV, HD, C, G = ly.H, ly.HKV, ly.HD, ly.C, ly.G
         if st.cur_len + t > C:
@@ -749,6 +769,9 @@ class Bolt3Decoder:
             raise RuntimeError(f"the step's tensors are on {h.device}; make that device current")
         if not (m_res.dtype == torch.float32 and m_res.is_contiguous() and tuple(m_res.shape) == (b, HKV, HD, HD)):
             raise ValueError(f"m_res must be a contiguous fp32 CUDA tensor [{b}, {HKV}, {HD}, {HD}]")
+        if dev_pos is not None and (t != 1 or dev_pos.ref != pos_start or st.cur_len + dev_pos.span > C):
+            raise ValueError("a device-position launch is a one-token step at its reference position whose span "
+                             "stays within the chunk")
         if st.cur_len == 0:
             st.slot_pos[st.cur_slot] = pos_start
         elif pos_start != st.slot_pos[st.cur_slot] + st.cur_len:
@@ -765,8 +788,9 @@ class Bolt3Decoder:
                 # the per-call set-up is small next to its work
                 if t <= Bolt3Decoder.PLAN_MAX_TOKENS:
                     st._plans[t] = plan
+        st._consts = plan.consts
         proj = F.linear(h.reshape(b * t, D).to(torch.bfloat16), plan.w_in, plan.b_in)
-        plan.args.launch_prep(proj, pos_start, st.cur_slot * C + st.cur_len)
+        plan.args.launch_prep(proj, pos_start, st.cur_slot * C + st.cur_len, dev_pos)
         has_prev = st.prev_slot >= 0
         p0 = st.prev_slot * C if has_prev else 0
         c0 = st.cur_slot * C
@@ -774,18 +798,25 @@ class Bolt3Decoder:
         plan.args.launch_attend(
             seg0_k=rk + p0 * row, seg0_v=rv + p0 * row, seg0_len=C if has_prev else 0,
             seg1_k=rk + c0 * row, seg1_v=rv + c0 * row, seg1_len=st.cur_len + t, len_before=st.cur_len,
-            has_sinks=st.sinks_set, has_bank=st.has_bank, bank_m=m_res.data_ptr())
+            has_sinks=st.sinks_set, has_bank=st.has_bank, bank_m=m_res.data_ptr(), dev_pos=dev_pos)
         y = plan.y
         if partial_fp32:
-            out = torch.mm(y.view(b * t, H * HD), plan.w_out.t(), out_dtype=torch.float32).view(b, t, -1)
-        else:
-            out = F.linear(y.view(b, t, H * HD), plan.w_out)
-        c = plan.consts
+            return torch.mm(y.view(b * t, H * HD), plan.w_out.t(), out_dtype=torch.float32).view(b, t, -1)
+        return F.linear(y.view(b, t, H * HD), plan.w_out)
+
+    @staticmethod
+    def _layer_advance(ly: Bolt3Attn, st: Bolt3LayerState, t: int, pos_start: int, m_res: torch.Tensor) -> None:
+        """Host side of a Bolt-3 layer step whose kernels are enqueued: the pending chunk grows by t
+        tokens, and a chunk that reaches C tokens consolidates the previous one into the bank and
+        M_res (bolt3.py:406-425) and becomes the previous chunk."""
+        b, HKV, HD, C = st.B, ly.HKV, ly.HD, ly.C
+        c = st._consts
         st.cur_len += t
         if st.cur_len >= C:                                                   # bolt3.py:406-425
             # errors of the previous chunk's kernels (their status copy finished long ago)
             st.status.check(block=True)
-            if has_prev:
+            if st.prev_slot >= 0:
+                p0 = st.prev_slot * C
                 skip = 0
                 if not st.sinks_set:
                     st.sink_k.copy_(st.ring_kp[:, p0:p0 + N_SINKS])
@@ -803,29 +834,44 @@ class Bolt3Decoder:
                 st.n_filled = nf if nf >= ly.S else nf + min(ly.S - nf, C - skip)
             st.prev_slot, st.cur_slot, st.cur_len = st.cur_slot, 1 - st.cur_slot, 0
             st.status.arm(f"Bolt-3 decode chunk ending at position {pos_start + t}")
-        return out
 
     @staticmethod
     def _anchor_attention(ly, cache: "AnchorKV", h: torch.Tensor, pos_start: int,
-                          partial_fp32: bool = False) -> torch.Tensor:
+                          partial_fp32: bool = False, dev_pos: "K.DevicePosition | None" = None) -> torch.Tensor:
         """A softmax anchor layer's attention branch for t new tokens (bolt3.py:426-445): RoPE at
         pos_start, the new k/v appended to the layer's cache, causal within the new block
-        (partial_fp32: o_proj's output in fp32, unrounded, as a tensor-parallel shard's partial sum)."""
+        (partial_fp32: o_proj's output in fp32, unrounded, as a tensor-parallel shard's partial sum).
+        One-token steps on the GPU run bolt3_anchor_decode (append and attention in one kernel); with
+        dev_pos (a step captured into a CUDA graph) the position comes from the device and the cache's
+        host count is left to the caller."""
         b, t, _ = h.shape
         q, k, v = ly.head_qkv(h)
-        q, k = ly.rope(q, pos_start=pos_start), ly.rope(k, pos_start=pos_start)
-        n_before = cache.n
-        keys, vals = cache.append(k, v)
-        mask = None
-        if t > 1:   # query i sees every cached key and the new keys up to itself
-            mask = torch.ones(t, n_before + t, dtype=torch.bool, device=h.device).tril(diagonal=n_before)
-        # one-token steps avoid the cuDNN backend: it builds a new plan for every cache length,
-        # milliseconds of host time per call when the cache grows by a token each step (prompt chunks,
-        # with their mask, keep the default choice)
-        with sdpa_kernel(_ANCHOR_SDPA) if t == 1 else contextlib.nullcontext():
+        if t == 1 and h.is_cuda and q.dtype == torch.bfloat16 and cache.buf.dtype == torch.bfloat16:
+            if dev_pos is None:
+                q, k = ly.rope(q, pos_start=pos_start), ly.rope(k, pos_start=pos_start)
+                cache.reserve(1)
+            else:
+                posf = dev_pos.word.to(torch.float32)
+                q, k = ly.rope.forward_at(q, posf), ly.rope.forward_at(k, posf)
+            y = torch.empty(b, ly.H, ly.HD, dtype=torch.bfloat16, device=h.device)
+            K.anchor_decode(q=q.reshape(b, ly.H, ly.HD).contiguous(), k_new=k.reshape(b, ly.HKV, ly.HD).contiguous(),
+                            v_new=v.reshape(b, ly.HKV, ly.HD).contiguous(), k_cache=cache.k, v_cache=cache.v,
+                            n=cache.n, y=y, scale=ly.HD ** -0.5, dev_pos=dev_pos)
+            if dev_pos is None:
+                cache.n += 1
+            y = y.view(b, 1, ly.H * ly.HD)
+        else:
+            if dev_pos is not None:
+                raise ValueError("device-position anchor steps are one bf16 token on the GPU")
+            q, k = ly.rope(q, pos_start=pos_start), ly.rope(k, pos_start=pos_start)
+            n_before = cache.n
+            keys, vals = cache.append(k, v)
+            mask = None
+            if t > 1:   # query i sees every cached key and the new keys up to itself
+                mask = torch.ones(t, n_before + t, dtype=torch.bool, device=h.device).tril(diagonal=n_before)
             y = F.scaled_dot_product_attention(q, keys.to(q.dtype), vals.to(q.dtype), attn_mask=mask,
                                                enable_gqa=ly.G > 1)
-        y = y.transpose(1, 2).reshape(b, t, ly.H * ly.HD)
+            y = y.transpose(1, 2).reshape(b, t, ly.H * ly.HD)
         if partial_fp32:
             w = ly.o_proj.weight
             return torch.mm(y.reshape(b * t, -1).to(w.dtype), w.t(), out_dtype=torch.float32).view(b, t, -1)
@@ -835,18 +881,50 @@ class Bolt3Decoder:
     def step(self, tokens: torch.Tensor, pos_start: int, states, kv_caches, record=None):
         """Run t new tokens [b, t] at positions pos_start.. through every block; returns the final
         normed hidden states [b, t, D] and the (updated in place) state lists (bolt3.py:335-447)."""
+        return self._blocks(tokens, pos_start, states, kv_caches), states, kv_caches
+
+    def _blocks(self, tokens: torch.Tensor, pos_start: int, states, kv_caches,
+                dev_pos: "K.DevicePosition | None" = None) -> torch.Tensor:
+        """The step's computation. With dev_pos only the kernels are enqueued (a step captured into a
+        CUDA graph: the position comes from the device, the host bookkeeping is _advance's)."""
         m = self.model
         with torch.autocast("cuda", torch.bfloat16, enabled=tokens.is_cuda):
             x = m.embed_tokens(tokens)
             for li, blk in enumerate(m.blocks):
                 h = blk.norm1(x)
                 if hasattr(blk, "vsa"):
-                    attn = self.layer_step(blk.vsa, kv_caches[li], h, pos_start, states[li])
+                    if dev_pos is None:
+                        attn = self.layer_step(blk.vsa, kv_caches[li], h, pos_start, states[li])
+                    else:
+                        attn = self._layer_launch(blk.vsa, kv_caches[li], h, pos_start, states[li], dev_pos=dev_pos)
                 else:
-                    attn = self._anchor_attention(blk.attn, kv_caches[li], h, pos_start)
+                    attn = self._anchor_attention(blk.attn, kv_caches[li], h, pos_start, dev_pos=dev_pos)
                 x = x + attn.to(x.dtype)
                 x = x + blk.mlp(blk.norm2(x))
-            return m.norm(x), states, kv_caches
+            return m.norm(x)
+
+    def _advance(self, t: int, pos_start: int, states, kv_caches) -> None:
+        """Host bookkeeping of a step whose kernels ran without it (a CUDA-graph replay)."""
+        for li, blk in enumerate(self.model.blocks):
+            if hasattr(blk, "vsa"):
+                self._layer_advance(blk.vsa, kv_caches[li], t, pos_start, states[li])
+            else:
+                kv_caches[li].n += t
+
+    def graphs_supported(self, device) -> bool:
+        """One-token steps may be replayed from CUDA graphs on this device: a CUDA model whose
+        parameters and buffers (the RoPE frequencies among them) all live on that device."""
+        device = torch.device(device)
+        if not (self.use_cuda_graphs and device.type == "cuda"):
+            return False
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        return all(t.device.type == "cuda" and t.device.index == idx
+                   for t in list(self.model.parameters()) + list(self.model.buffers()))
+
+    def step_graph(self, states, kv_caches) -> "DecodeGraph":
+        """A runner of one-token steps on (states, kv_caches) replayed from CUDA graphs (one capture
+        per chunk of C positions); results equal step()'s."""
+        return DecodeGraph(self, states, kv_caches)
 
     def _feed(self, ids: torch.Tensor, pos: int, states, kv_caches):
         """Run a prompt through step() in C-token slices from position `pos`; returns the last
@@ -889,6 +967,7 @@ class Bolt3Decoder:
             closed = torch.zeros(B, dtype=torch.bool, device=dev)
             trigger = max(64, max_new_tokens - 64)
         toks = []
+        runner = self.step_graph(states, kv) if self.graphs_supported(dev) else None
         for i in range(max_new_tokens):
             nxt = self._sample(logits, temperature, top_k=top_k, top_p=top_p)
             if forced is not None:
@@ -909,7 +988,10 @@ class Bolt3Decoder:
                 finished = finished | newly
                 if i % 16 == 15 and bool(finished.all()):
                     break
-            h, states, kv = self.step(nxt, T + i, states, kv)
+            if runner is not None:
+                h = runner.step(nxt, T + i)
+            else:
+                h, states, kv = self.step(nxt, T + i, states, kv)
             logits = self.model.lm_head(h[:, -1, :])
         return torch.cat(toks, dim=1), lengths
 
@@ -930,12 +1012,16 @@ class Bolt3Decoder:
         h, pos = self._feed(ids, start_pos, states, kv_caches)
         logits = self.model.lm_head(h[:, -1, :])
         toks = []
+        runner = self.step_graph(states, kv_caches) if self.graphs_supported(ids.device) else None
         for _ in range(max_new_tokens):
             nxt = self._sample(logits, temperature, top_k=top_k, top_p=top_p)
             toks.append(nxt)
             if eos_ids and int(nxt[0, 0]) in eos_ids:
                 break
-            h, states, kv_caches = self.step(nxt, pos, states, kv_caches)
+            if runner is not None:
+                h = runner.step(nxt, pos)
+            else:
+                h, states, kv_caches = self.step(nxt, pos, states, kv_caches)
             logits = self.model.lm_head(h[:, -1, :])
             pos += 1
         out = torch.cat(toks, dim=1) if toks else torch.empty(ids.shape[0], 0, dtype=torch.long, device=ids.device)
@@ -998,9 +1084,8 @@ class AnchorKV:
     def capacity(self) -> int:
         return self.buf.shape[3]
 
-    def append(self, k_new: torch.Tensor, v_new: torch.Tensor):
-        """Write L new keys/values [B, HKV, L, HD] after the held ones; returns views of all n."""
-        L = k_new.shape[2]
+    def reserve(self, L: int) -> None:
+        """Room for L more tokens: the capacity doubles (one copy of the held tokens) until they fit."""
         if self.n + L > self.capacity:
             cap = self.capacity
             while cap < self.n + L:
@@ -1009,14 +1094,94 @@ class AnchorKV:
                                 dtype=self.buf.dtype)
             grown[:, :, :, :self.n].copy_(self.buf[:, :, :, :self.n])
             self.buf = grown
+
+    def append(self, k_new: torch.Tensor, v_new: torch.Tensor):
+        """Write L new keys/values [B, HKV, L, HD] after the held ones; returns views of all n."""
+        L = k_new.shape[2]
+        self.reserve(L)
         self.buf[0, :, :, self.n:self.n + L].copy_(k_new)
         self.buf[1, :, :, self.n:self.n + L].copy_(v_new)
         self.n += L
         return self.buf[0, :, :, :self.n], self.buf[1, :, :, :self.n]
 
 
-# scaled-dot-product-attention backends of the softmax anchors' decode steps
-_ANCHOR_SDPA = [SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]
+class DecodeGraph:
+    """One-token decode steps of a Bolt3Decoder (or Bolt3DecoderTP) replayed from CUDA graphs.
+
+    A step of the hybrid model is hundreds of kernel launches (36 layers of norms, GEMMs, the Bolt-3
+    prep / attention / o_proj, the anchors' attention, the MLP), more host time than GPU time at
+    decode sizes. Every launch of a one-token step inside one chunk is the same except for the
+    token position, which the kernels read from the device (K.DevicePosition): so the step is
+    captured once per chunk (when the window slots change) at its first position and replayed for
+    every later position of the chunk, with only the token ids and the position written before
+    each replay. The chunk-boundary consolidation and the host bookkeeping run eagerly after the
+    replay (Bolt3Decoder._advance), so the results equal step()'s.
+
+    step() returns a static buffer that the next step overwrites."""
+
+    def __init__(self, dec: "Bolt3Decoder", states, kv_caches):
+        self.dec, self.states, self.kv = dec, states, kv_caches
+        bolt = [st for st in kv_caches if isinstance(st, Bolt3LayerState)]
+        anch = [c for c in kv_caches if isinstance(c, AnchorKV)]
+        ref = bolt[0].ring_kp if bolt else anch[0].buf
+        self.device = ref.device
+        self.B = bolt[0].B if bolt else anch[0].buf.shape[1]
+        self.tok = torch.zeros(self.B, 1, dtype=torch.long, device=self.device)
+        self.pos = K.DevicePosition(self.device)
+        self.graph, self.out = None, None
+        self.lo = self.hi = -1            # positions the current graph serves
+        self.next = None                  # the position the host state expects next
+        self.captures = 0
+
+    def _chunk_phase(self) -> int:
+        lens = {st.cur_len for st in self.kv if isinstance(st, Bolt3LayerState)}
+        if len(lens) > 1:
+            raise RuntimeError("the Bolt-3 layers of a decode state are at different chunk phases")
+        return lens.pop() if lens else 0
+
+    def _capture(self, pos: int) -> None:
+        dec = self.dec
+        self.graph = self.out = None      # the previous graph and its private memory are released
+        span = dec.C - self._chunk_phase()
+        # everything the captured launches point at exists before the capture: the layers' step
+        # plans (buffers and fused weights) and anchor caches with room for the whole span
+        for li, blk in enumerate(dec.model.blocks):
+            st = self.kv[li]
+            if hasattr(blk, "vsa"):
+                f = blk.vsa.fused(self.device)
+                plan = st._plans.get(1)
+                if plan is None or plan.key != f.key:
+                    st._plans[1] = Bolt3Decoder._step_plan(blk.vsa, st, self.B, 1, f, self.device)
+            else:
+                st.reserve(span)
+        self.pos.ref, self.pos.span = pos, span
+        self.pos.set(pos)
+        if self.captures == 0:
+            # first capture: one eager run of the same launches initialises the libraries' lazy state
+            # (it rewrites exactly what the replay below writes: this step's window row and cache row)
+            dec._blocks(self.tok, pos, self.states, self.kv, dev_pos=self.pos)
+        torch.cuda.current_stream().synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.out = dec._blocks(self.tok, pos, self.states, self.kv, dev_pos=self.pos)
+        self.graph, self.lo, self.hi = g, pos, pos + span
+        self.captures += 1
+
+    @torch.no_grad()
+    def step(self, tokens: torch.Tensor, pos: int) -> torch.Tensor:
+        """One token per sequence ([B, 1] ids on the device) at position pos; the final normed hidden
+        states [B, 1, D] (a static buffer)."""
+        if self.next is not None and pos != self.next:
+            raise ValueError(f"decode steps must be consecutive: expected position {self.next}, got {pos}")
+        self.tok.copy_(tokens)
+        if self.graph is None or not (self.lo <= pos < self.hi):
+            self._capture(pos)
+        self.pos.set(pos)
+        self.graph.replay()
+        self.dec._advance(1, pos, self.states, self.kv)
+        self.next = pos + 1
+        return self.out
+
 
 # the reference's name for the anchor-layer cache class (vsa_lm/decode.py:88)
 StaticKV = AnchorKV

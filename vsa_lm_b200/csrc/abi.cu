@@ -35,6 +35,17 @@ SnapLayout snap_layout(int n_chains, int64_t T, int HD) {
 
 extern "C" int bolt3_abi_version(void) { return BOLT3_ABI_VERSION; }
 
+extern "C" size_t bolt3_args_size(int which) {
+  switch (which) {
+    case 0: return sizeof(bolt3_prep_args);
+    case 1: return sizeof(bolt3_consolidate_args);
+    case 2: return sizeof(bolt3_attend_args);
+    case 3: return sizeof(bolt3_prefill_args);
+    case 4: return sizeof(bolt3_anchor_args);
+    default: return 0;
+  }
+}
+
 extern "C" const char* bolt3_status_string(int st) {
   switch (st) {
     case BOLT3_OK: return "ok";

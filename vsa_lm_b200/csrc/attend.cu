@@ -658,12 +658,18 @@ extern "C" int bolt3_attend(const bolt3_attend_args* a, void* stream) {
                     !a->bank_act || !a->bank_m))
     return BOLT3_ERR_ARG;
   if (!a->prefill) {
-    if (a->Tq > 128 || a->seg0_len < 0 || a->seg0_len > CC || a->seg1_len <= 0 || a->seg1_len > CC ||
+    // with a device step position, every size must hold for the largest shift as well
+    const int64_t dmax = a->pos_dev != nullptr ? a->pos_span - 1 : 0;
+    if (a->Tq > 128 || a->seg0_len < 0 || a->seg0_len > CC || a->seg1_len <= 0 || a->seg1_len + dmax > CC ||
         a->len_before < 0 || a->len_before + a->Tq != a->seg1_len)
       return BOLT3_ERR_SHAPE;
     if (a->has_sinks && (!a->sink_k || !a->sink_v)) return BOLT3_ERR_ARG;
+    // only the decode kernels (at most 16 query rows per chain) read a device step position
+    if (a->pos_dev != nullptr && (a->pos_span < 1 || (int64_t)a->G * a->Tq > 16)) return BOLT3_ERR_ARG;
   } else if (a->seg0_chain_tokens < a->Tq) {
     return BOLT3_ERR_CAPACITY;
+  } else if (a->pos_dev != nullptr) {
+    return BOLT3_ERR_ARG;
   }
   const uintptr_t al = (uintptr_t)a->q_rope | (uintptr_t)a->q_raw | (uintptr_t)a->seg0_k | (uintptr_t)a->seg0_v |
                        (uintptr_t)a->seg1_k | (uintptr_t)a->seg1_v | (uintptr_t)a->sink_k |

@@ -60,7 +60,17 @@ __global__ void __launch_bounds__(32 * warps_per_cta<NRM>()) attend_decode_kerne
   const int G = a.G, T = (int)a.Tq, NR = G * T, H = a.hkv * G;
   const bool has_sinks = a.has_sinks != 0, has_bank = a.has_bank != 0;
   const int n_sk = has_sinks ? 4 : 0, n_at = has_bank ? S : 0;
-  const int L0 = a.seg0_len, L1 = a.seg1_len;
+  // device step position: segment 1 holds d more keys, all visible d positions later
+  int dpos = 0;
+  if (a.pos_dev != nullptr) {
+    const int64_t d = *a.pos_dev - a.pos_ref;
+    if (d < 0 || d >= a.pos_span) {
+      if (lane == 0 && a.status) atomicOr(a.status, 8);
+      return;
+    }
+    dpos = (int)d;
+  }
+  const int L0 = a.seg0_len, L1 = a.seg1_len + dpos, len_before = a.len_before + dpos;
   const int L = n_sk + n_at + L0 + L1;
 
   const int64_t bofs = (int64_t)c * a.bank_cap;
@@ -154,7 +164,7 @@ __global__ void __launch_bounds__(32 * warps_per_cta<NRM>()) attend_decode_kerne
       const int i = r % T;  // the row's new token
       float s2 = __fmul_rn(acc[r], scale);
       if (seg == 1) s2 = __fadd_rn(s2, bias);
-      if (seg == 3 && j > a.len_before + i) s2 = neg_inf();
+      if (seg == 3 && j > len_before + i) s2 = neg_inf();
       sc[r * kLP + k] = s2;
     }
   }
@@ -434,7 +444,19 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
   }
   const int G = a.G, T = (int)a.Tq, NR = G * T, H = a.hkv * G;
   const bool has_bank = a.has_bank != 0, has_sinks = a.has_sinks != 0;
-  const int len[4] = {has_sinks ? 4 : 0, has_bank ? S : 0, a.seg0_len, a.seg1_len};
+  // device step position (written before the step's first kernel ran): segment 1 holds d more keys,
+  // all visible d positions later; out of range, the CTA reports it and does nothing
+  int dpos = 0;
+  if (a.pos_dev != nullptr) {
+    const int64_t d = *a.pos_dev - a.pos_ref;
+    if (d < 0 || d >= a.pos_span) {
+      if (tid == 0 && a.status) atomicOr(a.status, 8);
+      return;
+    }
+    dpos = (int)d;
+  }
+  const int len_before = a.len_before + dpos;
+  const int len[4] = {has_sinks ? 4 : 0, has_bank ? S : 0, a.seg0_len, a.seg1_len + dpos};
   // the segments that travel as ring pieces (the sinks travel in the R piece)
   int n_kv = 0, kv_list[3];
 #pragma unroll
@@ -713,7 +735,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) attend_stream_kernel(con
           if (r >= NR) continue;
           float s2 = __fmul_rn(__uint_as_float(v[sg][r]), scale);
           if (sg == 1) s2 = __fadd_rn(s2, sm.bias[bi][kq]);
-          if (sg == 3 && kq > a.len_before + r % T) s2 = neg_inf();
+          if (sg == 3 && kq > len_before + r % T) s2 = neg_inf();
           sv[sg][u] = s2;
           mx[u] = fmaxf(mx[u], s2);
         }
@@ -857,7 +879,10 @@ int launch(const bolt3_attend_args* a, cudaStream_t s) {
   if (!b3_encode_bf16_rows(&m.q, a->q_rope, HD, NR, NR, nc, 16)) return -1;
   const void* kb[4] = {a->sink_k, a->bank_ak_rope, a->seg0_k, a->seg1_k};
   const void* vb[4] = {a->sink_v, a->bank_av, a->seg0_v, a->seg1_v};
-  const int64_t rows[4] = {4, S, a->seg0_len, a->seg1_len};
+  // segment 1's map covers the longest window a device step position allows (rows past the current
+  // length are read and masked)
+  const int64_t dmax = a->pos_dev != nullptr ? a->pos_span - 1 : 0;
+  const int64_t rows[4] = {4, S, a->seg0_len, a->seg1_len + dmax};
   const int64_t stride[4] = {a->sink_chain_tokens, S, a->seg0_chain_tokens, a->seg1_chain_tokens};
   const int64_t slices[4] = {nc, nc * a->bank_cap, nc, nc};
   const bool on[4] = {a->has_sinks != 0, a->has_bank != 0, a->seg0_len > 0, a->seg1_len > 0};
@@ -895,7 +920,10 @@ int launch(const bolt3_attend_args* a, cudaStream_t s) {
 // Launch for bolt3_attend (prefill = 0, G * Tq <= 16); returns a bolt3 status.
 int b3_attend_decode_launch(const bolt3_attend_args* a, cudaStream_t s) {
   const int NR = a->G * (int)a->Tq;
-  if (NR > 16 || a->seg0_len + a->seg1_len > 256) return BOLT3_ERR_SHAPE;
+  if (a->pos_dev != nullptr && a->pos_span < 1) return BOLT3_ERR_ARG;
+  const int64_t dmax = a->pos_dev != nullptr ? a->pos_span - 1 : 0;
+  if (NR > 16 || a->seg0_len + a->seg1_len + dmax > 256 || a->seg1_len + dmax > a->seg1_chain_tokens)
+    return BOLT3_ERR_SHAPE;
   // HD = 128 with up to four query rows: the tensor-core streaming kernel, when its bulk copies'
   // alignment holds (the tensor maps are checked as they are encoded; a map that cannot be encoded
   // selects the warp-per-chain kernel below)

@@ -45,6 +45,14 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
   // the attention kernel that follows a decode step's prep may start its set-up now (it waits for
   // this grid's completion before it reads any of its outputs)
   grid_dep_launch();
+  // device step position (a step replayed from a CUDA graph): shift the RoPE position and the k/v
+  // write offset by d; a d outside the range the launch was checked for skips the step
+  int64_t dpos = 0;
+  if (a.pos_dev != nullptr) {
+    dpos = *a.pos_dev - a.pos_ref;
+    if (dpos < 0 || dpos >= a.pos_span) return;
+  }
+  const int64_t k_t_off = a.k_t_off + dpos, beta_t_off = a.beta_t_off + dpos;
 
   // bf16 cos/sin of the HD/2 frequencies for each of the block's tokens, shared by all their
   // heads, stored as pairs of adjacent frequencies (the operands of the packed RoPE below)
@@ -57,7 +65,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
   }
   for (int i = threadIdx.x; i < ntb * (HD / 4); i += blockDim.x) {
     const int tl = i / (HD / 4), fp = i % (HD / 4);
-    const float pos = (float)(a.pos0 + (tok0 + tl) % a.T);
+    const float pos = (float)(a.pos0 + dpos + (tok0 + tl) % a.T);
     float s0, c0, s1, c1;
     sincosf(__fmul_rn(pos, a.inv_freq[2 * fp]), &s0, &c0);
     sincosf(__fmul_rn(pos, a.inv_freq[2 * fp + 1]), &s1, &c1);
@@ -120,7 +128,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
     }
     const int nh = kind == 0 ? a.H : a.HKV;
     const int64_t hs = kind == 0 ? a.q_head_stride : a.k_head_stride;
-    const int64_t to = kind == 0 ? a.q_t_off : a.k_t_off;
+    const int64_t to = kind == 0 ? a.q_t_off : k_t_off;
     const int64_t off = (((int64_t)b * nh + head) * hs + to + t) * HD + l * 8;
     // per-row reductions stay inside the LPR lanes of the row
     auto row_sum = [&](float v) {
@@ -211,7 +219,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
     const bf16* row = reinterpret_cast<const bf16*>(a.proj) + tok * a.ld;
     if (do_kv && gi < a.HKV) {
       const float z = bf2f(row[a.beta_col + gi]);
-      a.beta[((int64_t)b * a.HKV + gi) * a.beta_head_stride + a.beta_t_off + t] = rbf(1.0f / (1.0f + expf(-z)));
+      a.beta[((int64_t)b * a.HKV + gi) * a.beta_head_stride + beta_t_off + t] = rbf(1.0f / (1.0f + expf(-z)));
     } else {
       const int h = gi - (do_kv ? a.HKV : 0);
       const float z = bf2f(row[a.eta_col + h]);
@@ -237,7 +245,9 @@ extern "C" int bolt3_prep(const bolt3_prep_args* a, void* stream) {
     return BOLT3_ERR_CAPACITY;
   if ((a->parts & 1) && (a->q_head_stride < a->q_t_off + a->T || a->eta_head_stride < a->eta_t_off + a->T))
     return BOLT3_ERR_CAPACITY;
-  if ((a->parts & 2) && (a->k_head_stride < a->k_t_off + a->T || a->beta_head_stride < a->beta_t_off + a->T))
+  if (a->pos_dev != nullptr && a->pos_span < 1) return BOLT3_ERR_ARG;
+  const int64_t dmax = a->pos_dev != nullptr ? a->pos_span - 1 : 0;  // largest device step shift
+  if ((a->parts & 2) && (a->k_head_stride < a->k_t_off + dmax + a->T || a->beta_head_stride < a->beta_t_off + dmax + a->T))
     return BOLT3_ERR_CAPACITY;
   // 16-byte vector access: rows of proj, and every output row, start on 16-byte boundaries
   const uintptr_t al = (uintptr_t)a->proj |

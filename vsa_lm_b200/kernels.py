@@ -306,23 +306,72 @@ class DecodeStepArgs:
         self.prep = _lib.PrepArgs(**prep_fields)
         self.attend = _lib.AttendArgs(**attend_fields)
 
-    def launch_prep(self, proj: torch.Tensor, pos0: int, k_t_off: int) -> None:
+    def launch_prep(self, proj: torch.Tensor, pos0: int, k_t_off: int, dev_pos: "DevicePosition | None" = None) -> None:
         a = self.prep
         _need(proj, torch.bfloat16, "proj", a.B * a.T * a.ld)
         if proj.stride(0) != a.ld:
             raise ValueError("proj must be a contiguous [tokens, ld] projection output")
         a.proj, a.pos0, a.k_t_off, a.beta_t_off = proj.data_ptr(), pos0, k_t_off, k_t_off
+        _set_dev_pos(a, dev_pos)
         _lib.check(self.lib.bolt3_prep(ctypes.byref(a), _stream()), "bolt3_prep")
         _count(1)
 
     def launch_attend(self, *, seg0_k: int, seg0_v: int, seg0_len: int, seg1_k: int, seg1_v: int,
-                      seg1_len: int, len_before: int, has_sinks: bool, has_bank: bool, bank_m: int) -> None:
+                      seg1_len: int, len_before: int, has_sinks: bool, has_bank: bool, bank_m: int,
+                      dev_pos: "DevicePosition | None" = None) -> None:
         a = self.attend
         a.seg0_k, a.seg0_v, a.seg0_len = seg0_k, seg0_v, seg0_len
         a.seg1_k, a.seg1_v, a.seg1_len, a.len_before = seg1_k, seg1_v, seg1_len, len_before
         a.has_sinks, a.has_bank, a.bank_m = int(has_sinks), int(has_bank), bank_m
+        _set_dev_pos(a, dev_pos)
         _lib.check(self.lib.bolt3_attend(ctypes.byref(a), _stream()), "bolt3_attend")
         _count(1)
+
+
+class DevicePosition:
+    """The device step position of a decode step replayed from a CUDA graph: an int64 on the device
+    that holds the step's token position, the position the launches were built for (`ref`), and how
+    many positions after it the launches stay valid for (`span`). Kernels shift the RoPE position,
+    the window write offset and the window length by (*word - ref)."""
+
+    def __init__(self, device):
+        self.word = torch.zeros(1, dtype=torch.int64, device=device)
+        self.ref, self.span = 0, 1
+
+    def set(self, pos: int) -> None:
+        """Stream-ordered write of the next step's position (a fill kernel, nothing waits)."""
+        self.word.fill_(pos)
+
+
+def _set_dev_pos(a, dev_pos: "DevicePosition | None") -> None:
+    if dev_pos is None:
+        a.pos_dev, a.pos_ref, a.pos_span = None, 0, 0
+    else:
+        a.pos_dev, a.pos_ref, a.pos_span = dev_pos.word.data_ptr(), dev_pos.ref, dev_pos.span
+
+
+def anchor_decode(*, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor,
+                  v_cache: torch.Tensor, n: int, y: torch.Tensor, scale: float, status=None,
+                  dev_pos: DevicePosition | None = None) -> None:
+    """bolt3_anchor_decode: append k_new / v_new [B, HKV, HD] at cache position n (n + the device
+    shift with dev_pos) of k_cache / v_cache [B, HKV, cap, HD] and write the one-token GQA attention
+    of q [B, H, HD] over positions 0..n to y [B, H, HD] (all bf16)."""
+    B, H, HD = q.shape
+    HKV, cap = k_cache.shape[1], k_cache.shape[2]
+    _need(q, torch.bfloat16, "q", B * H * HD)
+    _need(y, torch.bfloat16, "y", B * H * HD)
+    for t, name in ((k_new, "k_new"), (v_new, "v_new")):
+        _need(t, torch.bfloat16, name, B * HKV * HD)
+    for t, name in ((k_cache, "k_cache"), (v_cache, "v_cache")):
+        _need(t, torch.bfloat16, name, B * HKV * cap * HD)
+    if tuple(k_cache.shape) != (B, HKV, cap, HD) or tuple(v_cache.shape) != (B, HKV, cap, HD):
+        raise ValueError(f"caches must be [B, HKV, cap, HD] = [{B}, {HKV}, {cap}, {HD}]")
+    a = _lib.AnchorArgs(B=B, H=H, HKV=HKV, HD=HD, q=q.data_ptr(), k_new=k_new.data_ptr(), v_new=v_new.data_ptr(),
+                        k_cache=k_cache.data_ptr(), v_cache=v_cache.data_ptr(), cap=cap, n=n, y=y.data_ptr(),
+                        scale=scale, status=_status(status))
+    _set_dev_pos(a, dev_pos)
+    _lib.check(_lib.load().bolt3_anchor_decode(ctypes.byref(a), _stream()), "bolt3_anchor_decode")
+    _count(1)
 
 
 def prefill_workspace_bytes(n_chains: int, T: int, HD: int) -> int:

@@ -249,20 +249,31 @@ class Bolt3DecoderTP(Bolt3Decoder):
             raise TypeError("Bolt3DecoderTP drives a Bolt3LMTP")
         super().__init__(model, **kwargs)
 
-    @torch.no_grad()
-    def step(self, tokens: torch.Tensor, pos_start: int, states, kv_caches, record=None):
+    def _blocks(self, tokens: torch.Tensor, pos_start: int, states, kv_caches, dev_pos=None) -> torch.Tensor:
         m = self.model
         with torch.autocast("cuda", torch.bfloat16, enabled=tokens.is_cuda):
             x = m.embed_tokens(tokens)
             for li, blk in enumerate(m.blocks):
                 h = blk.norm1(x)
                 if hasattr(blk, "vsa"):
-                    part = self.layer_step(blk.vsa, kv_caches[li], h, pos_start, states[li], partial_fp32=True)
+                    if dev_pos is None:
+                        part = self.layer_step(blk.vsa, kv_caches[li], h, pos_start, states[li], partial_fp32=True)
+                    else:
+                        part = self._layer_launch(blk.vsa, kv_caches[li], h, pos_start, states[li],
+                                                  partial_fp32=True, dev_pos=dev_pos)
                 else:
-                    part = self._anchor_attention(blk.attn, kv_caches[li], h, pos_start, partial_fp32=True)
+                    part = self._anchor_attention(blk.attn, kv_caches[li], h, pos_start, partial_fp32=True,
+                                                  dev_pos=dev_pos)
                 x = x + m.reduce(part, x.dtype)
                 x = x + m.reduce(mlp_partial(blk.mlp, blk.norm2(x)), x.dtype)
-            return m.norm(x), states, kv_caches
+            return m.norm(x)
+
+    def graphs_supported(self, device) -> bool:
+        """CUDA graphs capture NCCL collectives; a gloo group's all-reduces run on the host."""
+        m = self.model
+        if m.world > 1 and dist.get_backend(m.group) != "nccl":
+            return False
+        return super().graphs_supported(device)
 
     def _sample(self, logits, temperature: float, top_k: int = 40, top_p: float = 0.95):
         nxt = Bolt3Decoder._sample(logits, temperature, top_k=top_k, top_p=top_p)

@@ -111,6 +111,10 @@ MODEL_SHAPES = {
     "tiny_lm": dict(vocab_size=512, dim=256, num_layers=3, num_heads=4, num_kv_heads=2, head_dim=64,
                     intermediate=512, hybrid_every=3, rope_theta=1e4, eps=1e-5, qk_norm=False,
                     tie_word_embeddings=False),
+    # head_dim 128 with qk_norm (the one-token streaming attention kernel), three Bolt-3 layers and an anchor
+    "small_lm": dict(vocab_size=1024, dim=512, num_layers=4, num_heads=8, num_kv_heads=2, head_dim=128,
+                     intermediate=1024, hybrid_every=4, rope_theta=1e6, eps=1e-6, qk_norm=True,
+                     tie_word_embeddings=True),
     # the Qwen3-4B architecture as a hybrid (27 Bolt-3 layers, 9 softmax anchors)
     "qwen3_4b_lm": dict(vocab_size=151936, dim=2560, num_layers=36, num_heads=32, num_kv_heads=8, head_dim=128,
                         intermediate=9728, hybrid_every=4, rope_theta=1e6, eps=1e-6, qk_norm=True,
