@@ -1105,82 +1105,105 @@ class AnchorKV:
         return self.buf[0, :, :, :self.n], self.buf[1, :, :, :self.n]
 
 
-class DecodeGraph:
-    """One-token decode steps of a Bolt3Decoder (or Bolt3DecoderTP) replayed from CUDA graphs.
+class _ChunkGraph:
+    """A one-token decode step captured into a CUDA graph at the first position it serves and
+    replayed for every later position of the same chunk. Every launch of such a step is the same
+    within a chunk except for the token position, which the kernels read from the device
+    (K.DevicePosition); a new chunk (the window slots change) takes a new capture. The host
+    bookkeeping, and a chunk boundary's consolidation, run eagerly after each replay. Subclasses
+    give the step's body, what it needs allocated before a capture, and its bookkeeping."""
 
-    A step of the hybrid model is hundreds of kernel launches (36 layers of norms, GEMMs, the Bolt-3
-    prep / attention / o_proj, the anchors' attention, the MLP), more host time than GPU time at
-    decode sizes. Every launch of a one-token step inside one chunk is the same except for the
-    token position, which the kernels read from the device (K.DevicePosition): so the step is
-    captured once per chunk (when the window slots change) at its first position and replayed for
-    every later position of the chunk, with only the token ids and the position written before
-    each replay. The chunk-boundary consolidation and the host bookkeeping run eagerly after the
-    replay (Bolt3Decoder._advance), so the results equal step()'s.
-
-    step() returns a static buffer that the next step overwrites."""
-
-    def __init__(self, dec: "Bolt3Decoder", states, kv_caches):
-        self.dec, self.states, self.kv = dec, states, kv_caches
-        bolt = [st for st in kv_caches if isinstance(st, Bolt3LayerState)]
-        anch = [c for c in kv_caches if isinstance(c, AnchorKV)]
-        ref = bolt[0].ring_kp if bolt else anch[0].buf
-        self.device = ref.device
-        self.B = bolt[0].B if bolt else anch[0].buf.shape[1]
-        self.tok = torch.zeros(self.B, 1, dtype=torch.long, device=self.device)
+    def __init__(self, device, C: int):
+        self.device, self.C = torch.device(device), C
         self.pos = K.DevicePosition(self.device)
         self.graph, self.out = None, None
         self.lo = self.hi = -1            # positions the current graph serves
         self.next = None                  # the position the host state expects next
         self.captures = 0
 
-    def _chunk_phase(self) -> int:
+    def _phase(self) -> int: ...
+    def _prepare(self, span: int) -> None: ...
+    def _body(self, pos: int) -> torch.Tensor: ...
+    def _advance(self, pos: int) -> None: ...
+
+    def _capture(self, pos: int) -> None:
+        self.graph = self.out = None      # the previous graph and its private memory are released
+        span = self.C - self._phase()
+        self._prepare(span)               # everything the captured launches point at exists first
+        self.pos.ref, self.pos.span = pos, span
+        self.pos.set(pos)
+        if self.captures == 0:
+            # first capture: one eager run of the same launches initialises the libraries' lazy state
+            # (it rewrites exactly what the replay below writes: this step's window and cache rows)
+            self._body(pos)
+        torch.cuda.current_stream().synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.out = self._body(pos)
+        self.graph, self.lo, self.hi = g, pos, pos + span
+        self.captures += 1
+
+    def _replay(self, pos: int) -> torch.Tensor:
+        if self.next is not None and pos != self.next:
+            raise ValueError(f"decode steps must be consecutive: expected position {self.next}, got {pos}")
+        if self.graph is None or not (self.lo <= pos < self.hi):
+            self._capture(pos)
+        self.pos.set(pos)
+        self.graph.replay()
+        self._advance(pos)
+        self.next = pos + 1
+        return self.out
+
+
+def _ensure_step_plan(ly: Bolt3Attn, st: Bolt3LayerState, device) -> None:
+    f = ly.fused(device)
+    plan = st._plans.get(1)
+    if plan is None or plan.key != f.key:
+        st._plans[1] = Bolt3Decoder._step_plan(ly, st, st.B, 1, f, device)
+
+
+class DecodeGraph(_ChunkGraph):
+    """One-token decode steps of a Bolt3Decoder (or Bolt3DecoderTP) replayed from CUDA graphs.
+
+    A step of the hybrid model is hundreds of kernel launches (36 layers of norms, GEMMs, the Bolt-3
+    prep / attention / o_proj, the anchors' attention, the MLP), more host time than GPU time at
+    decode sizes; replayed, the step costs the host one graph launch. Results equal step()'s.
+    step() returns a static buffer that the next step overwrites."""
+
+    def __init__(self, dec: "Bolt3Decoder", states, kv_caches):
+        bolt = [st for st in kv_caches if isinstance(st, Bolt3LayerState)]
+        anch = [c for c in kv_caches if isinstance(c, AnchorKV)]
+        ref = bolt[0].ring_kp if bolt else anch[0].buf
+        super().__init__(ref.device, dec.C)
+        self.dec, self.states, self.kv = dec, states, kv_caches
+        self.B = bolt[0].B if bolt else anch[0].buf.shape[1]
+        self.tok = torch.zeros(self.B, 1, dtype=torch.long, device=self.device)
+
+    def _phase(self) -> int:
         lens = {st.cur_len for st in self.kv if isinstance(st, Bolt3LayerState)}
         if len(lens) > 1:
             raise RuntimeError("the Bolt-3 layers of a decode state are at different chunk phases")
         return lens.pop() if lens else 0
 
-    def _capture(self, pos: int) -> None:
-        dec = self.dec
-        self.graph = self.out = None      # the previous graph and its private memory are released
-        span = dec.C - self._chunk_phase()
-        # everything the captured launches point at exists before the capture: the layers' step
-        # plans (buffers and fused weights) and anchor caches with room for the whole span
-        for li, blk in enumerate(dec.model.blocks):
-            st = self.kv[li]
+    def _prepare(self, span: int) -> None:
+        for li, blk in enumerate(self.dec.model.blocks):
             if hasattr(blk, "vsa"):
-                f = blk.vsa.fused(self.device)
-                plan = st._plans.get(1)
-                if plan is None or plan.key != f.key:
-                    st._plans[1] = Bolt3Decoder._step_plan(blk.vsa, st, self.B, 1, f, self.device)
+                _ensure_step_plan(blk.vsa, self.kv[li], self.device)
             else:
-                st.reserve(span)
-        self.pos.ref, self.pos.span = pos, span
-        self.pos.set(pos)
-        if self.captures == 0:
-            # first capture: one eager run of the same launches initialises the libraries' lazy state
-            # (it rewrites exactly what the replay below writes: this step's window row and cache row)
-            dec._blocks(self.tok, pos, self.states, self.kv, dev_pos=self.pos)
-        torch.cuda.current_stream().synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            self.out = dec._blocks(self.tok, pos, self.states, self.kv, dev_pos=self.pos)
-        self.graph, self.lo, self.hi = g, pos, pos + span
-        self.captures += 1
+                self.kv[li].reserve(span)
+
+    def _body(self, pos: int) -> torch.Tensor:
+        return self.dec._blocks(self.tok, pos, self.states, self.kv, dev_pos=self.pos)
+
+    def _advance(self, pos: int) -> None:
+        self.dec._advance(1, pos, self.states, self.kv)
 
     @torch.no_grad()
     def step(self, tokens: torch.Tensor, pos: int) -> torch.Tensor:
         """One token per sequence ([B, 1] ids on the device) at position pos; the final normed hidden
         states [B, 1, D] (a static buffer)."""
-        if self.next is not None and pos != self.next:
-            raise ValueError(f"decode steps must be consecutive: expected position {self.next}, got {pos}")
         self.tok.copy_(tokens)
-        if self.graph is None or not (self.lo <= pos < self.hi):
-            self._capture(pos)
-        self.pos.set(pos)
-        self.graph.replay()
-        self.dec._advance(1, pos, self.states, self.kv)
-        self.next = pos + 1
-        return self.out
+        return self._replay(pos)
 
 
 # the reference's name for the anchor-layer cache class (vsa_lm/decode.py:88)
