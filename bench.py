@@ -129,18 +129,19 @@ def timed(fn, steps: int, warmup: int, world: int, stream=None):
 def timed_e2e(m, xh, yh, dev, steps: int, warmup: int, world: int) -> float:
     """Seconds (max over ranks) for `steps` forwards through the public module, each with its input
     copied host -> device and its output device -> host inside the timed region. Copies run on their
-    own streams with two device input buffers, so step i's upload and step i-1's download overlap
-    step i's compute."""
+    own streams with three device input buffers, so uploads, the forward and downloads of
+    neighbouring steps overlap (the two PCIe directions run concurrently)."""
     main = torch.cuda.current_stream()
     h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
-    xd = [torch.empty(xh.shape, dtype=xh.dtype, device=dev) for _ in range(2)]
-    freed = [torch.cuda.Event() for _ in range(2)]   # compute has finished reading xd[slot]
+    n_buf = 3
+    xd = [torch.empty(xh.shape, dtype=xh.dtype, device=dev) for _ in range(n_buf)]
+    freed = [torch.cuda.Event() for _ in range(n_buf)]   # compute has finished reading xd[slot]
     for ev in freed:
         ev.record(main)
 
     def run(n):
         for i in range(n):
-            slot = i % 2
+            slot = i % n_buf
             with torch.cuda.stream(h2d):
                 h2d.wait_event(freed[slot])
                 xd[slot].copy_(xh, non_blocking=True)
@@ -153,7 +154,7 @@ def timed_e2e(m, xh, yh, dev, steps: int, warmup: int, world: int) -> float:
             done.record(main)
             with torch.cuda.stream(d2h):
                 d2h.wait_event(done)
-                yh[slot].copy_(y, non_blocking=True)
+                yh[i % len(yh)].copy_(y, non_blocking=True)
                 y.record_stream(d2h)
         main.wait_stream(d2h)
 
@@ -319,7 +320,7 @@ def run_native(args, rank, world, local):
     # and its output back to pinned host memory, pipelined as a serving host would run it
     xh = x.cpu().pin_memory()
     yh = [torch.empty(B, T, D, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    e2e_steps = max(12, args.steps)  # pipeline fill and drain amortised over the steps
+    e2e_steps = max(48, args.steps)  # pipeline fill and drain (one upload, one download) amortised
     t_e2e = timed_e2e(m, xh, yh, dev, e2e_steps, max(1, args.warmup), world)
     e2e_value = world * tok * e2e_steps / t_e2e
 
@@ -353,7 +354,7 @@ def run_native(args, rank, world, local):
         "phases": phase_rl,
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": xh.numel() * 2,
                 "d2h_bytes_per_step": yh[0].numel() * 2, "steps": e2e_steps,
-                "pipelining": "per-step copies on two copy streams, two device input buffers"},
+                "pipelining": "per-step copies on two copy streams, three device input buffers"},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
         "decode": decode,
@@ -501,6 +502,37 @@ def run_full_model(args, rank, world, dev):
             "prefill": {"value": B * T / t_pre, "unit": "tok/s", "ms": t_pre * 1e3},
             "decode": {"value": B * n_new / t_dec, "unit": "tok/s", "ms_per_step": t_dec / n_new * 1e3,
                        "steps": n_new, "sequences": B, "cuda_graphs": graphs, "graph_captures": captures[0]}}
+
+
+def run_anchor(args, dev, hbm):
+    """The softmax anchors' one-token attention (bolt3_anchor_decode) at configs[3]'s decode shape:
+    64 sequences x 8 KV heads x 4 query heads, HD 128, 2200 cached tokens (the middle of the 256
+    decode steps after a 2048-token prompt). L2 is flushed before every timed launch."""
+    from vsa_lm_b200 import kernels as K
+
+    B, HKV, G, HD, n, cap = FULL_B, 8, 4, 128, 2200, 2368
+    g = torch.Generator(device=dev).manual_seed(11)
+    mk = lambda *shape: torch.randn(*shape, generator=g, device=dev).to(torch.bfloat16)
+    q, kn, vn = mk(B, HKV * G, HD), mk(B, HKV, HD), mk(B, HKV, HD)
+    kc, vc = mk(B, HKV, cap, HD), mk(B, HKV, cap, HD)
+    y = torch.empty_like(q)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    ts = []
+    for i in range(args.warmup + args.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        K.anchor_decode(q=q, k_new=kn, v_new=vn, k_cache=kc, v_cache=vc, n=n, y=y, scale=HD ** -0.5)
+        e1.record()
+        torch.cuda.synchronize()
+        if i >= args.warmup:
+            ts.append(e0.elapsed_time(e1) / 1e3)
+    t = sorted(ts)[len(ts) // 2]
+    nb = B * HKV * (n + 1) * HD * 2 * 2
+    return {"workload": f"configs[3] anchor decode step: {B} sequences x {HKV} KV heads x {G} query heads, HD {HD}, "
+                        f"{n} cached tokens", "us": t * 1e6, "bytes": nb,
+            "roofline": {"bound": "hbm", "achieved": nb / t / 1e9, "peak": hbm, "unit": "GB/s",
+                         "frac": nb / t / 1e9 / hbm}}
 
 
 def run_decode_tp(args, rank, world, dev, m, cfg):
@@ -783,6 +815,8 @@ def main():
     ap.add_argument("--full-model", action="store_true", help="only the configs[3] whole-model leg")
     ap.add_argument("--no-full", action="store_true", help="skip the configs[3] leg of the default line")
     ap.add_argument("--full-new-tokens", type=int, default=FULL_NEW, help="greedy tokens of the configs[3] leg")
+    ap.add_argument("--anchor-only", action="store_true",
+                    help="only the configs[3] softmax anchors' one-token attention kernel (profiling)")
     ap.add_argument("--parity-decode-steps", type=int, default=DEC_STEPS,
                     help="one-token steps of the configs[2] parity sample")
     args = ap.parse_args()
@@ -810,6 +844,10 @@ def main():
             dev = torch.device("cuda", local)
             torch.cuda.set_device(dev)
             res = {"full_model": run_full_model(args, rank, world, dev)}
+        elif args.anchor_only:
+            dev = torch.device("cuda", local)
+            torch.cuda.set_device(dev)
+            res = {"anchor_decode": run_anchor(args, dev, peaks()[0])}
         elif args.decode_only:
             dev = torch.device("cuda", local)
             torch.cuda.set_device(dev)

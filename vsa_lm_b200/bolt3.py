@@ -1136,10 +1136,19 @@ class _ChunkGraph:
             # first capture: one eager run of the same launches initialises the libraries' lazy state
             # (it rewrites exactly what the replay below writes: this step's window and cache rows)
             self._body(pos)
-        torch.cuda.current_stream().synchronize()
+        # captured on a side stream that joins the current one; torch.cuda.graph() would also run a
+        # garbage collection and empty the allocator cache at every capture, once per chunk here
+        main = torch.cuda.current_stream()
+        side = self._side = getattr(self, "_side", None) or torch.cuda.Stream(self.device)
+        side.wait_stream(main)
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            self.out = self._body(pos)
+        with torch.cuda.stream(side):
+            g.capture_begin()
+            try:
+                self.out = self._body(pos)
+            finally:
+                g.capture_end()
+        main.wait_stream(side)
         self.graph, self.lo, self.hi = g, pos, pos + span
         self.captures += 1
 
