@@ -186,15 +186,3 @@ def test_memory_bank_flow_matches_model_oracle():
     _check_greedy([toks[:, i] for i in range(12)], logits, "continue_generate")
     Bolt3Decoder.check_status(kv2)
     ledger.report()
-
-
-def test_step_past_a_chunk_boundary_raises_clearly():
-    """A step that would push the pending chunk past C tokens is refused with a clear error (the
-    native kernels consolidate chunks of exactly C tokens)."""
-    mcfg, model, _ = _models()
-    dec = Bolt3Decoder(model)
-    states, kv = Bolt3Decoder.blank_state(model, 1, "cuda")
-    ids = torch.randint(0, mcfg["vocab_size"], (1, 300), generator=torch.Generator().manual_seed(2)).cuda()
-    dec.step(ids[:, :100], 0, states, kv)
-    with pytest.raises(NotImplementedError, match="split the step"):
-        dec.step(ids[:, 100:200], 100, states, kv)

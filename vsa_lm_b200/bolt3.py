@@ -21,6 +21,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import kernels as K
+from . import oversize
 
 N_SINKS = 4
 
@@ -495,6 +496,9 @@ class Bolt3LayerState:
         self.n_filled = 0
         self._plans = {}   # per step size: buffers and prebuilt launch arguments (Bolt3Decoder)
         self._consts = None  # the layer constants of the last step's plan (its chunk boundary uses them)
+        # a previous chunk of more than C tokens (kr, kp, v, beta, pos0), held outside the ring until
+        # it is consolidated (vsa_lm_b200/oversize.py); None in the common case
+        self.big_prev = None
         # device status word of this state's kernels, checked at every chunk boundary
         self.status = K.DeviceStatus(device)
 
@@ -618,7 +622,15 @@ class Bolt3Decoder:
             p0 = st.slot_pos[slot]
             d[tag + "_pos"] = torch.arange(p0, p0 + n, dtype=torch.float32, device=st.ring_kr.device).view(1, 1, n)
 
-        if st.prev_slot >= 0:
+        if st.big_prev is not None:
+            bp = st.big_prev
+            L = bp["kp"].shape[1]
+            for k in ("kr", "kp", "v"):
+                d["prev_" + k] = bp[k].reshape(B, HKV, L, HD).clone()
+            d["prev_b"] = bp["beta"].reshape(B, HKV, L).to(torch.bfloat16)
+            d["prev_pos"] = torch.arange(bp["pos0"], bp["pos0"] + L, dtype=torch.float32,
+                                         device=bp["kp"].device).view(1, 1, L)
+        elif st.prev_slot >= 0:
             window("prev", st.prev_slot, C)
         if st.cur_len > 0:
             window("cur", st.cur_slot, st.cur_len)
@@ -665,9 +677,16 @@ class Bolt3Decoder:
             return L
 
         if d.get("prev_kp") is not None:
-            if fill("prev", 0) != C:
-                raise NotImplementedError("native decoder state holds a previous chunk of exactly C tokens")
-            st.prev_slot, st.cur_slot = 0, 1
+            L = d["prev_kp"].shape[2]
+            if L == C:
+                fill("prev", 0)
+                st.prev_slot, st.cur_slot = 0, 1
+            else:   # a longer previous chunk stays outside the ring until it is consolidated
+                st.big_prev = dict(kr=d["prev_kr"].reshape(n, L, HD).to(**dev, dtype=torch.bfloat16).contiguous(),
+                                   kp=d["prev_kp"].reshape(n, L, HD).to(**dev, dtype=torch.bfloat16).contiguous(),
+                                   v=d["prev_v"].reshape(n, L, HD).to(**dev, dtype=torch.bfloat16).contiguous(),
+                                   beta=d["prev_b"].reshape(n, L).to(**dev, dtype=torch.float32).contiguous(),
+                                   pos0=int(d["prev_pos"].reshape(-1)[0].item()))
         if d.get("cur_kp") is not None:
             st.cur_len = fill("cur", st.cur_slot)
             if st.cur_len >= C:
@@ -741,10 +760,27 @@ class Bolt3Decoder:
     def layer_step(ly: Bolt3Attn, st: Bolt3LayerState, h: torch.Tensor, pos_start: int,
                    m_res: torch.Tensor, partial_fp32: bool = False) -> torch.Tensor:
         """Attention branch of one Bolt-3 layer for t new tokens: returns o_proj(y) [b, t, D] bf16
-        (fp32 and unrounded with partial_fp32: a tensor-parallel shard's partial sum)."""
+        (fp32 and unrounded with partial_fp32: a tensor-parallel shard's partial sum). A step that
+        pushes the pending chunk past C tokens, and every step while such a chunk is in the window,
+        runs vsa_lm_b200/oversize.py's path (bolt3.py:355-363, 406-425)."""
+        if st.cur_len + h.shape[1] > ly.C or st.big_prev is not None:
+            Bolt3Decoder._check_step(ly, st, h, m_res)
+            return oversize.layer_step(ly, st, h, pos_start, m_res, partial_fp32, Bolt3Decoder._consolidate_ring)
         out = Bolt3Decoder._layer_launch(ly, st, h, pos_start, m_res, partial_fp32)
         Bolt3Decoder._layer_advance(ly, st, h.shape[1], pos_start, m_res)
         return out
+
+    @staticmethod
+    def _check_step(ly: Bolt3Attn, st: Bolt3LayerState, h: torch.Tensor, m_res: torch.Tensor) -> None:
+        b, t, D = h.shape
+        if b != st.B or h.device != m_res.device or not h.is_cuda:
+            raise ValueError(f"hidden states [{b}, {t}, {D}] on {h.device} do not match a state of {st.B} sequences "
+                             f"with M_res on {m_res.device}")
+        if h.device.index != torch.cuda.current_device():
+            raise RuntimeError(f"the step's tensors are on {h.device}; make that device current")
+        if not (m_res.dtype == torch.float32 and m_res.is_contiguous()
+                and tuple(m_res.shape) == (b, ly.HKV, ly.HD, ly.HD)):
+            raise ValueError(f"m_res must be a contiguous fp32 CUDA tensor [{b}, {ly.HKV}, {ly.HD}, {ly.HD}]")
 
     @staticmethod
     def _layer_launch(ly: Bolt3Attn, st: Bolt3LayerState, h: torch.Tensor, pos_start: int, m_res: torch.Tensor,
@@ -755,20 +791,11 @@ class Bolt3Decoder:
         for position dev_pos.ref and stays valid for dev_pos.span positions of the current chunk."""
         b, t, D = h.shape
         H, HKV, HD, C, G = ly.H, ly.HKV, ly.HD, ly.C, ly.G
-        if st.cur_len + t > C:
-            # The reference then lets the pending chunk grow past C and later consolidates a chunk of
-            # up to 2C-1 tokens (bolt3.py:355-363, 406-425); the native kernels hold chunks of at
-            # most C tokens and windows of two such chunks.
-            raise NotImplementedError(
-                f"a step of {t} tokens on top of {st.cur_len} pending ones exceeds one chunk ({C}); the native "
-                f"decoder consolidates chunks of exactly {C} tokens: split the step at the chunk boundary")
-        if b != st.B or h.device != m_res.device or not h.is_cuda:
-            raise ValueError(f"hidden states [{b}, {t}, {D}] on {h.device} do not match a state of {st.B} sequences "
-                             f"with M_res on {m_res.device}")
-        if h.device.index != torch.cuda.current_device():
-            raise RuntimeError(f"the step's tensors are on {h.device}; make that device current")
-        if not (m_res.dtype == torch.float32 and m_res.is_contiguous() and tuple(m_res.shape) == (b, HKV, HD, HD)):
-            raise ValueError(f"m_res must be a contiguous fp32 CUDA tensor [{b}, {HKV}, {HD}, {HD}]")
+        if st.cur_len + t > C or st.big_prev is not None:
+            # the native kernels hold windows of two chunks of at most C tokens (layer_step takes
+            # oversize chunks through vsa_lm_b200/oversize.py)
+            raise ValueError(f"a native launch needs a window of chunks of at most {C} tokens")
+        Bolt3Decoder._check_step(ly, st, h, m_res)
         if dev_pos is not None and (t != 1 or dev_pos.ref != pos_start or st.cur_len + dev_pos.span > C):
             raise ValueError("a device-position launch is a one-token step at its reference position whose span "
                              "stays within the chunk")
@@ -809,31 +836,37 @@ class Bolt3Decoder:
         """Host side of a Bolt-3 layer step whose kernels are enqueued: the pending chunk grows by t
         tokens, and a chunk that reaches C tokens consolidates the previous one into the bank and
         M_res (bolt3.py:406-425) and becomes the previous chunk."""
-        b, HKV, HD, C = st.B, ly.HKV, ly.HD, ly.C
-        c = st._consts
+        C = ly.C
         st.cur_len += t
         if st.cur_len >= C:                                                   # bolt3.py:406-425
             # errors of the previous chunk's kernels (their status copy finished long ago)
             st.status.check(block=True)
             if st.prev_slot >= 0:
-                p0 = st.prev_slot * C
-                skip = 0
-                if not st.sinks_set:
-                    st.sink_k.copy_(st.ring_kp[:, p0:p0 + N_SINKS])
-                    st.sink_v.copy_(st.ring_v[:, p0:p0 + N_SINKS])
-                    st.sinks_set = True
-                    skip = N_SINKS
-                bank = dict(st.bank)
-                bank["m_res"] = m_res.view(b * HKV, HD, HD)
-                K.consolidate(n_chains=b * HKV, hkv=HKV, HD=HD, bank=bank, init_blank=not st.has_bank,
-                              kr=st.ring_kr, kp=st.ring_kp, v=st.ring_v, beta=st.ring_b, chain_tokens=2 * C,
-                              token0=p0, step_tokens=C, skip0=skip, chunk_len=C,
-                              pos0=st.slot_pos[st.prev_slot] - p0, n_steps=1, kappa=c["kappa"],
-                              gamma=c["gamma"], inv_freq=c["inv_freq"], status=st.status)
-                nf = st.n_filled
-                st.n_filled = nf if nf >= ly.S else nf + min(ly.S - nf, C - skip)
+                Bolt3Decoder._consolidate_ring(ly, st, m_res, st._consts)
             st.prev_slot, st.cur_slot, st.cur_len = st.cur_slot, 1 - st.cur_slot, 0
             st.status.arm(f"Bolt-3 decode chunk ending at position {pos_start + t}")
+
+    @staticmethod
+    def _consolidate_ring(ly: Bolt3Attn, st: Bolt3LayerState, m_res: torch.Tensor, c: dict) -> None:
+        """The native consolidation of the previous chunk (C tokens in its ring slot) into the bank
+        and M_res; the first one also sets the sinks and leaves them out (bolt3.py:408-425)."""
+        b, HKV, HD, C = st.B, ly.HKV, ly.HD, ly.C
+        p0 = st.prev_slot * C
+        skip = 0
+        if not st.sinks_set:
+            st.sink_k.copy_(st.ring_kp[:, p0:p0 + N_SINKS])
+            st.sink_v.copy_(st.ring_v[:, p0:p0 + N_SINKS])
+            st.sinks_set = True
+            skip = N_SINKS
+        bank = dict(st.bank)
+        bank["m_res"] = m_res.view(b * HKV, HD, HD)
+        K.consolidate(n_chains=b * HKV, hkv=HKV, HD=HD, bank=bank, init_blank=not st.has_bank,
+                      kr=st.ring_kr, kp=st.ring_kp, v=st.ring_v, beta=st.ring_b, chain_tokens=2 * C,
+                      token0=p0, step_tokens=C, skip0=skip, chunk_len=C,
+                      pos0=st.slot_pos[st.prev_slot] - p0, n_steps=1, kappa=c["kappa"],
+                      gamma=c["gamma"], inv_freq=c["inv_freq"], status=st.status)
+        nf = st.n_filled
+        st.n_filled = nf if nf >= ly.S else nf + min(ly.S - nf, C - skip)
 
     @staticmethod
     def _anchor_attention(ly, cache: "AnchorKV", h: torch.Tensor, pos_start: int,
@@ -1210,7 +1243,15 @@ class DecodeGraph(_ChunkGraph):
     @torch.no_grad()
     def step(self, tokens: torch.Tensor, pos: int) -> torch.Tensor:
         """One token per sequence ([B, 1] ids on the device) at position pos; the final normed hidden
-        states [B, 1, D] (a static buffer)."""
+        states [B, 1, D] (a static buffer). While a layer's window holds a chunk of more than C
+        tokens (after an unaligned prompt slice) the steps run eagerly."""
+        if any(isinstance(st, Bolt3LayerState) and st.big_prev is not None for st in self.kv):
+            if self.next is not None and pos != self.next:
+                raise ValueError(f"decode steps must be consecutive: expected position {self.next}, got {pos}")
+            self.graph = self.out = None
+            h, _, _ = self.dec.step(tokens, pos, self.states, self.kv)
+            self.next = pos + 1
+            return h
         self.tok.copy_(tokens)
         return self._replay(pos)
 
