@@ -177,6 +177,18 @@ typedef struct bolt3_anchor_args {
 } bolt3_anchor_args;
 int bolt3_anchor_decode(const bolt3_anchor_args* a, void* stream);
 
+/* ---- RMSNorm of bf16 rows (the hybrid model's block, final and per-head q/k norms).
+ * Replaces LlamaRMSNorm.forward (vsa_lm/surgery.py:43-53) for bf16 inputs: y[r] = bf16(x[r] *
+ * rsqrt(mean(x[r]^2) + eps) * w), in fp32 inside; one kernel instead of torch's casts and norm.
+ * x: bf16 rows of D values, row r at x + r * x_stride (elements); y: bf16 [rows][D]; w: [D], bf16
+ * (w_fp32 = 0) or fp32 (w_fp32 = 1). D a multiple of 8 up to 4096; pointers 16-byte aligned. */
+typedef struct bolt3_rmsnorm_args {
+  const void* x; const void* w; void* y;
+  int64_t rows; int64_t x_stride;
+  int D; int w_fp32; float eps;
+} bolt3_rmsnorm_args;
+int bolt3_rmsnorm(const bolt3_rmsnorm_args* a, void* stream);
+
 /* Bytes of snapshot workspace bolt3_prefill_fwd needs for n_chains chains of T tokens. */
 size_t bolt3_prefill_workspace_size(int n_chains, int64_t T, int HD);
 
@@ -221,7 +233,8 @@ int bolt3_prefill_fwd_noalloc(const bolt3_prefill_args* a, void* stream);
 /* ---- utilities */
 int bolt3_abi_version(void);
 const char* bolt3_status_string(int status);
-/* sizeof of an argument struct (0 prep, 1 consolidate, 2 attend, 3 prefill, 4 anchor; 0 for others), so a
+/* sizeof of an argument struct (0 prep, 1 consolidate, 2 attend, 3 prefill, 4 anchor, 5 rmsnorm; 0 for
+ * others), so a
  * binding can check its own layout of the structs against the compiled one */
 size_t bolt3_args_size(int which);
 /* Host-only: reorder indices 0..n-1 of `vals` into the order CPU torch.topk(vals, k, largest)

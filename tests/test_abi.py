@@ -32,10 +32,11 @@ def test_library_exports_every_declared_symbol():
 def test_struct_sizes_are_c_layout():
     # the ctypes mirrors have the compiled structs' sizes (a field added on one side only shows here)
     lib = _lib.load()
-    for i, st in enumerate((_lib.PrepArgs, _lib.ConsolidateArgs, _lib.AttendArgs, _lib.PrefillArgs, _lib.AnchorArgs)):
+    for i, st in enumerate((_lib.PrepArgs, _lib.ConsolidateArgs, _lib.AttendArgs, _lib.PrefillArgs, _lib.AnchorArgs,
+                            _lib.RMSNormArgs)):
         assert ctypes.sizeof(st) % 8 == 0
         assert lib.bolt3_args_size(i) == ctypes.sizeof(st), st.__name__
-    assert lib.bolt3_args_size(5) == 0
+    assert lib.bolt3_args_size(6) == 0
 
 
 def test_entry_points_reject_bad_arguments_without_a_gpu():
@@ -45,6 +46,11 @@ def test_entry_points_reject_bad_arguments_without_a_gpu():
     assert lib.bolt3_attend(None, None) == 1
     assert lib.bolt3_prefill_fwd(None, None) == 1
     assert lib.bolt3_anchor_decode(None, None) == 1
+    assert lib.bolt3_rmsnorm(None, None) == 1
+    rn = _lib.RMSNormArgs(x=16, w=32, y=48, rows=4, x_stride=100, D=100, eps=1e-6)
+    assert lib.bolt3_rmsnorm(ctypes.byref(rn), None) == 2          # D not a multiple of 8
+    rn.D, rn.x_stride, rn.y = 128, 128, 40
+    assert lib.bolt3_rmsnorm(ctypes.byref(rn), None) == 3          # misaligned output
     an = _lib.AnchorArgs(B=2, H=8, HKV=2, HD=128, q=16, k_new=32, v_new=48, k_cache=64, v_cache=80, cap=10, n=10,
                          y=96, scale=0.1)
     assert lib.bolt3_anchor_decode(ctypes.byref(an), None) == 4    # no room for the appended token

@@ -152,3 +152,20 @@ def test_generate_batch_graphs_equal_eager():
     a, la = Bolt3Decoder(model).generate_batch(ids, 150, temperature=0.0)
     b, lb = Bolt3Decoder(model, cuda_graphs=False).generate_batch(ids, 150, temperature=0.0)
     assert torch.equal(a, b) and torch.equal(la, lb)
+
+
+@pytest.mark.parametrize("rows,D,wdt", [(64, 2560, torch.bfloat16), (1000, 128, torch.bfloat16), (3, 64, torch.float32),
+                                        (130, 4096, torch.bfloat16)])
+def test_rmsnorm_kernel_matches_fp32_reference(rows, D, wdt):
+    """bolt3_rmsnorm against the fp32 formula of LlamaRMSNorm (surgery.py:43-53): within one bf16
+    rounding of the exact value."""
+    torch.manual_seed(rows)
+    x = (torch.randn(rows, D, device="cuda") * 3).bfloat16()
+    w = (1 + 0.1 * torch.randn(D, device="cuda")).to(wdt)
+    got = K.rmsnorm(x, w, 1e-6).float()
+    xf = x.float()
+    ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+    torch.testing.assert_close(got, ref, rtol=2 ** -7, atol=1e-6)
+    # a strided input (a slice of a wider row) gives the same result
+    wide = torch.cat([x, x[:, :8]], 1)
+    assert torch.equal(K.rmsnorm(wide[:, :D], w, 1e-6), K.rmsnorm(x, w, 1e-6))

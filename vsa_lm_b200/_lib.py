@@ -92,6 +92,14 @@ class AnchorArgs(ctypes.Structure):
     ]
 
 
+class RMSNormArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", _P), ("w", _P), ("y", _P),
+        ("rows", _I64), ("x_stride", _I64),
+        ("D", _I), ("w_fp32", _I), ("eps", _F),
+    ]
+
+
 class PrefillArgs(ctypes.Structure):
     _fields_ = [
         ("B", _I), ("T", _I), ("H", _I), ("HKV", _I), ("HD", _I),
@@ -114,6 +122,7 @@ SIGNATURES = {
     "bolt3_consolidate": ([ctypes.POINTER(ConsolidateArgs), _P], _I),
     "bolt3_attend": ([ctypes.POINTER(AttendArgs), _P], _I),
     "bolt3_anchor_decode": ([ctypes.POINTER(AnchorArgs), _P], _I),
+    "bolt3_rmsnorm": ([ctypes.POINTER(RMSNormArgs), _P], _I),
     "bolt3_prefill_fwd": ([ctypes.POINTER(PrefillArgs), _P], _I),
     "bolt3_prefill_fwd_noalloc": ([ctypes.POINTER(PrefillArgs), _P], _I),
     "bolt3_prefill_workspace_size": ([_I, _I64, _I], _SZ),
@@ -151,7 +160,7 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
             fn.restype = rest
         if lib.bolt3_abi_version() != ABI_VERSION:
             raise RuntimeError("libbolt3.so ABI version mismatch; rebuild with `python -m vsa_lm_b200.build`")
-        for i, st in enumerate((PrepArgs, ConsolidateArgs, AttendArgs, PrefillArgs, AnchorArgs)):
+        for i, st in enumerate((PrepArgs, ConsolidateArgs, AttendArgs, PrefillArgs, AnchorArgs, RMSNormArgs)):
             if lib.bolt3_args_size(i) != ctypes.sizeof(st):
                 raise RuntimeError(f"{st.__name__} has {ctypes.sizeof(st)} bytes here but "
                                    f"{lib.bolt3_args_size(i)} in libbolt3.so: the bindings and the header differ")

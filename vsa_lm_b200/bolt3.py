@@ -31,7 +31,8 @@ N_SINKS = 4
 
 class LlamaRMSNorm(nn.Module):
     """RMSNorm computed in fp32 and cast back to the input dtype; parameter `weight` as in the
-    reference (surgery.py:43-53), so checkpoints load."""
+    reference (surgery.py:43-53), so checkpoints load. bf16 CUDA inputs (outside autograd) take the
+    one-kernel bolt3_rmsnorm."""
 
     def __init__(self, dim: int, eps: float = 1e-5):
         super().__init__()
@@ -39,6 +40,9 @@ class LlamaRMSNorm(nn.Module):
         self.eps = eps
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if (x.is_cuda and x.dtype == torch.bfloat16 and x.shape[-1] % 8 == 0 and x.shape[-1] <= 4096
+                and not (torch.is_grad_enabled() and (x.requires_grad or self.weight.requires_grad))):
+            return K.rmsnorm(x, self.weight, self.eps)       # one kernel (csrc/rmsnorm.cu)
         out = F.rms_norm(x.float(), (x.shape[-1],), self.weight.float(), self.eps)
         return out.to(x.dtype)
 

@@ -42,6 +42,7 @@ extern "C" size_t bolt3_args_size(int which) {
     case 2: return sizeof(bolt3_attend_args);
     case 3: return sizeof(bolt3_prefill_args);
     case 4: return sizeof(bolt3_anchor_args);
+    case 5: return sizeof(bolt3_rmsnorm_args);
     default: return 0;
   }
 }

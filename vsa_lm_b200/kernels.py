@@ -350,6 +350,28 @@ def _set_dev_pos(a, dev_pos: "DevicePosition | None") -> None:
         a.pos_dev, a.pos_ref, a.pos_span = dev_pos.word.data_ptr(), dev_pos.ref, dev_pos.span
 
 
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """bolt3_rmsnorm: RMSNorm over the last dimension of bf16 `x` with weight `w` [D] (bf16 or fp32),
+    fp32 inside, one bf16 rounding of the result. Returns a new tensor shaped like x."""
+    D = x.shape[-1]
+    if not isinstance(x, torch.Tensor) or not x.is_cuda or x.dtype != torch.bfloat16:
+        raise TypeError("x must be a bf16 CUDA tensor (the Bolt-3 path has no CPU implementation)")
+    if x.device.index != torch.cuda.current_device():
+        raise RuntimeError(f"x is on {x.device}, but the current device is cuda:{torch.cuda.current_device()}")
+    if w.dtype not in (torch.bfloat16, torch.float32) or w.numel() != D or w.device != x.device:
+        raise ValueError(f"the weight must be [{D}] bf16 or fp32 on {x.device}")
+    x2 = x.reshape(-1, D)
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    wc = w.contiguous()
+    y = torch.empty(x2.shape[0], D, dtype=torch.bfloat16, device=x.device)
+    a = _lib.RMSNormArgs(x=x2.data_ptr(), w=wc.data_ptr(), y=y.data_ptr(), rows=x2.shape[0], x_stride=x2.stride(0),
+                         D=D, w_fp32=int(wc.dtype == torch.float32), eps=eps)
+    _lib.check(_lib.load().bolt3_rmsnorm(ctypes.byref(a), _stream()), "bolt3_rmsnorm")
+    _count(1)
+    return y.view(x.shape)
+
+
 def anchor_decode(*, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor,
                   v_cache: torch.Tensor, n: int, y: torch.Tensor, scale: float, status=None,
                   dev_pos: DevicePosition | None = None) -> None:
