@@ -465,7 +465,9 @@ def run_full_model(args, rank, world, dev):
             else:
                 h, states, kv = dec.step(nxt, T + i, states, kv)
             logits = model.lm_head(h[:, -1, :])
-        captures[0] = runner.captures if runner is not None else 0
+        if runner is not None:
+            captures[0] = runner.captures
+            runner.close()          # its graphs hold NCCL calls under torchrun: released before teardown
         return logits
 
     def ev():

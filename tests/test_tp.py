@@ -163,6 +163,10 @@ def _run_model_worker(tmp_path, backend: str, nproc: int):
     res = torch.load(out, weights_only=False)
     assert res["world"] == nproc
     output_close(res["got"], res["ref"], f"{nproc}-rank tensor-parallel model over {backend}")
+    if backend == "nccl":       # graph replay (captured NCCL all-reduces) equals the eager steps
+        assert res["graphed"] is not None and torch.equal(res["graphed"], res["got"])
+    else:                       # gloo all-reduces run on the host: no graphs
+        assert res["graphed"] is None
 
 
 @pytest.mark.gpu

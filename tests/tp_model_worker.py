@@ -24,6 +24,22 @@ from vsa_lm_b200.tp import Bolt3DecoderTP, Bolt3LMTP  # noqa: E402
 from vsa_lm_b200.workloads import MODEL_SHAPES, make_model_params  # noqa: E402
 
 
+def run_graphed(dec, ids, steps):
+    """The same as run() with the one-token steps replayed from CUDA graphs. The runner, whose graphs
+    hold captured NCCL all-reduces, is closed before this returns: a process group must not be
+    destroyed while such a graph exists."""
+    h, states, kv = dec.prefill(ids, max_kv_len=ids.shape[1] + steps.shape[1] + 8)
+    runner = dec.step_graph(states, kv)
+    try:
+        outs = [h[:, -1:]]
+        for i in range(steps.shape[1]):
+            outs.append(runner.step(steps[:, i:i + 1], ids.shape[1] + i).clone())
+        torch.cuda.synchronize()
+        return torch.cat(outs, 1).float().cpu()
+    finally:
+        runner.close()
+
+
 def run(dec, ids, steps):
     """Prefill ids [B, T], then one step per column of `steps` [B, n]; the hidden states of the
     prompt's last position and of every step, [B, 1 + n, D]."""
@@ -56,11 +72,15 @@ def main():
         ids = torch.randint(0, mcfg["vocab_size"], (B, T), generator=g).to(dev)
         steps = torch.randint(0, mcfg["vocab_size"], (B, n), generator=g).to(dev)
         tp = Bolt3LMTP(model)
-        got = run(Bolt3DecoderTP(tp), ids, steps)
+        dec = Bolt3DecoderTP(tp)
+        got = run(dec, ids, steps)
+        # the same steps replayed from CUDA graphs (NCCL all-reduces captured in them), where the group
+        # allows it; they must equal the eager steps bit for bit
+        graphed = run_graphed(dec, ids, steps) if dec.graphs_supported(dev) else None
         torch.cuda.synchronize()
         if rank == 0:
             ref = run(Bolt3Decoder(model), ids, steps)
-            torch.save({"got": got, "ref": ref, "world": dist.get_world_size()}, args.out)
+            torch.save({"got": got, "ref": ref, "graphed": graphed, "world": dist.get_world_size()}, args.out)
         dist.barrier()
     finally:
         dist.destroy_process_group()

@@ -1030,6 +1030,8 @@ class Bolt3Decoder:
             else:
                 h, states, kv = self.step(nxt, T + i, states, kv)
             logits = self.model.lm_head(h[:, -1, :])
+        if runner is not None:
+            runner.close()
         return torch.cat(toks, dim=1), lengths
 
     @torch.no_grad()
@@ -1061,6 +1063,8 @@ class Bolt3Decoder:
                 h, states, kv_caches = self.step(nxt, pos, states, kv_caches)
             logits = self.model.lm_head(h[:, -1, :])
             pos += 1
+        if runner is not None:
+            runner.close()
         out = torch.cat(toks, dim=1) if toks else torch.empty(ids.shape[0], 0, dtype=torch.long, device=ids.device)
         return out, states, kv_caches, pos
 
@@ -1188,6 +1192,12 @@ class _ChunkGraph:
         main.wait_stream(side)
         self.graph, self.lo, self.hi = g, pos, pos + span
         self.captures += 1
+
+    def close(self) -> None:
+        """Release the captured graph (and its memory). A graph that holds NCCL collectives (a
+        tensor-parallel decoder's) must be released before its process group is destroyed."""
+        self.graph = self.out = None
+        self.lo = self.hi = -1
 
     def _replay(self, pos: int) -> torch.Tensor:
         if self.next is not None and pos != self.next:
