@@ -3,15 +3,17 @@
 // of each KV head over every cached key.
 //
 // Replaces the anchor branch of Bolt3Decoder.step for one new token (vsa_lm/config/bolt3.py:426-445:
-// StaticKV.append, then scaled_dot_product_attention over the cache with enable_gqa). The softmax
-// is exact (a running maximum and sum over key blocks, fp32 throughout); the output is rounded to
-// bf16 once.
+// StaticKV.append, then scaled_dot_product_attention over the cache with enable_gqa). Scores, the
+// running maxima and sums and the output accumulate in fp32; the output is rounded to bf16 once.
 //
-// HBM-bound: each (sequence, KV head) streams its n cached keys and values once. One CTA of 256
-// threads per (sequence, KV head) walks the cache in blocks of 256 keys: a thread per key for the
-// G scores (its whole key row requested at once), the block's probabilities to shared memory, then
-// the P.V product with each thread owning eight value columns of all G heads for a sixteenth of the
-// block's keys (HD = 128), every value row read as 16-byte pieces that a warp's lanes share out.
+// HBM-bound: each (sequence, KV head) streams its n cached keys and values once. One CTA of three
+// warps per (sequence, KV head) walks the cache in blocks of 48 keys, double-buffered in shared memory
+// by cp.async (16-byte pieces, chunk index XOR-swizzled by row so that ldmatrix reads are free of bank
+// conflicts); 48 KB of stages per CTA lets four CTAs share an SM, so the 512 CTAs of configs[3] run
+// in one wave with up to 192 KB per SM in flight. Each warp takes 16 keys of every block: the scores
+// S = Q.K^T and the product P.V are mma.sync m16n8k16 tiles (the G query rows padded to 16), P is
+// rounded to bf16 for the product as the flash attention of the reference's SDPA does, and every
+// warp keeps a running maximum, sum and output of its own keys; the three are merged once at the end.
 //
 // The cache length comes from the launch (n) or, for a step replayed from a CUDA graph, from the
 // device (n + *pos_dev - pos_ref), like the Bolt-3 kernels' device step position.
@@ -22,30 +24,35 @@ namespace {
 
 using namespace b3;
 
-constexpr int kThreads = 256;
-constexpr int kBlockKeys = 256;  // one key per thread per block
+constexpr int kWarps = 3;
+constexpr int kThreads = 32 * kWarps;
+constexpr int kKeysPerWarp = 16;
+constexpr int kBlockKeys = kWarps * kKeysPerWarp;   // 48
 constexpr int kMaxG = 8;
 
-template <int HD, int G>
+template <int HD>
 struct AnchorSmem {
-  static constexpr int CG = HD / 8;             // 8-column groups of a value row
-  static constexpr int NKG = kThreads / CG;     // key groups of the P.V product
-  static constexpr size_t floats = G * HD + G * kBlockKeys + 8 * G + NKG * G * HD;
+  static constexpr int kStage = kBlockKeys * HD * 2;      // bytes of one K (or V) block
+  // two stages of K and V; the final merge reuses them for the warps' partial outputs
+  static constexpr size_t bytes = 2 * 2 * (size_t)kStage;
+  static_assert((size_t)kWarps * kMaxG * HD * 4 + 2 * kWarps * kMaxG * 4 <= bytes, "merge area fits the stages");
 };
+
+// byte offset of 16-byte chunk c of row r in a [rows][HD] bf16 block, chunk index XOR-swizzled by row
+template <int HD>
+B3_DEV uint32_t sw_off(int r, int c) { return (uint32_t)(r * HD * 2 + ((c ^ (r & 7)) << 4)); }
 
 template <int HD, int G>
 __global__ void __launch_bounds__(kThreads) anchor_decode_kernel(const bolt3_anchor_args a) {
-  using L_ = AnchorSmem<HD, G>;
-  constexpr int CG = L_::CG, NKG = L_::NKG;
+  constexpr int CPR = HD / 8;                    // 16-byte chunks per row
+  constexpr int KS = HD / 16;                    // k16 steps of a dot product
+  constexpr int NT = HD / 8;                     // n8 tiles of an output row
+  constexpr uint32_t kStage = AnchorSmem<HD>::kStage;
   constexpr float kLog2e = 1.4426950408889634f;
-  extern __shared__ __align__(16) float smem[];
-  float* qs = smem;                         // [G][HD] query rows (fp32)
-  float* ps = qs + G * HD;                  // [G][kBlockKeys] probabilities of the block
-  float* red = ps + G * kBlockKeys;         // [8 warps][G] reductions
-  float* op = red + 8 * G;                  // [NKG][G][HD] partial outputs
-
+  extern __shared__ __align__(128) unsigned char smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int c = blockIdx.x;                 // (sequence, KV head)
+  const int grp = lane >> 2, tig = lane & 3;
+  const int c = blockIdx.x;                      // (sequence, KV head)
   const int b = c / a.HKV, kvh = c % a.HKV;
   int64_t n = a.n;
   if (a.pos_dev != nullptr) {
@@ -56,143 +63,163 @@ __global__ void __launch_bounds__(kThreads) anchor_decode_kernel(const bolt3_anc
     }
     n += d;
   }
-  const int64_t L = n + 1;                  // keys after the append
+  const int64_t L = n + 1;                       // keys after the append
   bf16* kc = reinterpret_cast<bf16*>(a.k_cache) + (int64_t)c * a.cap * HD;
   bf16* vc = reinterpret_cast<bf16*>(a.v_cache) + (int64_t)c * a.cap * HD;
 
   // append the new key and value at position n
-  if (tid < HD / 8) {
+  if (tid < CPR) {
     const uint4* kn = reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(a.k_new) + (int64_t)c * HD);
     const uint4* vn = reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(a.v_new) + (int64_t)c * HD);
     reinterpret_cast<uint4*>(kc + n * HD)[tid] = kn[tid];
     reinterpret_cast<uint4*>(vc + n * HD)[tid] = vn[tid];
   }
-  // the query rows of the G heads that read this KV head
-  const bf16* q = reinterpret_cast<const bf16*>(a.q) + ((int64_t)b * a.H + (int64_t)kvh * G) * HD;
-  for (int i = tid; i < G * HD; i += kThreads) qs[i] = bf2f(q[i]);
-  __syncthreads();  // the appended row and the query rows are visible to the whole block
+  __threadfence_block();
+  __syncthreads();  // the appended row is visible to the block's copies below
 
-  float m_run[G], l_run[G], acc[G][8];
+  const int64_t n_blk = (L + kBlockKeys - 1) / kBlockKeys;
+  auto issue = [&](int64_t blk) {
+    unsigned char* ks = smem + (blk & 1) * 2 * kStage;
+    unsigned char* vs = ks + kStage;
+    for (int i = tid; i < kBlockKeys * CPR; i += kThreads) {
+      const int r = i / CPR, ch = i % CPR;
+      const int64_t key = blk * kBlockKeys + r;
+      const bool ok = key < L;
+      const int64_t src = (ok ? key : 0) * HD + ch * 8;
+      cp_async16(ks + sw_off<HD>(r, ch), kc + src, ok);
+      cp_async16(vs + sw_off<HD>(r, ch), vc + src, ok);
+    }
+    cp_async_commit();
+  };
+  issue(0);
+  if (n_blk > 1) issue(1);
+
+  // the query rows as A fragments (rows 0..G-1 real, the rest zero): a0 / a2 of every k16 step
+  uint32_t qa[KS][2];
+  {
+    const bf16* q = reinterpret_cast<const bf16*>(a.q) + ((int64_t)b * a.H + (int64_t)kvh * G) * HD;
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m_run[g] = neg_inf();
-    l_run[g] = 0.f;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[g][e] = 0.f;
-  }
-  const int cg = tid % CG, kg = tid / CG;
-  for (int64_t k0 = 0; k0 < L; k0 += kBlockKeys) {
-    // -- scores: thread tid takes key k0 + tid; its whole key row is requested at once
-    const int64_t j = k0 + tid;
-    float s[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) s[g] = 0.f;
-    if (j < L) {
-      uint4 kr[HD / 8];
-#pragma unroll
-      for (int ch = 0; ch < HD / 8; ++ch) kr[ch] = reinterpret_cast<const uint4*>(kc + j * HD)[ch];
-#pragma unroll
-      for (int ch = 0; ch < HD / 8; ++ch) {
-        const uint32_t w[4] = {kr[ch].x, kr[ch].y, kr[ch].z, kr[ch].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 kf = unpack_bf16(w[e]);
-#pragma unroll
-          for (int g = 0; g < G; ++g) {
-            const float2 qf = *reinterpret_cast<const float2*>(&qs[g * HD + ch * 8 + 2 * e]);
-            s[g] = fmaf(qf.x, kf.x, s[g]);
-            s[g] = fmaf(qf.y, kf.y, s[g]);
-          }
-        }
+    for (int ks = 0; ks < KS; ++ks) {
+      if (grp < G) {
+        qa[ks][0] = *reinterpret_cast<const uint32_t*>(q + grp * HD + ks * 16 + tig * 2);
+        qa[ks][1] = *reinterpret_cast<const uint32_t*>(q + grp * HD + ks * 16 + 8 + tig * 2);
+      } else {
+        qa[ks][0] = qa[ks][1] = 0u;
       }
     }
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      s[g] = j < L ? __fmul_rn(s[g], a.scale) : neg_inf();
-      const float m = warp_max(s[g]);
-      if (lane == 0) red[warp * G + g] = m;
-    }
-    __syncthreads();
-    float alpha[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float bm = neg_inf();
-#pragma unroll
-      for (int w = 0; w < 8; ++w) bm = fmaxf(bm, red[w * G + g]);
-      const float m_new = fmaxf(m_run[g], bm);   // finite: every block holds at least one key
-      alpha[g] = exp2f((m_run[g] - m_new) * kLog2e);
-      const float p = j < L ? exp2f((s[g] - m_new) * kLog2e) : 0.f;
-      ps[g * kBlockKeys + tid] = p;
-      m_run[g] = m_new;
-      s[g] = p;
-    }
-    __syncthreads();  // red is reused for the sums; ps is complete
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float sm = warp_sum(s[g]);
-      if (lane == 0) red[warp * G + g] = sm;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float bs = 0.f;
-#pragma unroll
-      for (int w = 0; w < 8; ++w) bs += red[w * G + g];
-      l_run[g] = fmaf(l_run[g], alpha[g], bs);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[g][e] *= alpha[g];
-    }
-    // -- P.V: thread (8-column group cg, key group kg) over keys kg, kg + NKG, ... of the block, a
-    // 16-byte load of the value row per key (a warp reads whole rows)
-    const int nb = L - k0 < kBlockKeys ? (int)(L - k0) : kBlockKeys;
-    constexpr int KPT = kBlockKeys / NKG;       // keys per thread per block
-    uint4 vr[KPT];
-#pragma unroll
-    for (int i = 0; i < KPT; ++i) {
-      const int kk = kg + i * NKG;
-      vr[i] = kk < nb ? reinterpret_cast<const uint4*>(vc + (k0 + kk) * HD)[cg] : make_uint4(0, 0, 0, 0);
-    }
-#pragma unroll
-    for (int i = 0; i < KPT; ++i) {
-      const int kk = kg + i * NKG;
-      const uint32_t w[4] = {vr[i].x, vr[i].y, vr[i].z, vr[i].w};
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float p = kk < nb ? ps[g * kBlockKeys + kk] : 0.f;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 vf = unpack_bf16(w[e]);
-          acc[g][2 * e] = fmaf(p, vf.x, acc[g][2 * e]);
-          acc[g][2 * e + 1] = fmaf(p, vf.y, acc[g][2 * e + 1]);
-        }
-      }
-    }
-    __syncthreads();  // ps and red are rewritten by the next block
   }
-  // -- the key groups' partial outputs summed, normalised and rounded once
+  const float sl2 = a.scale * kLog2e;             // scores in the log2 domain
+  float m_run = neg_inf(), l_run = 0.f;           // row grp of this warp's keys
+  float o[NT][4];
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float4* dst = reinterpret_cast<float4*>(&op[(kg * G + g) * HD + cg * 8]);
-    dst[0] = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
-    dst[1] = make_float4(acc[g][4], acc[g][5], acc[g][6], acc[g][7]);
+  for (int t = 0; t < NT; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
+
+  for (int64_t blk = 0; blk < n_blk; ++blk) {
+    if (blk + 1 < n_blk) cp_async_wait<1>();
+    else cp_async_wait<0>();
+    __syncthreads();  // block blk has landed for every thread
+    const unsigned char* ks_ = smem + (blk & 1) * 2 * kStage;
+    const unsigned char* vs_ = ks_ + kStage;
+    const int r0 = warp * kKeysPerWarp;           // this warp's 16 keys of the block
+    // -- S = Q K^T: two n8 tiles (keys r0..r0+7, r0+8..r0+15)
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int kst = 0; kst < KS; ++kst) {
+      uint32_t bfr[4];
+      const int m = lane >> 3;                    // matrix: (key half, dim half)
+      const int row = r0 + ((m >> 1) << 3) + (lane & 7);
+      const int ch = kst * 2 + (m & 1);
+      ldsm_x4(bfr, ks_ + sw_off<HD>(row, ch));
+      const uint32_t afr[4] = {qa[kst][0], 0u, qa[kst][1], 0u};
+      mma16816(sc[0], afr, bfr[0], bfr[1]);
+      mma16816(sc[1], afr, bfr[2], bfr[3]);
+    }
+    // -- running softmax of row grp over this warp's keys (the padding rows grp + 8 are not used)
+    const int64_t kbase = blk * kBlockKeys + r0;
+    float p[2][2];
+    float bm = neg_inf();
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int64_t key = kbase + t * 8 + tig * 2 + e;
+        p[t][e] = key < L ? __fmul_rn(sc[t][e], sl2) : neg_inf();
+        bm = fmaxf(bm, p[t][e]);
+      }
+    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 1));
+    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 2));
+    const float m_new = fmaxf(m_run, bm);
+    const float mref = m_new == neg_inf() ? 0.f : m_new;   // a warp whose keys are all past L so far
+    const float alpha = exp2f(m_run - mref);
+    float rs = 0.f;
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        p[t][e] = exp2f(p[t][e] - mref);
+        rs += p[t][e];
+      }
+    rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+    rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+    l_run = fmaf(l_run, alpha, rs);
+    m_run = m_new;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      o[t][0] *= alpha;
+      o[t][1] *= alpha;
+    }
+    // -- O += P V: P (bf16) as the A fragment of a k16 step over the warp's 16 keys
+    const uint32_t pa[4] = {pack_bf16(p[0][0], p[0][1]), 0u, pack_bf16(p[1][0], p[1][1]), 0u};
+#pragma unroll
+    for (int t2 = 0; t2 < NT / 2; ++t2) {
+      uint32_t bfr[4];
+      const int m = lane >> 3;                    // matrix: (key half, dim tile)
+      const int row = r0 + ((m & 1) << 3) + (lane & 7);
+      const int ch = t2 * 2 + (m >> 1);
+      ldsm_x4_t(bfr, vs_ + sw_off<HD>(row, ch));
+      mma16816(o[2 * t2], pa, bfr[0], bfr[1]);
+      mma16816(o[2 * t2 + 1], pa, bfr[2], bfr[3]);
+    }
+    __syncthreads();  // every warp is done with stage blk & 1 before it is refilled
+    if (blk + 2 < n_blk) issue(blk + 2);
+  }
+
+  // -- merge the warps' running states: m = max m_w, O = sum O_w 2^(m_w - m), l likewise
+  float* op = reinterpret_cast<float*>(smem);                 // [kWarps][kMaxG][HD]
+  float* ml = op + kWarps * kMaxG * HD;                       // [kWarps][kMaxG] maxima, then sums
+  if (grp < G) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      op[(warp * kMaxG + grp) * HD + t * 8 + tig * 2] = o[t][0];
+      op[(warp * kMaxG + grp) * HD + t * 8 + tig * 2 + 1] = o[t][1];
+    }
+    if (tig == 0) {
+      ml[warp * kMaxG + grp] = m_run;
+      ml[kWarps * kMaxG + warp * kMaxG + grp] = l_run;
+    }
   }
   __syncthreads();
   bf16* y = reinterpret_cast<bf16*>(a.y) + ((int64_t)b * a.H + (int64_t)kvh * G) * HD;
   for (int i = tid; i < G * HD; i += kThreads) {
     const int g = i / HD, e = i % HD;
-    float o = 0.f;
-    for (int k = 0; k < NKG; ++k) o += op[(k * G + g) * HD + e];
-    float lg = 0.f;
+    float m = neg_inf();
 #pragma unroll
-    for (int gg = 0; gg < G; ++gg)
-      if (gg == g) lg = l_run[gg];
-    y[i] = __float2bfloat16_rn(o / lg);
+    for (int w = 0; w < kWarps; ++w) m = fmaxf(m, ml[w * kMaxG + g]);
+    float acc = 0.f, l = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float mw = ml[w * kMaxG + g];
+      const float f = mw == neg_inf() ? 0.f : exp2f(mw - m);
+      acc = fmaf(op[(w * kMaxG + g) * HD + e], f, acc);
+      l = fmaf(ml[kWarps * kMaxG + w * kMaxG + g], f, l);
+    }
+    y[i] = __float2bfloat16_rn(acc / l);
   }
 }
 
 template <int HD, int G>
 int launch_g(const bolt3_anchor_args* a, cudaStream_t s) {
-  const size_t smem = sizeof(float) * AnchorSmem<HD, G>::floats;
+  const size_t smem = AnchorSmem<HD>::bytes;
   auto kern = anchor_decode_kernel<HD, G>;
   if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return BOLT3_ERR_CUDA;
