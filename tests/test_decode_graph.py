@@ -155,10 +155,11 @@ def test_generate_batch_graphs_equal_eager():
 
 
 @pytest.mark.parametrize("rows,D,wdt", [(64, 2560, torch.bfloat16), (1000, 128, torch.bfloat16), (3, 64, torch.float32),
-                                        (130, 4096, torch.bfloat16)])
+                                        (130, 4096, torch.bfloat16), (5, 2048, torch.float32),
+                                        (5000, 1024, torch.bfloat16)])
 def test_rmsnorm_kernel_matches_fp32_reference(rows, D, wdt):
     """bolt3_rmsnorm against the fp32 formula of LlamaRMSNorm (surgery.py:43-53): within one bf16
-    rounding of the exact value."""
+    rounding of the exact value (a warp per row, and a block per row for few wide rows)."""
     torch.manual_seed(rows)
     x = (torch.randn(rows, D, device="cuda") * 3).bfloat16()
     w = (1 + 0.1 * torch.randn(D, device="cuda")).to(wdt)
