@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define BOLT3_ABI_VERSION 7
+#define BOLT3_ABI_VERSION 8
 
 enum bolt3_status {
   BOLT3_OK = 0,
@@ -163,10 +163,13 @@ int bolt3_attend(const bolt3_attend_args* a, void* stream);
  * the cache append of vsa_lm/decode.py:88-106, then scaled_dot_product_attention with enable_gqa).
  * For every (sequence b, KV head): writes k_new / v_new at cache position n, then the exact softmax
  * attention of its G = H / HKV query heads over cache positions 0..n (scores q.k * scale in fp32),
- * y rounded to bf16 once. q: bf16 [B][H][HD] (RoPE applied); k_new, v_new: bf16 [B][HKV][HD];
- * k_cache, v_cache: bf16 [B][HKV][cap][HD]; y: bf16 [B][H][HD]. HD 64 or 128, G <= 8. With pos_dev
- * (the device step position of bolt3_prep) the position is n + *pos_dev - pos_ref, within
- * [n, n + pos_span); outside it the step is skipped and status gets 8. */
+ * y rounded to bf16 once. q: bf16 [B][H][HD]; k_new, v_new: bf16 [B][HKV][HD]; k_cache, v_cache:
+ * bf16 [B][HKV][cap][HD]; y: bf16 [B][H][HD]. HD 64 or 128, G <= 8. inv_freq NULL: q and k_new
+ * come with RoPE applied. inv_freq non-NULL (fp32 [HD/2]): the kernel applies rotate-half RoPE to q
+ * and k_new at position pos0 as LlamaRoPE does in bf16 (vsa_lm/surgery.py:80-93: cos and sin rounded
+ * to bf16, each product and the sum rounded to bf16). With pos_dev (the device step position of
+ * bolt3_prep), d = *pos_dev - pos_ref shifts both the cache position (n + d) and pos0 (pos0 + d),
+ * within [0, pos_span); outside it the step is skipped and status gets 8. */
 typedef struct bolt3_anchor_args {
   int B, H, HKV, HD;
   const void* q; const void* k_new; const void* v_new;
@@ -174,6 +177,7 @@ typedef struct bolt3_anchor_args {
   void* y; float scale;
   int32_t* status;                     /* optional device int (bit 8: device position out of range) */
   const int64_t* pos_dev; int64_t pos_ref; int64_t pos_span;
+  const float* inv_freq; int64_t pos0;  /* optional RoPE of q and k_new (see above) */
 } bolt3_anchor_args;
 int bolt3_anchor_decode(const bolt3_anchor_args* a, void* stream);
 

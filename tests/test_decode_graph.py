@@ -46,6 +46,33 @@ def test_anchor_decode_matches_fp32_reference(HD, G, n):
     torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2 * ref.pow(2).mean().sqrt().item())
 
 
+@pytest.mark.parametrize("HD,G", [(128, 4), (64, 2)])
+def test_anchor_decode_rope_in_kernel(HD, G):
+    """RoPE of q and the new key inside bolt3_anchor_decode (inv_freq, pos0) against LlamaRoPE applied
+    by torch before the call: the appended key within one bf16 rounding (the cos / sin come from a
+    different routine), the output within the attention tolerance."""
+    from vsa_lm_b200.bolt3 import LlamaRoPE
+
+    torch.manual_seed(HD + G)
+    B, HKV, cap, n, pos = 3, 2, 512, 300, 1234
+    rope = LlamaRoPE(HD, 1e6, None).cuda()
+    q = torch.randn(B, HKV * G, HD, device="cuda").bfloat16()
+    kn = torch.randn(B, HKV, HD, device="cuda").bfloat16()
+    vn = torch.randn(B, HKV, HD, device="cuda").bfloat16()
+    kc = torch.randn(B, HKV, cap, HD, device="cuda").bfloat16()
+    vc = torch.randn(B, HKV, cap, HD, device="cuda").bfloat16()
+    qr = rope(q.unsqueeze(2), pos_start=pos).squeeze(2)
+    kr = rope(kn.unsqueeze(2), pos_start=pos).squeeze(2)
+    ya, yb = torch.empty_like(q), torch.empty_like(q)
+    kca, kcb = kc.clone(), kc.clone()
+    K.anchor_decode(q=qr, k_new=kr, v_new=vn, k_cache=kca, v_cache=vc.clone(), n=n, y=ya, scale=HD ** -0.5)
+    K.anchor_decode(q=q, k_new=kn, v_new=vn, k_cache=kcb, v_cache=vc.clone(), n=n, y=yb, scale=HD ** -0.5,
+                    inv_freq=rope.inv_freq.float(), pos0=pos)
+    torch.testing.assert_close(kcb[:, :, n].float(), kca[:, :, n].float(), rtol=2 ** -7, atol=1e-6)
+    ref = ya.float()
+    torch.testing.assert_close(yb.float(), ref, rtol=2e-2, atol=2e-2 * ref.pow(2).mean().sqrt().item())
+
+
 def test_anchor_decode_device_position():
     """The same launch, built for position 40 with a span of 8, replayed at 40 + d from the device."""
     torch.manual_seed(5)

@@ -89,6 +89,7 @@ class AnchorArgs(ctypes.Structure):
         ("y", _P), ("scale", _F),
         ("status", _P),
         ("pos_dev", _P), ("pos_ref", _I64), ("pos_span", _I64),
+        ("inv_freq", _P), ("pos0", _I64),
     ]
 
 
@@ -132,7 +133,7 @@ SIGNATURES = {
     "bolt3_topk_order_host": ([_P, _I, _I, _I, _P], _I),
 }
 
-ABI_VERSION = 7   # BOLT3_ABI_VERSION in include/bolt3.h
+ABI_VERSION = 8   # BOLT3_ABI_VERSION in include/bolt3.h
 
 # Fixed scratch of bolt3_prefill_fwd_noalloc (BOLT3_NOALLOC_SCRATCH_BYTES in include/bolt3.h)
 NOALLOC_SCRATCH_BYTES = 32 << 20

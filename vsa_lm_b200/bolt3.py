@@ -885,15 +885,13 @@ class Bolt3Decoder:
         q, k, v = ly.head_qkv(h)
         if t == 1 and h.is_cuda and q.dtype == torch.bfloat16 and cache.buf.dtype == torch.bfloat16:
             if dev_pos is None:
-                q, k = ly.rope(q, pos_start=pos_start), ly.rope(k, pos_start=pos_start)
                 cache.reserve(1)
-            else:
-                posf = dev_pos.word.to(torch.float32)
-                q, k = ly.rope.forward_at(q, posf), ly.rope.forward_at(k, posf)
+            # RoPE of q and the new key inside the kernel, at pos_start (shifted with the device position)
             y = torch.empty(b, ly.H, ly.HD, dtype=torch.bfloat16, device=h.device)
             K.anchor_decode(q=q.reshape(b, ly.H, ly.HD).contiguous(), k_new=k.reshape(b, ly.HKV, ly.HD).contiguous(),
                             v_new=v.reshape(b, ly.HKV, ly.HD).contiguous(), k_cache=cache.k, v_cache=cache.v,
-                            n=cache.n, y=y, scale=ly.HD ** -0.5, dev_pos=dev_pos)
+                            n=cache.n, y=y, scale=ly.HD ** -0.5, dev_pos=dev_pos,
+                            inv_freq=_fp32_inv_freq(ly.rope, h.device), pos0=pos_start)
             if dev_pos is None:
                 cache.n += 1
             y = y.view(b, 1, ly.H * ly.HD)
@@ -1099,6 +1097,18 @@ class Bolt3Decoder:
             decay = ly.gamma_delta().to(delta.device).view(1, -1, 1, 1) ** k
             states[li] = (states[li] - decay * delta).contiguous()
         return states
+
+
+def _fp32_inv_freq(rope: "LlamaRoPE", device) -> torch.Tensor:
+    """The RoPE module's frequencies as a contiguous fp32 tensor on `device`, kept between calls (made
+    again when the buffer is replaced or changed in place): a kernel argument, not a per-step copy."""
+    t = rope.inv_freq
+    key = (t.data_ptr(), t._version, t.dtype, str(torch.device(device)))
+    cached = getattr(rope, "_fp32_cache", None)
+    if cached is None or cached[0] != key:
+        cached = (key, t.detach().to(device=device, dtype=torch.float32).contiguous())
+        rope._fp32_cache = cached
+    return cached[1]
 
 
 class AnchorKV:

@@ -33,9 +33,11 @@ constexpr int kMaxG = 8;
 template <int HD>
 struct AnchorSmem {
   static constexpr int kStage = kBlockKeys * HD * 2;      // bytes of one K (or V) block
-  // two stages of K and V; the final merge reuses them for the warps' partial outputs
-  static constexpr size_t bytes = 2 * 2 * (size_t)kStage;
-  static_assert((size_t)kWarps * kMaxG * HD * 4 + 2 * kWarps * kMaxG * 4 <= bytes, "merge area fits the stages");
+  // two stages of K and V (the final merge reuses them for the warps' partial outputs), then the RoPE
+  // cos / sin table
+  static constexpr size_t stages = 2 * 2 * (size_t)kStage;
+  static constexpr size_t bytes = stages + HD / 2 * 4;
+  static_assert((size_t)kWarps * kMaxG * HD * 4 + 2 * kWarps * kMaxG * 4 <= stages, "merge area fits the stages");
 };
 
 // byte offset of 16-byte chunk c of row r in a [rows][HD] bf16 block, chunk index XOR-swizzled by row
@@ -54,9 +56,9 @@ __global__ void __launch_bounds__(kThreads) anchor_decode_kernel(const bolt3_anc
   const int grp = lane >> 2, tig = lane & 3;
   const int c = blockIdx.x;                      // (sequence, KV head)
   const int b = c / a.HKV, kvh = c % a.HKV;
-  int64_t n = a.n;
+  int64_t n = a.n, d = 0;
   if (a.pos_dev != nullptr) {
-    const int64_t d = *a.pos_dev - a.pos_ref;
+    d = *a.pos_dev - a.pos_ref;
     if (d < 0 || d >= a.pos_span) {
       if (tid == 0 && a.status) atomicOr(a.status, 8);
       return;
@@ -66,13 +68,48 @@ __global__ void __launch_bounds__(kThreads) anchor_decode_kernel(const bolt3_anc
   const int64_t L = n + 1;                       // keys after the append
   bf16* kc = reinterpret_cast<bf16*>(a.k_cache) + (int64_t)c * a.cap * HD;
   bf16* vc = reinterpret_cast<bf16*>(a.v_cache) + (int64_t)c * a.cap * HD;
+  const bool rope = a.inv_freq != nullptr;
 
-  // append the new key and value at position n
-  if (tid < CPR) {
+  // bf16 cos / sin of the HD/2 frequencies at the token's position, as pairs of adjacent
+  // frequencies (the operands of the packed rotations below), after the stages
+  uint32_t* trig = reinterpret_cast<uint32_t*>(smem + AnchorSmem<HD>::stages);   // [HD/4] cos, [HD/4] sin
+  if (rope) {
+    if (tid < HD / 4) {
+      const float pos = (float)(a.pos0 + d);
+      float s0, c0, s1, c1;
+      sincosf(__fmul_rn(pos, a.inv_freq[2 * tid]), &s0, &c0);
+      sincosf(__fmul_rn(pos, a.inv_freq[2 * tid + 1]), &s1, &c1);
+      trig[tid] = pack_bf16(c0, c1);
+      trig[HD / 4 + tid] = pack_bf16(s0, s1);
+    }
+    __syncthreads();
+  }
+  // rotate-half RoPE of the packed bf16 pairs x1 (dims f, f+1 of the first half) and x2 (their partners
+  // HD/2 later) with the pair's cos / sin words: x1' = x1 c - x2 s, x2' = x2 c + x1 s, every product and
+  // sum rounded to bf16 (the same single roundings as LlamaRoPE's bf16 tensor arithmetic)
+  auto rot = [&](uint32_t& x1, uint32_t& x2, int fpair) {
+    const uint32_t cw = trig[fpair], sw = trig[HD / 4 + fpair];
+    const uint32_t n1 = add_bf16x2(mul_bf16x2(x1, cw), neg_bf16x2(mul_bf16x2(x2, sw)));
+    const uint32_t n2 = add_bf16x2(mul_bf16x2(x2, cw), mul_bf16x2(x1, sw));
+    x1 = n1;
+    x2 = n2;
+  };
+
+  // append the new key (rotated) and value at position n
+  if (tid < CPR / 2) {
     const uint4* kn = reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(a.k_new) + (int64_t)c * HD);
     const uint4* vn = reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(a.v_new) + (int64_t)c * HD);
-    reinterpret_cast<uint4*>(kc + n * HD)[tid] = kn[tid];
+    uint4 k1 = kn[tid], k2 = kn[tid + CPR / 2];     // dims 8 tid .. 8 tid + 7 and their partners
+    if (rope) {
+      rot(k1.x, k2.x, 4 * tid + 0);
+      rot(k1.y, k2.y, 4 * tid + 1);
+      rot(k1.z, k2.z, 4 * tid + 2);
+      rot(k1.w, k2.w, 4 * tid + 3);
+    }
+    reinterpret_cast<uint4*>(kc + n * HD)[tid] = k1;
+    reinterpret_cast<uint4*>(kc + n * HD)[tid + CPR / 2] = k2;
     reinterpret_cast<uint4*>(vc + n * HD)[tid] = vn[tid];
+    reinterpret_cast<uint4*>(vc + n * HD)[tid + CPR / 2] = vn[tid + CPR / 2];
   }
   __threadfence_block();
   __syncthreads();  // the appended row is visible to the block's copies below
@@ -107,7 +144,17 @@ __global__ void __launch_bounds__(kThreads) anchor_decode_kernel(const bolt3_anc
         qa[ks][0] = qa[ks][1] = 0u;
       }
     }
+    // RoPE: the partner of a fragment's dims (ks, offset) is (ks + KS/2, same offset), held by the
+    // same thread; frequency pair (16 ks + 2 tig) / 2 for a0, 8 more for a2
+    if (rope) {
+#pragma unroll
+      for (int ks = 0; ks < KS / 2; ++ks) {
+        rot(qa[ks][0], qa[ks + KS / 2][0], 8 * ks + tig);
+        rot(qa[ks][1], qa[ks + KS / 2][1], 8 * ks + 4 + tig);
+      }
+    }
   }
+
   const float sl2 = a.scale * kLog2e;             // scores in the log2 domain
   float m_run = neg_inf(), l_run = 0.f;           // row grp of this warp's keys
   float o[NT][4];

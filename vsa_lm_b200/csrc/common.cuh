@@ -32,6 +32,20 @@ B3_DEV float2 rbf2(float lo, float hi, uint32_t& packed) {
   return unpack_bf16(packed);
 }
 
+// ---- packed bf16 pair arithmetic, each result rounded to nearest even on its own (no contraction of
+// a multiply into a following add)
+B3_DEV uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+B3_DEV uint32_t add_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+B3_DEV uint32_t neg_bf16x2(uint32_t a) { return a ^ 0x80008000u; }
+
 // ---- warp reductions
 B3_DEV float warp_sum(float v) {
 #pragma unroll

@@ -16,20 +16,6 @@ namespace {
 
 using namespace b3;
 
-// Packed bf16 pair arithmetic, each result rounded to nearest even on its own (no contraction of a
-// multiply into a following add).
-B3_DEV uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.bf16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-B3_DEV uint32_t add_bf16x2(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("add.rn.bf16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-B3_DEV uint32_t neg_bf16x2(uint32_t a) { return a ^ 0x80008000u; }
-
 template <int HD, int TB>
 __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
   constexpr int LPR = HD / 8;          // lanes per head row

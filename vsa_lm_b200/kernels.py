@@ -374,10 +374,12 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 
 def anchor_decode(*, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor,
                   v_cache: torch.Tensor, n: int, y: torch.Tensor, scale: float, status=None,
-                  dev_pos: DevicePosition | None = None) -> None:
+                  dev_pos: DevicePosition | None = None, inv_freq: torch.Tensor | None = None,
+                  pos0: int = 0) -> None:
     """bolt3_anchor_decode: append k_new / v_new [B, HKV, HD] at cache position n (n + the device
     shift with dev_pos) of k_cache / v_cache [B, HKV, cap, HD] and write the one-token GQA attention
-    of q [B, H, HD] over positions 0..n to y [B, H, HD] (all bf16)."""
+    of q [B, H, HD] over positions 0..n to y [B, H, HD] (all bf16). With inv_freq (fp32 [HD/2]) the
+    kernel applies RoPE at position pos0 (shifted like n) to q and k_new first."""
     B, H, HD = q.shape
     HKV, cap = k_cache.shape[1], k_cache.shape[2]
     _need(q, torch.bfloat16, "q", B * H * HD)
@@ -388,9 +390,10 @@ def anchor_decode(*, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, 
         _need(t, torch.bfloat16, name, B * HKV * cap * HD)
     if tuple(k_cache.shape) != (B, HKV, cap, HD) or tuple(v_cache.shape) != (B, HKV, cap, HD):
         raise ValueError(f"caches must be [B, HKV, cap, HD] = [{B}, {HKV}, {cap}, {HD}]")
+    _opt(inv_freq, torch.float32, "inv_freq", HD // 2)
     a = _lib.AnchorArgs(B=B, H=H, HKV=HKV, HD=HD, q=q.data_ptr(), k_new=k_new.data_ptr(), v_new=v_new.data_ptr(),
                         k_cache=k_cache.data_ptr(), v_cache=v_cache.data_ptr(), cap=cap, n=n, y=y.data_ptr(),
-                        scale=scale, status=_status(status))
+                        scale=scale, status=_status(status), inv_freq=_ptr(inv_freq), pos0=pos0)
     _set_dev_pos(a, dev_pos)
     _lib.check(_lib.load().bolt3_anchor_decode(ctypes.byref(a), _stream()), "bolt3_anchor_decode")
     _count(1)
