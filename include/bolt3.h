@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define BOLT3_ABI_VERSION 8
+#define BOLT3_ABI_VERSION 9
 
 enum bolt3_status {
   BOLT3_OK = 0,
@@ -185,11 +185,15 @@ int bolt3_anchor_decode(const bolt3_anchor_args* a, void* stream);
  * Replaces LlamaRMSNorm.forward (vsa_lm/surgery.py:43-53) for bf16 inputs: y[r] = bf16(x[r] *
  * rsqrt(mean(x[r]^2) + eps) * w), in fp32 inside; one kernel instead of torch's casts and norm.
  * x: bf16 rows of D values, row r at x + r * x_stride (elements); y: bf16 [rows][D]; w: [D], bf16
- * (w_fp32 = 0) or fp32 (w_fp32 = 1). D a multiple of 8 up to 4096; pointers 16-byte aligned. */
+ * (w_fp32 = 0) or fp32 (w_fp32 = 1). D a multiple of 8 up to 4096; pointers 16-byte aligned.
+ * With r (bf16 [rows][D]) the row normalised is the residual sum s = bf16(x + r), each element added
+ * in fp32 and rounded once as torch's bf16 addition does, and s is written to sum (bf16 [rows][D]):
+ * the hybrid model's `x = x + branch; h = norm(x)` in one kernel. */
 typedef struct bolt3_rmsnorm_args {
   const void* x; const void* w; void* y;
   int64_t rows; int64_t x_stride;
   int D; int w_fp32; float eps;
+  const void* r; void* sum;             /* optional residual input and sum output (see above) */
 } bolt3_rmsnorm_args;
 int bolt3_rmsnorm(const bolt3_rmsnorm_args* a, void* stream);
 

@@ -24,7 +24,7 @@ def test_library_exports_every_declared_symbol():
     for n in names:
         assert hasattr(lib, n), f"{n} declared in include/bolt3.h but not exported"
         assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
-    assert lib.bolt3_abi_version() == _lib.ABI_VERSION == 8
+    assert lib.bolt3_abi_version() == _lib.ABI_VERSION == 9
     assert lib.bolt3_status_string(0) == b"ok"
     assert b"shape" in lib.bolt3_status_string(2)
 

@@ -197,3 +197,16 @@ def test_rmsnorm_kernel_matches_fp32_reference(rows, D, wdt):
     # a strided input (a slice of a wider row) gives the same result
     wide = torch.cat([x, x[:, :8]], 1)
     assert torch.equal(K.rmsnorm(wide[:, :D], w, 1e-6), K.rmsnorm(x, w, 1e-6))
+
+
+@pytest.mark.parametrize("rows,D", [(64, 2560), (1000, 128)])
+def test_add_rmsnorm_matches_torch(rows, D):
+    """The residual form of bolt3_rmsnorm: the sum equals torch's bf16 addition bit for bit, and the
+    norm equals bolt3_rmsnorm of that sum bit for bit."""
+    torch.manual_seed(rows + D)
+    x = (torch.randn(rows, D, device="cuda") * 2).bfloat16()
+    r = torch.randn(rows, D, device="cuda").bfloat16()
+    w = (1 + 0.1 * torch.randn(D, device="cuda")).bfloat16()
+    s, y = K.add_rmsnorm(x, r, w, 1e-6)
+    assert torch.equal(s, x + r)
+    assert torch.equal(y, K.rmsnorm(x + r, w, 1e-6))

@@ -98,6 +98,7 @@ class RMSNormArgs(ctypes.Structure):
         ("x", _P), ("w", _P), ("y", _P),
         ("rows", _I64), ("x_stride", _I64),
         ("D", _I), ("w_fp32", _I), ("eps", _F),
+        ("r", _P), ("sum", _P),
     ]
 
 
@@ -133,7 +134,7 @@ SIGNATURES = {
     "bolt3_topk_order_host": ([_P, _I, _I, _I, _P], _I),
 }
 
-ABI_VERSION = 8   # BOLT3_ABI_VERSION in include/bolt3.h
+ABI_VERSION = 9   # BOLT3_ABI_VERSION in include/bolt3.h
 
 # Fixed scratch of bolt3_prefill_fwd_noalloc (BOLT3_NOALLOC_SCRATCH_BYTES in include/bolt3.h)
 NOALLOC_SCRATCH_BYTES = 32 << 20

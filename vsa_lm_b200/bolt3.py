@@ -39,12 +39,23 @@ class LlamaRMSNorm(nn.Module):
         self.weight = nn.Parameter(torch.ones(dim))
         self.eps = eps
 
+    def _kernel_ok(self, x: torch.Tensor) -> bool:
+        return (x.is_cuda and x.dtype == torch.bfloat16 and x.shape[-1] % 8 == 0 and x.shape[-1] <= 4096
+                and not (torch.is_grad_enabled() and (x.requires_grad or self.weight.requires_grad)))
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        if (x.is_cuda and x.dtype == torch.bfloat16 and x.shape[-1] % 8 == 0 and x.shape[-1] <= 4096
-                and not (torch.is_grad_enabled() and (x.requires_grad or self.weight.requires_grad))):
+        if self._kernel_ok(x):
             return K.rmsnorm(x, self.weight, self.eps)       # one kernel (csrc/rmsnorm.cu)
         out = F.rms_norm(x.float(), (x.shape[-1],), self.weight.float(), self.eps)
         return out.to(x.dtype)
+
+    def add_forward(self, x: torch.Tensor, d: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """The residual update and the norm of its result, (x + d, norm(x + d)): one kernel for bf16
+        CUDA tensors (the sum rounded to bf16 as torch's bf16 addition rounds it)."""
+        if self._kernel_ok(x) and d.dtype == x.dtype and d.shape == x.shape:
+            return K.add_rmsnorm(x, d, self.weight, self.eps)
+        x = x + d
+        return x, self(x)
 
 
 def llama_inv_freq(head_dim: int, theta: float, rope_scaling: dict | None, device=None) -> torch.Tensor:
@@ -923,10 +934,11 @@ class Bolt3Decoder:
         """The step's computation. With dev_pos only the kernels are enqueued (a step captured into a
         CUDA graph: the position comes from the device, the host bookkeeping is _advance's)."""
         m = self.model
+        blocks = m.blocks
         with torch.autocast("cuda", torch.bfloat16, enabled=tokens.is_cuda):
             x = m.embed_tokens(tokens)
-            for li, blk in enumerate(m.blocks):
-                h = blk.norm1(x)
+            h = blocks[0].norm1(x)
+            for li, blk in enumerate(blocks):
                 if hasattr(blk, "vsa"):
                     if dev_pos is None:
                         attn = self.layer_step(blk.vsa, kv_caches[li], h, pos_start, states[li])
@@ -934,9 +946,11 @@ class Bolt3Decoder:
                         attn = self._layer_launch(blk.vsa, kv_caches[li], h, pos_start, states[li], dev_pos=dev_pos)
                 else:
                     attn = self._anchor_attention(blk.attn, kv_caches[li], h, pos_start, dev_pos=dev_pos)
-                x = x + attn.to(x.dtype)
-                x = x + blk.mlp(blk.norm2(x))
-            return m.norm(x)
+                # each residual update and the norm that reads its result are one kernel
+                x, h2 = blk.norm2.add_forward(x, attn.to(x.dtype))
+                nxt = blocks[li + 1].norm1 if li + 1 < len(blocks) else m.norm
+                x, h = nxt.add_forward(x, blk.mlp(h2).to(x.dtype))
+            return h
 
     def _advance(self, t: int, pos_start: int, states, kv_caches) -> None:
         """Host bookkeeping of a step whose kernels ran without it (a CUDA-graph replay)."""

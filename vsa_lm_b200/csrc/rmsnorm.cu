@@ -16,6 +16,18 @@ using namespace b3;
 
 constexpr int kWarps = 8;
 
+// x + r for eight bf16 pairs: each element added in fp32 and rounded to bf16 once (torch's bf16 add)
+B3_DEV uint4 add_round(const uint4 x, const uint4 r) {
+  const uint32_t xw[4] = {x.x, x.y, x.z, x.w}, rw[4] = {r.x, r.y, r.z, r.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 a = unpack_bf16(xw[e]), b = unpack_bf16(rw[e]);
+    o[e] = pack_bf16(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 template <int MAXV, bool WF32>
 __global__ void __launch_bounds__(32 * kWarps) rmsnorm_kernel(const bolt3_rmsnorm_args a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -25,10 +37,16 @@ __global__ void __launch_bounds__(32 * kWarps) rmsnorm_kernel(const bolt3_rmsnor
   const uint4* xr = reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(a.x) + row * a.x_stride);
   uint4 u[MAXV];
   float ss = 0.f;
+  const uint4* rr = a.r ? reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(a.r) + row * a.D) : nullptr;
+  uint4* sr = a.r ? reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(a.sum) + row * a.D) : nullptr;
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
     const int c = lane + 32 * i;
     u[i] = c < nv ? xr[c] : make_uint4(0, 0, 0, 0);
+    if (rr != nullptr && c < nv) {
+      u[i] = add_round(u[i], rr[c]);
+      sr[c] = u[i];
+    }
     const uint32_t w4[4] = {u[i].x, u[i].y, u[i].z, u[i].w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -82,10 +100,16 @@ __global__ void __launch_bounds__(256) rmsnorm_row_kernel(const bolt3_rmsnorm_ar
   const uint4* xr = reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(a.x) + row * a.x_stride);
   uint4 u[MAXC];
   float ss = 0.f;
+  const uint4* rr = a.r ? reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(a.r) + row * a.D) : nullptr;
+  uint4* sr = a.r ? reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(a.sum) + row * a.D) : nullptr;
 #pragma unroll
   for (int i = 0; i < MAXC; ++i) {
     const int c = tid + 256 * i;
     u[i] = c < nv ? xr[c] : make_uint4(0, 0, 0, 0);
+    if (rr != nullptr && c < nv) {
+      u[i] = add_round(u[i], rr[c]);
+      sr[c] = u[i];
+    }
     const uint32_t w4[4] = {u[i].x, u[i].y, u[i].z, u[i].w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -146,6 +170,8 @@ extern "C" int bolt3_rmsnorm(const bolt3_rmsnorm_args* a, void* stream) {
   if (a->rows < 0 || a->D <= 0 || a->D % 8 || a->D > 32 * 8 * 16 || a->x_stride < a->D) return BOLT3_ERR_SHAPE;
   if (a->rows == 0) return BOLT3_OK;
   if ((uintptr_t)a->x % 16 || (uintptr_t)a->y % 16 || (uintptr_t)a->w % 16 || a->x_stride % 8) return BOLT3_ERR_ALIGN;
+  if ((a->r == nullptr) != (a->sum == nullptr)) return BOLT3_ERR_ARG;
+  if (a->r && ((uintptr_t)a->r % 16 || (uintptr_t)a->sum % 16)) return BOLT3_ERR_ALIGN;
   if (a->rows / kWarps >= 0x7fffffff) return BOLT3_ERR_SHAPE;
   cudaStream_t s = (cudaStream_t)stream;
   const int nv = a->D / 8;

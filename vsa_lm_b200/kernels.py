@@ -350,9 +350,21 @@ def _set_dev_pos(a, dev_pos: "DevicePosition | None") -> None:
         a.pos_dev, a.pos_ref, a.pos_span = dev_pos.word.data_ptr(), dev_pos.ref, dev_pos.span
 
 
+def add_rmsnorm(x: torch.Tensor, r: torch.Tensor, w: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """bolt3_rmsnorm with a residual: s = bf16(x + r) and RMSNorm(s) in one kernel. x and r are bf16
+    tensors of the same shape (r contiguous); returns (s, normed), both new tensors shaped like x."""
+    if not isinstance(r, torch.Tensor) or r.shape != x.shape or r.dtype != torch.bfloat16 or r.device != x.device:
+        raise ValueError(f"the residual must be a bf16 tensor shaped like x {tuple(x.shape)} on {x.device}")
+    return _rmsnorm(x, w, eps, r.contiguous())
+
+
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     """bolt3_rmsnorm: RMSNorm over the last dimension of bf16 `x` with weight `w` [D] (bf16 or fp32),
     fp32 inside, one bf16 rounding of the result. Returns a new tensor shaped like x."""
+    return _rmsnorm(x, w, eps, None)
+
+
+def _rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, r: torch.Tensor | None):
     D = x.shape[-1]
     if not isinstance(x, torch.Tensor) or not x.is_cuda or x.dtype != torch.bfloat16:
         raise TypeError("x must be a bf16 CUDA tensor (the Bolt-3 path has no CPU implementation)")
@@ -365,11 +377,12 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
         x2 = x2.contiguous()
     wc = w.contiguous()
     y = torch.empty(x2.shape[0], D, dtype=torch.bfloat16, device=x.device)
+    sm = torch.empty_like(y) if r is not None else None
     a = _lib.RMSNormArgs(x=x2.data_ptr(), w=wc.data_ptr(), y=y.data_ptr(), rows=x2.shape[0], x_stride=x2.stride(0),
-                         D=D, w_fp32=int(wc.dtype == torch.float32), eps=eps)
+                         D=D, w_fp32=int(wc.dtype == torch.float32), eps=eps, r=_ptr(r), sum=_ptr(sm))
     _lib.check(_lib.load().bolt3_rmsnorm(ctypes.byref(a), _stream()), "bolt3_rmsnorm")
     _count(1)
-    return y.view(x.shape)
+    return y.view(x.shape) if r is None else (sm.view(x.shape), y.view(x.shape))
 
 
 def anchor_decode(*, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor,

@@ -251,10 +251,11 @@ class Bolt3DecoderTP(Bolt3Decoder):
 
     def _blocks(self, tokens: torch.Tensor, pos_start: int, states, kv_caches, dev_pos=None) -> torch.Tensor:
         m = self.model
+        blocks = m.blocks
         with torch.autocast("cuda", torch.bfloat16, enabled=tokens.is_cuda):
             x = m.embed_tokens(tokens)
-            for li, blk in enumerate(m.blocks):
-                h = blk.norm1(x)
+            h = blocks[0].norm1(x)
+            for li, blk in enumerate(blocks):
                 if hasattr(blk, "vsa"):
                     if dev_pos is None:
                         part = self.layer_step(blk.vsa, kv_caches[li], h, pos_start, states[li], partial_fp32=True)
@@ -264,9 +265,10 @@ class Bolt3DecoderTP(Bolt3Decoder):
                 else:
                     part = self._anchor_attention(blk.attn, kv_caches[li], h, pos_start, partial_fp32=True,
                                                   dev_pos=dev_pos)
-                x = x + m.reduce(part, x.dtype)
-                x = x + m.reduce(mlp_partial(blk.mlp, blk.norm2(x)), x.dtype)
-            return m.norm(x)
+                x, h2 = blk.norm2.add_forward(x, m.reduce(part, x.dtype))
+                nxt = blocks[li + 1].norm1 if li + 1 < len(blocks) else m.norm
+                x, h = nxt.add_forward(x, m.reduce(mlp_partial(blk.mlp, h2), x.dtype))
+            return h
 
     def graphs_supported(self, device) -> bool:
         """CUDA graphs capture NCCL collectives; a gloo group's all-reduces run on the host."""
