@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define BOLT3_ABI_VERSION 9
+#define BOLT3_ABI_VERSION 10
 
 enum bolt3_status {
   BOLT3_OK = 0,
@@ -197,6 +197,16 @@ typedef struct bolt3_rmsnorm_args {
 } bolt3_rmsnorm_args;
 int bolt3_rmsnorm(const bolt3_rmsnorm_args* a, void* stream);
 
+/* ---- SwiGLU's elementwise step (the hybrid model's MLP, vsa_lm/surgery.py:202-211).
+ * gu: bf16 [rows][2I], the gate projection in columns [0, I) and the up projection in [I, 2I) (both
+ * projections as one GEMM); y: bf16 [rows][I] = bf16(bf16(silu(g)) * u), silu in fp32 as torch
+ * computes it. I a multiple of 8; pointers 16-byte aligned. */
+typedef struct bolt3_silu_mul_args {
+  const void* gu; void* y;
+  int64_t rows; int64_t I;
+} bolt3_silu_mul_args;
+int bolt3_silu_mul(const bolt3_silu_mul_args* a, void* stream);
+
 /* Bytes of snapshot workspace bolt3_prefill_fwd needs for n_chains chains of T tokens. */
 size_t bolt3_prefill_workspace_size(int n_chains, int64_t T, int HD);
 
@@ -241,8 +251,8 @@ int bolt3_prefill_fwd_noalloc(const bolt3_prefill_args* a, void* stream);
 /* ---- utilities */
 int bolt3_abi_version(void);
 const char* bolt3_status_string(int status);
-/* sizeof of an argument struct (0 prep, 1 consolidate, 2 attend, 3 prefill, 4 anchor, 5 rmsnorm; 0 for
- * others), so a
+/* sizeof of an argument struct (0 prep, 1 consolidate, 2 attend, 3 prefill, 4 anchor, 5 rmsnorm,
+ * 6 silu_mul; 0 for others), so a
  * binding can check its own layout of the structs against the compiled one */
 size_t bolt3_args_size(int which);
 /* Host-only: reorder indices 0..n-1 of `vals` into the order CPU torch.topk(vals, k, largest)

@@ -24,7 +24,7 @@ def test_library_exports_every_declared_symbol():
     for n in names:
         assert hasattr(lib, n), f"{n} declared in include/bolt3.h but not exported"
         assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
-    assert lib.bolt3_abi_version() == _lib.ABI_VERSION == 9
+    assert lib.bolt3_abi_version() == _lib.ABI_VERSION == 10
     assert lib.bolt3_status_string(0) == b"ok"
     assert b"shape" in lib.bolt3_status_string(2)
 
@@ -33,10 +33,10 @@ def test_struct_sizes_are_c_layout():
     # the ctypes mirrors have the compiled structs' sizes (a field added on one side only shows here)
     lib = _lib.load()
     for i, st in enumerate((_lib.PrepArgs, _lib.ConsolidateArgs, _lib.AttendArgs, _lib.PrefillArgs, _lib.AnchorArgs,
-                            _lib.RMSNormArgs)):
+                            _lib.RMSNormArgs, _lib.SiluMulArgs)):
         assert ctypes.sizeof(st) % 8 == 0
         assert lib.bolt3_args_size(i) == ctypes.sizeof(st), st.__name__
-    assert lib.bolt3_args_size(6) == 0
+    assert lib.bolt3_args_size(7) == 0
 
 
 def test_entry_points_reject_bad_arguments_without_a_gpu():
@@ -47,6 +47,9 @@ def test_entry_points_reject_bad_arguments_without_a_gpu():
     assert lib.bolt3_prefill_fwd(None, None) == 1
     assert lib.bolt3_anchor_decode(None, None) == 1
     assert lib.bolt3_rmsnorm(None, None) == 1
+    assert lib.bolt3_silu_mul(None, None) == 1
+    sm = _lib.SiluMulArgs(gu=16, y=32, rows=4, I=100)
+    assert lib.bolt3_silu_mul(ctypes.byref(sm), None) == 2         # I not a multiple of 8
     rn = _lib.RMSNormArgs(x=16, w=32, y=48, rows=4, x_stride=100, D=100, eps=1e-6)
     assert lib.bolt3_rmsnorm(ctypes.byref(rn), None) == 2          # D not a multiple of 8
     rn.D, rn.x_stride, rn.y = 128, 128, 40

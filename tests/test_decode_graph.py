@@ -210,3 +210,24 @@ def test_add_rmsnorm_matches_torch(rows, D):
     s, y = K.add_rmsnorm(x, r, w, 1e-6)
     assert torch.equal(s, x + r)
     assert torch.equal(y, K.rmsnorm(x + r, w, 1e-6))
+
+
+def test_swiglu_fused_equals_torch():
+    """LlamaMLP with the gate and up projections as one GEMM and the fused silu * up kernel against
+    torch's two projections, silu and product on the same bf16 weights (within one bf16 rounding: the
+    GEMMs may sum in another order), and its weights still the module's parameters afterwards."""
+    from vsa_lm_b200.model import LlamaMLP
+
+    torch.manual_seed(7)
+    mlp = LlamaMLP(dict(dim=256, intermediate=512)).cuda().bfloat16()
+    x = torch.randn(64, 256, device="cuda").bfloat16()
+    with torch.no_grad():
+        ref = torch.nn.functional.silu(mlp.gate_proj(x)) * mlp.up_proj(x)
+        got = mlp.act(x)
+        w = mlp._gate_up_weight()
+        assert w.data_ptr() == mlp.gate_proj.weight.data_ptr()
+        mlp.up_proj.weight.add_(1.0)                      # an in-place weight edit reaches the fused weight
+        ref2 = torch.nn.functional.silu(mlp.gate_proj(x)) * mlp.up_proj(x)
+        got2 = mlp.act(x)
+    torch.testing.assert_close(got.float(), ref.float(), rtol=2 ** -7, atol=1e-3)
+    torch.testing.assert_close(got2.float(), ref2.float(), rtol=2 ** -7, atol=1e-3)

@@ -102,6 +102,10 @@ class RMSNormArgs(ctypes.Structure):
     ]
 
 
+class SiluMulArgs(ctypes.Structure):
+    _fields_ = [("gu", _P), ("y", _P), ("rows", _I64), ("I", _I64)]
+
+
 class PrefillArgs(ctypes.Structure):
     _fields_ = [
         ("B", _I), ("T", _I), ("H", _I), ("HKV", _I), ("HD", _I),
@@ -125,6 +129,7 @@ SIGNATURES = {
     "bolt3_attend": ([ctypes.POINTER(AttendArgs), _P], _I),
     "bolt3_anchor_decode": ([ctypes.POINTER(AnchorArgs), _P], _I),
     "bolt3_rmsnorm": ([ctypes.POINTER(RMSNormArgs), _P], _I),
+    "bolt3_silu_mul": ([ctypes.POINTER(SiluMulArgs), _P], _I),
     "bolt3_prefill_fwd": ([ctypes.POINTER(PrefillArgs), _P], _I),
     "bolt3_prefill_fwd_noalloc": ([ctypes.POINTER(PrefillArgs), _P], _I),
     "bolt3_prefill_workspace_size": ([_I, _I64, _I], _SZ),
@@ -134,7 +139,7 @@ SIGNATURES = {
     "bolt3_topk_order_host": ([_P, _I, _I, _I, _P], _I),
 }
 
-ABI_VERSION = 9   # BOLT3_ABI_VERSION in include/bolt3.h
+ABI_VERSION = 10   # BOLT3_ABI_VERSION in include/bolt3.h
 
 # Fixed scratch of bolt3_prefill_fwd_noalloc (BOLT3_NOALLOC_SCRATCH_BYTES in include/bolt3.h)
 NOALLOC_SCRATCH_BYTES = 32 << 20
@@ -162,7 +167,8 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
             fn.restype = rest
         if lib.bolt3_abi_version() != ABI_VERSION:
             raise RuntimeError("libbolt3.so ABI version mismatch; rebuild with `python -m vsa_lm_b200.build`")
-        for i, st in enumerate((PrepArgs, ConsolidateArgs, AttendArgs, PrefillArgs, AnchorArgs, RMSNormArgs)):
+        for i, st in enumerate((PrepArgs, ConsolidateArgs, AttendArgs, PrefillArgs, AnchorArgs, RMSNormArgs,
+                                SiluMulArgs)):
             if lib.bolt3_args_size(i) != ctypes.sizeof(st):
                 raise RuntimeError(f"{st.__name__} has {ctypes.sizeof(st)} bytes here but "
                                    f"{lib.bolt3_args_size(i)} in libbolt3.so: the bindings and the header differ")

@@ -43,6 +43,7 @@ extern "C" size_t bolt3_args_size(int which) {
     case 3: return sizeof(bolt3_prefill_args);
     case 4: return sizeof(bolt3_anchor_args);
     case 5: return sizeof(bolt3_rmsnorm_args);
+    case 6: return sizeof(bolt3_silu_mul_args);
     default: return 0;
   }
 }

@@ -350,6 +350,21 @@ def _set_dev_pos(a, dev_pos: "DevicePosition | None") -> None:
         a.pos_dev, a.pos_ref, a.pos_span = dev_pos.word.data_ptr(), dev_pos.ref, dev_pos.span
 
 
+def silu_mul(gu: torch.Tensor) -> torch.Tensor:
+    """bolt3_silu_mul: bf16(bf16(silu(g)) * u) for gu = [..., 2I] holding the gate projection in the
+    first I columns and the up projection in the last I. Returns [..., I]."""
+    I2 = gu.shape[-1]
+    if I2 % 16:
+        raise ValueError(f"the gate/up width {I2} must be a multiple of 16")
+    g2 = gu.reshape(-1, I2)
+    _need(g2, torch.bfloat16, "gu")
+    y = torch.empty(*gu.shape[:-1], I2 // 2, dtype=torch.bfloat16, device=gu.device)
+    a = _lib.SiluMulArgs(gu=g2.data_ptr(), y=y.data_ptr(), rows=g2.shape[0], I=I2 // 2)
+    _lib.check(_lib.load().bolt3_silu_mul(ctypes.byref(a), _stream()), "bolt3_silu_mul")
+    _count(1)
+    return y
+
+
 def add_rmsnorm(x: torch.Tensor, r: torch.Tensor, w: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
     """bolt3_rmsnorm with a residual: s = bf16(x + r) and RMSNorm(s) in one kernel. x and r are bf16
     tensors of the same shape (r contiguous); returns (s, normed), both new tensors shaped like x."""

@@ -30,8 +30,35 @@ class LlamaMLP(nn.Module):
         self.up_proj = nn.Linear(D, I, bias=False)
         self.down_proj = nn.Linear(I, D, bias=False)
 
+    def _gate_up_weight(self) -> torch.Tensor:
+        """One [2I, D] weight whose halves are the gate and up parameters' own storage: the first call
+        moves the two parameters into it (no second copy of the weights), later calls return it as long
+        as the parameters still live there (a weight load copies into them in place; a replaced
+        parameter or a device move makes it again)."""
+        g, u = self.gate_proj.weight, self.up_proj.weight
+        w = getattr(self, "_gu", None)
+        if w is None or w.data_ptr() != g.data_ptr() or w[g.shape[0]:].data_ptr() != u.data_ptr() \
+                or w.dtype != g.dtype or w.device != g.device:
+            with torch.no_grad():
+                w = torch.cat([g, u], 0)
+                self.gate_proj.weight.data = w[:g.shape[0]]
+                self.up_proj.weight.data = w[g.shape[0]:]
+            self._gu = w
+        return w
+
+    def act(self, x):
+        """silu(gate_proj(x)) * up_proj(x): for bf16 CUDA inputs outside autograd the two projections
+        are one GEMM and the elementwise step one kernel (csrc/silu_mul.cu), with torch's roundings."""
+        g = self.gate_proj.weight
+        if (x.is_cuda and g.is_cuda and g.dtype == torch.bfloat16 and g.shape[0] % 8 == 0
+                and not (torch.is_grad_enabled() and (x.requires_grad or g.requires_grad))):
+            from . import kernels as K
+
+            return K.silu_mul(F.linear(x.to(g.dtype), self._gate_up_weight()))
+        return F.silu(self.gate_proj(x)) * self.up_proj(x)
+
     def forward(self, x):
-        return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
+        return self.down_proj(self.act(x))
 
 
 class SoftmaxAttn(nn.Module):

@@ -176,7 +176,7 @@ def _mm_fp32(x: torch.Tensor, lin: nn.Linear) -> torch.Tensor:
 def mlp_partial(mlp: LlamaMLP, x: torch.Tensor) -> torch.Tensor:
     """A column shard's share of the SwiGLU MLP: its intermediate features are complete, down_proj
     gives an fp32 partial sum."""
-    return _mm_fp32(F.silu(mlp.gate_proj(x)) * mlp.up_proj(x), mlp.down_proj)
+    return _mm_fp32(mlp.act(x), mlp.down_proj)
 
 
 def anchor_partial(attn: SoftmaxAttn, x: torch.Tensor) -> torch.Tensor:
