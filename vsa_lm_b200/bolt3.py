@@ -326,6 +326,7 @@ class Bolt3Attn(nn.Module):
         return y
 
     @torch.no_grad()
+    @K.traced("Bolt3Attn.forward")
     def _native_forward(self, x: torch.Tensor, partial_fp32: bool = False) -> torch.Tensor:
         """The forward on CUDA. partial_fp32: return o_proj's output in fp32, unrounded (a tensor-
         parallel shard's partial sum, rounded once after the all-reduce)."""
@@ -772,6 +773,7 @@ class Bolt3Decoder:
         return plan
 
     @staticmethod
+    @K.traced("Bolt3Decoder.layer_step")
     def layer_step(ly: Bolt3Attn, st: Bolt3LayerState, h: torch.Tensor, pos_start: int,
                    m_res: torch.Tensor, partial_fp32: bool = False) -> torch.Tensor:
         """Attention branch of one Bolt-3 layer for t new tokens: returns o_proj(y) [b, t, D] bf16
@@ -862,6 +864,7 @@ class Bolt3Decoder:
             st.status.arm(f"Bolt-3 decode chunk ending at position {pos_start + t}")
 
     @staticmethod
+    @K.traced("Bolt3Decoder.consolidate")
     def _consolidate_ring(ly: Bolt3Attn, st: Bolt3LayerState, m_res: torch.Tensor, c: dict) -> None:
         """The native consolidation of the previous chunk (C tokens in its ring slot) into the bank
         and M_res; the first one also sets the sinks and leaves them out (bolt3.py:408-425)."""
@@ -924,6 +927,7 @@ class Bolt3Decoder:
         return ly.o_proj(y)
 
     @torch.no_grad()
+    @K.traced("Bolt3Decoder.step")
     def step(self, tokens: torch.Tensor, pos_start: int, states, kv_caches, record=None):
         """Run t new tokens [b, t] at positions pos_start.. through every block; returns the final
         normed hidden states [b, t, D] and the (updated in place) state lists (bolt3.py:335-447)."""
@@ -1191,6 +1195,7 @@ class _ChunkGraph:
     def _body(self, pos: int) -> torch.Tensor: ...
     def _advance(self, pos: int) -> None: ...
 
+    @K.traced("DecodeGraph.capture")
     def _capture(self, pos: int) -> None:
         self.graph = self.out = None      # the previous graph and its private memory are released
         span = self.C - self._phase()
@@ -1223,6 +1228,7 @@ class _ChunkGraph:
         self.graph = self.out = None
         self.lo = self.hi = -1
 
+    @K.traced("DecodeGraph.replay")
     def _replay(self, pos: int) -> torch.Tensor:
         if self.next is not None and pos != self.next:
             raise ValueError(f"decode steps must be consecutive: expected position {self.next}, got {pos}")

@@ -72,7 +72,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if failed:
         raise RuntimeError(f"nvcc failed for {failed}")
     tmp = LIB + ".tmp"
-    subprocess.check_call([nvcc, *ARCH, "-shared", "-o", tmp, *objs])
+    # -ldl: the NVTX ranges load a profiler's injection library with dlopen when one is attached
+    subprocess.check_call([nvcc, *ARCH, "-shared", "-o", tmp, *objs, "-ldl"])
     os.replace(tmp, LIB)
     return LIB
 

@@ -1,6 +1,7 @@
 // C-ABI utilities and the two-phase prefill driver (consolidation scan, then attention).
 #include "../../include/bolt3.h"
 #include "common.cuh"
+#include "trace.h"
 #include "stl_select.h"
 
 namespace {
@@ -75,6 +76,7 @@ extern "C" size_t bolt3_prefill_workspace_size(int n_chains, int64_t T, int HD) 
 }
 
 extern "C" int bolt3_prefill_fwd(const bolt3_prefill_args* a, void* stream) {
+  const b3::TraceRange trace_range("bolt3_prefill_fwd");
   if (!a) return BOLT3_ERR_ARG;
   if (a->B <= 0 || a->T <= 0 || a->HKV <= 0 || a->H % a->HKV || (a->HD != 64 && a->HD != 128))
     return BOLT3_ERR_SHAPE;

@@ -19,6 +19,7 @@
 // device (n + *pos_dev - pos_ref), like the Bolt-3 kernels' device step position.
 #include "../../include/bolt3.h"
 #include "common.cuh"
+#include "trace.h"
 
 namespace {
 
@@ -288,6 +289,7 @@ int launch_hd(const bolt3_anchor_args* a, cudaStream_t s) {
 }  // namespace
 
 extern "C" int bolt3_anchor_decode(const bolt3_anchor_args* a, void* stream) {
+  const b3::TraceRange trace_range("bolt3_anchor_decode");
   if (!a || !a->q || !a->k_new || !a->v_new || !a->k_cache || !a->v_cache || !a->y) return BOLT3_ERR_ARG;
   if (a->B <= 0 || a->HKV <= 0 || a->H <= 0 || a->H % a->HKV || a->H / a->HKV > kMaxG) return BOLT3_ERR_SHAPE;
   if ((int64_t)a->B * a->HKV > 0x7fffffff) return BOLT3_ERR_SHAPE;

@@ -25,6 +25,7 @@
 // cp.async by every thread, and warpgroup 1 converts the fp32 M_res into the split operand.
 #include "../../include/bolt3.h"
 #include "common.cuh"
+#include "trace.h"
 #include "tc5.cuh"
 
 #include <cuda.h>
@@ -646,6 +647,7 @@ static bool encode_rows(CUtensorMap* m, const void* base, int hd, int64_t tokens
 int b3_attend_decode_launch(const bolt3_attend_args* a, cudaStream_t s);
 
 extern "C" int bolt3_attend(const bolt3_attend_args* a, void* stream) {
+  const b3::TraceRange trace_range("bolt3_attend");
   if (!a || !a->q_rope || !a->q_raw || !a->eta || !a->y || !a->kappa || !a->seg0_k || !a->seg0_v ||
       !a->seg1_k || !a->seg1_v)
     return BOLT3_ERR_ARG;

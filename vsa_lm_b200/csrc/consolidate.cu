@@ -19,6 +19,7 @@
 // (bolt3.py:133-134, 183).
 #include "../../include/bolt3.h"
 #include "common.cuh"
+#include "trace.h"
 #include "stl_select.h"
 #include "tc5.cuh"
 
@@ -997,6 +998,7 @@ int launch(const bolt3_consolidate_args& a, cudaStream_t s) {
 }  // namespace
 
 extern "C" int bolt3_consolidate(const bolt3_consolidate_args* a, void* stream) {
+  const b3::TraceRange trace_range("bolt3_consolidate");
   if (!a || !a->ak || !a->av || !a->mass || !a->util || !a->pm || !a->act || !a->m_res ||
       !a->n_filled || !a->kr || !a->kp || !a->v || !a->beta || !a->kappa || !a->gamma || !a->inv_freq)
     return BOLT3_ERR_ARG;

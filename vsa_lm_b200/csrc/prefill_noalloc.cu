@@ -13,6 +13,7 @@
 
 #include "../../include/bolt3.h"
 #include "common.cuh"
+#include "trace.h"
 
 namespace {
 
@@ -94,6 +95,7 @@ int scratch_in_current_context(void** out) {
 }  // namespace
 
 extern "C" int bolt3_prefill_fwd_noalloc(const bolt3_prefill_args* a, void* stream) {
+  const b3::TraceRange trace_range("bolt3_prefill_fwd_noalloc");
   if (!a) return BOLT3_ERR_ARG;
   if (a->B <= 0 || a->T <= 0 || a->HKV <= 0 || a->H % a->HKV || (a->HD != 64 && a->HD != 128))
     return BOLT3_ERR_SHAPE;

@@ -11,6 +11,7 @@
 // values with one shuffle. cos/sin are computed once per (token, frequency) into shared memory.
 #include "../../include/bolt3.h"
 #include "common.cuh"
+#include "trace.h"
 
 namespace {
 
@@ -217,6 +218,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const bolt3_prep_args a) {
 }  // namespace
 
 extern "C" int bolt3_prep(const bolt3_prep_args* a, void* stream) {
+  const b3::TraceRange trace_range("bolt3_prep");
   if (!a || !a->proj || !a->inv_freq) return BOLT3_ERR_ARG;
   if (a->parts < 1 || a->parts > 3) return BOLT3_ERR_ARG;
   if ((a->parts & 1) && (!a->q_raw || !a->q_rope || !a->eta)) return BOLT3_ERR_ARG;

@@ -9,6 +9,7 @@
 // block each instead (rmsnorm_row_kernel).
 #include "../../include/bolt3.h"
 #include "common.cuh"
+#include "trace.h"
 
 namespace {
 
@@ -166,6 +167,7 @@ void launch_v(const bolt3_rmsnorm_args* a, cudaStream_t s) {
 }  // namespace
 
 extern "C" int bolt3_rmsnorm(const bolt3_rmsnorm_args* a, void* stream) {
+  const b3::TraceRange trace_range("bolt3_rmsnorm");
   if (!a || !a->x || !a->w || !a->y) return BOLT3_ERR_ARG;
   if (a->rows < 0 || a->D <= 0 || a->D % 8 || a->D > 32 * 8 * 16 || a->x_stride < a->D) return BOLT3_ERR_SHAPE;
   if (a->rows == 0) return BOLT3_OK;

@@ -6,6 +6,7 @@
 // product rounded to bf16. HBM-bound elementwise work, 16-byte accesses.
 #include "../../include/bolt3.h"
 #include "common.cuh"
+#include "trace.h"
 
 #include <algorithm>
 
@@ -37,6 +38,7 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const bolt3_silu_mul_args
 }  // namespace
 
 extern "C" int bolt3_silu_mul(const bolt3_silu_mul_args* a, void* stream) {
+  const b3::TraceRange trace_range("bolt3_silu_mul");
   if (!a || !a->gu || !a->y) return BOLT3_ERR_ARG;
   if (a->rows < 0 || a->I <= 0 || a->I % 8) return BOLT3_ERR_SHAPE;
   if (a->rows == 0) return BOLT3_OK;

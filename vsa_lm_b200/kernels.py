@@ -38,6 +38,25 @@ def _count(n: int) -> None:
     _launches += n
 
 
+def traced(name: str):
+    """Decorator: run the function inside an NVTX range `name` (torch.cuda.nvtx, NVTX's default
+    domain, the one the C-ABI entry points write their own ranges to, so they nest). With no
+    profiler attached a push or pop costs a fraction of a microsecond."""
+    import functools
+    from torch.cuda import nvtx
+
+    def wrap(fn):
+        @functools.wraps(fn)
+        def run(*args, **kwargs):
+            nvtx.range_push(name)
+            try:
+                return fn(*args, **kwargs)
+            finally:
+                nvtx.range_pop()
+        return run
+    return wrap
+
+
 def _need(t: torch.Tensor, dtype: torch.dtype, name: str, numel: int | None = None) -> None:
     """`t` is a contiguous `dtype` tensor on the current CUDA device holding at least `numel`
     elements (when given)."""

@@ -203,6 +203,7 @@ def consolidate(ly, st, consts: dict, m_res: torch.Tensor, kr: torch.Tensor, kp:
 
 
 @torch.no_grad()
+@K.traced("oversize.layer_step")
 def layer_step(ly, st, h: torch.Tensor, pos_start: int, m_res: torch.Tensor, partial_fp32: bool,
                consolidate_ring) -> torch.Tensor:
     """A Bolt-3 decoder step whose window holds, or whose step makes, a chunk of more than C tokens.
