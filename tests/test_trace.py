@@ -4,7 +4,7 @@ The C side is observed through a test-only NVTX injection library (tests/nvtx_pr
 itself loads in a child process and that logs every push and pop; the entry points are called with
 null arguments, which open and close their range and return an error before any CUDA call, so this
 runs without a GPU. The GPU test checks the ranges of a real forward and of decode steps across a
-chunk boundary (a consolidation).
+second chunk boundary (position 256, the first consolidation).
 """
 import os
 import shutil
@@ -128,7 +128,7 @@ def test_forward_and_decode_ranges_nest(probe, tmp_path):
         "with torch.no_grad():\n"
         "    model(ids)\n"
         "dec = Bolt3Decoder(model, cuda_graphs=False)\n"
-        "toks, _ = dec.generate_batch(ids, 100, temperature=0.0)\n"
+        "toks, _ = dec.generate_batch(ids, 220, temperature=0.0)\n"
         "torch.cuda.synchronize()\n")
     lines = _run_probed(probe, code, tmp_path / "log.txt")
     assert _balanced(lines)
