@@ -1,8 +1,9 @@
 """KV-head tensor parallelism (vsa_lm_b200/tp.py): the shards' partial outputs sum to the full
 layer's output. CPU: two gloo ranks run the oracle on their shards and all-reduce; two gloo ranks
 split a softmax anchor by KV head and a SwiGLU MLP by feature. GPU: the native shards of one layer
-on one device, for the forward and the decode step; the whole hybrid model split over two ranks
-(gloo, one GPU; NCCL, two GPUs) against the unsharded decoder."""
+on one device, for the forward and the decode step; a Qwen3-4B-width softmax anchor and MLP split
+four and eight ways on one device; the whole hybrid model split over two ranks (gloo, one GPU;
+NCCL, two GPUs) against the unsharded decoder."""
 import os
 
 import pytest
@@ -12,7 +13,7 @@ import torch.multiprocessing as mp
 
 from helpers import BF16, bf16_module, oracle_cfg_of, oracle_params, output_close
 from oracle import Store, forward
-from vsa_lm_b200 import Bolt3Attn, Bolt3Decoder, Bolt3LayerState
+from vsa_lm_b200 import AnchorKV, Bolt3Attn, Bolt3Decoder, Bolt3LayerState
 from vsa_lm_b200.model import LlamaMLP, SoftmaxAttn
 from vsa_lm_b200.tp import anchor_partial, kv_head_range, mlp_partial, shard_by_kv_head, shard_mlp, shard_softmax_attn
 from vsa_lm_b200.workloads import layer_cfg, make_input, make_params
@@ -218,6 +219,42 @@ def test_tp_decode_shards_sum_to_layer():
         got = sum(Bolt3Decoder.layer_step(s, so, h, p, mr, partial_fp32=True) for s, (so, mr) in zip(shards, states))
         got = got.to(torch.bfloat16)
         output_close(got.cpu(), ref.float().cpu(), f"decode step at {p}")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [4, 8])
+def test_tp_anchor_and_mlp_shards_at_4b_widths(world):
+    """A Qwen3-4B-width softmax anchor (32 query heads, 8 KV heads, per-head q/k norms) and SwiGLU
+    MLP (9728 features) split `world` ways on one device, as Bolt3LMTP splits them: the anchors'
+    one-token decode kernel with 1-2 KV heads per shard and the MLP's gate/up GEMM and silu_mul at
+    9728 / world features. The shards' fp32 partial sums, rounded once, against the unsharded
+    modules over a prompt and six decode steps."""
+    torch.manual_seed(0)
+    cfg = dict(dim=2560, num_heads=32, num_kv_heads=8, head_dim=128, eps=1e-6, rope_theta=1e6, qk_norm=True)
+    attn = SoftmaxAttn(cfg)
+    with torch.no_grad():
+        attn.q_norm.weight.uniform_(0.5, 1.5)
+        attn.k_norm.weight.uniform_(0.5, 1.5)
+    attn = attn.to(device="cuda", dtype=torch.bfloat16).eval()
+    mlp = LlamaMLP(dict(dim=2560, intermediate=9728)).to(device="cuda", dtype=torch.bfloat16).eval()
+    B, prompt, steps = 4, 40, 6
+    g = torch.Generator(device="cuda").manual_seed(1)
+    x = torch.randn(B, prompt + steps, 2560, generator=g, device="cuda").to(torch.bfloat16)
+    with torch.no_grad():
+        shards = [shard_softmax_attn(attn, r, world) for r in range(world)]
+        assert {s.HKV for s in shards} == {8 // world} and all(s.G == 4 for s in shards)
+        caches = [AnchorKV(B, s.HKV, 256, s.HD, "cuda") for s in shards]
+        cache = AnchorKV(B, attn.HKV, 256, attn.HD, "cuda")
+        for p, n in [(0, prompt)] + [(prompt + i, 1) for i in range(steps)]:
+            h = x[:, p:p + n]
+            ref = Bolt3Decoder._anchor_attention(attn, cache, h, p)
+            got = sum(Bolt3Decoder._anchor_attention(s, c, h, p, partial_fp32=True) for s, c in zip(shards, caches))
+            output_close(got.to(torch.bfloat16), ref, f"anchor step at {p}, {world} shards")
+        mlps = [shard_mlp(mlp, r, world) for r in range(world)]
+        for h in (x[:, -1:], x[:, :prompt]):
+            ref = mlp(h)
+            got = sum(mlp_partial(m, h) for m in mlps)
+            output_close(got.to(torch.bfloat16), ref, f"MLP of {h.shape[1]} tokens, {world} shards")
 
 
 
