@@ -59,3 +59,30 @@ def test_anchor_cache_reserve_and_append():
     assert c.capacity == 512 and torch.equal(c.k[:, :, :200], k)
     c.reserve(10)
     assert c.capacity == 512                                  # room already there
+
+
+def test_layer_state_holds_what_state_bytes_counts(monkeypatch):
+    """A Bolt-3 layer's decode state allocates exactly Bolt3LayerState.bytes_per_sequence per
+    sequence, with M_res counted once: it is the caller's states[li], and the state's bank holds
+    no second copy. Decoder.state_bytes sums those over the Bolt-3 layers, plus the anchors' bf16
+    k and v per token. (The device status word is the one CUDA-only member; it is stubbed here.)"""
+    from vsa_lm_b200 import Bolt3Attn, Bolt3Decoder, Bolt3LayerState, kernels as K
+    from vsa_lm_b200.model import Bolt3LM
+    from vsa_lm_b200.workloads import MODEL_SHAPES, layer_cfg
+
+    monkeypatch.setattr(K, "DeviceStatus", lambda device: None)
+    m = Bolt3Attn(layer_cfg("tiny"))
+    B = 3
+    st = Bolt3LayerState(m, B, "cpu")
+    assert "m_res" not in st.bank
+    held = [st.ring_kr, st.ring_kp, st.ring_v, st.ring_b, st.sink_k, st.sink_v, *st.bank.values()]
+    m_res = B * m.HKV * m.HD * m.HD * 4
+    assert sum(t.numel() * t.element_size() for t in held) + m_res == B * Bolt3LayerState.bytes_per_sequence(m)
+
+    model = Bolt3LM(**dict(MODEL_SHAPES["tiny_lm"]))
+    fixed, per_token = Bolt3Decoder.state_bytes(model)
+    vsa = [b.vsa for b in model.blocks if hasattr(b, "vsa")]
+    anchors = [b.attn for b in model.blocks if not hasattr(b, "vsa")]
+    assert vsa and anchors
+    assert fixed == sum(Bolt3LayerState.bytes_per_sequence(ly) for ly in vsa)
+    assert per_token == sum(2 * a.HKV * a.HD * 2 for a in anchors)

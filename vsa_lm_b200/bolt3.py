@@ -504,7 +504,9 @@ class Bolt3LayerState:
         self.ring_b = torch.empty(n, 2 * self.C, dtype=torch.float32, device=device)
         self.sink_k = torch.empty(n, N_SINKS, self.HD, **bf)
         self.sink_v = torch.empty_like(self.sink_k)
-        self.bank = K.new_bank(n, self.HD, device)
+        # the bank without an M_res of its own: M_res is the caller's states[li], which every kernel
+        # call is given (a second [n, HD, HD] fp32 array here would never be read)
+        self.bank = K.new_bank(n, self.HD, device, m_res=False)
         self.slot_pos = [0, 0]
         self.cur_slot, self.cur_len = 0, 0
         self.prev_slot = -1

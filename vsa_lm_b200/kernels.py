@@ -570,13 +570,17 @@ def prefill_noalloc(*, B: int, T: int, H: int, HKV: int, HD: int, q_rope, q_raw,
     _count(2)
 
 
-def new_bank(n_chains: int, HD: int, device, S: int = S_SLOTS) -> dict:
-    """Uninitialised bank tensors (the consolidation kernel initialises them with init_blank)."""
+def new_bank(n_chains: int, HD: int, device, S: int = S_SLOTS, m_res: bool = True) -> dict:
+    """Uninitialised bank tensors (the consolidation kernel initialises them with init_blank).
+    m_res=False leaves out the [n_chains, HD, HD] fp32 M_res, for a holder whose M_res lives
+    elsewhere (a decoder's M_res is the caller's states[li]) and is put into the dict per call."""
     bf = dict(dtype=torch.bfloat16, device=device)
     f32 = dict(dtype=torch.float32, device=device)
-    return dict(ak=torch.empty(n_chains, S, HD, **bf), av=torch.empty(n_chains, S, HD, **bf),
+    bank = dict(ak=torch.empty(n_chains, S, HD, **bf), av=torch.empty(n_chains, S, HD, **bf),
                 ak_rope=torch.empty(n_chains, S, HD, **bf), mass=torch.empty(n_chains, S, **f32),
                 util=torch.empty(n_chains, S, **f32), pm=torch.empty(n_chains, S, **f32),
                 act=torch.zeros(n_chains, S, dtype=torch.uint8, device=device),
-                m_res=torch.zeros(n_chains, HD, HD, **f32),
                 n_filled=torch.zeros(n_chains, dtype=torch.int32, device=device))
+    if m_res:
+        bank["m_res"] = torch.zeros(n_chains, HD, HD, **f32)
+    return bank
