@@ -1,6 +1,7 @@
-"""bench.py's host-side measurement helpers, without a GPU: the clocks summary that goes into the
-bench line (median SM clock under load, the maximum, the throttle reasons seen while the timed
-region ran) and the PCI bus id that selects the GPU for nvidia-smi."""
+"""bench.py without a GPU: the clocks summary that goes into the bench line (median SM clock under
+load, the maximum, the throttle reasons seen while the timed region ran), the PCI bus id that
+selects the GPU for nvidia-smi, and the `--impl reference` arm end to end (one process, and two
+ranks under torchrun, where rank 0 alone prints)."""
 import types
 
 import torch
@@ -51,3 +52,40 @@ def test_pci_bus_id_in_nvidia_smi_form(monkeypatch):
     props = types.SimpleNamespace(pci_domain_id=0, pci_bus_id=0x1B, pci_device_id=0)
     monkeypatch.setattr(torch.cuda, "get_device_properties", lambda dev: props)
     assert bench.pci_bus_id(0) == "00000000:1B:00.0"
+
+
+def _reference_arm(launcher=()):
+    import json
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    cmd = [*launcher, os.path.join(root, "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "3",
+           "--cpu-tokens", "256", "--cpu-seconds", "1"]
+    if not launcher:
+        cmd = [sys.executable, *cmd]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=240, cwd=root)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    return [json.loads(ln) for ln in lines]
+
+
+def test_reference_arm_prints_one_line_with_the_contract_keys():
+    (line,) = _reference_arm()
+    assert line["impl"] == "reference" and line["unit"] == "tok/s" and line["value"] > 0
+    assert line["warmup"] >= 3 and line["higher_is_better"] is True and line["n_gpus"] == 1
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == line["value"]
+    assert line["cpu_baseline"]["cores"] >= 1
+    assert line["e2e"] == {"value": line["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert line["decode"]["value"] > 0 and line["config"]["workload"].startswith("configs[1]")
+
+
+def test_reference_arm_under_torchrun_prints_from_rank_0_only():
+    import os
+    import sys
+
+    launcher = (sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+                "--master-addr=127.0.0.1", f"--master-port={32700 + os.getpid() % 500}")
+    lines = _reference_arm(launcher=launcher)
+    assert len(lines) == 1 and lines[0]["n_gpus"] == 2
