@@ -71,6 +71,51 @@ def _gloo_anchor_mlp_worker(rank: int, world: int, port: int, out):
         dist.destroy_process_group()
 
 
+def _gloo_failing_rank_worker(rank: int, world: int, port: int, out, mode: str):
+    """Rank 1 fails on the host: it leaves between steps before its all-reduce ("dies") or never
+    joins the group ("absent"). Rank 0 reports what its next group call raised and how long it took."""
+    import time
+    from datetime import timedelta
+
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    if rank == 1 and mode == "absent":
+        return
+    t0 = time.monotonic()
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+        attn, mlp, x = _anchor_mlp()
+        with torch.no_grad():
+            ym = mlp_partial(shard_mlp(mlp, rank, world), x)
+        if rank == 1:
+            dist.destroy_process_group()
+            return
+        dist.all_reduce(ym, op=dist.ReduceOp.SUM)
+        out.put(("no error", time.monotonic() - t0))
+    except Exception as exc:  # noqa: BLE001
+        out.put((type(exc).__name__, time.monotonic() - t0))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode", ["dies", "absent"])
+def test_tp_rank_failure_ends_the_others_collective_with_an_error(mode):
+    """A tensor-parallel rank that leaves before its all-reduce, or never joins, makes the surviving
+    rank's next group call raise within the process group's short timeout instead of waiting for
+    good: the failure reaches the host, no GPU is involved."""
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = 33600 + os.getpid() % 500 + (0 if mode == "dies" else 500)
+    procs = [ctx.Process(target=_gloo_failing_rank_worker, args=(r, 2, port, out, mode)) for r in range(2)]
+    for p in procs:
+        p.start()
+    what, seconds = _get_while_alive(out, procs, deadline_s=120)
+    for p in procs:
+        p.join(timeout=60)
+    assert what != "no error", "the surviving rank's collective completed without its peer"
+    assert seconds < 60
+
+
 def _get_while_alive(q, procs, deadline_s: float):
     """The first item of `q`, polling in short waits; fails as soon as a rank has exited with an
     error or the deadline passes, instead of blocking on a rank that died."""
