@@ -1,7 +1,8 @@
-"""include/bolt3.h from a C host: a C99 program compiled with gcc against the header and linked to
-libbolt3.so. The C compiler's struct layouts must equal the library's (bolt3_args_size), the ABI
-version must match the header's, and the entry points must reject null arguments with
-BOLT3_ERR_ARG (no GPU needed: they return before any CUDA call)."""
+"""include/bolt3.h from a C or C++ host: one program compiled as C99 (gcc) and as C++17 (g++)
+against the header, pedantic with warnings as errors, and linked to libbolt3.so. The compiler's
+struct layouts must equal the library's (bolt3_args_size), the ABI version must match the
+header's, and the entry points must reject null arguments with BOLT3_ERR_ARG (no GPU needed: they
+return before any CUDA call)."""
 import os
 import shutil
 import subprocess
@@ -49,16 +50,18 @@ int main(void) {
 """
 
 
-def test_header_compiles_as_c_and_matches_the_library(tmp_path):
-    if shutil.which("gcc") is None:
-        pytest.skip("gcc is not here")
+@pytest.mark.parametrize("compiler,std,suffix", [("gcc", "-std=c99", "c"), ("g++", "-std=c++17", "cpp")])
+def test_header_compiles_and_matches_the_library(tmp_path, compiler, std, suffix):
+    if shutil.which(compiler) is None:
+        pytest.skip(f"{compiler} is not here")
     from vsa_lm_b200 import _lib
 
     _lib.load()                                   # builds the library if it is missing
-    src = tmp_path / "host.c"
+    src = tmp_path / f"host.{suffix}"
     src.write_text(C_SOURCE)
     exe = tmp_path / "host"
-    subprocess.check_call(["gcc", "-std=c99", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"), str(src),
-                           "-L", LIBDIR, "-lbolt3", f"-Wl,-rpath,{LIBDIR}", "-o", str(exe)])
+    subprocess.check_call([compiler, std, "-Wall", "-Wextra", "-pedantic", "-Werror", "-I",
+                           os.path.join(ROOT, "include"), str(src), "-L", LIBDIR, "-lbolt3",
+                           f"-Wl,-rpath,{LIBDIR}", "-o", str(exe)])
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0 and r.stdout.strip().endswith("OK"), r.stdout + r.stderr
